@@ -1,0 +1,290 @@
+"""B200 (sm_100a) grouped GEMM: Python mirror of the reference's C++ API.
+
+The names, argument meanings and error behaviour follow the reference header
+(reference include/grouped_gemm/grouped_gemm.cuh:9-132): functions that can fail return the
+cudaError_t value as an int (0 = success), ``prepare_problem_set`` is pure host code, and device
+buffers are passed as raw device pointers (ints). Every call goes through the C-ABI of
+``libgrouped_gemm_b200.so`` (include/grouped_gemm_b200.h); nothing here computes a GEMM.
+
+    import grouped_gemm_gpu_kernel_b200 as gg
+    probs = [gg.problem_from_tensors(A, B, C, D, alpha=1.0, beta=0.0), ...]
+    cfg = gg.KernelConfig(cta_m=128, cta_n=128, cta_k=64)
+    prep = gg.prepare_problem_set(probs, cfg, gg.SortMode.kByTiles)
+    ex = gg.GroupedGemmExecutor(); assert ex.build(prep, cfg) == 0; ex.run(stream)
+"""
+from __future__ import annotations
+
+import ctypes
+import enum
+from dataclasses import dataclass, field
+from typing import List, Optional, Sequence
+
+from . import capi
+
+__all__ = [
+    "SortMode", "ProblemDesc", "KernelConfig", "PreparedProblemSet", "OccupancyInfo", "GroupedGemmExecutor",
+    "prepare_problem_set", "sort_mode_name", "query_occupancy", "run_grouped_gemm_once",
+    "run_baseline_per_problem", "count_non_empty_problems", "partition", "ShardPiece", "problem_from_tensors",
+    "NATIVE_CONFIGS", "REFERENCE_CONFIGS", "selftest_wait_timeout", "capi",
+]
+
+
+class SortMode(enum.IntEnum):
+    kNone = 0
+    kByK = 1
+    kByTiles = 2
+    kByTilesThenK = 3
+
+
+@dataclass
+class ProblemDesc:
+    """D = alpha * A x B + beta * C; A m x k FP16, B k x n FP16, C/D m x n FP32, all row-major."""
+
+    m: int
+    n: int
+    k: int
+    a: Optional[int]
+    b: Optional[int]
+    c: Optional[int]
+    d: Optional[int]
+    lda: int
+    ldb: int
+    ldc: int
+    ldd: int
+    alpha: float = 1.0
+    beta: float = 0.0
+
+    def to_c(self) -> capi.GGProblem:
+        return capi.GGProblem(self.m, self.n, self.k, self.a or None, self.b or None, self.c or None, self.d or None,
+                              self.lda, self.ldb, self.ldc, self.ldd, self.alpha, self.beta)
+
+    @staticmethod
+    def from_c(p: capi.GGProblem) -> "ProblemDesc":
+        return ProblemDesc(p.m, p.n, p.k, p.a, p.b, p.c, p.d, p.lda, p.ldb, p.ldc, p.ldd, p.alpha, p.beta)
+
+
+@dataclass
+class KernelConfig:
+    cta_m: int = 64
+    cta_n: int = 64
+    cta_k: int = 16
+    threads: int = 256
+    persistent_ctas: int = 0
+    use_tensor_cores: bool = True
+
+    def to_c(self) -> capi.GGConfig:
+        return capi.GGConfig(self.cta_m, self.cta_n, self.cta_k, self.threads, self.persistent_ctas,
+                             1 if self.use_tensor_cores else 0)
+
+
+# The reference's three tile shapes (reference src/grouped_gemm.cu:67-81) and the sm_100a ones.
+REFERENCE_CONFIGS = (KernelConfig(64, 64, 16), KernelConfig(128, 64, 32), KernelConfig(64, 128, 32))
+NATIVE_CONFIGS = (KernelConfig(128, 128, 64), KernelConfig(128, 256, 64), KernelConfig(128, 64, 64))
+
+
+@dataclass
+class PreparedProblemSet:
+    sorted_problems: List[ProblemDesc] = field(default_factory=list)
+    sorted_to_original: List[int] = field(default_factory=list)
+    tile_offsets: List[int] = field(default_factory=list)
+    total_tiles: int = 0
+
+
+@dataclass
+class OccupancyInfo:
+    sm_count: int = 0
+    max_blocks_per_sm: int = 0
+    active_blocks_per_sm: int = 0
+    threads_per_block: int = 0
+    max_threads_per_sm: int = 0
+    warps_per_block: int = 0
+    max_warps_per_sm: int = 0
+    active_warps_per_sm: int = 0
+    max_registers_per_sm: int = 0
+    max_registers_per_block: int = 0
+    estimated_registers_per_thread: int = 0
+    estimated_registers_per_block: int = 0
+    registers_per_thread: int = 0
+    registers_per_block: int = 0
+    register_limited_blocks_per_sm: int = 0
+    static_shared_bytes: int = 0
+    dynamic_shared_bytes: int = 0
+    theoretical_occupancy: float = 0.0
+    using_tensor_cores: bool = False
+
+
+@dataclass
+class ShardPiece:
+    problem: int
+    row0: int
+    rows: int
+    col0: int
+    cols: int
+
+
+def _problems_array(problems: Sequence[ProblemDesc]):
+    arr = (capi.GGProblem * max(1, len(problems)))()
+    for i, p in enumerate(problems):
+        arr[i] = p.to_c()
+    return arr
+
+
+def _stream_ptr(stream) -> Optional[int]:
+    """Accepts None (legacy default stream), an int handle or a torch.cuda.Stream."""
+    if stream is None:
+        return None
+    if isinstance(stream, int):
+        return stream or None
+    return getattr(stream, "cuda_stream", None) or None
+
+
+def sort_mode_name(sort_mode: int) -> str:
+    return capi.load().gg_sort_mode_name(int(sort_mode)).decode()
+
+
+def prepare_problem_set(problems: Sequence[ProblemDesc], config: KernelConfig, sort_mode: int) -> PreparedProblemSet:
+    lib = capi.load()
+    count = len(problems)
+    src = _problems_array(problems)
+    dst = (capi.GGProblem * max(1, count))()
+    s2o = (ctypes.c_int * max(1, count))()
+    offs = (ctypes.c_int * (count + 1))()
+    total = ctypes.c_int(0)
+    cfg = config.to_c()
+    st = lib.gg_prepare(src, count, ctypes.byref(cfg), int(sort_mode), dst, s2o, offs, ctypes.byref(total))
+    if st != 0:
+        raise ValueError(f"gg_prepare failed with status {st}")
+    return PreparedProblemSet([ProblemDesc.from_c(dst[i]) for i in range(count)], list(s2o)[:count], list(offs),
+                              total.value)
+
+
+def query_occupancy(config: KernelConfig, info: Optional[OccupancyInfo] = None):
+    """Returns (status, OccupancyInfo)."""
+    o = capi.GGOccupancy()
+    cfg = config.to_c()
+    st = capi.load().gg_query_occupancy(ctypes.byref(cfg), ctypes.byref(o))
+    out = info if info is not None else OccupancyInfo()
+    if st == 0:
+        for name, _ in capi.GGOccupancy._fields_:
+            val = getattr(o, name)
+            setattr(out, name, bool(val) if name == "using_tensor_cores" else val)
+    return st, out
+
+
+class GroupedGemmExecutor:
+    """Owns the device problem table of one prepared set (reference src/grouped_gemm.cu:1085-1277)."""
+
+    def __init__(self):
+        self._lib = capi.load()
+        self._h = ctypes.c_void_p()
+        st = self._lib.gg_executor_create(ctypes.byref(self._h))
+        if st != 0:
+            raise MemoryError(f"gg_executor_create failed with status {st}")
+
+    def close(self):
+        if self._h:
+            self._lib.gg_executor_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def build(self, prepared: PreparedProblemSet, config: KernelConfig) -> int:
+        if not self._h:
+            return capi.CUDA_ERROR_INVALID_DEVICE_POINTER
+        count = len(prepared.sorted_problems)
+        arr = _problems_array(prepared.sorted_problems)
+        offs = (ctypes.c_int * max(1, len(prepared.tile_offsets)))(*prepared.tile_offsets)
+        cfg = config.to_c()
+        return self._lib.gg_executor_build(self._h, arr, count, offs, len(prepared.tile_offsets),
+                                           int(prepared.total_tiles), ctypes.byref(cfg))
+
+    def run(self, stream=None) -> int:
+        if not self._h:
+            return capi.CUDA_ERROR_INVALID_DEVICE_POINTER
+        return self._lib.gg_executor_run(self._h, _stream_ptr(stream))
+
+    def status(self) -> int:
+        """Synchronises and returns (then clears) the GG_STATUS_* bits raised by this executor."""
+        out = ctypes.c_int(0)
+        st = self._lib.gg_executor_status(self._h, ctypes.byref(out))
+        if st != 0:
+            raise RuntimeError(f"gg_executor_status failed with status {st}")
+        return out.value
+
+    def problem_count(self) -> int:
+        return self._lib.gg_executor_problem_count(self._h)
+
+    def total_tiles(self) -> int:
+        return self._lib.gg_executor_total_tiles(self._h)
+
+    def grid_ctas(self) -> int:
+        return self._lib.gg_executor_grid_ctas(self._h)
+
+
+def run_grouped_gemm_once(problems: Sequence[ProblemDesc], sort_mode: int, config: KernelConfig, stream=None) -> int:
+    cfg = config.to_c()
+    return capi.load().gg_run_grouped_gemm_once(_problems_array(problems), len(problems), int(sort_mode),
+                                                ctypes.byref(cfg), _stream_ptr(stream))
+
+
+def run_baseline_per_problem(problems: Sequence[ProblemDesc], config: KernelConfig, stream=None) -> int:
+    cfg = config.to_c()
+    return capi.load().gg_run_baseline_per_problem(_problems_array(problems), len(problems), ctypes.byref(cfg),
+                                                   _stream_ptr(stream))
+
+
+def count_non_empty_problems(problems: Sequence[ProblemDesc], config: KernelConfig) -> int:
+    cfg = config.to_c()
+    return capi.load().gg_count_non_empty_problems(_problems_array(problems), len(problems), ctypes.byref(cfg))
+
+
+def partition(problems: Sequence[ProblemDesc], config: KernelConfig, world_size: int, rank: int):
+    """Pieces of the problem set assigned to `rank` of `world_size` GPUs, and their weight."""
+    lib = capi.load()
+    arr = _problems_array(problems)
+    cfg = config.to_c()
+    n = ctypes.c_int(0)
+    w = ctypes.c_double(0.0)
+    st = lib.gg_partition(arr, len(problems), ctypes.byref(cfg), world_size, rank, None, 0, ctypes.byref(n), None)
+    if st != 0:
+        raise ValueError(f"gg_partition failed with status {st}")
+    out = (capi.GGShardPiece * max(1, n.value))()
+    st = lib.gg_partition(arr, len(problems), ctypes.byref(cfg), world_size, rank, out, n.value, ctypes.byref(n),
+                          ctypes.byref(w))
+    if st != 0:
+        raise ValueError(f"gg_partition failed with status {st}")
+    return [ShardPiece(o.problem, o.row0, o.rows, o.col0, o.cols) for o in out[:n.value]], w.value
+
+
+def selftest_wait_timeout(timeout_ns: int = 20_000_000):
+    """(status, device bits) of the bounded-wait self-test (see gg_selftest_wait_timeout)."""
+    out = ctypes.c_int(0)
+    st = capi.load().gg_selftest_wait_timeout(int(timeout_ns), ctypes.byref(out))
+    return st, out.value
+
+
+def problem_from_tensors(a, b, c, d, alpha: float = 1.0, beta: float = 0.0) -> ProblemDesc:
+    """ProblemDesc over torch tensors: a (m, k) fp16, b (k, n) fp16, c (m, n) fp32 or None, d (m, n) fp32.
+
+    Rows may be padded (row stride >= columns) but columns must be contiguous.
+    """
+    m, k = a.shape
+    k2, n = b.shape
+    if k2 != k or tuple(d.shape) != (m, n):
+        raise ValueError("shape mismatch")
+    for t in (a, b, d) + ((c,) if c is not None else ()):
+        if t.dim() == 2 and t.shape[1] > 1 and t.stride(1) != 1:
+            raise ValueError("columns must be contiguous")
+    return ProblemDesc(m, n, k, a.data_ptr(), b.data_ptr(), c.data_ptr() if c is not None else None, d.data_ptr(),
+                       max(1, a.stride(0)), max(1, b.stride(0)), max(1, c.stride(0)) if c is not None else max(1, n),
+                       max(1, d.stride(0)), float(alpha), float(beta))

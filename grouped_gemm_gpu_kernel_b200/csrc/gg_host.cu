@@ -1,0 +1,567 @@
+// gg_host.cu -- host runtime of the B200 grouped GEMM and its C-ABI (grouped_gemm_b200.h):
+// problem-set preparation, per-problem TMA descriptor encoding, the executor that owns the
+// device problem table, the per-problem baseline, the occupancy report and the multi-GPU
+// partitioner. The C++ API (grouped_gemm_api.cpp) is a wrapper over these entry points.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <numeric>
+#include <vector>
+
+#include "gg_internal.h"
+#include "grouped_gemm_b200.h"
+
+using grouped_gemm::DeviceProblemDesc;
+
+namespace gg {
+namespace {
+
+static_assert(sizeof(gg_problem) == 72, "gg_problem mirrors grouped_gemm::ProblemDesc");
+static_assert(offsetof(gg_problem, a) == 16 && offsetof(gg_problem, lda) == 48 && offsetof(gg_problem, alpha) == 64,
+              "gg_problem field offsets");
+
+constexpr int kMaxDevices = 64;
+constexpr int kDefaultRasterGroup = 16;
+
+int ceil_div(int x, int y) { return (x + y - 1) / y; }
+
+// ---- environment knobs -------------------------------------------------------------------------
+unsigned long long wait_timeout_ns() {
+  static const unsigned long long v = [] {
+    const char* s = std::getenv("GG_WAIT_TIMEOUT_MS");
+    const long long ms = s ? std::atoll(s) : 2000;
+    return static_cast<unsigned long long>(ms > 0 ? ms : 2000) * 1000000ull;
+  }();
+  return v;
+}
+
+int raster_group() {
+  static const int v = [] {
+    const char* s = std::getenv("GG_RASTER_GROUP");
+    const int g = s ? std::atoi(s) : kDefaultRasterGroup;
+    return g > 0 ? g : kDefaultRasterGroup;
+  }();
+  return v;
+}
+
+// ---- tile counting and sorting (reference src/grouped_gemm.cu:54-65, 967-1022) -----------------
+int tile_count(int m, int n, int cta_m, int cta_n) {
+  if (m <= 0 || n <= 0) return 0;
+  return ceil_div(m, cta_m) * ceil_div(n, cta_n);
+}
+
+// True when problem x is ordered strictly before problem y under the by-K rule: larger K first,
+// equal K -> larger m*n first (64-bit product).
+bool k_rule_before(const gg_problem& x, const gg_problem& y) {
+  if (x.k != y.k) return x.k > y.k;
+  return static_cast<int64_t>(x.m) * x.n > static_cast<int64_t>(y.m) * y.n;
+}
+
+void sorted_order(const gg_problem* ps, int count, int cta_m, int cta_n, int mode, std::vector<int>& order) {
+  order.resize(static_cast<size_t>(count));
+  std::iota(order.begin(), order.end(), 0);
+  if (mode == GG_SORT_BY_K) {
+    std::stable_sort(order.begin(), order.end(),
+                     [ps](int x, int y) { return k_rule_before(ps[x], ps[y]); });
+  } else if (mode == GG_SORT_BY_TILES || mode == GG_SORT_BY_TILES_THEN_K) {
+    // by-tiles and by-tiles-then-K share one rule: more tiles first, ties by the K rule.
+    std::vector<int> tiles(static_cast<size_t>(count));
+    for (int i = 0; i < count; ++i) tiles[static_cast<size_t>(i)] = tile_count(ps[i].m, ps[i].n, cta_m, cta_n);
+    std::stable_sort(order.begin(), order.end(), [&](int x, int y) {
+      const int tx = tiles[static_cast<size_t>(x)], ty = tiles[static_cast<size_t>(y)];
+      if (tx != ty) return tx > ty;
+      return k_rule_before(ps[x], ps[y]);
+    });
+  }
+}
+
+// ---- TMA descriptor encoding ----------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 2-D row-major tensor (inner x outer elements, row pitch in bytes), 128-byte swizzled boxes.
+bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, int inner, int outer,
+               int64_t row_bytes, int box_inner, int box_outer) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc || inner <= 0 || outer <= 0 || row_bytes <= 0 || (row_bytes % 16) != 0 || !aligned16(base)) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
+  const cuuint32_t elem_strides[2] = {1, 1};
+  const CUresult r = enc(map, type, 2, const_cast<void*>(base), dims, strides, box, elem_strides,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Device record of one problem plus its A, B and D tensor maps. TMA is used for A/B only when
+// both operands qualify, for D when it qualifies; everything else takes the zero-fill load path
+// and masked direct stores.
+DeviceProblemDesc make_device_problem(const gg_problem& p, int bm, int bn, CUtensorMap maps[3]) {
+  DeviceProblemDesc d{};
+  d.m = p.m;
+  d.n = p.n;
+  d.k = p.k;
+  d.a = static_cast<const __half*>(p.a);
+  d.b = static_cast<const __half*>(p.b);
+  d.c = p.c;
+  d.d = p.d;
+  d.lda = p.lda;
+  d.ldb = p.ldb;
+  d.ldc = p.ldc;
+  d.ldd = p.ldd;
+  d.alpha = p.alpha;
+  d.beta = p.beta;
+  const bool has_tiles = p.m > 0 && p.n > 0;
+  d.tiles_m = has_tiles ? ceil_div(p.m, bm) : 0;
+  d.tiles_n = has_tiles ? ceil_div(p.n, bn) : 0;
+  d.k_blocks = p.k > 0 ? ceil_div(p.k, kBK) : 0;
+  unsigned flags = 0;
+  std::memset(maps, 0, 3 * sizeof(CUtensorMap));
+  if (has_tiles && p.k > 0 &&
+      encode_2d(&maps[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, p.a, p.k, p.m, static_cast<int64_t>(p.lda) * 2, kBK, bm) &&
+      encode_2d(&maps[1], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, p.b, p.n, p.k, static_cast<int64_t>(p.ldb) * 2, 64, kBK))
+    flags |= grouped_gemm::kFlagTmaAB;
+  if (has_tiles &&
+      encode_2d(&maps[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.d, p.n, p.m, static_cast<int64_t>(p.ldd) * 4, 32, 32))
+    flags |= grouped_gemm::kFlagTmaD;
+  if (p.c != nullptr && p.beta != 0.0f) flags |= grouped_gemm::kFlagReadC;
+  if (aligned16(p.c) && (p.ldc % 4) == 0) flags |= grouped_gemm::kFlagCVec;
+  if (aligned16(p.d) && (p.ldd % 4) == 0) flags |= grouped_gemm::kFlagDVec;
+  d.flags = flags;
+  return d;
+}
+
+// Per-device status word for launches that have no executor (the per-problem baseline).
+int* device_status_word() {
+  static std::mutex mu;
+  static int* words[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!words[dev]) {
+    int* w = nullptr;
+    if (cudaMalloc(&w, sizeof(int)) != cudaSuccess) return nullptr;
+    if (cudaMemset(w, 0, sizeof(int)) != cudaSuccess) {
+      cudaFree(w);
+      return nullptr;
+    }
+    words[dev] = w;
+  }
+  return words[dev];
+}
+
+cudaError_t sm_count_and_slots(Variant v, int* sms, int* active) {
+  int dev = 0;
+  cudaError_t st = cudaGetDevice(&dev);
+  if (st != cudaSuccess) return st;
+  st = cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev);
+  if (st != cudaSuccess) return st;
+  cudaFuncAttributes attrs{};
+  st = kernel_occupancy(v, active, &attrs);
+  if (st != cudaSuccess) return st;
+  if (*active < 1) *active = 1;
+  return cudaSuccess;
+}
+
+Variant variant_of(const gg_config* c) {
+  if (!c) return Variant::kUnsupported;
+  return resolve_variant(c->cta_m, c->cta_n, c->cta_k, c->threads);
+}
+
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace
+}  // namespace gg
+
+// ---- the executor ------------------------------------------------------------------------------
+struct gg_executor {
+  void* block = nullptr;  // one device allocation: maps | problems | offsets | counter | status
+  CUtensorMap* d_maps = nullptr;
+  DeviceProblemDesc* d_problems = nullptr;
+  int* d_offsets = nullptr;
+  int* d_counter = nullptr;
+  int* d_status = nullptr;
+  int problem_count = 0;
+  int total_tiles = 0;
+  int grid_ctas = 0;
+  gg::Variant variant = gg::Variant::kUnsupported;
+  gg::KernelParams params{};
+
+  void release() {
+    if (block) cudaFree(block);
+    block = nullptr;
+    d_maps = nullptr;
+    d_problems = nullptr;
+    d_offsets = nullptr;
+    d_counter = nullptr;
+    d_status = nullptr;
+  }
+};
+
+extern "C" {
+
+int gg_abi_version(void) { return GG_ABI_VERSION; }
+
+const char* gg_sort_mode_name(int sort_mode) {
+  switch (sort_mode) {
+    case GG_SORT_NONE:
+      return "none";
+    case GG_SORT_BY_K:
+      return "sort_by_k";
+    case GG_SORT_BY_TILES:
+      return "sort_by_tiles";
+    case GG_SORT_BY_TILES_THEN_K:
+      return "sort_by_tiles_then_k";
+    default:
+      return "unknown";
+  }
+}
+
+int gg_tile_count(const gg_problem* problem, const gg_config* config) {
+  if (!problem || !config || config->cta_m <= 0 || config->cta_n <= 0) return 0;
+  return gg::tile_count(problem->m, problem->n, config->cta_m, config->cta_n);
+}
+
+int gg_prepare(const gg_problem* problems, int count, const gg_config* config, int sort_mode,
+               gg_problem* sorted_problems, int* sorted_to_original, int* tile_offsets, int* total_tiles) {
+  if (count < 0 || !config || !tile_offsets || !total_tiles || config->cta_m <= 0 || config->cta_n <= 0)
+    return cudaErrorInvalidValue;
+  if (count > 0 && (!problems || !sorted_problems || !sorted_to_original)) return cudaErrorInvalidValue;
+  std::vector<int> order;
+  gg::sorted_order(problems, count, config->cta_m, config->cta_n, sort_mode, order);
+  tile_offsets[0] = 0;
+  for (int s = 0; s < count; ++s) {
+    const int o = order[static_cast<size_t>(s)];
+    sorted_to_original[s] = o;
+    sorted_problems[s] = problems[o];
+    tile_offsets[s + 1] = tile_offsets[s] + gg::tile_count(problems[o].m, problems[o].n, config->cta_m, config->cta_n);
+  }
+  *total_tiles = tile_offsets[count];
+  return cudaSuccess;
+}
+
+int gg_query_occupancy(const gg_config* config, gg_occupancy* info) {
+  if (!info) return cudaErrorInvalidValue;
+  const gg::Variant v = gg::variant_of(config);
+  if (v == gg::Variant::kUnsupported) return cudaErrorInvalidValue;
+  int dev = 0;
+  cudaError_t st = cudaGetDevice(&dev);
+  if (st != cudaSuccess) return st;
+  auto attr = [&](cudaDeviceAttr a) {
+    int x = 0;
+    if (st == cudaSuccess) st = cudaDeviceGetAttribute(&x, a, dev);
+    return x;
+  };
+  gg_occupancy o{};
+  o.sm_count = attr(cudaDevAttrMultiProcessorCount);
+  o.max_blocks_per_sm = attr(cudaDevAttrMaxBlocksPerMultiprocessor);
+  o.max_threads_per_sm = attr(cudaDevAttrMaxThreadsPerMultiProcessor);
+  const int warp_size = attr(cudaDevAttrWarpSize);
+  o.max_registers_per_sm = attr(cudaDevAttrMaxRegistersPerMultiprocessor);
+  o.max_registers_per_block = attr(cudaDevAttrMaxRegistersPerBlock);
+  if (st != cudaSuccess) return st;
+  o.threads_per_block = gg::kThreads;
+  o.warps_per_block = gg::kThreads / (warp_size > 0 ? warp_size : 32);
+  o.max_warps_per_sm = o.max_threads_per_sm / (warp_size > 0 ? warp_size : 32);
+  // Register model of the widest role, an epilogue thread: one 32-column TMEM chunk (32), the
+  // matching C values (32) and ~24 for addresses, flags and loop state.
+  o.estimated_registers_per_thread = 32 + 32 + 24;
+  o.estimated_registers_per_block = o.estimated_registers_per_thread * gg::kThreads;
+  o.dynamic_shared_bytes = gg::variant_dynamic_smem(v);
+  o.using_tensor_cores = 1;
+  cudaFuncAttributes fa{};
+  st = gg::kernel_occupancy(v, &o.active_blocks_per_sm, &fa);
+  if (st != cudaSuccess) return st;
+  o.registers_per_thread = fa.numRegs;
+  o.static_shared_bytes = static_cast<int>(fa.sharedSizeBytes);
+  o.registers_per_block = o.registers_per_thread * o.threads_per_block;
+  o.register_limited_blocks_per_sm =
+      o.registers_per_block > 0 ? std::min(o.max_blocks_per_sm, o.max_registers_per_sm / o.registers_per_block)
+                                : o.max_blocks_per_sm;
+  o.active_warps_per_sm = o.active_blocks_per_sm * o.warps_per_block;
+  o.theoretical_occupancy =
+      o.max_warps_per_sm > 0 ? static_cast<float>(o.active_warps_per_sm) / static_cast<float>(o.max_warps_per_sm) : 0.0f;
+  *info = o;
+  return cudaSuccess;
+}
+
+int gg_executor_create(gg_executor** out) {
+  if (!out) return cudaErrorInvalidValue;
+  *out = new (std::nothrow) gg_executor();
+  return *out ? cudaSuccess : cudaErrorMemoryAllocation;
+}
+
+void gg_executor_destroy(gg_executor* executor) {
+  if (!executor) return;
+  executor->release();
+  delete executor;
+}
+
+int gg_executor_build(gg_executor* ex, const gg_problem* sorted_problems, int count, const int* tile_offsets,
+                      int offsets_len, int total_tiles, const gg_config* config) {
+  if (!ex) return cudaErrorInvalidDevicePointer;
+  const gg::Variant v = gg::variant_of(config);
+  if (v == gg::Variant::kUnsupported) return cudaErrorInvalidValue;
+  if (count < 0 || offsets_len != count + 1) return cudaErrorInvalidValue;
+  if (offsets_len > 0 && (!tile_offsets || tile_offsets[offsets_len - 1] != total_tiles)) return cudaErrorInvalidValue;
+  if (count > 0 && !sorted_problems) return cudaErrorInvalidValue;
+
+  ex->release();
+  ex->problem_count = 0;
+  ex->total_tiles = 0;
+  ex->grid_ctas = 0;
+  ex->variant = v;
+
+  const int bm = gg::variant_bm(v), bn = gg::variant_bn(v);
+  std::vector<DeviceProblemDesc> descs(static_cast<size_t>(count));
+  std::vector<CUtensorMap> maps(static_cast<size_t>(count) * 3);
+  for (int i = 0; i < count; ++i) {
+    const gg_problem& p = sorted_problems[i];
+    if (p.m < 0 || p.n < 0 || p.k < 0) return cudaErrorInvalidValue;
+    if (!p.a || !p.b || !p.d) return cudaErrorInvalidDevicePointer;
+    descs[static_cast<size_t>(i)] = gg::make_device_problem(p, bm, bn, &maps[static_cast<size_t>(i) * 3]);
+  }
+  if (count == 0 || total_tiles <= 0) {
+    ex->problem_count = count;
+    ex->total_tiles = total_tiles > 0 ? total_tiles : 0;
+    return cudaSuccess;  // nothing to launch
+  }
+
+  int sms = 0, active = 0;
+  cudaError_t st = gg::sm_count_and_slots(v, &sms, &active);
+  if (st != cudaSuccess) return st;
+
+  const size_t maps_bytes = maps.size() * sizeof(CUtensorMap);
+  const size_t descs_off = gg::round_up(maps_bytes, 128);
+  const size_t offs_off = gg::round_up(descs_off + descs.size() * sizeof(DeviceProblemDesc), 128);
+  const size_t counter_off = gg::round_up(offs_off + static_cast<size_t>(offsets_len) * sizeof(int), 128);
+  const size_t bytes = counter_off + 128;
+  std::vector<unsigned char> image(bytes, 0);
+  std::memcpy(image.data(), maps.data(), maps_bytes);
+  std::memcpy(image.data() + descs_off, descs.data(), descs.size() * sizeof(DeviceProblemDesc));
+  std::memcpy(image.data() + offs_off, tile_offsets, static_cast<size_t>(offsets_len) * sizeof(int));
+
+  st = cudaMalloc(&ex->block, bytes);
+  if (st != cudaSuccess) {
+    ex->block = nullptr;
+    return st;
+  }
+  st = cudaMemcpy(ex->block, image.data(), bytes, cudaMemcpyHostToDevice);
+  if (st != cudaSuccess) {
+    ex->release();
+    return st;
+  }
+  unsigned char* base = static_cast<unsigned char*>(ex->block);
+  ex->d_maps = reinterpret_cast<CUtensorMap*>(base);
+  ex->d_problems = reinterpret_cast<DeviceProblemDesc*>(base + descs_off);
+  ex->d_offsets = reinterpret_cast<int*>(base + offs_off);
+  ex->d_counter = reinterpret_cast<int*>(base + counter_off);
+  ex->d_status = reinterpret_cast<int*>(base + counter_off + 64);
+
+  ex->problem_count = count;
+  ex->total_tiles = total_tiles;
+  const int resident = sms * active;
+  ex->grid_ctas = config->persistent_ctas > 0 ? config->persistent_ctas : std::min(resident, total_tiles);
+  ex->grid_ctas = std::max(1, ex->grid_ctas);
+
+  gg::KernelParams& kp = ex->params;
+  std::memset(&kp, 0, sizeof(kp));
+  kp.problems = ex->d_problems;
+  kp.tmaps = ex->d_maps;
+  kp.tile_offsets = ex->d_offsets;
+  kp.tile_counter = ex->d_counter;
+  kp.status = ex->d_status;
+  kp.timeout_ns = gg::wait_timeout_ns();
+  kp.problem_count = count;
+  kp.total_tiles = total_tiles;
+  kp.raster_group = gg::raster_group();
+  kp.single_mode = 0;
+  return cudaSuccess;
+}
+
+int gg_executor_run(const gg_executor* ex, void* stream) {
+  if (!ex) return cudaErrorInvalidDevicePointer;
+  if (ex->total_tiles == 0 || ex->problem_count == 0) return cudaSuccess;
+  if (!ex->block) return cudaErrorInvalidDevicePointer;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t st = cudaMemsetAsync(ex->d_counter, 0, sizeof(int), s);
+  if (st != cudaSuccess) return st;
+  return gg::launch_grouped_kernel(ex->variant, ex->params, ex->grid_ctas, s);
+}
+
+int gg_executor_problem_count(const gg_executor* ex) { return ex ? ex->problem_count : 0; }
+int gg_executor_total_tiles(const gg_executor* ex) { return ex ? ex->total_tiles : 0; }
+int gg_executor_grid_ctas(const gg_executor* ex) { return ex ? ex->grid_ctas : 0; }
+
+int gg_executor_status(const gg_executor* ex, int* device_status) {
+  if (!ex) return cudaErrorInvalidDevicePointer;
+  if (!device_status) return cudaErrorInvalidValue;
+  *device_status = 0;
+  if (!ex->d_status) return cudaSuccess;
+  cudaError_t st = cudaDeviceSynchronize();
+  if (st != cudaSuccess) return st;
+  st = cudaMemcpy(device_status, ex->d_status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (st != cudaSuccess) return st;
+  return cudaMemset(ex->d_status, 0, sizeof(int));
+}
+
+int gg_run_grouped_gemm_once(const gg_problem* problems, int count, int sort_mode, const gg_config* config,
+                             void* stream) {
+  if (count < 0 || (count > 0 && !problems) || !config) return cudaErrorInvalidValue;
+  std::vector<gg_problem> sorted(static_cast<size_t>(count > 0 ? count : 1));
+  std::vector<int> s2o(sorted.size());
+  std::vector<int> offs(static_cast<size_t>(count) + 1);
+  int total = 0;
+  int st = gg_prepare(problems, count, config, sort_mode, sorted.data(), s2o.data(), offs.data(), &total);
+  if (st != cudaSuccess) return st;
+  gg_executor ex;
+  st = gg_executor_build(&ex, sorted.data(), count, offs.data(), count + 1, total, config);
+  if (st == cudaSuccess) st = gg_executor_run(&ex, stream);
+  ex.release();  // like the reference, freeing the temporary state synchronises
+  return st;
+}
+
+int gg_run_baseline_per_problem(const gg_problem* problems, int count, const gg_config* config, void* stream) {
+  const gg::Variant v = gg::variant_of(config);
+  if (v == gg::Variant::kUnsupported) return cudaErrorInvalidValue;
+  if (count < 0 || (count > 0 && !problems)) return cudaErrorInvalidValue;
+  const int bm = gg::variant_bm(v), bn = gg::variant_bn(v);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int sms = 0, active = 0;
+  int* status = nullptr;
+  gg::KernelParams kp;
+  for (int i = 0; i < count; ++i) {
+    const gg_problem& p = problems[i];
+    // Checked problem by problem in input order, as the reference does (src/grouped_gemm.cu:1304-1313).
+    if (!p.a || !p.b || !p.d) return cudaErrorInvalidDevicePointer;
+    if (gg::tile_count(p.m, p.n, bm, bn) == 0) continue;
+    if (!status) {
+      cudaError_t st = gg::sm_count_and_slots(v, &sms, &active);
+      if (st != cudaSuccess) return st;
+      status = gg::device_status_word();
+      if (!status) return cudaErrorMemoryAllocation;
+    }
+    std::memset(&kp, 0, sizeof(kp));
+    kp.single_desc = gg::make_device_problem(p, bm, bn, kp.single_maps);
+    const int tiles = kp.single_desc.tiles_m * kp.single_desc.tiles_n;
+    kp.status = status;
+    kp.timeout_ns = gg::wait_timeout_ns();
+    kp.problem_count = 1;
+    kp.total_tiles = tiles;
+    kp.raster_group = gg::raster_group();
+    kp.single_mode = 1;
+    const cudaError_t st = gg::launch_grouped_kernel(v, kp, std::min(tiles, sms * active), s);
+    if (st != cudaSuccess) return st;
+  }
+  return cudaSuccess;
+}
+
+int gg_count_non_empty_problems(const gg_problem* problems, int count, const gg_config* config) {
+  if (!problems || !config || count <= 0 || config->cta_m <= 0 || config->cta_n <= 0) return 0;
+  int non_empty = 0;
+  for (int i = 0; i < count; ++i)
+    if (gg::tile_count(problems[i].m, problems[i].n, config->cta_m, config->cta_n) > 0) ++non_empty;
+  return non_empty;
+}
+
+int gg_partition(const gg_problem* problems, int count, const gg_config* config, int world_size, int rank,
+                 gg_shard_piece* out, int capacity, int* out_count, double* out_weight) {
+  if (!config || !out_count || world_size < 1 || rank < 0 || rank >= world_size || count < 0 ||
+      (count > 0 && !problems) || config->cta_m <= 0 || config->cta_n <= 0)
+    return cudaErrorInvalidValue;
+  const int cm = config->cta_m, cn = config->cta_n;
+  // The epilogue of a tile writes cm*cn*4 bytes of D; a K block loads (cm+cn)*64*2 bytes. The
+  // fixed per-tile cost is expressed in K-block units so that the weight tracks both.
+  const double epi = std::max(1.0, (cm * cn * 4.0) / ((cm + cn) * gg::kBK * 2.0));
+  std::vector<double> per_tile(static_cast<size_t>(count), 0.0);
+  std::vector<int> tiles(static_cast<size_t>(count), 0);
+  double total = 0.0;
+  for (int i = 0; i < count; ++i) {
+    const gg_problem& p = problems[i];
+    tiles[static_cast<size_t>(i)] = gg::tile_count(p.m, p.n, cm, cn);
+    per_tile[static_cast<size_t>(i)] = static_cast<double>(p.k > 0 ? gg::ceil_div(p.k, gg::kBK) : 0) + epi;
+    total += per_tile[static_cast<size_t>(i)] * tiles[static_cast<size_t>(i)];
+  }
+  int n = 0;
+  double weight = 0.0, cum = 0.0;
+  auto emit = [&](int problem, int row0, int rows, int col0, int cols) {
+    if (rows <= 0 || cols <= 0) return;
+    if (out && n < capacity) out[n] = gg_shard_piece{problem, row0, rows, col0, cols};
+    ++n;
+  };
+  for (int i = 0; i < count; ++i) {
+    const int T = tiles[static_cast<size_t>(i)];
+    const double w = per_tile[static_cast<size_t>(i)];
+    if (T == 0) continue;
+    // Tiles are taken in row-major order; each one goes to the rank whose share of the total
+    // weight holds the tile's midpoint, so a rank owns one contiguous tile range per problem.
+    int t0 = -1, t1 = -1;
+    for (int t = 0; t < T; ++t) {
+      const double mid = cum + (t + 0.5) * w;
+      int owner = total > 0.0 ? static_cast<int>(std::floor(mid * world_size / total)) : 0;
+      owner = std::min(std::max(owner, 0), world_size - 1);
+      if (owner == rank) {
+        if (t0 < 0) t0 = t;
+        t1 = t + 1;
+      }
+    }
+    cum += w * T;
+    if (t0 < 0) continue;
+    weight += w * (t1 - t0);
+    // Cut the tile range [t0, t1) of the tm x tn tile grid into at most three rectangles: the
+    // tail of the first row band, whole row bands, the head of the last row band.
+    const gg_problem& p = problems[i];
+    const int tn = gg::ceil_div(p.n, cn);
+    auto col_end = [&](int c) { return std::min(p.n, c * cn); };
+    auto row_end = [&](int r) { return std::min(p.m, r * cm); };
+    int r_first = t0 / tn, c_first = t0 % tn;
+    const int r_last = (t1 - 1) / tn, c_last = (t1 - 1) % tn;
+    if (r_first == r_last) {
+      emit(i, r_first * cm, row_end(r_first + 1) - r_first * cm, c_first * cn, col_end(c_last + 1) - c_first * cn);
+      continue;
+    }
+    if (c_first != 0) {
+      emit(i, r_first * cm, row_end(r_first + 1) - r_first * cm, c_first * cn, p.n - c_first * cn);
+      ++r_first;
+    }
+    const int full_end = (c_last == tn - 1) ? r_last + 1 : r_last;  // bands [r_first, full_end) are whole
+    if (full_end > r_first) emit(i, r_first * cm, row_end(full_end) - r_first * cm, 0, p.n);
+    if (c_last != tn - 1) emit(i, r_last * cm, row_end(r_last + 1) - r_last * cm, 0, col_end(c_last + 1));
+  }
+  *out_count = n;
+  if (out_weight) *out_weight = weight;
+  if (out && n > capacity) return cudaErrorInvalidValue;
+  return cudaSuccess;
+}
+
+int gg_selftest_wait_timeout(unsigned long long timeout_ns, int* status) {
+  if (!status) return cudaErrorInvalidValue;
+  int* d = nullptr;
+  cudaError_t st = cudaMalloc(&d, sizeof(int));
+  if (st != cudaSuccess) return st;
+  st = cudaMemset(d, 0, sizeof(int));
+  if (st == cudaSuccess) st = gg::launch_wait_selftest(d, timeout_ns, nullptr);
+  if (st == cudaSuccess) st = cudaDeviceSynchronize();
+  if (st == cudaSuccess) st = cudaMemcpy(status, d, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  return st;
+}
+
+}  // extern "C"

@@ -1,0 +1,36 @@
+// gg_internal.h -- declarations shared by the kernel unit (gg_kernels.cu) and the host runtime
+// (gg_host.cu). Not installed; callers use grouped_gemm_b200.h or grouped_gemm/grouped_gemm.cuh.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstddef>
+
+#include "gg_params.cuh"
+
+namespace gg {
+
+// Compiled tile variants (BM x BN output tiles; K is always consumed 64 deep).
+enum class Variant : int {
+  k64x64 = 0,
+  k128x64 = 1,
+  k64x128 = 2,
+  k128x128 = 3,
+  k128x256 = 4,
+  kCount = 5,
+  kUnsupported = -1,
+};
+
+// Maps a (cta_m, cta_n, cta_k, threads) request to a variant, kUnsupported otherwise. Accepts the
+// reference's three shapes (reference src/grouped_gemm.cu:67-81) and the sm_100a-native ones.
+Variant resolve_variant(int cta_m, int cta_n, int cta_k, int threads);
+int variant_bm(Variant v);
+int variant_bn(Variant v);
+int variant_dynamic_smem(Variant v);
+
+// Raises the kernel's dynamic shared-memory limit on the current device (once per device).
+cudaError_t prepare_kernel(Variant v);
+cudaError_t launch_grouped_kernel(Variant v, const KernelParams& params, int grid, cudaStream_t stream);
+cudaError_t kernel_occupancy(Variant v, int* active_blocks_per_sm, cudaFuncAttributes* attrs);
+cudaError_t launch_wait_selftest(int* status, unsigned long long timeout_ns, cudaStream_t stream);
+
+}  // namespace gg

@@ -1,0 +1,81 @@
+// gg_params.cuh -- constants, shared-memory layout and launch parameters of the grouped GEMM
+// kernel, shared by the kernel unit and the host runtime (no device code here).
+#pragma once
+
+#include <cuda.h>
+#include <cstddef>
+#include <cstdint>
+
+#include "grouped_gemm/device_problem_desc.cuh"
+
+namespace gg {
+
+using grouped_gemm::DeviceProblemDesc;
+
+constexpr int kThreads = 256;
+constexpr int kBK = 64;     // K elements per pipeline stage: one 128-byte swizzle row of FP16
+constexpr int kMmaM = 128;  // tcgen05 M used by every variant
+constexpr int kMmaK = 16;   // tcgen05 K for 16-bit inputs
+constexpr int kRing = 4;    // scheduler ring depth
+constexpr int kEpiWarps = 4;
+constexpr int kMmaWarp = 4;
+constexpr int kSchedWarp = 5;
+constexpr int kProdWarp0 = 6;
+constexpr int kProdThreads = 64;
+constexpr int kRingConsumerWarps = kEpiWarps + 1 + 2;  // arrivals that free one ring slot
+constexpr int kEpiTileBytes = 32 * 128;                // one warp's 32 rows x 32 FP32 columns
+constexpr int kDescWords = static_cast<int>(sizeof(DeviceProblemDesc) / 4);
+
+struct TileSlot {
+  int problem;  // sorted problem index; -1 = no more work for this CTA
+  int tile_m;
+  int tile_n;
+  int reserved;
+  DeviceProblemDesc desc;
+};
+
+template <int BN>
+struct StageCount {
+  static constexpr int value = BN >= 256 ? 4 : (BN >= 128 ? 5 : 6);
+};
+
+template <int BM, int BN>
+struct SmemLayout {
+  static constexpr int kStages = StageCount<BN>::value;
+  static constexpr int kABytes = kMmaM * 128;
+  static constexpr int kBBytes = BN * 128;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kEpiOffset = kStages * kStageBytes;
+  static constexpr int kEpiBytes = kEpiWarps * 2 * kEpiTileBytes;
+  static constexpr int kRingOffset = kEpiOffset + kEpiBytes;
+  static constexpr int kBarOffset = kRingOffset + kRing * static_cast<int>(sizeof(TileSlot));
+  static constexpr int kNumBars = 2 * kStages + 4 + 2 * kRing + 1;
+  static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
+  static constexpr int kBytes = kMiscOffset + 16;
+  static constexpr int kDynamicSmem = kBytes + 1024;  // slack to align the base to 1024 bytes
+  static constexpr uint32_t kATxBytes = static_cast<uint32_t>(BM) * 128;
+  static constexpr uint32_t kBTxBytes = static_cast<uint32_t>(BN) * 128;
+  static constexpr uint32_t kTmemCols = 2 * BN;
+  static_assert(kRingOffset % 1024 == 0, "stage and staging tiles stay 1024-byte aligned");
+  static_assert(kBarOffset % 8 == 0, "mbarriers are 8-byte aligned");
+  static_assert(kDynamicSmem <= 232448, "fits the 227 KB opt-in shared memory of a CTA");
+  static_assert(kDynamicSmem > 232448 / 2 + 1024, "one CTA per SM, so TMEM allocation never contends");
+  static_assert(kTmemCols >= 32 && kTmemCols <= 512 && (kTmemCols & (kTmemCols - 1)) == 0, "TMEM alloc size");
+};
+
+struct KernelParams {
+  CUtensorMap single_maps[3];         // baseline launch: A, B, D maps of its one problem
+  DeviceProblemDesc single_desc;      // baseline launch: its one problem
+  const DeviceProblemDesc* problems;  // grouped launch: problem table in sorted order
+  const CUtensorMap* tmaps;           // grouped launch: A, B, D maps per problem (64-byte aligned)
+  const int* tile_offsets;            // grouped launch: problem_count + 1 prefix sums
+  int* tile_counter;                  // grouped launch: claim counter, zero at launch
+  int* status;                        // GG_STATUS_* bits
+  unsigned long long timeout_ns;      // limit of every wait
+  int problem_count;
+  int total_tiles;
+  int raster_group;  // M-tiles per raster group inside a problem (L2 reuse of A and B panels)
+  int single_mode;   // 1: baseline launch, tiles blockIdx.x + i*gridDim.x of single_desc
+};
+
+}  // namespace gg

@@ -1,0 +1,201 @@
+"""Seeded synthetic problem sets with the shapes and value laws of the five benchmark configurations.
+
+The reference measures on no public suite; these generators stand in for its inputs:
+
+  small16   16 problems, M, N, K ~ U{16..256}; A, B FP16 ~ U[-1,1]; C FP32 ~ U[-1,1]; alpha 1, beta 0.5
+  mixed512  512 problems, M, N, K log-uniform on [64, 1024] rounded to multiples of 8; U[-1,1];
+            C ~ U[-1,1] (allocated, not read: beta 0); alpha 1
+  moe       64 experts, M_i = tokens routed to expert i when 16384 tokens each draw an expert from a
+            Zipf(s=1.1) law over 64 ranks (zero-token experts are kept), N 14336, K 4096;
+            A ~ N(0,1), B ~ N(0,0.02) FP16; no C; alpha 1, beta 0
+  tiny4096  4096 problems, M, N, K ~ U{1..64}; U[-1,1]; alpha 1.5, beta -0.5
+  skew      one 8192^3 problem followed by 1023 problems of 128^3; U[-1,1]; no C; alpha 1, beta 0
+
+Leading dimensions are packed (lda = K, ldb = ldc = ldd = N, as the reference test packs them,
+reference tests/test_correctness.cu:128-131), so odd K or N give problems that TMA cannot load
+and the kernel's zero-fill loader takes. Each operand of each problem starts on a 256-byte
+boundary inside one slab per operand kind. Shapes come from numpy's PCG64 seeded by `seed`;
+values from a CUDA torch generator seeded by `seed`.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Tuple
+
+import numpy as np
+
+CONFIG_NAMES = ("small16", "mixed512", "moe", "tiny4096", "skew")
+ALIGN_BYTES = 256
+
+
+@dataclass
+class Shapes:
+    name: str
+    dims: List[Tuple[int, int, int]]
+    alpha: List[float]
+    beta: List[float]
+    has_c: bool
+    a_law: str = "uniform"   # "uniform": U[-1,1]; "normal": N(0, a_std)
+    a_std: float = 1.0
+    b_law: str = "uniform"
+    b_std: float = 1.0
+
+    @property
+    def flops(self) -> float:
+        return float(sum(2.0 * m * n * k for m, n, k in self.dims))
+
+    def algorithmic_bytes(self) -> float:
+        """A and B read once, D written once, C read when beta != 0 (FP16 A/B, FP32 C/D)."""
+        tot = 0.0
+        for (m, n, k), b in zip(self.dims, self.beta):
+            if m <= 0 or n <= 0:
+                continue
+            tot += 2.0 * m * k + 2.0 * k * n + 4.0 * m * n
+            if self.has_c and b != 0.0:
+                tot += 4.0 * m * n
+        return tot
+
+
+def _log_uniform8(rng, size):
+    x = np.exp(rng.uniform(np.log(64.0), np.log(1024.0), size=size))
+    return np.clip(np.round(x / 8.0) * 8.0, 64, 1024).astype(np.int64)
+
+
+def zipf_split(total_tokens: int, experts: int, s: float, rng) -> np.ndarray:
+    """Token counts per expert: each token draws a rank with P(r) ~ r^-s, ranks map to experts
+    through a seeded permutation; experts that draw no token keep M_i = 0."""
+    p = np.arange(1, experts + 1, dtype=np.float64) ** (-s)
+    p /= p.sum()
+    ranks = rng.choice(experts, size=total_tokens, p=p)
+    perm = rng.permutation(experts)
+    return np.bincount(perm[ranks], minlength=experts).astype(np.int64)
+
+
+def make_shapes(name: str, seed: int = 42) -> Shapes:
+    rng = np.random.default_rng(seed)
+    if name == "small16":
+        d = rng.integers(16, 257, size=(16, 3))
+        dims = [tuple(int(x) for x in r) for r in d]
+        return Shapes(name, dims, [1.0] * 16, [0.5] * 16, True)
+    if name == "mixed512":
+        d = _log_uniform8(rng, (512, 3))
+        dims = [tuple(int(x) for x in r) for r in d]
+        return Shapes(name, dims, [1.0] * 512, [0.0] * 512, True)
+    if name == "moe":
+        counts = zipf_split(16384, 64, 1.1, rng)
+        dims = [(int(c), 14336, 4096) for c in counts]
+        return Shapes(name, dims, [1.0] * 64, [0.0] * 64, False, "normal", 1.0, "normal", 0.02)
+    if name == "tiny4096":
+        d = rng.integers(1, 65, size=(4096, 3))
+        dims = [tuple(int(x) for x in r) for r in d]
+        return Shapes(name, dims, [1.5] * 4096, [-0.5] * 4096, True)
+    if name == "skew":
+        dims = [(8192, 8192, 8192)] + [(128, 128, 128)] * 1023
+        return Shapes(name, dims, [1.0] * 1024, [0.0] * 1024, False)
+    raise ValueError(f"unknown workload {name!r}; expected one of {CONFIG_NAMES}")
+
+
+def _aligned(n_elems: int, elem_bytes: int) -> int:
+    per = ALIGN_BYTES // elem_bytes
+    return (max(n_elems, 1) + per - 1) // per * per
+
+
+@dataclass
+class DeviceProblemSet:
+    """Device slabs + per-problem offsets (elements) for one workload."""
+
+    shapes: Shapes
+    a: "object"  # torch fp16 slab
+    b: "object"
+    c: Optional["object"]
+    d: "object"  # torch fp32 slab
+    a_off: List[int] = field(default_factory=list)
+    b_off: List[int] = field(default_factory=list)
+    c_off: List[int] = field(default_factory=list)
+    d_off: List[int] = field(default_factory=list)
+
+    def problems(self):
+        from . import ProblemDesc
+        out = []
+        ab, bb, db = self.a.data_ptr(), self.b.data_ptr(), self.d.data_ptr()
+        cb = self.c.data_ptr() if self.c is not None else None
+        for i, ((m, n, k), al, be) in enumerate(zip(self.shapes.dims, self.shapes.alpha, self.shapes.beta)):
+            out.append(ProblemDesc(m, n, k, ab + 2 * self.a_off[i], bb + 2 * self.b_off[i],
+                                   (cb + 4 * self.c_off[i]) if cb is not None else None, db + 4 * self.d_off[i],
+                                   max(1, k), max(1, n), max(1, n), max(1, n), al, be))
+        return out
+
+    def views(self, i: int):
+        """(A, B, C or None, D) torch views of problem i."""
+        m, n, k = self.shapes.dims[i]
+        A = self.a[self.a_off[i]:self.a_off[i] + max(m * k, 0)].view(max(m, 0), max(k, 0)) if m * k > 0 else None
+        B = self.b[self.b_off[i]:self.b_off[i] + max(k * n, 0)].view(k, n) if k * n > 0 else None
+        C = None
+        if self.c is not None and m * n > 0:
+            C = self.c[self.c_off[i]:self.c_off[i] + m * n].view(m, n)
+        D = self.d[self.d_off[i]:self.d_off[i] + m * n].view(m, n) if m * n > 0 else None
+        return A, B, C, D
+
+
+def allocate(shapes: Shapes, device="cuda", seed: int = 42, d_fill: float = float("nan")) -> DeviceProblemSet:
+    """Device slabs for `shapes`, filled with the config's value laws (seeded on the device)."""
+    import torch
+
+    a_off, b_off, c_off, d_off = [], [], [], []
+    na = nb = nc = nd = 0
+    for m, n, k in shapes.dims:
+        a_off.append(na)
+        na += _aligned(max(m, 0) * max(k, 0), 2)
+        b_off.append(nb)
+        nb += _aligned(max(k, 0) * max(n, 0), 2)
+        c_off.append(nc)
+        nc += _aligned(max(m, 0) * max(n, 0), 4)
+        d_off.append(nd)
+        nd += _aligned(max(m, 0) * max(n, 0), 4)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+
+    def fill16(count, law, std):
+        t = torch.empty(count, dtype=torch.float16, device=device)
+        if law == "normal":
+            t.normal_(0.0, std, generator=g)
+        else:
+            t.uniform_(-1.0, 1.0, generator=g)
+        return t
+
+    a = fill16(na, shapes.a_law, shapes.a_std)
+    b = fill16(nb, shapes.b_law, shapes.b_std)
+    c = None
+    if shapes.has_c:
+        c = torch.empty(nc, dtype=torch.float32, device=device)
+        c.uniform_(-1.0, 1.0, generator=g)
+    d = torch.full((nd,), d_fill, dtype=torch.float32, device=device)
+    return DeviceProblemSet(shapes, a, b, c, d, a_off, b_off, c_off, d_off)
+
+
+def host_inputs(ps: DeviceProblemSet, i: int, rows: Optional[np.ndarray] = None,
+                cols: Optional[np.ndarray] = None) -> Dict[str, object]:
+    """Host copies (FP16 bits as uint16, C as float32) of problem i for the CPU oracle.
+
+    With `rows`/`cols` only those rows of A (and C) and those columns of B (and C) are copied,
+    so a full-size problem can be checked on a sample."""
+    import torch
+
+    m, n, k = ps.shapes.dims[i]
+    A, B, C, D = ps.views(i)
+    if rows is not None:
+        ridx = torch.as_tensor(rows, device=ps.a.device, dtype=torch.long)
+        A = A.index_select(0, ridx) if A is not None else None
+        C = C.index_select(0, ridx) if C is not None else None
+        D = D.index_select(0, ridx) if D is not None else None
+    if cols is not None:
+        cidx = torch.as_tensor(cols, device=ps.a.device, dtype=torch.long)
+        B = B.index_select(1, cidx) if B is not None else None
+        C = C.index_select(1, cidx) if C is not None else None
+        D = D.index_select(1, cidx) if D is not None else None
+    out = {}
+    out["a"] = A.contiguous().view(torch.int16).cpu().numpy().view(np.uint16) if A is not None else np.zeros(1, np.uint16)
+    out["b"] = B.contiguous().view(torch.int16).cpu().numpy().view(np.uint16) if B is not None else np.zeros(1, np.uint16)
+    out["c"] = C.contiguous().cpu().numpy() if C is not None else None
+    out["d"] = D.contiguous().cpu().numpy() if D is not None else None
+    return out

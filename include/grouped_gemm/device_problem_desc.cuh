@@ -1,0 +1,48 @@
+// grouped_gemm/device_problem_desc.cuh -- the per-problem record the B200 kernel reads from HBM.
+//
+// It extends the reference's DeviceProblemDesc (reference src/grouped_gemm.cu:25-45, internal
+// there) -- the ProblemDesc fields followed by tiles_m / tiles_n -- with the k-block count of
+// the kernel's K tiling and the problem's data-path flags, so the kernel never recomputes them
+// per tile. 88 bytes, a multiple of 4 so a warp can copy it word by word.
+#pragma once
+
+#include <cuda_fp16.h>
+
+namespace grouped_gemm {
+
+enum DeviceProblemFlags : unsigned {
+  kFlagTmaAB = 1u,   // A and B are loaded by TMA (16-byte aligned bases, lda and ldb % 8 == 0)
+  kFlagTmaD = 2u,    // D is stored by TMA (16-byte aligned base, ldd % 4 == 0)
+  kFlagReadC = 4u,   // c != nullptr && beta != 0: the epilogue reads C
+  kFlagCVec = 8u,    // C rows can be read as 16-byte vectors
+  kFlagDVec = 16u,   // D rows can be written as 16-byte vectors (direct-store path)
+};
+
+struct DeviceProblemDesc {
+  int m;
+  int n;
+  int k;
+
+  const __half* a;
+  const __half* b;
+  const float* c;
+  float* d;
+
+  int lda;
+  int ldb;
+  int ldc;
+  int ldd;
+
+  float alpha;
+  float beta;
+
+  int tiles_m;   // ceil(m / cta_m), 0 when m <= 0 or n <= 0
+  int tiles_n;   // ceil(n / cta_n), 0 when m <= 0 or n <= 0
+  int k_blocks;  // ceil(k / 64): 64-deep K blocks of the tcgen05 mainloop
+  unsigned flags;  // DeviceProblemFlags
+};
+
+static_assert(sizeof(DeviceProblemDesc) == 88, "DeviceProblemDesc layout");
+static_assert(sizeof(DeviceProblemDesc) % 4 == 0, "copied word by word");
+
+}  // namespace grouped_gemm

@@ -1,0 +1,192 @@
+/*
+ * grouped_gemm_b200.h -- C-ABI of the B200 (sm_100a) grouped GEMM library libgrouped_gemm_b200.so.
+ *
+ * One launch runs many independent GEMMs  D_i = alpha_i * A_i x B_i + beta_i * C_i  with
+ * A_i (m x k) and B_i (k x n) FP16 row-major, C_i and D_i FP32 row-major, FP32 accumulation.
+ * This is the boundary a foreign-language caller binds (ctypes, cgo, JNI, ...): plain C types,
+ * opaque handles, device pointers as void*, CUDA streams as void* (cudaStream_t; NULL = legacy
+ * default stream). Every function that can fail returns an int holding a cudaError_t value:
+ *   0  cudaSuccess
+ *   1  cudaErrorInvalidValue          unsupported config, negative dims, inconsistent prepared set,
+ *                                     null output argument
+ *   17 cudaErrorInvalidDevicePointer  null a/b/d in a problem, or a null/destroyed executor
+ *   other values are CUDA runtime errors passed through unchanged.
+ * An empty problem set (or one with zero tiles) is a successful no-op that launches nothing.
+ *
+ * Each entry point replaces one function of the reference C++ API
+ * (reference include/grouped_gemm/grouped_gemm.cuh, implemented in src/grouped_gemm.cu); the
+ * citation is given beside each. The C++ API itself is provided on top of this ABI by
+ * include/grouped_gemm/grouped_gemm.cuh.
+ */
+#ifndef GROUPED_GEMM_B200_H_
+#define GROUPED_GEMM_B200_H_
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GG_ABI_VERSION 1
+
+/* Sort modes; reference grouped_gemm.cuh:11-16 (SortMode). */
+#define GG_SORT_NONE 0
+#define GG_SORT_BY_K 1
+#define GG_SORT_BY_TILES 2
+#define GG_SORT_BY_TILES_THEN_K 3
+
+/* Bits of the device status word (gg_executor_status): a bounded wait inside the kernel ran out.
+ * The kernel then stops, frees its tensor memory and returns instead of hanging. */
+#define GG_STATUS_TIMEOUT_PRODUCER 0x1
+#define GG_STATUS_TIMEOUT_MMA 0x2
+#define GG_STATUS_TIMEOUT_EPILOGUE 0x4
+#define GG_STATUS_TIMEOUT_SCHEDULER 0x8
+
+/* One GEMM problem. Layout-identical to the reference's ProblemDesc (grouped_gemm.cuh:18-35);
+ * a and b point to FP16 (__half) device memory. */
+typedef struct gg_problem {
+  int m;
+  int n;
+  int k;
+  const void* a;
+  const void* b;
+  const float* c;
+  float* d;
+  int lda;
+  int ldb;
+  int ldc;
+  int ldd;
+  float alpha;
+  float beta;
+} gg_problem;
+
+/* Kernel configuration; the reference's KernelConfig (grouped_gemm.cuh:37-45) with the bool as
+ * an int. Accepted (cta_m, cta_n, cta_k) with threads == 256:
+ *   sm_100a-native tiles   128x128x64, 128x256x64, 128x64x64
+ *   the reference's tiles  64x64x16, 128x64x32, 64x128x32  (same tile decomposition, run on the
+ *                          same tcgen05 kernel; cta_k only selects the variant)
+ * use_tensor_cores is accepted either way: every variant runs on tcgen05 tensor cores. */
+typedef struct gg_config {
+  int cta_m;
+  int cta_n;
+  int cta_k;
+  int threads;
+  int persistent_ctas; /* > 0: fixed persistent grid size; 0: one CTA per SM slot, capped by tiles */
+  int use_tensor_cores;
+} gg_config;
+
+/* Resource report; field-for-field the reference's OccupancyInfo (grouped_gemm.cuh:54-83). */
+typedef struct gg_occupancy {
+  int sm_count;
+  int max_blocks_per_sm;
+  int active_blocks_per_sm;
+  int threads_per_block;
+  int max_threads_per_sm;
+  int warps_per_block;
+  int max_warps_per_sm;
+  int active_warps_per_sm;
+  int max_registers_per_sm;
+  int max_registers_per_block;
+  int estimated_registers_per_thread;
+  int estimated_registers_per_block;
+  int registers_per_thread;
+  int registers_per_block;
+  int register_limited_blocks_per_sm;
+  int static_shared_bytes;
+  int dynamic_shared_bytes;
+  float theoretical_occupancy;
+  int using_tensor_cores;
+} gg_occupancy;
+
+/* A contiguous piece of one problem assigned to one GPU by gg_partition: rows
+ * [row0, row0+rows) x columns [col0, col0+cols) of problem `problem` (index into the input). */
+typedef struct gg_shard_piece {
+  int problem;
+  int row0;
+  int rows;
+  int col0;
+  int cols;
+} gg_shard_piece;
+
+typedef struct gg_executor gg_executor;
+
+int gg_abi_version(void);
+
+/* reference src/grouped_gemm.cu:952-965 (sort_mode_name): "none", "sort_by_k", "sort_by_tiles",
+ * "sort_by_tiles_then_k", or "unknown". */
+const char* gg_sort_mode_name(int sort_mode);
+
+/* reference src/grouped_gemm.cu:58-65 (tile_count_for_problem): 0 when m <= 0 or n <= 0,
+ * else ceil(m/cta_m) * ceil(n/cta_n). K = 0 still owns tiles (D = beta*C there). */
+int gg_tile_count(const gg_problem* problem, const gg_config* config);
+
+/* reference src/grouped_gemm.cu:967-1022 (prepare_problem_set). Host only, no CUDA call.
+ * Writes count entries to sorted_problems and sorted_to_original, count+1 to tile_offsets
+ * (tile_offsets[0] = 0) and the total to *total_tiles. Bit-identical to the reference. */
+int gg_prepare(const gg_problem* problems, int count, const gg_config* config, int sort_mode,
+               gg_problem* sorted_problems, int* sorted_to_original, int* tile_offsets,
+               int* total_tiles);
+
+/* reference src/grouped_gemm.cu:1024-1083 (query_occupancy) for the kernel the config selects. */
+int gg_query_occupancy(const gg_config* config, gg_occupancy* info);
+
+/* reference src/grouped_gemm.cu:1099-1130 (GroupedGemmExecutor constructor / destructor). */
+int gg_executor_create(gg_executor** out);
+void gg_executor_destroy(gg_executor* executor);
+
+/* reference src/grouped_gemm.cu:1132-1239 (GroupedGemmExecutor::build). Takes the fields of a
+ * PreparedProblemSet: `count` sorted problems, `offsets_len` tile offsets (must be count+1) and
+ * total_tiles (must equal the last offset). Validates, encodes per-problem TMA descriptors and
+ * uploads the problem table; the device state is owned by the executor. */
+int gg_executor_build(gg_executor* executor, const gg_problem* sorted_problems, int count,
+                      const int* tile_offsets, int offsets_len, int total_tiles,
+                      const gg_config* config);
+
+/* reference src/grouped_gemm.cu:1241-1265 (GroupedGemmExecutor::run): resets the tile counter
+ * and launches the persistent kernel on `stream`. Runs of one executor on two streams at the
+ * same time race on its tile counter: use one executor per concurrent stream. */
+int gg_executor_run(const gg_executor* executor, void* stream);
+
+/* reference src/grouped_gemm.cu:1267-1277 (problem_count / total_tiles / grid_ctas). */
+int gg_executor_problem_count(const gg_executor* executor);
+int gg_executor_total_tiles(const gg_executor* executor);
+int gg_executor_grid_ctas(const gg_executor* executor);
+
+/* No reference counterpart (the reference kernels cannot time out). Synchronises the device and
+ * returns in *device_status the GG_STATUS_* bits raised by this executor's launches so far, then
+ * clears them. */
+int gg_executor_status(const gg_executor* executor, int* device_status);
+
+/* reference src/grouped_gemm.cu:1279-1291 (run_grouped_gemm_once): prepare + build + run. Like
+ * the reference, the temporary executor is freed before returning, which synchronises. */
+int gg_run_grouped_gemm_once(const gg_problem* problems, int count, int sort_mode,
+                             const gg_config* config, void* stream);
+
+/* reference src/grouped_gemm.cu:1293-1317 (run_baseline_per_problem): one kernel launch per
+ * non-empty problem, in input order, on the same tile code. */
+int gg_run_baseline_per_problem(const gg_problem* problems, int count, const gg_config* config,
+                                void* stream);
+
+/* reference src/grouped_gemm.cu:1319-1329 (count_non_empty_problems). */
+int gg_count_non_empty_problems(const gg_problem* problems, int count, const gg_config* config);
+
+/* No reference counterpart (the reference is single-GPU). Splits the problem set over
+ * world_size GPUs: every output tile of the config's tiling is weighted by its 64-deep K blocks
+ * plus a fixed epilogue cost, tiles are numbered in input order (row-major inside a problem),
+ * and each tile goes to the rank whose 1/world_size share of the total weight holds the tile's
+ * midpoint. A rank therefore owns one contiguous tile range per problem, returned as at most
+ * three rectangles (pieces). Writes the pieces of `rank` to out (at most capacity), their number
+ * to *out_count and their weight to *out_weight (nullable). With out == NULL only the count is
+ * returned. Host only. */
+int gg_partition(const gg_problem* problems, int count, const gg_config* config, int world_size,
+                 int rank, gg_shard_piece* out, int capacity, int* out_count, double* out_weight);
+
+/* No reference counterpart. Runs the kernel's bounded-wait helper on an mbarrier that nothing
+ * ever completes, with the given limit, and returns the device status it recorded in *status
+ * (GG_STATUS_TIMEOUT_* expected). Shows that a stuck wait ends with an error code instead of a
+ * hang and that the context stays usable. */
+int gg_selftest_wait_timeout(unsigned long long timeout_ns, int* status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GROUPED_GEMM_B200_H_ */
