@@ -1,0 +1,477 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 grouped GEMM on the BASELINE workloads (default: mixed512, 1 GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload mixed512] [--impl reference]
+
+One step = one executor run (tile-counter reset + one persistent kernel launch) over the rank's
+problem set, inputs resident in HBM. Prints ONE JSON line on rank 0:
+
+  value      aggregate TFLOP/s = 2*sum(MNK) of all ranks / max-over-ranks device time
+  e2e        the same metric through the C-ABI with the inputs copied from pinned host memory
+             and D copied back inside every timed step
+  roofline   the kernel's algorithmic bytes (or FLOPs) per launch / its event-timed duration
+             against the measured peak in MEASURED_PEAKS.json
+  cpu_baseline  the reference's own host GEMM (compute_reference, built from its sources into
+             oracle/_ref) on a bounded sample, one host thread, as the reference runs it
+  ref_gpu    the reference's own CUDA kernels (built for sm_100a) on the same device buffers
+
+Multi-GPU (torchrun, one process per GPU): weak scaling. The global problem set is N seeded
+replicas of the workload (seeds 42..42+N-1); gg_partition cuts it into N tile-weighted shards
+and each rank materialises and runs only its own. No collective touches the data path; NCCL is
+used for the barrier and the max-over-ranks timing reduction only.
+
+--impl reference times the reference's CPU implementation of the path (compute_reference) on
+all host threads, on a bounded sample of the same workload per step (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "aggregate TFLOP/s (2·ΣMNK/s) at 1/2/4/8 B200, % of dense FP16 peak"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+DEFAULT_CTA = {"small16": (128, 128, 64), "mixed512": (128, 128, 64), "moe": (128, 256, 64),
+               "tiny4096": (128, 64, 64), "skew": (128, 256, 64)}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", default="mixed512", choices=["small16", "mixed512", "moe", "tiny4096", "skew"])
+    ap.add_argument("--sort-mode", type=int, default=2, help="0 none, 1 by K, 2 by tiles, 3 by tiles then K")
+    ap.add_argument("--cta", default=None, help="tile shape MxNxK (default per workload)")
+    ap.add_argument("--no-extras", action="store_true", help="skip the sort-mode sweep and the reference GPU row")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU work of the cpu_baseline sample")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        d["source"] = "measured"
+        return d
+    return dict(FALLBACK_PEAKS)
+
+
+# ---- clocks ------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons around the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+        self.t0 = self.t1 = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu=timestamp,{self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "20"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+
+    def mark(self, start: bool):
+        if start:
+            self.t0 = time.time()
+        else:
+            self.t1 = time.time()
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 10:
+                    continue
+                try:
+                    ts = time.mktime(time.strptime(parts[0].split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                    rows.append((ts, float(parts[2]), float(parts[3]), parts[5:]))
+                except Exception:
+                    continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        # timestamps have 1 s resolution: keep samples within the timed window +- 1 s
+        inwin = [r for r in rows if self.t0 is not None and self.t0 - 1.0 <= r[0] <= (self.t1 or self.t0) + 1.0] or rows
+        load = [r for r in inwin if r[1] > 0.5 * r[2]] or inwin
+        reasons = set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in load:
+            for nm, val in zip(names, r[3][1:]):
+                if val.lower() in ("active", "yes"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(r[1] for r in load), "sm_max_mhz": max(r[2] for r in load),
+                "samples": len(load), "reasons": sorted(reasons)}
+
+
+# ---- workload sharding -------------------------------------------------------------------------
+def rank_shapes(workload: str, world: int, rank: int, cfg):
+    """This rank's shard of the N-replica problem set, as a Shapes of independent pieces."""
+    import grouped_gemm_gpu_kernel_b200 as gg
+    from grouped_gemm_gpu_kernel_b200 import workloads as W
+
+    reps = [W.make_shapes(workload, seed=42 + r) for r in range(world)]
+    if world == 1:
+        return reps[0], reps[0].flops
+    glob_dims, glob_alpha, glob_beta = [], [], []
+    for s in reps:
+        glob_dims += s.dims
+        glob_alpha += s.alpha
+        glob_beta += s.beta
+    probs = [gg.ProblemDesc(m, n, k, 1, 1, None, 1, max(1, k), max(1, n), max(1, n), max(1, n)) for m, n, k in glob_dims]
+    pieces, _ = gg.partition(probs, cfg, world, rank)
+    base = reps[0]
+    dims = [(pc.rows, pc.cols, glob_dims[pc.problem][2]) for pc in pieces]
+    out = W.Shapes(workload, dims, [glob_alpha[pc.problem] for pc in pieces], [glob_beta[pc.problem] for pc in pieces],
+                   base.has_c, base.a_law, base.a_std, base.b_law, base.b_std)
+    return out, float(sum(s.flops for s in reps))
+
+
+# ---- CPU baselines -----------------------------------------------------------------------------
+def host_problem(m, n, k, alpha, beta, shapes, rng):
+    def draw(count, law, std):
+        if law == "normal":
+            return rng.normal(0.0, std, size=max(count, 1)).astype(np.float16).view(np.uint16)
+        return rng.uniform(-1.0, 1.0, size=max(count, 1)).astype(np.float16).view(np.uint16)
+
+    return dict(m=m, n=n, k=k, lda=max(1, k), ldb=max(1, n), ldc=max(1, n), ldd=max(1, n), alpha=alpha, beta=beta,
+                a=draw(m * k, shapes.a_law, shapes.a_std), b=draw(k * n, shapes.b_law, shapes.b_std),
+                c=rng.uniform(-1, 1, size=max(m * n, 1)).astype(np.float32))
+
+
+def cpu_sample(shapes, target_flops, seed=1234):
+    """Problems of the workload, in order, until their FLOPs reach target_flops (at least one);
+    a problem larger than the target is cut to a row band of the needed height."""
+    rng = np.random.default_rng(seed)
+    out, fl = [], 0.0
+    for (m, n, k), al, be in zip(shapes.dims, shapes.alpha, shapes.beta):
+        if m <= 0 or n <= 0:
+            continue
+        f = 2.0 * m * n * k
+        if fl + f > target_flops and out:
+            break
+        if f > target_flops:
+            m = max(1, int(target_flops / (2.0 * n * max(k, 1))))
+            f = 2.0 * m * n * k
+        out.append(host_problem(m, n, k, al, be, shapes, rng))
+        fl += f
+        if fl >= target_flops:
+            break
+    return out, fl
+
+
+def time_cpu(problems, threads):
+    """(seconds, kind): the reference's compute_reference when built, else the oracle's port."""
+    import oracle as O
+
+    if O.ref_available():
+        _, secs = O.ref_host_gemm(problems, threads=threads)
+        return secs, "reference"
+    t0 = time.perf_counter()
+    for p in problems:
+        O.gemm_f32_refloop(p["m"], p["n"], p["k"], p["a"], p["lda"], p["b"], p["ldb"], p["c"], p["ldc"], p["alpha"],
+                           p["beta"], p["ldd"])
+    return time.perf_counter() - t0, "port"
+
+
+def cpu_baseline(shapes, seconds_target):
+    probe, pf = cpu_sample(shapes, 2e8)
+    secs, kind = time_cpu(probe, 1)
+    rate = pf / max(secs, 1e-6)
+    sample, fl = cpu_sample(shapes, max(pf, rate * seconds_target))
+    secs, kind = time_cpu(sample, 1)
+    return {"value": fl / secs / 1e12, "unit": "TFLOP/s", "cores": 1, "kind": kind,
+            "sample": f"first {len(sample)} problems of the workload in input order ({fl / 1e9:.2f} GFLOP, "
+                      f"host-generated with the workload's value laws), FP32 host GEMM "
+                      f"tests/test_correctness.cu:85-102, {secs:.1f} s single-thread"}
+
+
+def run_reference_arm(args):
+    from grouped_gemm_gpu_kernel_b200 import workloads as W
+
+    shapes = W.make_shapes(args.workload)
+    threads = os.cpu_count() or 1
+    # size one step so that warmup + steps take about a minute in total
+    probe, pf = cpu_sample(shapes, 2e8)
+    secs, kind = time_cpu(probe, threads)
+    rate = pf / max(secs, 1e-6)
+    per_step = max(pf, rate * min(5.0, 60.0 / max(1, args.steps + args.warmup)))
+    sample, fl = cpu_sample(shapes, per_step)
+    for _ in range(args.warmup):
+        time_cpu(sample, threads)
+    times = []
+    for _ in range(args.steps):
+        s, kind = time_cpu(sample, threads)
+        times.append(s)
+    total = sum(times)
+    value = fl * args.steps / total / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "sample_problems": len(sample), "sample_gflop": fl / 1e9,
+                   "threads": threads},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind,
+                         "sample": f"first {len(sample)} problems of {args.workload} ({fl / 1e9:.2f} GFLOP) per step, "
+                                   f"reference compute_reference over problems on {threads} host threads"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---- the B200 arm ------------------------------------------------------------------------------
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference_arm(args)
+        return
+
+    import torch
+
+    import grouped_gemm_gpu_kernel_b200 as gg
+    from grouped_gemm_gpu_kernel_b200 import workloads as W
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    cta = tuple(int(x) for x in args.cta.split("x")) if args.cta else DEFAULT_CTA[args.workload]
+    cfg = gg.KernelConfig(*cta)
+    shapes, global_flops = rank_shapes(args.workload, world, rank, cfg)
+    ps = W.allocate(shapes, dev, seed=42 + rank, d_fill=0.0)
+    problems = ps.problems()
+    prep_t0 = time.perf_counter()
+    prep = gg.prepare_problem_set(problems, cfg, args.sort_mode)
+    ex = gg.GroupedGemmExecutor()
+    st = ex.build(prep, cfg)
+    prep_ms = 1e3 * (time.perf_counter() - prep_t0)
+    if st != 0:
+        raise RuntimeError(f"executor build failed: {st}")
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(args.warmup, 3)):
+        assert ex.run(stream) == 0
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    for _ in range(max(args.warmup, 3)):
+        assert ex.run(stream) == 0
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.mark(True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        ex.run(stream)
+    e1.record(stream)
+    barrier()
+    clocks.mark(False)
+    clock_info = clocks.stop()
+    local_ms = e0.elapsed_time(e1) / args.steps
+    if ex.status() != 0:
+        raise RuntimeError("a bounded wait timed out inside the kernel during the timed region")
+    ms = max_over_ranks(local_ms)
+    value = global_flops / (ms * 1e-3) / 1e12
+
+    peaks = load_peaks()
+    alg_bytes = shapes.algorithmic_bytes()
+    local_flops = shapes.flops
+    ai = local_flops / alg_bytes
+    ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    if ai < ridge:
+        achieved = alg_bytes / (local_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": None, "peak_source": peaks["source"],
+                "algorithmic_bytes_per_launch": alg_bytes}
+    else:
+        achieved = local_flops / (local_ms * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": achieved / peaks["bf16_tflops"], "traffic": None, "peak_source": peaks["source"],
+                "algorithmic_flops_per_launch": local_flops}
+    traffic_path = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(traffic_path):
+        with open(traffic_path) as f:
+            tr = json.load(f).get(f"{args.workload}/{cta[0]}x{cta[1]}x{cta[2]}")
+        if tr:
+            roof["traffic"] = tr
+
+    # ---- e2e through the C-ABI with host buffers (pinned), copies inside the timed step ----
+    e2e = None
+    if args.e2e_steps > 0:
+        h_a = torch.empty(ps.a.shape, dtype=ps.a.dtype, pin_memory=True)
+        h_b = torch.empty(ps.b.shape, dtype=ps.b.dtype, pin_memory=True)
+        h_a.copy_(ps.a)
+        h_b.copy_(ps.b)
+        reads_c = ps.c is not None and any(b != 0.0 for b in shapes.beta)
+        h_c = None
+        if reads_c:
+            h_c = torch.empty(ps.c.shape, dtype=ps.c.dtype, pin_memory=True)
+            h_c.copy_(ps.c)
+        h_d = torch.empty(ps.d.shape, dtype=ps.d.dtype, pin_memory=True)
+        h2d = h_a.numel() * 2 + h_b.numel() * 2 + (h_c.numel() * 4 if h_c is not None else 0)
+        d2h = h_d.numel() * 4
+
+        def e2e_step():
+            with torch.cuda.stream(stream):
+                ps.a.copy_(h_a, non_blocking=True)
+                ps.b.copy_(h_b, non_blocking=True)
+                if h_c is not None:
+                    ps.c.copy_(h_c, non_blocking=True)
+                assert ex.run(stream) == 0
+                h_d.copy_(ps.d, non_blocking=True)
+
+        e2e_step()
+        barrier()
+        e2 = torch.cuda.Event(enable_timing=True)
+        e3 = torch.cuda.Event(enable_timing=True)
+        e2.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e3.record(stream)
+        barrier()
+        e2e_ms = max_over_ranks(e2.elapsed_time(e3) / args.e2e_steps)
+        e2e = {"value": global_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+               "path": "pinned host A/B(/C) -> cudaMemcpyAsync -> gg_executor_run -> D back to pinned host"}
+
+    extras = {}
+    if not args.no_extras and world == 1:
+        sweep = {}
+        for mode in range(4):
+            p2 = gg.prepare_problem_set(problems, cfg, mode)
+            ex2 = gg.GroupedGemmExecutor()
+            assert ex2.build(p2, cfg) == 0
+            for _ in range(5):
+                ex2.run(stream)
+            torch.cuda.synchronize()
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            for _ in range(50):
+                ex2.run(stream)
+            a1.record(stream)
+            torch.cuda.synchronize()
+            t = a0.elapsed_time(a1) / 50
+            sweep[gg.sort_mode_name(mode)] = {"ms": t, "tflops": local_flops / (t * 1e-3) / 1e12,
+                                             "grid": ex2.grid_ctas(), "tiles": ex2.total_tiles()}
+            ex2.close()
+        extras["sort_modes"] = sweep
+        extras["ref_gpu"] = reference_gpu_row(problems, stream, local_flops)
+
+    cpu = None
+    if rank == 0 and world == 1:
+        cpu = cpu_baseline(shapes, args.cpu_seconds)
+
+    if rank == 0:
+        n_tiles = ex.total_tiles()
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": args.workload, "problems_per_gpu": len(shapes.dims), "cta": "x".join(map(str, cta)),
+                       "sort_mode": gg.sort_mode_name(args.sort_mode), "tiles": n_tiles, "grid_ctas": ex.grid_ctas(),
+                       "global_gflop": global_flops / 1e9, "l2": f"inputs larger than L2 ({alg_bytes / 1e9:.2f} GB "
+                       "algorithmic footprint per GPU > 126 MB), no flush", "accumulate": "f32",
+                       "prep_build_ms": prep_ms, "parallelism": f"dp{world} (tile-balanced shards)"},
+            "pct_dense_fp16_peak": 100.0 * value / (world * peaks["bf16_tflops"]),
+            "peak_source": peaks["source"],
+            "roofline": roof,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "clocks": clock_info,
+            "gpu_launches": args.steps,
+        }
+        line.update(extras)
+        print(json.dumps(line), flush=True)
+    ex.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def reference_gpu_row(problems, stream, flops):
+    """The reference's own kernels (sm_100a build of its sources) on the same device buffers."""
+    import ctypes
+
+    import oracle as O
+
+    if not O.ref_available():
+        return {"unavailable": "oracle/_ref/libgg_ref.so not built"}
+    lib = O.load_ref()
+    arr = (O.RefProblem * max(1, len(problems)))()
+    for i, p in enumerate(problems):
+        arr[i] = O.RefProblem(p.m, p.n, p.k, p.a, p.b, p.c, p.d, p.lda, p.ldb, p.ldc, p.ldd, p.alpha, p.beta)
+    rows = {}
+    best = None
+    for cm, cn, ck in ((64, 64, 16), (128, 64, 32), (64, 128, 32)):
+        for mode in (0, 2):
+            ms, tiles, grid = ctypes.c_float(0), ctypes.c_int(0), ctypes.c_int(0)
+            st = lib.ref_time_grouped(arr, len(problems), mode, cm, cn, ck, 1, 3, 10, ctypes.c_void_p(stream.cuda_stream),
+                                      ctypes.byref(ms), ctypes.byref(tiles), ctypes.byref(grid))
+            key = f"{cm}x{cn}x{ck}/{'none' if mode == 0 else 'sort_by_tiles'}"
+            if st != 0:
+                rows[key] = {"error": st}
+                continue
+            tf = flops / (ms.value * 1e-3) / 1e12
+            rows[key] = {"ms": ms.value, "tflops": tf}
+            if best is None or tf > best[1]:
+                best = (key, tf)
+    return {"best": best[0] if best else None, "best_tflops": best[1] if best else None, "runs": rows}
+
+
+if __name__ == "__main__":
+    main()

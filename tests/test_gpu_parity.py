@@ -1,0 +1,452 @@
+"""Parity of the sm_100a kernel with the oracle, through the C-ABI (needs a B200).
+
+Accuracy bar: for every checked element
+    |D - D_fp64| / max(|D_fp64|, scale)  <=  2e-3 * sqrt(max(K, 1) / 1024)
+with scale = |alpha| * sqrt(sum_k (a_ik b_kj)^2) + |beta c_ij| from the FP64 oracle
+(oracle.rel_err / oracle.tolerance). Small configurations are checked in full; the full-size
+ones (mixed512, moe, skew) on sampled rows and columns. The reference test's own inputs are
+also held to its own absolute tolerance of 2e-2 against its own host GEMM output
+(reference tests/test_correctness.cu:357).
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+from concurrent.futures import ThreadPoolExecutor
+
+import numpy as np
+import pytest
+
+import grouped_gemm_gpu_kernel_b200 as gg
+import oracle as O
+from grouped_gemm_gpu_kernel_b200 import capi
+from grouped_gemm_gpu_kernel_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ALL_CONFIGS = gg.REFERENCE_CONFIGS + gg.NATIVE_CONFIGS
+MODES = (gg.SortMode.kNone, gg.SortMode.kByK, gg.SortMode.kByTiles, gg.SortMode.kByTilesThenK)
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def run_grouped(problems, cfg, mode, stream=None, check_status=True):
+    torch = _torch()
+    prep = gg.prepare_problem_set(problems, cfg, mode)
+    ex = gg.GroupedGemmExecutor()
+    st = ex.build(prep, cfg)
+    assert st == 0, f"build failed: {st}"
+    st = ex.run(stream)
+    assert st == 0, f"run failed: {st}"
+    torch.cuda.synchronize()
+    if check_status:
+        assert ex.status() == 0, "a bounded wait timed out inside the kernel"
+    return ex
+
+
+class HostSlabs:
+    """Host copies of a DeviceProblemSet's slabs, sliced per problem for the oracle."""
+
+    def __init__(self, ps: W.DeviceProblemSet):
+        torch = _torch()
+        self.ps = ps
+        self.a = ps.a.view(torch.int16).cpu().numpy().view(np.uint16)
+        self.b = ps.b.view(torch.int16).cpu().numpy().view(np.uint16)
+        self.c = ps.c.cpu().numpy() if ps.c is not None else None
+        self.d = ps.d.cpu().numpy()
+
+    def problem(self, i):
+        m, n, k = self.ps.shapes.dims[i]
+        a = self.a[self.ps.a_off[i]:self.ps.a_off[i] + max(m * k, 1)]
+        b = self.b[self.ps.b_off[i]:self.ps.b_off[i] + max(k * n, 1)]
+        c = self.c[self.ps.c_off[i]:self.ps.c_off[i] + max(m * n, 1)] if self.c is not None else None
+        d = self.d[self.ps.d_off[i]:self.ps.d_off[i] + max(m * n, 0)]
+        return a, b, c, d
+
+
+def check_full(ps: W.DeviceProblemSet, threads: int = 8) -> float:
+    """Every element of every problem against the FP64 oracle; returns the worst error/tolerance."""
+    hs = HostSlabs(ps)
+
+    def one(i):
+        m, n, k = ps.shapes.dims[i]
+        if m <= 0 or n <= 0:
+            return 0.0
+        a, b, c, d = hs.problem(i)
+        ref, scale = O.gemm_f64(m, n, k, a, max(1, k), b, max(1, n), c, max(1, n), ps.shapes.alpha[i], ps.shapes.beta[i])
+        return O.rel_err(d.reshape(m, n), ref, scale) / O.tolerance(k)
+
+    with ThreadPoolExecutor(threads) as pool:
+        worst = max(pool.map(one, range(len(ps.shapes.dims))), default=0.0)
+    return worst
+
+
+def check_sampled(ps: W.DeviceProblemSet, rows_per=4, cols_per=96, seed=0, threads=8) -> float:
+    rng = np.random.default_rng(seed)
+    jobs = []
+    for i, (m, n, k) in enumerate(ps.shapes.dims):
+        if m <= 0 or n <= 0:
+            continue
+        rows = np.unique(np.concatenate([[0, m - 1], rng.integers(0, m, size=rows_per)])).astype(np.int64)
+        cols = np.unique(np.concatenate([[0, n - 1], rng.integers(0, n, size=cols_per)])).astype(np.int64)
+        h = W.host_inputs(ps, i, rows, cols)
+        jobs.append((i, len(rows), len(cols), k, h))
+
+    def one(job):
+        i, r, c, k, h = job
+        ref, scale = O.gemm_f64(r, c, k, h["a"], max(1, k), h["b"], c, h["c"], c, ps.shapes.alpha[i], ps.shapes.beta[i])
+        return O.rel_err(h["d"], ref, scale) / O.tolerance(k)
+
+    with ThreadPoolExecutor(threads) as pool:
+        return max(pool.map(one, jobs), default=0.0)
+
+
+# ---------------------------------------------------------------------------------------------
+def test_bounded_wait_selftest_reports_timeout_and_context_survives(cuda):
+    torch = _torch()
+    st, bits = gg.selftest_wait_timeout(5_000_000)
+    assert st == 0
+    assert bits & capi.GG_STATUS_TIMEOUT_MMA and not (bits & 0x100)
+    x = torch.ones(1024, device=cuda)
+    assert float(x.sum()) == 1024.0
+
+
+def test_occupancy_report(cuda):
+    for cfg in ALL_CONFIGS:
+        st, info = gg.query_occupancy(cfg)
+        assert st == 0
+        assert info.sm_count >= 100 and info.active_blocks_per_sm == 1 and info.threads_per_block == 256
+        assert info.warps_per_block == 8 and info.using_tensor_cores
+        assert 100_000 < info.dynamic_shared_bytes <= 232_448
+        assert 0 < info.registers_per_thread <= 255 and info.registers_per_block == info.registers_per_thread * 256
+        assert info.theoretical_occupancy == pytest.approx(8 / info.max_warps_per_sm)
+
+
+def test_single_tile_tma_path(cuda):
+    torch = _torch()
+    g = torch.Generator(device=cuda).manual_seed(1)
+    A = torch.empty(128, 64, dtype=torch.float16, device=cuda).uniform_(-1, 1, generator=g)
+    B = torch.empty(64, 128, dtype=torch.float16, device=cuda).uniform_(-1, 1, generator=g)
+    D = torch.full((128, 128), float("nan"), device=cuda)
+    p = gg.problem_from_tensors(A, B, None, D)
+    run_grouped([p], gg.KernelConfig(128, 128, 64), gg.SortMode.kNone)
+    ref = A.double() @ B.double()
+    assert torch.allclose(D.double(), ref, rtol=1e-5, atol=1e-4)
+
+
+def _fixture_problems(cuda):
+    """The reference test's eight problems with its own inputs, on the device."""
+    torch = _torch()
+    from tests.test_oracle import ref_test_problems
+
+    probs, keep, refs = [], [], []
+    for p in ref_test_problems():
+        a = torch.from_numpy(p["a"].view(np.int16).copy()).to(cuda).view(torch.float16)
+        b = torch.from_numpy(p["b"].view(np.int16).copy()).to(cuda).view(torch.float16)
+        c = torch.from_numpy(p["c"].copy()).to(cuda)
+        d = torch.full((O.safe_elems(p["m"], p["ldd"]),), float("nan"), device=cuda)
+        keep += [a, b, c, d]
+        probs.append(gg.ProblemDesc(p["m"], p["n"], p["k"], a.data_ptr(), b.data_ptr(), c.data_ptr(), d.data_ptr(),
+                                    p["lda"], p["ldb"], p["ldc"], p["ldd"], p["alpha"], p["beta"]))
+        refs.append((p, d))
+    return probs, keep, refs
+
+
+def _check_fixture(refs):
+    for p, d in refs:
+        m, n, k = p["m"], p["n"], p["k"]
+        if m <= 0 or n <= 0:
+            continue
+        got = d.cpu().numpy()[:m * n].reshape(m, n)
+        want = p["ref"][:m * n].reshape(m, n)
+        assert np.abs(got - want).max() <= 2e-2  # the reference test's own bar
+        ref64, scale = O.gemm_f64(m, n, k, p["a"], p["lda"], p["b"], p["ldb"], p["c"], p["ldc"], p["alpha"], p["beta"])
+        assert O.rel_err(got, ref64, scale) <= O.tolerance(k), (m, n, k)
+
+
+@pytest.mark.parametrize("cfg", ALL_CONFIGS, ids=lambda c: f"{c.cta_m}x{c.cta_n}x{c.cta_k}")
+def test_reference_test_set_all_modes_and_baseline(cuda, cfg):
+    """The reference test's matrix (tests/test_correctness.cu:309-362) on every config."""
+    torch = _torch()
+    probs, keep, refs = _fixture_problems(cuda)
+    for mode in MODES:
+        for _, d in refs:
+            d.fill_(float("nan"))
+        assert gg.run_grouped_gemm_once(probs, mode, cfg) == 0
+        torch.cuda.synchronize()
+        _check_fixture(refs)
+    for _, d in refs:
+        d.fill_(float("nan"))
+    assert gg.run_baseline_per_problem(probs, cfg) == 0
+    torch.cuda.synchronize()
+    _check_fixture(refs)
+    assert gg.run_grouped_gemm_once([], gg.SortMode.kByTiles, cfg) == 0
+    assert gg.run_baseline_per_problem([], cfg) == 0
+
+
+@pytest.mark.parametrize("cfg", [gg.KernelConfig(128, 128, 64), gg.KernelConfig(64, 64, 16),
+                                 gg.KernelConfig(128, 256, 64)], ids=lambda c: f"{c.cta_m}x{c.cta_n}")
+def test_small16_full(cuda, cfg):
+    ps = W.allocate(W.make_shapes("small16"), cuda)
+    for mode in MODES:
+        ps.d.fill_(float("nan"))
+        run_grouped(ps.problems(), cfg, mode)
+        assert check_full(ps) <= 1.0
+    ps.d.fill_(float("nan"))
+    assert gg.run_baseline_per_problem(ps.problems(), cfg) == 0
+    _torch().cuda.synchronize()
+    assert check_full(ps) <= 1.0
+
+
+@pytest.mark.parametrize("cfg", [gg.KernelConfig(128, 128, 64), gg.KernelConfig(64, 64, 16)],
+                         ids=lambda c: f"{c.cta_m}x{c.cta_n}")
+def test_tiny4096_full(cuda, cfg):
+    ps = W.allocate(W.make_shapes("tiny4096"), cuda)
+    run_grouped(ps.problems(), cfg, gg.SortMode.kByTiles)
+    assert check_full(ps) <= 1.0
+
+
+def test_mixed512_all_modes_sampled(cuda):
+    ps = W.allocate(W.make_shapes("mixed512"), cuda)
+    for mode in MODES:
+        ps.d.fill_(float("nan"))
+        run_grouped(ps.problems(), gg.KernelConfig(128, 128, 64), mode)
+        assert check_sampled(ps, seed=int(mode)) <= 1.0
+    ps.d.fill_(float("nan"))
+    run_grouped(ps.problems(), gg.KernelConfig(128, 256, 64), gg.SortMode.kByTiles)
+    assert check_sampled(ps, seed=7) <= 1.0
+    # canaries: the 256-byte alignment gaps between problems' D are never written
+    d = ps.d.cpu().numpy()
+    written = np.zeros(d.size, bool)
+    for i, (m, n, k) in enumerate(ps.shapes.dims):
+        written[ps.d_off[i]:ps.d_off[i] + m * n] = True
+    assert np.isnan(d[~written]).all()
+    assert np.isfinite(d[written]).all()
+
+
+@pytest.mark.slow
+def test_moe_full_size_sampled(cuda):
+    ps = W.allocate(W.make_shapes("moe"), cuda)
+    run_grouped(ps.problems(), gg.KernelConfig(128, 256, 64), gg.SortMode.kByTiles)
+    assert check_sampled(ps, rows_per=3, cols_per=64) <= 1.0
+    del ps
+
+
+@pytest.mark.slow
+def test_skew_full_size_sampled(cuda):
+    ps = W.allocate(W.make_shapes("skew"), cuda)
+    run_grouped(ps.problems(), gg.KernelConfig(128, 256, 64), gg.SortMode.kByTiles)
+    assert check_sampled(ps, rows_per=6, cols_per=64) <= 1.0
+
+
+def test_determinism_bitwise(cuda):
+    torch = _torch()
+    ps = W.allocate(W.make_shapes("mixed512"), cuda)
+    cfg = gg.KernelConfig(128, 128, 64)
+    run_grouped(ps.problems(), cfg, gg.SortMode.kByTiles)
+    first = ps.d.clone()
+    ps.d.fill_(0.0)
+    run_grouped(ps.problems(), cfg, gg.SortMode.kNone)
+    assert torch.equal(first, ps.d)
+
+
+def _edge_problem(cuda, m, n, k, lda=None, ldb=None, ldc=None, ldd=None, alpha=1.0, beta=0.0, a_shift=0,
+                  b_shift=0, c_mode="rand", seed=0):
+    """One problem with its own buffers; shifts misalign the base pointers by 2-byte steps."""
+    torch = _torch()
+    lda = lda or max(1, k)
+    ldb = ldb or max(1, n)
+    ldc = ldc or max(1, n)
+    ldd = ldd or max(1, n)
+    g = torch.Generator(device=cuda).manual_seed(seed)
+    A = torch.empty(O.safe_elems(m, lda) + 8, dtype=torch.float16, device=cuda).uniform_(-1, 1, generator=g)
+    B = torch.empty(O.safe_elems(k, ldb) + 8, dtype=torch.float16, device=cuda).uniform_(-1, 1, generator=g)
+    C = torch.empty(O.safe_elems(m, ldc), dtype=torch.float32, device=cuda).uniform_(-1, 1, generator=g)
+    if c_mode == "nan":
+        C.fill_(float("nan"))
+    D = torch.full((O.safe_elems(m, ldd) + 64,), float("nan"), device=cuda)
+    cptr = None if c_mode == "null" else C.data_ptr()
+    p = gg.ProblemDesc(m, n, k, A.data_ptr() + 2 * a_shift, B.data_ptr() + 2 * b_shift, cptr, D.data_ptr(),
+                       lda, ldb, ldc, ldd, alpha, beta)
+    return p, (A, B, C, D, a_shift, b_shift, c_mode)
+
+
+def _check_edge(p, bufs):
+    A, B, C, D, a_shift, b_shift, c_mode = bufs
+    m, n, k = p.m, p.n, p.k
+    a = A.view(_torch().int16).cpu().numpy().view(np.uint16)[a_shift:]
+    b = B.view(_torch().int16).cpu().numpy().view(np.uint16)[b_shift:]
+    c = None if c_mode == "null" else C.cpu().numpy()
+    d = D.cpu().numpy()
+    if m <= 0 or n <= 0:
+        assert np.isnan(d).all()
+        return
+    ref, scale = O.gemm_f64(m, n, k, a, p.lda, b, p.ldb, c, p.ldc, p.alpha, p.beta)
+    got = np.stack([d[r * p.ldd:r * p.ldd + n] for r in range(m)])
+    assert O.rel_err(got, ref, scale) <= O.tolerance(k), (m, n, k)
+    # nothing outside the m x n window of D was written (row padding and the trailing guard)
+    mask = np.ones(d.size, bool)
+    for r in range(m):
+        mask[r * p.ldd:r * p.ldd + n] = False
+    assert np.isnan(d[mask]).all()
+
+
+EDGE_CASES = {
+    "k0_beta_c": dict(m=70, n=50, k=0, beta=0.75),
+    "k0_beta0": dict(m=130, n=136, k=0, beta=0.0),
+    "beta0_nan_c": dict(m=96, n=80, k=64, beta=0.0, c_mode="nan"),
+    "null_c_beta": dict(m=40, n=72, k=24, beta=0.9, c_mode="null"),
+    "alpha0": dict(m=33, n=65, k=17, alpha=0.0, beta=1.0),
+    "one_by_one": dict(m=1, n=1, k=1),
+    "k1_wide": dict(m=3, n=300, k=1),
+    "k_not_mult_64": dict(m=128, n=128, k=1000),
+    "deep_k": dict(m=130, n=264, k=4160),
+    "padded_aligned_ld": dict(m=200, n=136, k=72, lda=80, ldb=144, ldc=140, ldd=144, beta=-1.0),
+    "padded_odd_ld": dict(m=77, n=51, k=35, lda=41, ldb=53, ldc=55, ldd=57, beta=0.5),
+    "misaligned_a": dict(m=128, n=128, k=128, a_shift=1),
+    "misaligned_b": dict(m=100, n=256, k=192, b_shift=3),
+    "lda_lt_8_mult": dict(m=64, n=64, k=64, lda=68),
+    "n8": dict(m=300, n=8, k=96),
+    "m_exact_tiles": dict(m=256, n=512, k=128, beta=0.25),
+}
+
+
+@pytest.mark.parametrize("cfg", [gg.KernelConfig(128, 128, 64), gg.KernelConfig(64, 128, 32),
+                                 gg.KernelConfig(128, 64, 32)], ids=lambda c: f"{c.cta_m}x{c.cta_n}")
+def test_edge_cases(cuda, cfg):
+    cases = [(_edge_problem(cuda, seed=i, **kw)) for i, kw in enumerate(EDGE_CASES.values())]
+    probs = [p for p, _ in cases]
+    run_grouped(probs, cfg, gg.SortMode.kByTiles)
+    for (p, bufs), name in zip(cases, EDGE_CASES):
+        try:
+            _check_edge(p, bufs)
+        except AssertionError as e:
+            raise AssertionError(f"edge case {name}: {e}") from e
+
+
+def test_zero_dim_problems_untouched(cuda):
+    cases = [_edge_problem(cuda, m=0, n=64, k=16), _edge_problem(cuda, m=64, n=0, k=16),
+             _edge_problem(cuda, m=64, n=64, k=16)]
+    run_grouped([p for p, _ in cases], gg.KernelConfig(128, 128, 64), gg.SortMode.kNone)
+    for p, bufs in cases:
+        _check_edge(p, bufs)
+
+
+def test_two_executors_two_streams(cuda):
+    torch = _torch()
+    ps1 = W.allocate(W.make_shapes("small16"), cuda, seed=1)
+    ps2 = W.allocate(W.make_shapes("mixed512"), cuda, seed=2)
+    cfg = gg.KernelConfig(128, 128, 64)
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    torch.cuda.synchronize()  # inputs were written on the default stream
+    e1, e2 = gg.GroupedGemmExecutor(), gg.GroupedGemmExecutor()
+    assert e1.build(gg.prepare_problem_set(ps1.problems(), cfg, 2), cfg) == 0
+    assert e2.build(gg.prepare_problem_set(ps2.problems(), cfg, 2), cfg) == 0
+    for _ in range(3):
+        assert e1.run(s1) == 0
+        assert e2.run(s2) == 0
+    torch.cuda.synchronize()
+    assert e1.status() == 0 and e2.status() == 0
+    assert check_full(ps1) <= 1.0
+    assert check_sampled(ps2) <= 1.0
+
+
+def test_executor_rebuild_and_reuse(cuda):
+    ps1 = W.allocate(W.make_shapes("small16"), cuda, seed=3)
+    ps2 = W.allocate(W.make_shapes("tiny4096"), cuda, seed=4)
+    cfg = gg.KernelConfig(128, 128, 64)
+    ex = gg.GroupedGemmExecutor()
+    assert ex.build(gg.prepare_problem_set(ps1.problems(), cfg, 0), cfg) == 0
+    assert ex.run() == 0 and ex.run() == 0
+    assert ex.build(gg.prepare_problem_set(ps2.problems(), cfg, 3), cfg) == 0
+    assert ex.problem_count() == 4096 and ex.total_tiles() == 4096
+    assert 0 < ex.grid_ctas() <= ex.total_tiles()
+    assert ex.run() == 0
+    _torch().cuda.synchronize()
+    assert ex.status() == 0
+    assert check_full(ps1) <= 1.0 and check_full(ps2) <= 1.0
+
+
+def test_persistent_ctas_override(cuda):
+    ps = W.allocate(W.make_shapes("small16"), cuda, seed=5)
+    for ctas in (1, 3, 1000):
+        cfg = gg.KernelConfig(128, 128, 64, persistent_ctas=ctas)
+        ps.d.fill_(float("nan"))
+        ex = run_grouped(ps.problems(), cfg, gg.SortMode.kByK)
+        assert ex.grid_ctas() == ctas
+        assert check_full(ps) <= 1.0
+
+
+# ---- the reference's own build, run on the same inputs ---------------------------------------
+needs_ref = pytest.mark.skipif(not O.ref_available(), reason="reference build oracle/_ref absent")
+
+
+@needs_ref
+def test_golden_inputs_are_the_reference_generators(cuda):
+    """The fixture's inputs equal what the reference test's own init_problem_buffers makes."""
+    import ctypes
+
+    fx = np.load(os.path.join(REPO, "tests", "golden", "ref_test_shapes.npz"))
+    lib = O.load_ref()
+    a, b, c, r = (np.zeros_like(fx[x]) for x in ("a", "b", "c", "ref"))
+    al, be = np.zeros_like(fx["alpha"]), np.zeros_like(fx["beta"])
+    shapes = np.ascontiguousarray(fx["shapes"].reshape(-1).astype(np.int32))
+    P = ctypes.POINTER
+    rc = lib.ref_test_inputs(shapes.ctypes.data_as(P(ctypes.c_int)), len(fx["shapes"]),
+                             a.ctypes.data_as(P(ctypes.c_uint16)), b.ctypes.data_as(P(ctypes.c_uint16)),
+                             c.ctypes.data_as(P(ctypes.c_float)), al.ctypes.data_as(P(ctypes.c_float)),
+                             be.ctypes.data_as(P(ctypes.c_float)), r.ctypes.data_as(P(ctypes.c_float)))
+    assert rc == 0
+    for x, y in ((a, "a"), (b, "b"), (c, "c"), (r, "ref"), (al, "alpha"), (be, "beta")):
+        assert np.array_equal(x, fx[y]), y
+
+
+def _ref_problems(problems):
+    arr = (O.RefProblem * max(1, len(problems)))()
+    for i, p in enumerate(problems):
+        arr[i] = O.RefProblem(p.m, p.n, p.k, p.a, p.b, p.c, p.d, p.lda, p.ldb, p.ldc, p.ldd, p.alpha, p.beta)
+    return arr
+
+
+@needs_ref
+@pytest.mark.parametrize("name", ["small16", "tiny4096", "mixed512"])
+def test_agrees_with_reference_cuda_build(cuda, name):
+    """The reference's own kernels (sm_100a build) and this kernel agree on the same inputs."""
+    torch = _torch()
+    ps = W.allocate(W.make_shapes(name), cuda)
+    probs = ps.problems()
+    lib = O.load_ref()
+    assert lib.ref_run_grouped_once(_ref_problems(probs), len(probs), 2, 64, 64, 16, 1, None) == 0
+    torch.cuda.synchronize()
+    ref_d = ps.d.clone()
+    ps.d.fill_(float("nan"))
+    run_grouped(probs, gg.KernelConfig(128, 128, 64), gg.SortMode.kByTiles)
+    ours = ps.d.clone()
+    worst = 0.0
+    for i, (m, n, k) in enumerate(ps.shapes.dims):
+        if m <= 0 or n <= 0:
+            continue
+        sl = slice(ps.d_off[i], ps.d_off[i] + m * n)
+        x, y = ours[sl].double(), ref_d[sl].double()
+        scale = torch.maximum(y.abs(), torch.full_like(y, np.sqrt(max(k, 1)) / 3.0))
+        worst = max(worst, float(((x - y).abs() / scale).max()) / O.tolerance(k))
+    assert worst <= 1.0
+    if name != "mixed512":
+        ps.d.copy_(ref_d)
+        assert check_full(ps) <= 1.0  # the reference itself meets the bar on these inputs
+
+
+@needs_ref
+def test_reference_test_program_passes_on_this_library(cuda):
+    """The reference's own test program, compiled against this library's drop-in header."""
+    exe = os.path.join(REPO, "oracle", "_ref", "ref_test_on_b200")
+    if not os.path.exists(exe):
+        pytest.skip("drop-in test program not built (make -C oracle dropin)")
+    out = subprocess.run([exe], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stdout + out.stderr
+    assert "All correctness checks passed." in out.stdout
