@@ -18,8 +18,9 @@ EXPORTED_SYMBOLS = (
     "gg_executor_create", "gg_executor_destroy", "gg_executor_build", "gg_executor_run",
     "gg_executor_problem_count", "gg_executor_total_tiles", "gg_executor_grid_ctas", "gg_executor_status",
     "gg_run_grouped_gemm_once", "gg_run_baseline_per_problem", "gg_count_non_empty_problems",
-    "gg_partition", "gg_selftest_wait_timeout",
+    "gg_partition", "gg_selftest_wait_timeout", "gg_run_grouped_gemm_noalloc",
 )
+GG_NOALLOC_MAX_PROBLEMS = 1024
 
 GG_STATUS_TIMEOUT_PRODUCER = 0x1
 GG_STATUS_TIMEOUT_MMA = 0x2
@@ -93,6 +94,7 @@ def load() -> ctypes.CDLL:
         "gg_partition": ([pp, ctypes.c_int, pc, ctypes.c_int, ctypes.c_int, P(GGShardPiece), ctypes.c_int, i32p,
                           P(ctypes.c_double)], ctypes.c_int),
         "gg_selftest_wait_timeout": ([ctypes.c_ulonglong, i32p], ctypes.c_int),
+        "gg_run_grouped_gemm_noalloc": ([pp, ctypes.c_int, ctypes.c_int, pc, vp], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

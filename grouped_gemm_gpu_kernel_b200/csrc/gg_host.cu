@@ -565,3 +565,150 @@ int gg_selftest_wait_timeout(unsigned long long timeout_ns, int* status) {
 }
 
 }  // extern "C"
+
+// ---- grouped GEMM without any allocation ------------------------------------------------------
+// For callers that cannot call cudaMalloc: code running under a caching allocator or a memory
+// pool that owns the whole device and forbids side allocations, code on a latency-critical path
+// where an allocation (and the synchronisation cudaFree implies) is not acceptable, or code that
+// must not grow its memory footprint after start-up. Everything the persistent kernel needs
+// besides the caller's A/B/C/D -- the problem table, the TMA descriptors, the tile offsets, the
+// tile counter and the status word -- lives in one fixed file-scope device array, sized for at
+// most GG_NOALLOC_MAX_PROBLEMS problems (480 KiB, held by every GPU that loads this library until
+// the process exits). Host-side preparation uses fixed static buffers as well.
+namespace gg {
+namespace {
+
+constexpr int kNoAllocMaxProblems = GG_NOALLOC_MAX_PROBLEMS;
+constexpr size_t kNoAllocMapsBytes = static_cast<size_t>(kNoAllocMaxProblems) * 3 * sizeof(CUtensorMap);
+constexpr size_t kNoAllocDescsOff = kNoAllocMapsBytes;
+constexpr size_t kNoAllocOffsOff =
+    (kNoAllocDescsOff + static_cast<size_t>(kNoAllocMaxProblems) * sizeof(DeviceProblemDesc) + 127) / 128 * 128;
+constexpr size_t kNoAllocCounterOff =
+    (kNoAllocOffsOff + static_cast<size_t>(kNoAllocMaxProblems + 1) * sizeof(int) + 127) / 128 * 128;
+constexpr size_t kNoAllocBytes = (kNoAllocCounterOff + 128 + 4095) / 4096 * 4096;
+static_assert(kNoAllocBytes == 480 * 1024, "the documented size of the no-allocation scratch");
+
+// The scratch itself. Host code must never pass this name to a kernel: on the host it only
+// names a stand-in, not device memory. Its device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+std::mutex g_noalloc_mu;                           // guards the host staging buffers below
+unsigned char g_noalloc_image[kNoAllocBytes];      // host image of the scratch, uploaded per call
+int g_noalloc_order[kNoAllocMaxProblems];          // sorted_to_original
+int g_noalloc_tmp[kNoAllocMaxProblems];            // merge-sort buffer
+void* g_noalloc_dev_ptr[kMaxDevices] = {};         // device address of the scratch, per device
+
+// Stable order of the problems for a sort mode: the reference's rule (src/grouped_gemm.cu:977-1005),
+// applied with a bottom-up merge sort over fixed buffers (no heap use). On ties the element from
+// the left run comes first, so equal keys keep their input order, as std::stable_sort does.
+bool noalloc_before(const gg_problem* ps, int mode, int cta_m, int cta_n, int x, int y) {
+  if (mode == GG_SORT_BY_TILES || mode == GG_SORT_BY_TILES_THEN_K) {
+    const int tx = tile_count(ps[x].m, ps[x].n, cta_m, cta_n), ty = tile_count(ps[y].m, ps[y].n, cta_m, cta_n);
+    if (tx != ty) return tx > ty;
+  }
+  return k_rule_before(ps[x], ps[y]);
+}
+
+void noalloc_sort(const gg_problem* ps, int count, int mode, int cta_m, int cta_n) {
+  for (int i = 0; i < count; ++i) g_noalloc_order[i] = i;
+  if (mode != GG_SORT_BY_K && mode != GG_SORT_BY_TILES && mode != GG_SORT_BY_TILES_THEN_K) return;
+  int* src = g_noalloc_order;
+  int* dst = g_noalloc_tmp;
+  for (int width = 1; width < count; width *= 2) {
+    for (int lo = 0; lo < count; lo += 2 * width) {
+      const int mid = std::min(lo + width, count), hi = std::min(lo + 2 * width, count);
+      int i = lo, j = mid, o = lo;
+      while (i < mid && j < hi) dst[o++] = noalloc_before(ps, mode, cta_m, cta_n, src[j], src[i]) ? src[j++] : src[i++];
+      while (i < mid) dst[o++] = src[i++];
+      while (j < hi) dst[o++] = src[j++];
+    }
+    std::swap(src, dst);
+  }
+  if (src != g_noalloc_order) std::memcpy(g_noalloc_order, src, static_cast<size_t>(count) * sizeof(int));
+}
+
+// Device address of the scratch on the current device, looked up once per device.
+cudaError_t noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t st = cudaGetDevice(&dev);
+  if (st != cudaSuccess) return st;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (!g_noalloc_dev_ptr[dev]) {
+    void* p = nullptr;
+    st = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (st != cudaSuccess) return st;
+    g_noalloc_dev_ptr[dev] = p;
+  }
+  *out = g_noalloc_dev_ptr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace gg
+
+extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count, int sort_mode,
+                                           const gg_config* config, void* stream) {
+  const gg::Variant v = gg::variant_of(config);
+  if (v == gg::Variant::kUnsupported) return cudaErrorInvalidValue;
+  if (count < 0 || (count > 0 && !problems)) return cudaErrorInvalidValue;
+  if (count > gg::kNoAllocMaxProblems) return cudaErrorMemoryAllocation;  // does not fit the fixed scratch
+  for (int i = 0; i < count; ++i) {
+    if (problems[i].m < 0 || problems[i].n < 0 || problems[i].k < 0) return cudaErrorInvalidValue;
+    if (!problems[i].a || !problems[i].b || !problems[i].d) return cudaErrorInvalidDevicePointer;
+  }
+  if (count == 0) return cudaSuccess;
+
+  std::lock_guard<std::mutex> lock(gg::g_noalloc_mu);
+  const int bm = gg::variant_bm(v), bn = gg::variant_bn(v);
+  gg::noalloc_sort(problems, count, sort_mode, config->cta_m, config->cta_n);
+  auto* maps = reinterpret_cast<CUtensorMap*>(gg::g_noalloc_image);
+  auto* descs = reinterpret_cast<DeviceProblemDesc*>(gg::g_noalloc_image + gg::kNoAllocDescsOff);
+  auto* offs = reinterpret_cast<int*>(gg::g_noalloc_image + gg::kNoAllocOffsOff);
+  offs[0] = 0;
+  for (int s = 0; s < count; ++s) {
+    const gg_problem& p = problems[gg::g_noalloc_order[s]];
+    offs[s + 1] = offs[s] + gg::tile_count(p.m, p.n, config->cta_m, config->cta_n);
+    descs[s] = gg::make_device_problem(p, bm, bn, &maps[static_cast<size_t>(s) * 3]);
+  }
+  const int total = offs[count];
+  if (total == 0) return cudaSuccess;
+
+  void* scratch = nullptr;
+  cudaError_t st = gg::noalloc_scratch(&scratch);
+  if (st != cudaSuccess) return st;
+  int sms = 0, active = 0;
+  st = gg::sm_count_and_slots(v, &sms, &active);
+  if (st != cudaSuccess) return st;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  unsigned char* dev = static_cast<unsigned char*>(scratch);
+  // Only the used prefix of each region is uploaded. A pageable-source copy returns once the
+  // host image has been staged, so the image can be refilled by the next call.
+  st = cudaMemcpyAsync(dev, gg::g_noalloc_image, static_cast<size_t>(count) * 3 * sizeof(CUtensorMap),
+                       cudaMemcpyHostToDevice, s);
+  if (st == cudaSuccess)
+    st = cudaMemcpyAsync(dev + gg::kNoAllocDescsOff, gg::g_noalloc_image + gg::kNoAllocDescsOff,
+                         static_cast<size_t>(count) * sizeof(DeviceProblemDesc), cudaMemcpyHostToDevice, s);
+  if (st == cudaSuccess)
+    st = cudaMemcpyAsync(dev + gg::kNoAllocOffsOff, gg::g_noalloc_image + gg::kNoAllocOffsOff,
+                         static_cast<size_t>(count + 1) * sizeof(int), cudaMemcpyHostToDevice, s);
+  // The tile counter and the status word must start at zero; the scratch keeps the last call's
+  // contents otherwise.
+  if (st == cudaSuccess) st = cudaMemsetAsync(dev + gg::kNoAllocCounterOff, 0, 2 * sizeof(int), s);
+  if (st != cudaSuccess) return st;
+
+  gg::KernelParams kp;
+  std::memset(&kp, 0, sizeof(kp));
+  kp.problems = reinterpret_cast<const DeviceProblemDesc*>(dev + gg::kNoAllocDescsOff);
+  kp.tmaps = reinterpret_cast<const CUtensorMap*>(dev);
+  kp.tile_offsets = reinterpret_cast<const int*>(dev + gg::kNoAllocOffsOff);
+  kp.tile_counter = reinterpret_cast<int*>(dev + gg::kNoAllocCounterOff);
+  kp.status = reinterpret_cast<int*>(dev + gg::kNoAllocCounterOff + sizeof(int));
+  kp.timeout_ns = gg::wait_timeout_ns();
+  kp.problem_count = count;
+  kp.total_tiles = total;
+  kp.raster_group = gg::raster_group();
+  kp.single_mode = 0;
+  const int grid = config->persistent_ctas > 0 ? config->persistent_ctas : std::max(1, std::min(sms * active, total));
+  return gg::launch_grouped_kernel(v, kp, grid, s);
+}

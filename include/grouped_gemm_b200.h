@@ -185,6 +185,26 @@ int gg_partition(const gg_problem* problems, int count, const gg_config* config,
  * hang and that the context stays usable. */
 int gg_selftest_wait_timeout(unsigned long long timeout_ns, int* status);
 
+/* No counterpart in the reference. The grouped GEMM of gg_run_grouped_gemm_once for callers that
+ * cannot allocate device memory: code whose device memory is owned by a caching allocator or a
+ * pool that forbids side allocations, latency-critical paths where cudaMalloc/cudaFree and the
+ * synchronisation they imply are not acceptable, or processes that must not grow their device
+ * footprint after start-up. It calls no cudaMalloc, cudaFree or other allocating routine, on
+ * the device or the host: the problem table, TMA descriptors, tile offsets, tile counter and
+ * status word live in one fixed device array of this library (480 KiB, held on every GPU that
+ * loads the library until the process exits). The caller still provides A, B, C and D.
+ *   - At most GG_NOALLOC_MAX_PROBLEMS problems; more returns cudaErrorMemoryAllocation (2) and
+ *     launches nothing. Other errors as for gg_run_grouped_gemm_once.
+ *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress);
+ *     make that first call before any stream capture.
+ *   - Every call uses the same array and it keeps the last call's contents (the tile counter
+ *     and status word are cleared by each call). Calls whose work overlaps on the GPU -- on two
+ *     streams, or from two host threads on different streams -- race on it: order them on one
+ *     stream. Results match gg_run_grouped_gemm_once bit for bit. */
+#define GG_NOALLOC_MAX_PROBLEMS 1024
+int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count, int sort_mode,
+                                const gg_config* config, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
