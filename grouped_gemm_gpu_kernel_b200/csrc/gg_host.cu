@@ -110,10 +110,28 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, int
   return r == CUDA_SUCCESS;
 }
 
-// Device record of one problem plus its A, B and D tensor maps. TMA is used for A/B only when
-// both operands qualify, for D when it qualifies; everything else takes the zero-fill load path
-// and masked direct stores.
-DeviceProblemDesc make_device_problem(const gg_problem& p, int bm, int bn, CUtensorMap maps[3]) {
+// B (k x n FP16, row pitch ldb) seen as 64 columns x k rows x (n / 64) full column chunks, the
+// chunk dimension 128 bytes apart: one box {64, 64, chunks} fills a whole B stage in the layout
+// the MMA reads (chunk-major, 8 KB per 64x64 chunk). Only full chunks are mapped, so no box can
+// read past a row end; tiles that reach past the last full chunk use the 2-D map instead.
+bool encode_b_chunks(CUtensorMap* map, const void* base, int k, int n, int64_t row_bytes, int chunks_per_box) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  const int full_chunks = n / 64;
+  if (!enc || k <= 0 || full_chunks <= 0 || row_bytes <= 0 || (row_bytes % 16) != 0 || !aligned16(base)) return false;
+  const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(full_chunks)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_bytes), 128};
+  const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(chunks_per_box)};
+  const cuuint32_t elem_strides[3] = {1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+                         elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Device record of one problem plus its kMapsPerProblem tensor maps. TMA is used for A/B only
+// when both operands qualify, for D when it qualifies; everything else takes the zero-fill load
+// path and masked direct stores.
+DeviceProblemDesc make_device_problem(const gg_problem& p, int bm, int bn, CUtensorMap* maps) {
   DeviceProblemDesc d{};
   d.m = p.m;
   d.n = p.n;
@@ -133,13 +151,18 @@ DeviceProblemDesc make_device_problem(const gg_problem& p, int bm, int bn, CUten
   d.tiles_n = has_tiles ? ceil_div(p.n, bn) : 0;
   d.k_blocks = p.k > 0 ? ceil_div(p.k, kBK) : 0;
   unsigned flags = 0;
-  std::memset(maps, 0, 3 * sizeof(CUtensorMap));
+  std::memset(maps, 0, kMapsPerProblem * sizeof(CUtensorMap));
   if (has_tiles && p.k > 0 &&
-      encode_2d(&maps[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, p.a, p.k, p.m, static_cast<int64_t>(p.lda) * 2, kBK, bm) &&
-      encode_2d(&maps[1], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, p.b, p.n, p.k, static_cast<int64_t>(p.ldb) * 2, 64, kBK))
+      encode_2d(&maps[kMapA], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, p.a, p.k, p.m, static_cast<int64_t>(p.lda) * 2, kBK,
+                bm) &&
+      encode_2d(&maps[kMapB], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, p.b, p.n, p.k, static_cast<int64_t>(p.ldb) * 2, 64,
+                kBK)) {
     flags |= grouped_gemm::kFlagTmaAB;
+    if (encode_b_chunks(&maps[kMapB3], p.b, p.k, p.n, static_cast<int64_t>(p.ldb) * 2, bn / 64))
+      flags |= grouped_gemm::kFlagTmaB3;
+  }
   if (has_tiles &&
-      encode_2d(&maps[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.d, p.n, p.m, static_cast<int64_t>(p.ldd) * 4, 32, 32))
+      encode_2d(&maps[kMapD], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.d, p.n, p.m, static_cast<int64_t>(p.ldd) * 4, 32, bm))
     flags |= grouped_gemm::kFlagTmaD;
   if (p.c != nullptr && p.beta != 0.0f) flags |= grouped_gemm::kFlagReadC;
   if (aligned16(p.c) && (p.ldc % 4) == 0) flags |= grouped_gemm::kFlagCVec;
@@ -331,12 +354,12 @@ int gg_executor_build(gg_executor* ex, const gg_problem* sorted_problems, int co
 
   const int bm = gg::variant_bm(v), bn = gg::variant_bn(v);
   std::vector<DeviceProblemDesc> descs(static_cast<size_t>(count));
-  std::vector<CUtensorMap> maps(static_cast<size_t>(count) * 3);
+  std::vector<CUtensorMap> maps(static_cast<size_t>(count) * gg::kMapsPerProblem);
   for (int i = 0; i < count; ++i) {
     const gg_problem& p = sorted_problems[i];
     if (p.m < 0 || p.n < 0 || p.k < 0) return cudaErrorInvalidValue;
     if (!p.a || !p.b || !p.d) return cudaErrorInvalidDevicePointer;
-    descs[static_cast<size_t>(i)] = gg::make_device_problem(p, bm, bn, &maps[static_cast<size_t>(i) * 3]);
+    descs[static_cast<size_t>(i)] = gg::make_device_problem(p, bm, bn, &maps[static_cast<size_t>(i) * gg::kMapsPerProblem]);
   }
   if (count == 0 || total_tiles <= 0) {
     ex->problem_count = count;
@@ -573,20 +596,20 @@ int gg_selftest_wait_timeout(unsigned long long timeout_ns, int* status) {
 // must not grow its memory footprint after start-up. Everything the persistent kernel needs
 // besides the caller's A/B/C/D -- the problem table, the TMA descriptors, the tile offsets, the
 // tile counter and the status word -- lives in one fixed file-scope device array, sized for at
-// most GG_NOALLOC_MAX_PROBLEMS problems (480 KiB, held by every GPU that loads this library until
+// most GG_NOALLOC_MAX_PROBLEMS problems (608 KiB, held by every GPU that loads this library until
 // the process exits). Host-side preparation uses fixed static buffers as well.
 namespace gg {
 namespace {
 
 constexpr int kNoAllocMaxProblems = GG_NOALLOC_MAX_PROBLEMS;
-constexpr size_t kNoAllocMapsBytes = static_cast<size_t>(kNoAllocMaxProblems) * 3 * sizeof(CUtensorMap);
+constexpr size_t kNoAllocMapsBytes = static_cast<size_t>(kNoAllocMaxProblems) * kMapsPerProblem * sizeof(CUtensorMap);
 constexpr size_t kNoAllocDescsOff = kNoAllocMapsBytes;
 constexpr size_t kNoAllocOffsOff =
     (kNoAllocDescsOff + static_cast<size_t>(kNoAllocMaxProblems) * sizeof(DeviceProblemDesc) + 127) / 128 * 128;
 constexpr size_t kNoAllocCounterOff =
     (kNoAllocOffsOff + static_cast<size_t>(kNoAllocMaxProblems + 1) * sizeof(int) + 127) / 128 * 128;
 constexpr size_t kNoAllocBytes = (kNoAllocCounterOff + 128 + 4095) / 4096 * 4096;
-static_assert(kNoAllocBytes == 480 * 1024, "the documented size of the no-allocation scratch");
+static_assert(kNoAllocBytes == 608 * 1024, "the documented size of the no-allocation scratch");
 
 // The scratch itself. Host code must never pass this name to a kernel: on the host it only
 // names a stand-in, not device memory. Its device address comes from cudaGetSymbolAddress.
@@ -668,7 +691,7 @@ extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count
   for (int s = 0; s < count; ++s) {
     const gg_problem& p = problems[gg::g_noalloc_order[s]];
     offs[s + 1] = offs[s] + gg::tile_count(p.m, p.n, config->cta_m, config->cta_n);
-    descs[s] = gg::make_device_problem(p, bm, bn, &maps[static_cast<size_t>(s) * 3]);
+    descs[s] = gg::make_device_problem(p, bm, bn, &maps[static_cast<size_t>(s) * gg::kMapsPerProblem]);
   }
   const int total = offs[count];
   if (total == 0) return cudaSuccess;
@@ -684,7 +707,7 @@ extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count
   unsigned char* dev = static_cast<unsigned char*>(scratch);
   // Only the used prefix of each region is uploaded. A pageable-source copy returns once the
   // host image has been staged, so the image can be refilled by the next call.
-  st = cudaMemcpyAsync(dev, gg::g_noalloc_image, static_cast<size_t>(count) * 3 * sizeof(CUtensorMap),
+  st = cudaMemcpyAsync(dev, gg::g_noalloc_image, static_cast<size_t>(count) * gg::kMapsPerProblem * sizeof(CUtensorMap),
                        cudaMemcpyHostToDevice, s);
   if (st == cudaSuccess)
     st = cudaMemcpyAsync(dev + gg::kNoAllocDescsOff, gg::g_noalloc_image + gg::kNoAllocDescsOff,

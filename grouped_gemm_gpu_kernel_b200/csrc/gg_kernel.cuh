@@ -2,10 +2,11 @@
 //
 // One CTA per SM (shared memory > half an SM's), 256 threads in five warp roles:
 //
-//   warps 0-3  epilogue   TMEM -> registers (tcgen05.ld), D = alpha*acc + beta*C, then a 128-byte
-//                         swizzled shared-memory staging tile stored by TMA (clipped at the
-//                         problem edge), or masked direct stores when D is not TMA-eligible.
-//                         Warp w reads TMEM lanes 32w..32w+31 = tile rows 32w..32w+31.
+//   warps 0-3  epilogue   TMEM -> registers (tcgen05.ld), D = alpha*acc + beta*C, then per 32-column
+//                         chunk one 128-byte-swizzled staging tile of all BM rows that a single
+//                         TMA store writes out (clipped at the problem edge), or masked direct
+//                         stores when D is not TMA-eligible. Warp w reads TMEM lanes
+//                         32w..32w+31 = tile rows 32w..32w+31.
 //   warp 4     MMA        allocates 2*BN TMEM columns (two accumulators, so the epilogue of one
 //                         tile overlaps the mainloop of the next); one thread issues
 //                         tcgen05.mma.kind::f16 (M=128, N=BN, K=16) and tcgen05.commit.
@@ -15,7 +16,8 @@
 //                         reference's binary search, src/grouped_gemm.cu:219-234), copies the
 //                         problem record into a 4-deep shared-memory ring read by every role.
 //   warps 6-7  producers  fill a multi-stage ring of A/B shared-memory tiles: one thread issues
-//                         TMA tensor loads for aligned problems; all 64 threads load with zero
+//                         TMA tensor loads for aligned problems (one box for A and, for tiles
+//                         inside N, one 3-D box for all of B); all 64 threads load with zero
 //                         fill for problems whose base or leading dimension TMA cannot take (the
 //                         reference's scalar zero-fill path, src/grouped_gemm.cu:273-371), writing
 //                         the same 128-byte-swizzled layout the TMA would.
@@ -146,6 +148,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOffset);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 4);
   volatile int* prod_go = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 8);
+  volatile int* epi_go = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 12);  // two words
 
   const int warp = static_cast<int>(threadIdx.x >> 5);
   const int lane = static_cast<int>(threadIdx.x & 31);
@@ -166,6 +169,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
     ptx::mbar_init(drain_bar, 1);
     *abort_flag = 0;
     *prod_go = 0;
+    epi_go[0] = 0;
+    epi_go[1] = 0;
     ptx::fence_mbar_init();
   }
   if (warp == kMmaWarp) {
@@ -216,6 +221,15 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
         if (local < 0 || tiles_m <= 0 || tiles_n <= 0 || local >= tiles_m * tiles_n) continue;
         raster_tile(local, tiles_m, tiles_n, p.raster_group, tile_m, tile_n);
         if (lane < kDescWords) reinterpret_cast<int*>(&s->desc)[lane] = w;
+        // Warm the tensor maps this tile will use (only those that were encoded) while the tile
+        // waits in the ring.
+        const unsigned fl = static_cast<unsigned>(
+            __shfl_sync(0xffffffffu, w, static_cast<int>(offsetof(DeviceProblemDesc, flags) / 4)));
+        const bool map_valid = (lane == kMapA || lane == kMapB) ? (fl & grouped_gemm::kFlagTmaAB) != 0u
+                               : lane == kMapB3                 ? (fl & grouped_gemm::kFlagTmaB3) != 0u
+                               : lane == kMapD                  ? (fl & grouped_gemm::kFlagTmaD) != 0u
+                                                                : false;
+        if (map_valid) ptx::prefetch_tensormap(maps + kMapsPerProblem * q + lane);
         pidx = q;
         break;
       }
@@ -235,7 +249,6 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
     // ======================= producers =======================
     const int ptid = static_cast<int>(threadIdx.x) - kProdWarp0 * 32;
     uint32_t it = 0;  // global k-block counter: stage = it % S, phase = (it / S) & 1
-    int last_problem = -1;
     bool aborted = false;
     for (int t = 0;; ++t) {
       const int slot = t % kRing;
@@ -259,12 +272,12 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
 
       if (flags & grouped_gemm::kFlagTmaAB) {
         if (ptid == 0) {
-          const CUtensorMap* ma = maps + 3 * q;
-          const CUtensorMap* mb = ma + 1;
-          if (q != last_problem) {
-            ptx::prefetch_tensormap(ma);
-            ptx::prefetch_tensormap(mb);
-          }
+          const CUtensorMap* ma = maps + kMapsPerProblem * q + kMapA;
+          const CUtensorMap* mb = maps + kMapsPerProblem * q + kMapB;
+          const CUtensorMap* mb3 = maps + kMapsPerProblem * q + kMapB3;
+          // One 3-D box loads the whole B stage when every 64-column chunk of the tile lies
+          // inside N; an edge tile loads chunk by chunk so columns past N are zero-filled.
+          const bool b_one_box = (flags & grouped_gemm::kFlagTmaB3) && (tile_n + 1) * BN <= n;
           for (int kb = 0; kb < kb_count; ++kb) {
             const int st = static_cast<int>(it % S);
             const uint32_t ph = (it / S) & 1u;
@@ -276,15 +289,18 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
             const uint32_t b_dst = a_dst + L::kABytes;
             ptx::mbar_arrive_expect_tx(full_bar(st), L::kATxBytes + L::kBTxBytes);
             ptx::tma_load_2d(a_dst, ma, full_bar(st), kb * kBK, tile_m * BM);
+            if (b_one_box) {
+              ptx::tma_load_3d(b_dst, mb3, full_bar(st), 0, kb * kBK, tile_n * (BN / 64));
+            } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              ptx::tma_load_2d(b_dst + j * 8192u, mb, full_bar(st), tile_n * BN + j * 64, kb * kBK);
+              for (int j = 0; j < BN / 64; ++j)
+                ptx::tma_load_2d(b_dst + j * 8192u, mb, full_bar(st), tile_n * BN + j * 64, kb * kBK);
+            }
             ++it;
           }
         } else {
           it += static_cast<uint32_t>(kb_count);
         }
-        last_problem = q;
         if (aborted) break;
       } else {
         for (int kb = 0; kb < kb_count; ++kb) {
@@ -386,15 +402,19 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
     __syncwarp();
   } else {
     // ======================= epilogue (warps 0-3) =======================
-    const int qw = warp;  // TMEM lane quarter
+    // The four warps move in step: thread 0 waits on the ring and accumulator barriers and
+    // broadcasts the outcome through epi_go after a named barrier, so a timed-out wait ends
+    // the loop in every warp at the same point (no warp is left inside a named barrier).
+    const int qw = warp;  // TMEM lane quarter = tile rows 32*qw .. 32*qw+31
+    const int et = static_cast<int>(threadIdx.x);
     uint32_t store_count = 0;
     for (int t = 0;; ++t) {
       const int slot = t % kRing;
       const uint32_t par = static_cast<uint32_t>(t / kRing) & 1u;
-      int ok = 1;
-      if (lane == 0) ok = wait_phase(ringf_bar(slot), par, abort_flag, p.status, tmo, GG_STATUS_TIMEOUT_EPILOGUE);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
+      if (et == 0)
+        epi_go[0] = wait_phase(ringf_bar(slot), par, abort_flag, p.status, tmo, GG_STATUS_TIMEOUT_EPILOGUE) ? 1 : 0;
+      ptx::named_bar_sync(2, kEpiThreads);
+      if (!epi_go[0]) break;
       const TileSlot* s = &ring[slot];
       const int q = s->problem;
       const int tile_m = s->tile_m, tile_n = s->tile_n;
@@ -409,25 +429,26 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
       if (lane == 0) ptx::mbar_arrive(ringe_bar(slot));
       if (q < 0) break;
       const int buf = t & 1;
-      if (lane == 0)
-        ok = wait_phase(accf_bar(buf), static_cast<uint32_t>(t >> 1) & 1u, abort_flag, p.status, tmo,
-                        GG_STATUS_TIMEOUT_EPILOGUE);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
+      if (et == 0)
+        epi_go[1] = wait_phase(accf_bar(buf), static_cast<uint32_t>(t >> 1) & 1u, abort_flag, p.status, tmo,
+                               GG_STATUS_TIMEOUT_EPILOGUE) ? 1 : 0;
+      ptx::named_bar_sync(2, kEpiThreads);
+      if (!epi_go[1]) break;
       ptx::tc_fence_after_sync();
 
       const int row0 = tile_m * BM + qw * 32;
       const int row = row0 + lane;
       const int col0 = tile_n * BN;
-      int nchunks = 0;
-      if (qw * 32 < BM && row0 < m) nchunks = min(BN / 32, (n - col0 + 31) / 32);
+      const bool warp_rows = qw * 32 < BM && row0 < m;  // warp-uniform
+      const int nchunks = min(BN / 32, (n - col0 + 31) / 32);  // tile-uniform
       const uint32_t t_addr = tmem_base + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(qw * 32) << 16);
       const bool read_c = (flags & grouped_gemm::kFlagReadC) != 0u;
-      const CUtensorMap* md = maps + 3 * q + 2;
+      const bool tma_d = (flags & grouped_gemm::kFlagTmaD) != 0u;
+      const CUtensorMap* md = maps + kMapsPerProblem * q + kMapD;
 
       for (int c = 0; c < nchunks; ++c) {
         float acc[32];
-        if (kb_count > 0) {
+        if (warp_rows && kb_count > 0) {
           uint32_t r[32];
           ptx::tmem_load_32cols(t_addr + static_cast<uint32_t>(c * 32), r);
 #pragma unroll
@@ -446,7 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
         float cv[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) cv[j] = 0.0f;
-        if (read_c && row < m) {
+        if (read_c && warp_rows && row < m) {
           const float* crow = cptr + static_cast<int64_t>(row) * ldc + cc;
           if ((flags & grouped_gemm::kFlagCVec) && cc + 32 <= n) {
 #pragma unroll
@@ -469,23 +490,29 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
 #pragma unroll
         for (int j = 0; j < 32; ++j) out[j] = alpha * acc[j] + beta * cv[j];
 
-        if (flags & grouped_gemm::kFlagTmaD) {
-          uint8_t* stile = smem + L::kEpiOffset + (qw * 2 + static_cast<int>(store_count & 1u)) * kEpiTileBytes;
-          if (lane == 0) ptx::bulk_wait_read_le1();  // the store that last used this tile is done reading
-          __syncwarp();
+        if (tma_d) {
+          // All BM rows of this 32-column chunk go out in one TMA store from a shared staging
+          // tile (two tiles alternate; the store that used this one two chunks ago must have
+          // finished reading it). Rows past M are clipped by the tensor map.
+          uint8_t* stile = smem + L::kEpiOffset + static_cast<int>(store_count & 1u) * kEpiTileBytes;
+          if (et == 0) ptx::bulk_wait_read_le1();
+          ptx::named_bar_sync(2, kEpiThreads);
+          if (qw * 32 < BM) {
+            const int r = qw * 32 + lane;
 #pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4) {
-            *reinterpret_cast<float4*>(stile + lane * 128 + ((j4 ^ (lane & 7)) << 4)) =
-                make_float4(out[4 * j4], out[4 * j4 + 1], out[4 * j4 + 2], out[4 * j4 + 3]);
+            for (int j4 = 0; j4 < 8; ++j4) {
+              *reinterpret_cast<float4*>(stile + r * 128 + ((j4 ^ (r & 7)) << 4)) =
+                  make_float4(out[4 * j4], out[4 * j4 + 1], out[4 * j4 + 2], out[4 * j4 + 3]);
+            }
           }
           ptx::fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            ptx::tma_store_2d(md, ptx::smem_addr(stile), cc, row0);
+          ptx::named_bar_sync(2, kEpiThreads);
+          if (et == 0) {
+            ptx::tma_store_2d(md, ptx::smem_addr(stile), cc, tile_m * BM);
             ptx::bulk_commit_group();
           }
           ++store_count;
-        } else if (row < m) {
+        } else if (warp_rows && row < m) {
           float* drow = dptr + static_cast<int64_t>(row) * ldd + cc;
           if ((flags & grouped_gemm::kFlagDVec) && cc + 32 <= n) {
 #pragma unroll
@@ -499,13 +526,13 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
           }
         }
       }
-      if (nchunks == 0) {
+      if (nchunks <= 0) {
         ptx::tc_fence_before_sync();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(acce_bar(buf));
       }
     }
-    if (lane == 0) ptx::bulk_wait_all();
+    if (et == 0) ptx::bulk_wait_all();
     __syncwarp();
   }
 

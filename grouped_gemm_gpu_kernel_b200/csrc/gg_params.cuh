@@ -23,7 +23,15 @@ constexpr int kSchedWarp = 5;
 constexpr int kProdWarp0 = 6;
 constexpr int kProdThreads = 64;
 constexpr int kRingConsumerWarps = kEpiWarps + 1 + 2;  // arrivals that free one ring slot
-constexpr int kEpiTileBytes = 32 * 128;                // one warp's 32 rows x 32 FP32 columns
+constexpr int kEpiTileBytes = 128 * 128;               // 128 rows x 32 FP32 columns of D
+constexpr int kEpiThreads = kEpiWarps * 32;
+// Tensor maps per problem, in this order: A (64 K x BM rows), B by 64-column chunk (64 N x 64 K),
+// B as one 3-D box per stage (64 N x 64 K x BN/64 chunks; full chunks only), D (32 cols x BM rows).
+constexpr int kMapsPerProblem = 4;
+constexpr int kMapA = 0;
+constexpr int kMapB = 1;
+constexpr int kMapB3 = 2;
+constexpr int kMapD = 3;
 constexpr int kDescWords = static_cast<int>(sizeof(DeviceProblemDesc) / 4);
 
 struct TileSlot {
@@ -36,7 +44,7 @@ struct TileSlot {
 
 template <int BN>
 struct StageCount {
-  static constexpr int value = BN >= 256 ? 4 : (BN >= 128 ? 5 : 6);
+  static constexpr int value = BN >= 256 ? 4 : 6;
 };
 
 template <int BM, int BN>
@@ -46,12 +54,12 @@ struct SmemLayout {
   static constexpr int kBBytes = BN * 128;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiOffset = kStages * kStageBytes;
-  static constexpr int kEpiBytes = kEpiWarps * 2 * kEpiTileBytes;
+  static constexpr int kEpiBytes = 2 * kEpiTileBytes;  // double-buffered staging tile
   static constexpr int kRingOffset = kEpiOffset + kEpiBytes;
   static constexpr int kBarOffset = kRingOffset + kRing * static_cast<int>(sizeof(TileSlot));
   static constexpr int kNumBars = 2 * kStages + 4 + 2 * kRing + 1;
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
-  static constexpr int kBytes = kMiscOffset + 16;
+  static constexpr int kBytes = kMiscOffset + 32;
   static constexpr int kDynamicSmem = kBytes + 1024;  // slack to align the base to 1024 bytes
   static constexpr uint32_t kATxBytes = static_cast<uint32_t>(BM) * 128;
   static constexpr uint32_t kBTxBytes = static_cast<uint32_t>(BN) * 128;
@@ -64,10 +72,10 @@ struct SmemLayout {
 };
 
 struct KernelParams {
-  CUtensorMap single_maps[3];         // baseline launch: A, B, D maps of its one problem
+  CUtensorMap single_maps[kMapsPerProblem];  // baseline launch: the maps of its one problem
   DeviceProblemDesc single_desc;      // baseline launch: its one problem
   const DeviceProblemDesc* problems;  // grouped launch: problem table in sorted order
-  const CUtensorMap* tmaps;           // grouped launch: A, B, D maps per problem (64-byte aligned)
+  const CUtensorMap* tmaps;           // grouped launch: kMapsPerProblem maps per problem (64-byte aligned)
   const int* tile_offsets;            // grouped launch: problem_count + 1 prefix sums
   int* tile_counter;                  // grouped launch: claim counter, zero at launch
   int* status;                        // GG_STATUS_* bits

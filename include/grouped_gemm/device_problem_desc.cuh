@@ -16,6 +16,7 @@ enum DeviceProblemFlags : unsigned {
   kFlagReadC = 4u,   // c != nullptr && beta != 0: the epilogue reads C
   kFlagCVec = 8u,    // C rows can be read as 16-byte vectors
   kFlagDVec = 16u,   // D rows can be written as 16-byte vectors (direct-store path)
+  kFlagTmaB3 = 32u,  // B also has a 3-D map that loads a whole stage of full 64-column chunks at once
 };
 
 struct DeviceProblemDesc {

@@ -191,7 +191,7 @@ int gg_selftest_wait_timeout(unsigned long long timeout_ns, int* status);
  * synchronisation they imply are not acceptable, or processes that must not grow their device
  * footprint after start-up. It calls no cudaMalloc, cudaFree or other allocating routine, on
  * the device or the host: the problem table, TMA descriptors, tile offsets, tile counter and
- * status word live in one fixed device array of this library (480 KiB, held on every GPU that
+ * status word live in one fixed device array of this library (608 KiB, held on every GPU that
  * loads the library until the process exits). The caller still provides A, B, C and D.
  *   - At most GG_NOALLOC_MAX_PROBLEMS problems; more returns cudaErrorMemoryAllocation (2) and
  *     launches nothing. Other errors as for gg_run_grouped_gemm_once.
