@@ -42,7 +42,7 @@ sys.path.insert(0, REPO)
 
 METRIC = "aggregate TFLOP/s (2·ΣMNK/s) at 1/2/4/8 B200, % of dense FP16 peak"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
-DEFAULT_CTA = {"small16": (128, 128, 64), "mixed512": (128, 128, 64), "moe": (128, 256, 64),
+DEFAULT_CTA = {"small16": (128, 128, 64), "mixed512": (128, 256, 64), "moe": (128, 256, 64),
                "tiny4096": (128, 64, 64), "skew": (128, 256, 64)}
 
 
@@ -53,7 +53,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", default="mixed512", choices=["small16", "mixed512", "moe", "tiny4096", "skew"])
-    ap.add_argument("--sort-mode", type=int, default=2, help="0 none, 1 by K, 2 by tiles, 3 by tiles then K")
+    ap.add_argument("--sort-mode", type=int, default=1, help="0 none, 1 by K, 2 by tiles, 3 by tiles then K")
     ap.add_argument("--cta", default=None, help="tile shape MxNxK (default per workload)")
     ap.add_argument("--no-extras", action="store_true", help="skip the sort-mode sweep and the reference GPU row")
     ap.add_argument("--e2e-steps", type=int, default=10)
@@ -348,7 +348,8 @@ def main():
         with open(traffic_path) as f:
             tr = json.load(f).get(f"{args.workload}/{cta[0]}x{cta[1]}x{cta[2]}")
         if tr:
-            roof["traffic"] = tr
+            roof["traffic"] = tr["bytes_per_launch"]
+            roof["traffic_source"] = tr["source"]
 
     # ---- e2e through the C-ABI with host buffers (pinned), copies inside the timed step ----
     e2e = None
