@@ -25,7 +25,7 @@ __all__ = [
     "SortMode", "ProblemDesc", "KernelConfig", "PreparedProblemSet", "OccupancyInfo", "GroupedGemmExecutor",
     "prepare_problem_set", "sort_mode_name", "query_occupancy", "run_grouped_gemm_once",
     "run_baseline_per_problem", "count_non_empty_problems", "partition", "ShardPiece", "problem_from_tensors",
-    "NATIVE_CONFIGS", "REFERENCE_CONFIGS", "selftest_wait_timeout", "capi",
+    "NATIVE_CONFIGS", "REFERENCE_CONFIGS", "PAIR_CONFIGS", "selftest_wait_timeout", "capi",
 ]
 
 
@@ -79,7 +79,10 @@ class KernelConfig:
 
 # The reference's three tile shapes (reference src/grouped_gemm.cu:67-81) and the sm_100a ones.
 REFERENCE_CONFIGS = (KernelConfig(64, 64, 16), KernelConfig(128, 64, 32), KernelConfig(64, 128, 32))
-NATIVE_CONFIGS = (KernelConfig(128, 128, 64), KernelConfig(128, 256, 64), KernelConfig(128, 64, 64))
+NATIVE_CONFIGS = (KernelConfig(128, 128, 64), KernelConfig(128, 256, 64), KernelConfig(128, 64, 64),
+                  KernelConfig(256, 128, 64), KernelConfig(256, 256, 64))
+# Tiles computed by a cluster of two CTAs (tcgen05 cta_group::2).
+PAIR_CONFIGS = (KernelConfig(256, 128, 64), KernelConfig(256, 256, 64))
 
 
 @dataclass

@@ -131,7 +131,10 @@ bool encode_b_chunks(CUtensorMap* map, const void* base, int k, int n, int64_t r
 // Device record of one problem plus its kMapsPerProblem tensor maps. TMA is used for A/B only
 // when both operands qualify, for D when it qualifies; everything else takes the zero-fill load
 // path and masked direct stores.
-DeviceProblemDesc make_device_problem(const gg_problem& p, int bm, int bn, CUtensorMap* maps) {
+DeviceProblemDesc make_device_problem(const gg_problem& p, Variant v, CUtensorMap* maps) {
+  const int bm = variant_bm(v), bn = variant_bn(v);
+  const int cta_rows = variant_cta_rows(v);  // A and D rows one CTA moves per tile
+  const int cta_cols = variant_cta_cols(v);  // B columns one CTA loads per tile
   DeviceProblemDesc d{};
   d.m = p.m;
   d.n = p.n;
@@ -154,15 +157,16 @@ DeviceProblemDesc make_device_problem(const gg_problem& p, int bm, int bn, CUten
   std::memset(maps, 0, kMapsPerProblem * sizeof(CUtensorMap));
   if (has_tiles && p.k > 0 &&
       encode_2d(&maps[kMapA], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, p.a, p.k, p.m, static_cast<int64_t>(p.lda) * 2, kBK,
-                bm) &&
+                cta_rows) &&
       encode_2d(&maps[kMapB], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, p.b, p.n, p.k, static_cast<int64_t>(p.ldb) * 2, 64,
                 kBK)) {
     flags |= grouped_gemm::kFlagTmaAB;
-    if (encode_b_chunks(&maps[kMapB3], p.b, p.k, p.n, static_cast<int64_t>(p.ldb) * 2, bn / 64))
+    if (encode_b_chunks(&maps[kMapB3], p.b, p.k, p.n, static_cast<int64_t>(p.ldb) * 2, cta_cols / 64))
       flags |= grouped_gemm::kFlagTmaB3;
   }
   if (has_tiles &&
-      encode_2d(&maps[kMapD], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.d, p.n, p.m, static_cast<int64_t>(p.ldd) * 4, 32, bm))
+      encode_2d(&maps[kMapD], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.d, p.n, p.m, static_cast<int64_t>(p.ldd) * 4, 32,
+                cta_rows))
     flags |= grouped_gemm::kFlagTmaD;
   if (p.c != nullptr && p.beta != 0.0f) flags |= grouped_gemm::kFlagReadC;
   if (aligned16(p.c) && (p.ldc % 4) == 0) flags |= grouped_gemm::kFlagCVec;
@@ -190,16 +194,19 @@ int* device_status_word() {
   return words[dev];
 }
 
-cudaError_t sm_count_and_slots(Variant v, int* sms, int* active) {
-  int dev = 0;
-  cudaError_t st = cudaGetDevice(&dev);
+// Persistent grid: whole CTA pairs for pair variants, at most one tile per CTA (pair) and at
+// most what fits on the device at once; persistent_ctas > 0 overrides (rounded up to whole pairs).
+cudaError_t persistent_grid(Variant v, int total_tiles, int persistent_ctas, int* grid) {
+  const int per_tile = variant_ctas_per_tile(v);
+  if (persistent_ctas > 0) {
+    *grid = (persistent_ctas + per_tile - 1) / per_tile * per_tile;
+    return cudaSuccess;
+  }
+  int resident = 0;
+  const cudaError_t st = kernel_resident_ctas(v, &resident);
   if (st != cudaSuccess) return st;
-  st = cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev);
-  if (st != cudaSuccess) return st;
-  cudaFuncAttributes attrs{};
-  st = kernel_occupancy(v, active, &attrs);
-  if (st != cudaSuccess) return st;
-  if (*active < 1) *active = 1;
+  const int units = std::max(1, std::min(resident / per_tile, total_tiles));
+  *grid = units * per_tile;
   return cudaSuccess;
 }
 
@@ -352,14 +359,13 @@ int gg_executor_build(gg_executor* ex, const gg_problem* sorted_problems, int co
   ex->grid_ctas = 0;
   ex->variant = v;
 
-  const int bm = gg::variant_bm(v), bn = gg::variant_bn(v);
   std::vector<DeviceProblemDesc> descs(static_cast<size_t>(count));
   std::vector<CUtensorMap> maps(static_cast<size_t>(count) * gg::kMapsPerProblem);
   for (int i = 0; i < count; ++i) {
     const gg_problem& p = sorted_problems[i];
     if (p.m < 0 || p.n < 0 || p.k < 0) return cudaErrorInvalidValue;
     if (!p.a || !p.b || !p.d) return cudaErrorInvalidDevicePointer;
-    descs[static_cast<size_t>(i)] = gg::make_device_problem(p, bm, bn, &maps[static_cast<size_t>(i) * gg::kMapsPerProblem]);
+    descs[static_cast<size_t>(i)] = gg::make_device_problem(p, v, &maps[static_cast<size_t>(i) * gg::kMapsPerProblem]);
   }
   if (count == 0 || total_tiles <= 0) {
     ex->problem_count = count;
@@ -367,8 +373,8 @@ int gg_executor_build(gg_executor* ex, const gg_problem* sorted_problems, int co
     return cudaSuccess;  // nothing to launch
   }
 
-  int sms = 0, active = 0;
-  cudaError_t st = gg::sm_count_and_slots(v, &sms, &active);
+  int grid = 0;
+  cudaError_t st = gg::persistent_grid(v, total_tiles, config->persistent_ctas, &grid);
   if (st != cudaSuccess) return st;
 
   const size_t maps_bytes = maps.size() * sizeof(CUtensorMap);
@@ -400,9 +406,7 @@ int gg_executor_build(gg_executor* ex, const gg_problem* sorted_problems, int co
 
   ex->problem_count = count;
   ex->total_tiles = total_tiles;
-  const int resident = sms * active;
-  ex->grid_ctas = config->persistent_ctas > 0 ? config->persistent_ctas : std::min(resident, total_tiles);
-  ex->grid_ctas = std::max(1, ex->grid_ctas);
+  ex->grid_ctas = grid;
 
   gg::KernelParams& kp = ex->params;
   std::memset(&kp, 0, sizeof(kp));
@@ -467,7 +471,6 @@ int gg_run_baseline_per_problem(const gg_problem* problems, int count, const gg_
   if (count < 0 || (count > 0 && !problems)) return cudaErrorInvalidValue;
   const int bm = gg::variant_bm(v), bn = gg::variant_bn(v);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int sms = 0, active = 0;
   int* status = nullptr;
   gg::KernelParams kp;
   for (int i = 0; i < count; ++i) {
@@ -476,13 +479,11 @@ int gg_run_baseline_per_problem(const gg_problem* problems, int count, const gg_
     if (!p.a || !p.b || !p.d) return cudaErrorInvalidDevicePointer;
     if (gg::tile_count(p.m, p.n, bm, bn) == 0) continue;
     if (!status) {
-      cudaError_t st = gg::sm_count_and_slots(v, &sms, &active);
-      if (st != cudaSuccess) return st;
       status = gg::device_status_word();
       if (!status) return cudaErrorMemoryAllocation;
     }
     std::memset(&kp, 0, sizeof(kp));
-    kp.single_desc = gg::make_device_problem(p, bm, bn, kp.single_maps);
+    kp.single_desc = gg::make_device_problem(p, v, kp.single_maps);
     const int tiles = kp.single_desc.tiles_m * kp.single_desc.tiles_n;
     kp.status = status;
     kp.timeout_ns = gg::wait_timeout_ns();
@@ -490,7 +491,10 @@ int gg_run_baseline_per_problem(const gg_problem* problems, int count, const gg_
     kp.total_tiles = tiles;
     kp.raster_group = gg::raster_group();
     kp.single_mode = 1;
-    const cudaError_t st = gg::launch_grouped_kernel(v, kp, std::min(tiles, sms * active), s);
+    int grid = 0;
+    cudaError_t st = gg::persistent_grid(v, tiles, 0, &grid);
+    if (st != cudaSuccess) return st;
+    st = gg::launch_grouped_kernel(v, kp, grid, s);
     if (st != cudaSuccess) return st;
   }
   return cudaSuccess;
@@ -682,7 +686,6 @@ extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count
   if (count == 0) return cudaSuccess;
 
   std::lock_guard<std::mutex> lock(gg::g_noalloc_mu);
-  const int bm = gg::variant_bm(v), bn = gg::variant_bn(v);
   gg::noalloc_sort(problems, count, sort_mode, config->cta_m, config->cta_n);
   auto* maps = reinterpret_cast<CUtensorMap*>(gg::g_noalloc_image);
   auto* descs = reinterpret_cast<DeviceProblemDesc*>(gg::g_noalloc_image + gg::kNoAllocDescsOff);
@@ -691,7 +694,7 @@ extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count
   for (int s = 0; s < count; ++s) {
     const gg_problem& p = problems[gg::g_noalloc_order[s]];
     offs[s + 1] = offs[s] + gg::tile_count(p.m, p.n, config->cta_m, config->cta_n);
-    descs[s] = gg::make_device_problem(p, bm, bn, &maps[static_cast<size_t>(s) * gg::kMapsPerProblem]);
+    descs[s] = gg::make_device_problem(p, v, &maps[static_cast<size_t>(s) * gg::kMapsPerProblem]);
   }
   const int total = offs[count];
   if (total == 0) return cudaSuccess;
@@ -699,8 +702,8 @@ extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count
   void* scratch = nullptr;
   cudaError_t st = gg::noalloc_scratch(&scratch);
   if (st != cudaSuccess) return st;
-  int sms = 0, active = 0;
-  st = gg::sm_count_and_slots(v, &sms, &active);
+  int grid = 0;
+  st = gg::persistent_grid(v, total, config->persistent_ctas, &grid);
   if (st != cudaSuccess) return st;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -732,6 +735,5 @@ extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count
   kp.total_tiles = total;
   kp.raster_group = gg::raster_group();
   kp.single_mode = 0;
-  const int grid = config->persistent_ctas > 0 ? config->persistent_ctas : std::max(1, std::min(sms * active, total));
   return gg::launch_grouped_kernel(v, kp, grid, s);
 }

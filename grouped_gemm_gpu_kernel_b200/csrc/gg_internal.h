@@ -16,21 +16,29 @@ enum class Variant : int {
   k64x128 = 2,
   k128x128 = 3,
   k128x256 = 4,
-  kCount = 5,
+  k256x128 = 5,  // CTA pair (cta_group::2), 128 rows per CTA
+  k256x256 = 6,  // CTA pair (cta_group::2), 128 rows per CTA
+  kCount = 7,
   kUnsupported = -1,
 };
 
 // Maps a (cta_m, cta_n, cta_k, threads) request to a variant, kUnsupported otherwise. Accepts the
 // reference's three shapes (reference src/grouped_gemm.cu:67-81) and the sm_100a-native ones.
 Variant resolve_variant(int cta_m, int cta_n, int cta_k, int threads);
-int variant_bm(Variant v);
-int variant_bn(Variant v);
+int variant_bm(Variant v);   // output tile rows
+int variant_bn(Variant v);   // output tile columns
+bool variant_is_pair(Variant v);
+int variant_cta_rows(Variant v);  // A / D rows one CTA loads and stores (the TMA box height)
+int variant_cta_cols(Variant v);  // B columns one CTA loads
 int variant_dynamic_smem(Variant v);
+int variant_ctas_per_tile(Variant v);
 
 // Raises the kernel's dynamic shared-memory limit on the current device (once per device).
 cudaError_t prepare_kernel(Variant v);
 cudaError_t launch_grouped_kernel(Variant v, const KernelParams& params, int grid, cudaStream_t stream);
 cudaError_t kernel_occupancy(Variant v, int* active_blocks_per_sm, cudaFuncAttributes* attrs);
+// CTAs of this variant that can be resident on the device at once (whole pairs for pair variants).
+cudaError_t kernel_resident_ctas(Variant v, int* ctas);
 cudaError_t launch_wait_selftest(int* status, unsigned long long timeout_ns, cudaStream_t stream);
 
 }  // namespace gg

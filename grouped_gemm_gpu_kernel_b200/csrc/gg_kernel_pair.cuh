@@ -1,0 +1,529 @@
+// gg_kernel_pair.cuh -- the persistent grouped GEMM kernel on CTA pairs (tcgen05 cta_group::2).
+//
+// A cluster of two CTAs on two SMs computes one 256 x BN output tile with M=256 MMAs: CTA rank r
+// loads rows [256*tile_m + 128*r, +128) of A and columns [BN*tile_n + (BN/2)*r, +BN/2) of B into
+// its own shared memory, the MMA reads both halves of both operands and leaves rows
+// 128*r .. 128*r+127 of the accumulator in CTA r's tensor memory, and each CTA's epilogue stores
+// its own 128 rows. Per SM this moves 3/4 (BN=256) or 2/3 (BN=128) of the operand bytes a one-CTA
+// 128 x BN tile moves for the same tensor work, so the same shared memory holds more pipeline
+// stages (6 x 32 KB or 8 x 24 KB) and covers more load latency.
+//
+// Roles are those of gg_kernel.cuh, with the pair split:
+//   leader (rank 0)  the scheduler warp claims tiles and writes each ring slot into both CTAs'
+//                    shared memory (remote stores, then a cluster-release arrive on the peer's
+//                    ring barrier); the MMA thread issues tcgen05.mma.cta_group::2 and commits to
+//                    the empty / accumulator barriers of both CTAs at once (commit multicast).
+//   both CTAs        producers load their own halves; the TMA byte counts complete on the
+//                    leader's stage barrier (cp.async.bulk.tensor.cta_group::2, no multicast) and
+//                    each CTA's producer adds one arrival there, so TMA and zero-fill stages use
+//                    the same count. Epilogues drain their own TMEM; the peer's release of an
+//                    accumulator is a remote arrive on the leader's barrier.
+// Waits stay bounded as in the one-CTA kernel; a cluster barrier precedes TMEM release and exit so
+// neither CTA leaves while the other may still touch its shared memory.
+#pragma once
+
+#include "gg_kernel.cuh"
+
+namespace gg {
+
+template <int BN>
+struct PairLayout {
+  static constexpr int kBHalf = BN / 2;
+  static constexpr int kStages = BN >= 256 ? 6 : 8;
+  static constexpr int kABytes = 128 * 128;     // 128 rows x 64 K
+  static constexpr int kBBytes = kBHalf * 128;  // BN/2 columns (chunks of 64) x 64 K
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kEpiOffset = kStages * kStageBytes;
+  static constexpr int kEpiBytes = 2 * kEpiTileBytes;
+  static constexpr int kRingOffset = kEpiOffset + kEpiBytes;
+  static constexpr int kBarOffset = kRingOffset + kRing * static_cast<int>(sizeof(TileSlot));
+  static constexpr int kNumBars = 2 * kStages + 4 + 2 * kRing + 1;
+  static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
+  static constexpr int kBytes = kMiscOffset + 32;
+  static constexpr int kDynamicSmem = kBytes + 1024;
+  static constexpr uint32_t kStageTxPair = 2u * static_cast<uint32_t>(kStageBytes);  // both CTAs' halves
+  static constexpr uint32_t kTmemCols = 2 * BN;
+  static_assert(kRingOffset % 1024 == 0, "stage and staging tiles stay 1024-byte aligned");
+  static_assert(kDynamicSmem <= 232448, "fits the 227 KB opt-in shared memory of a CTA");
+  static_assert(kDynamicSmem > 232448 / 2 + 1024, "one CTA per SM");
+};
+
+constexpr int kPairRingConsumersLeader = kEpiWarps + 1 + 2;  // epilogue, MMA, producers
+constexpr int kPairRingConsumersPeer = kEpiWarps + 2;        // epilogue, producers
+
+// Bounded wait with cluster-scope acquire (ring slots the leader wrote into this CTA remotely).
+__device__ __noinline__ bool wait_slow_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                               unsigned long long timeout_ns, int code) {
+  const uint64_t t0 = ptx::global_timer_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (ptx::mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 31u) == 31u) {
+      if (*abort_flag) return false;
+      if (ptx::global_timer_ns() - t0 > timeout_ns || i > 0x40000000u) {
+        *abort_flag = 1;
+        atomicOr(status, code);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ bool wait_phase_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                                   int* status, unsigned long long timeout_ns, int code) {
+  if (ptx::mbar_try_wait_cluster(bar, parity)) return true;
+  return wait_slow_cluster(bar, parity, abort_flag, status, timeout_ns, code);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_sm100_pair_kernel(const __grid_constant__ KernelParams p) {
+  using L = PairLayout<BN>;
+  constexpr int S = L::kStages;
+  constexpr int BM = 256;          // output rows per pair tile
+  constexpr int HB = BN / 2;       // B columns per CTA
+  static_assert(BN == 128 || BN == 256, "pair tile columns");
+
+  extern __shared__ uint8_t smem_dyn[];
+  const uint32_t raw_addr = ptx::smem_addr(smem_dyn);
+  uint8_t* smem = smem_dyn + ((1024u - (raw_addr & 1023u)) & 1023u);
+  const uint32_t sbase = ptx::smem_addr(smem);
+
+  TileSlot* ring = reinterpret_cast<TileSlot*>(smem + L::kRingOffset);
+  const uint32_t bar0 = sbase + L::kBarOffset;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (S + s); };
+  auto accf_bar = [&](int b) { return bar0 + 8u * (2 * S + b); };
+  auto acce_bar = [&](int b) { return bar0 + 8u * (2 * S + 2 + b); };
+  auto ringf_bar = [&](int r) { return bar0 + 8u * (2 * S + 4 + r); };
+  auto ringe_bar = [&](int r) { return bar0 + 8u * (2 * S + 4 + kRing + r); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * S + 4 + 2 * kRing);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOffset);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 4);
+  volatile int* prod_go = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 8);
+  volatile int* epi_go = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 12);
+
+  const int warp = static_cast<int>(threadIdx.x >> 5);
+  const int lane = static_cast<int>(threadIdx.x & 31);
+  const uint32_t rank = ptx::cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      ptx::mbar_init(full_bar(s), 2);   // leader producer (with the byte count) + peer producer
+      ptx::mbar_init(empty_bar(s), 1);  // the MMA commit, multicast to both CTAs
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(accf_bar(b), 1);
+      ptx::mbar_init(acce_bar(b), 2 * kEpiWarps);  // epilogue warps of both CTAs (leader's copy used)
+    }
+    for (int r = 0; r < kRing; ++r) {
+      ptx::mbar_init(ringf_bar(r), 1);
+      ptx::mbar_init(ringe_bar(r), kPairRingConsumersLeader + kPairRingConsumersPeer);
+    }
+    ptx::mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    *prod_go = 0;
+    epi_go[0] = 0;
+    epi_go[1] = 0;
+    ptx::fence_mbar_init();
+  }
+  ptx::cluster_sync();  // both CTAs' barriers exist before either touches the other's
+  if (warp == kMmaWarp) {
+    ptx::tmem_alloc_pair(ptx::smem_addr(tmem_slot), L::kTmemCols);
+    ptx::tmem_relinquish_pair();
+  }
+  ptx::tc_fence_before_sync();
+  __syncthreads();
+  ptx::tc_fence_after_sync();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+  const DeviceProblemDesc* problems = p.single_mode ? &p.single_desc : p.problems;
+  const CUtensorMap* maps = p.single_mode ? p.single_maps : p.tmaps;
+  const unsigned long long tmo = p.timeout_ns;
+  // Ring slots are released on the leader's barrier; the peer arrives there remotely.
+  auto release_slot = [&](int slot) {
+    if (leader) ptx::mbar_arrive(ringe_bar(slot));
+    else ptx::mbar_arrive_cluster(ptx::mapa_shared(ringe_bar(slot), 0));
+  };
+
+  if (warp == kSchedWarp) {
+    // ======================= scheduler (leader only) =======================
+    if (leader) {
+      const int pair_id = static_cast<int>(blockIdx.x >> 1);
+      const int pairs = static_cast<int>(gridDim.x >> 1);
+      int static_next = pair_id;
+      for (int t = 0;; ++t) {
+        const int slot = t % kRing;
+        const uint32_t par = static_cast<uint32_t>(t / kRing) & 1u;
+        int ok = 1;
+        if (lane == 0)
+          ok = wait_phase_cluster(ringe_bar(slot), par ^ 1u, abort_flag, p.status, tmo, GG_STATUS_TIMEOUT_SCHEDULER);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        TileSlot* s = &ring[slot];
+        int pidx = -1, tile_m = 0, tile_n = 0;
+        for (;;) {
+          int tile = 0;
+          if (lane == 0) {
+            if (p.single_mode) {
+              tile = static_next;
+              static_next += pairs;
+            } else {
+              tile = atomicAdd(p.tile_counter, 1);
+            }
+          }
+          tile = __shfl_sync(0xffffffffu, tile, 0);
+          if (tile >= p.total_tiles) break;
+          const int q = p.single_mode ? 0 : find_problem_warp(p.tile_offsets, p.problem_count, tile, lane);
+          const int local = tile - (p.single_mode ? 0 : __ldg(p.tile_offsets + q));
+          const int* src = reinterpret_cast<const int*>(problems + q);
+          const int w = lane < kDescWords ? src[lane] : 0;
+          const int tiles_m = __shfl_sync(0xffffffffu, w, static_cast<int>(offsetof(DeviceProblemDesc, tiles_m) / 4));
+          const int tiles_n = __shfl_sync(0xffffffffu, w, static_cast<int>(offsetof(DeviceProblemDesc, tiles_n) / 4));
+          if (local < 0 || tiles_m <= 0 || tiles_n <= 0 || local >= tiles_m * tiles_n) continue;
+          raster_tile(local, tiles_m, tiles_n, p.raster_group, tile_m, tile_n);
+          if (lane < kDescWords) reinterpret_cast<int*>(&s->desc)[lane] = w;
+          const unsigned fl = static_cast<unsigned>(
+              __shfl_sync(0xffffffffu, w, static_cast<int>(offsetof(DeviceProblemDesc, flags) / 4)));
+          const bool map_valid = (lane == kMapA || lane == kMapB) ? (fl & grouped_gemm::kFlagTmaAB) != 0u
+                                 : lane == kMapB3                 ? (fl & grouped_gemm::kFlagTmaB3) != 0u
+                                 : lane == kMapD                  ? (fl & grouped_gemm::kFlagTmaD) != 0u
+                                                                  : false;
+          if (map_valid) ptx::prefetch_tensormap(maps + kMapsPerProblem * q + lane);
+          pidx = q;
+          break;
+        }
+        if (lane == 0) {
+          s->problem = pidx;
+          s->tile_m = tile_m;
+          s->tile_n = tile_n;
+        }
+        __syncwarp();
+        if (lane == 0) {
+          // Copy the slot into the peer's ring, then publish it on both sides. The remote arrive
+          // releases at cluster scope, after this thread's remote stores.
+          const uint32_t local_slot = ptx::smem_addr(s);
+          const uint32_t remote_slot = ptx::mapa_shared(local_slot, 1);
+          const uint32_t* words = reinterpret_cast<const uint32_t*>(s);
+          for (int i = 0; i < static_cast<int>(sizeof(TileSlot) / 4); ++i)
+            ptx::st_shared_cluster_u32(remote_slot + 4u * i, words[i]);
+          __threadfence_block();
+          ptx::mbar_arrive(ringf_bar(slot));
+          ptx::mbar_arrive_cluster(ptx::mapa_shared(ringf_bar(slot), 1));
+        }
+        if (pidx < 0) break;
+      }
+    }
+  } else if (warp >= kProdWarp0) {
+    // ======================= producers (both CTAs) =======================
+    const int ptid = static_cast<int>(threadIdx.x) - kProdWarp0 * 32;
+    uint32_t it = 0;
+    bool aborted = false;
+    for (int t = 0;; ++t) {
+      const int slot = t % kRing;
+      const uint32_t par = static_cast<uint32_t>(t / kRing) & 1u;
+      int ok = 1;
+      if (lane == 0)
+        ok = wait_phase_cluster(ringf_bar(slot), par, abort_flag, p.status, tmo, GG_STATUS_TIMEOUT_PRODUCER);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      const TileSlot* s = &ring[slot];
+      const int q = s->problem;
+      const int tile_m = s->tile_m, tile_n = s->tile_n;
+      const int kb_count = s->desc.k_blocks;
+      const unsigned flags = s->desc.flags;
+      const int m = s->desc.m, n = s->desc.n, k = s->desc.k;
+      const __half* a = s->desc.a;
+      const __half* b = s->desc.b;
+      const int lda = s->desc.lda, ldb = s->desc.ldb;
+      __syncwarp();
+      if (lane == 0) release_slot(slot);
+      if (q < 0) break;
+      const int row_base = tile_m * BM + static_cast<int>(rank) * 128;  // this CTA's rows of A
+      const int col_base = tile_n * BN + static_cast<int>(rank) * HB;   // this CTA's columns of B
+
+      if (flags & grouped_gemm::kFlagTmaAB) {
+        if (ptid == 0) {
+          const CUtensorMap* ma = maps + kMapsPerProblem * q + kMapA;
+          const CUtensorMap* mb = maps + kMapsPerProblem * q + kMapB;
+          const CUtensorMap* mb3 = maps + kMapsPerProblem * q + kMapB3;
+          const bool b_one_box = HB > 64 && (flags & grouped_gemm::kFlagTmaB3) && col_base + HB <= n;
+          for (int kb = 0; kb < kb_count; ++kb) {
+            const int st = static_cast<int>(it % S);
+            const uint32_t ph = (it / S) & 1u;
+            if (!wait_phase(empty_bar(st), ph ^ 1u, abort_flag, p.status, tmo, GG_STATUS_TIMEOUT_PRODUCER)) {
+              aborted = true;
+              break;
+            }
+            const uint32_t a_dst = sbase + static_cast<uint32_t>(st * L::kStageBytes);
+            const uint32_t b_dst = a_dst + L::kABytes;
+            const uint32_t bar_leader = ptx::mapa_shared(full_bar(st), 0);
+            if (leader) ptx::mbar_arrive_expect_tx(full_bar(st), L::kStageTxPair);
+            ptx::tma_load_2d_pair(a_dst, ma, bar_leader, kb * kBK, row_base);
+            if (b_one_box) {
+              ptx::tma_load_3d_pair(b_dst, mb3, bar_leader, 0, kb * kBK, col_base / 64);
+            } else {
+#pragma unroll
+              for (int j = 0; j < HB / 64; ++j)
+                ptx::tma_load_2d_pair(b_dst + j * 8192u, mb, bar_leader, col_base + j * 64, kb * kBK);
+            }
+            // The peer's arrival only counts: its TMA bytes are tracked by complete_tx.
+            if (!leader) ptx::mbar_arrive_cluster_relaxed(bar_leader);
+            ++it;
+          }
+        } else {
+          it += static_cast<uint32_t>(kb_count);
+        }
+        if (aborted) break;
+      } else {
+        for (int kb = 0; kb < kb_count; ++kb) {
+          const int st = static_cast<int>(it % S);
+          const uint32_t ph = (it / S) & 1u;
+          if (ptid == 0) {
+            const bool got = wait_phase(empty_bar(st), ph ^ 1u, abort_flag, p.status, tmo, GG_STATUS_TIMEOUT_PRODUCER);
+            *prod_go = got ? 1 : 0;
+          }
+          ptx::named_bar_sync(1, kProdThreads);
+          if (!*prod_go) {
+            aborted = true;
+            break;
+          }
+          uint8_t* as = smem + st * L::kStageBytes;
+          uint8_t* bs = as + L::kABytes;
+          for (int idx = ptid; idx < 128 * 8; idx += kProdThreads) {
+            const int r = idx >> 3, j = idx & 7;
+            const uint4 v = load8_zero_fill(a, lda, row_base + r, kb * kBK + j * 8, m, k);
+            *reinterpret_cast<uint4*>(as + r * 128 + ((j ^ (r & 7)) << 4)) = v;
+          }
+          constexpr int kChunksPerRow = HB / 8;
+          for (int idx = ptid; idx < kBK * kChunksPerRow; idx += kProdThreads) {
+            const int kr = idx / kChunksPerRow, jn = idx % kChunksPerRow;
+            const int c = jn >> 3, j = jn & 7;
+            const uint4 v = load8_zero_fill(b, ldb, kb * kBK + kr, col_base + jn * 8, k, n);
+            *reinterpret_cast<uint4*>(bs + c * 8192 + kr * 128 + ((j ^ (kr & 7)) << 4)) = v;
+          }
+          ptx::fence_proxy_async_all();  // the leader's tensor cores read this CTA's shared memory
+          ptx::named_bar_sync(1, kProdThreads);
+          if (ptid == 0) {
+            if (leader) ptx::mbar_arrive(full_bar(st));
+            else ptx::mbar_arrive_cluster(ptx::mapa_shared(full_bar(st), 0));
+          }
+          ++it;
+        }
+        if (aborted) break;
+      }
+    }
+    if (aborted && ptid == 0 && leader) {
+      // Loads issued for the last stages may still be landing: wait for them before exit.
+      const uint32_t n_back = it < static_cast<uint32_t>(S) ? it : static_cast<uint32_t>(S);
+      for (uint32_t j = 1; j <= n_back; ++j) {
+        const uint32_t i2 = it - j;
+        wait_drain(full_bar(static_cast<int>(i2 % S)), (i2 / S) & 1u, 100000000ull);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ======================= MMA issuer (leader only) =======================
+    if (leader && lane == 0) {
+      constexpr uint32_t kIdesc = ptx::idesc_f16_f32_kA_mnB(256, BN);
+      uint32_t it = 0;
+      for (int t = 0;; ++t) {
+        const int slot = t % kRing;
+        const uint32_t par = static_cast<uint32_t>(t / kRing) & 1u;
+        if (!wait_phase(ringf_bar(slot), par, abort_flag, p.status, tmo, GG_STATUS_TIMEOUT_MMA)) break;
+        const int q = ring[slot].problem;
+        const int kb_count = ring[slot].desc.k_blocks;
+        // TMA stages are ordered by their byte counts (async proxy); zero-fill stages carry the
+        // peer's generic stores and need the cluster-scope acquire.
+        const bool lsu_tile = (ring[slot].desc.flags & grouped_gemm::kFlagTmaAB) == 0u;
+        ptx::mbar_arrive(ringe_bar(slot));
+        if (q < 0) break;
+        const int buf = t & 1;
+        if (!wait_phase_cluster(acce_bar(buf), (static_cast<uint32_t>(t >> 1) & 1u) ^ 1u, abort_flag, p.status, tmo,
+                                GG_STATUS_TIMEOUT_MMA))
+          break;
+        ptx::tc_fence_after_sync();
+        if (kb_count <= 0) {
+          ptx::mbar_arrive(accf_bar(buf));  // K = 0: both epilogues use a zero accumulator
+          ptx::mbar_arrive_cluster(ptx::mapa_shared(accf_bar(buf), 1));
+          continue;
+        }
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
+        bool aborted = false;
+        for (int kb = 0; kb < kb_count; ++kb) {
+          const int st = static_cast<int>(it % S);
+          const uint32_t ph = (it / S) & 1u;
+          const bool got = lsu_tile ? wait_phase_cluster(full_bar(st), ph, abort_flag, p.status, tmo, GG_STATUS_TIMEOUT_MMA)
+                                    : wait_phase(full_bar(st), ph, abort_flag, p.status, tmo, GG_STATUS_TIMEOUT_MMA);
+          if (!got) {
+            aborted = true;
+            break;
+          }
+          ptx::tc_fence_after_sync();
+          const uint32_t a0 = sbase + static_cast<uint32_t>(st * L::kStageBytes);
+          const uint32_t b0 = a0 + L::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / kMmaK; ++kk) {
+            const uint64_t adesc = ptx::smem_desc_sw128(a0 + kk * 32u, 16u, 1024u);
+            const uint64_t bdesc = ptx::smem_desc_sw128(b0 + kk * 2048u, 8192u, 1024u);
+            ptx::tc_mma_f16_pair(d_tmem, adesc, bdesc, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          ptx::tc_commit_pair_mc(empty_bar(st), 0x3);  // both CTAs' stage is free
+          ++it;
+        }
+        if (aborted) break;
+        ptx::tc_commit_pair_mc(accf_bar(buf), 0x3);  // both halves of the accumulator are ready
+      }
+      ptx::tc_commit_pair(drain_bar);
+      wait_drain(drain_bar, 0u, 100000000ull);
+    }
+    __syncwarp();
+  } else {
+    // ======================= epilogue (warps 0-3, both CTAs) =======================
+    const int qw = warp;
+    const int et = static_cast<int>(threadIdx.x);
+    uint32_t store_count = 0;
+    for (int t = 0;; ++t) {
+      const int slot = t % kRing;
+      const uint32_t par = static_cast<uint32_t>(t / kRing) & 1u;
+      if (et == 0)
+        epi_go[0] =
+            wait_phase_cluster(ringf_bar(slot), par, abort_flag, p.status, tmo, GG_STATUS_TIMEOUT_EPILOGUE) ? 1 : 0;
+      ptx::named_bar_sync(2, kEpiThreads);
+      if (!epi_go[0]) break;
+      const TileSlot* s = &ring[slot];
+      const int q = s->problem;
+      const int tile_m = s->tile_m, tile_n = s->tile_n;
+      const int m = s->desc.m, n = s->desc.n;
+      const int kb_count = s->desc.k_blocks;
+      const unsigned flags = s->desc.flags;
+      const float alpha = s->desc.alpha, beta = s->desc.beta;
+      const float* cptr = s->desc.c;
+      float* dptr = s->desc.d;
+      const int ldc = s->desc.ldc, ldd = s->desc.ldd;
+      __syncwarp();
+      if (lane == 0) release_slot(slot);
+      if (q < 0) break;
+      const int buf = t & 1;
+      if (et == 0)
+        epi_go[1] = wait_phase(accf_bar(buf), static_cast<uint32_t>(t >> 1) & 1u, abort_flag, p.status, tmo,
+                               GG_STATUS_TIMEOUT_EPILOGUE) ? 1 : 0;
+      ptx::named_bar_sync(2, kEpiThreads);
+      if (!epi_go[1]) break;
+      ptx::tc_fence_after_sync();
+
+      const int cta_row0 = tile_m * BM + static_cast<int>(rank) * 128;  // this CTA's first row
+      const int row0 = cta_row0 + qw * 32;
+      const int row = row0 + lane;
+      const int col0 = tile_n * BN;
+      const bool warp_rows = row0 < m;
+      const int nchunks = min(BN / 32, (n - col0 + 31) / 32);
+      const uint32_t t_addr = tmem_base + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(qw * 32) << 16);
+      const bool read_c = (flags & grouped_gemm::kFlagReadC) != 0u;
+      const bool tma_d = (flags & grouped_gemm::kFlagTmaD) != 0u && cta_row0 < m;
+      const CUtensorMap* md = maps + kMapsPerProblem * q + kMapD;
+
+      for (int c = 0; c < nchunks; ++c) {
+        float acc[32];
+        if (warp_rows && kb_count > 0) {
+          uint32_t r[32];
+          ptx::tmem_load_32cols(t_addr + static_cast<uint32_t>(c * 32), r);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(r[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
+        }
+        if (c == nchunks - 1) {
+          ptx::tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) {
+            if (leader) ptx::mbar_arrive(acce_bar(buf));
+            else ptx::mbar_arrive_cluster(ptx::mapa_shared(acce_bar(buf), 0));
+          }
+        }
+        const int cc = col0 + c * 32;
+        float cv[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) cv[j] = 0.0f;
+        if (read_c && warp_rows && row < m) {
+          const float* crow = cptr + static_cast<int64_t>(row) * ldc + cc;
+          if ((flags & grouped_gemm::kFlagCVec) && cc + 32 <= n) {
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+              const float4 v = *reinterpret_cast<const float4*>(crow + 4 * j4);
+              cv[4 * j4] = v.x;
+              cv[4 * j4 + 1] = v.y;
+              cv[4 * j4 + 2] = v.z;
+              cv[4 * j4 + 3] = v.w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (cc + j < n) cv[j] = crow[j];
+          }
+        }
+        float out[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) out[j] = alpha * acc[j] + beta * cv[j];
+
+        if (tma_d) {
+          uint8_t* stile = smem + L::kEpiOffset + static_cast<int>(store_count & 1u) * kEpiTileBytes;
+          if (et == 0) ptx::bulk_wait_read_le1();
+          ptx::named_bar_sync(2, kEpiThreads);
+          {
+            const int r = qw * 32 + lane;
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+              *reinterpret_cast<float4*>(stile + r * 128 + ((j4 ^ (r & 7)) << 4)) =
+                  make_float4(out[4 * j4], out[4 * j4 + 1], out[4 * j4 + 2], out[4 * j4 + 3]);
+            }
+          }
+          ptx::fence_proxy_async_smem();
+          ptx::named_bar_sync(2, kEpiThreads);
+          if (et == 0) {
+            ptx::tma_store_2d(md, ptx::smem_addr(stile), cc, cta_row0);
+            ptx::bulk_commit_group();
+          }
+          ++store_count;
+        } else if (warp_rows && row < m) {
+          float* drow = dptr + static_cast<int64_t>(row) * ldd + cc;
+          if ((flags & grouped_gemm::kFlagDVec) && cc + 32 <= n) {
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4)
+              *reinterpret_cast<float4*>(drow + 4 * j4) =
+                  make_float4(out[4 * j4], out[4 * j4 + 1], out[4 * j4 + 2], out[4 * j4 + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (cc + j < n) drow[j] = out[j];
+          }
+        }
+      }
+      if (nchunks <= 0) {
+        ptx::tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) {
+          if (leader) ptx::mbar_arrive(acce_bar(buf));
+          else ptx::mbar_arrive_cluster(ptx::mapa_shared(acce_bar(buf), 0));
+        }
+      }
+    }
+    if (et == 0) ptx::bulk_wait_all();
+    __syncwarp();
+  }
+
+  // Neither CTA leaves (or frees TMEM) while the other may still read or signal its shared memory.
+  ptx::cluster_sync();
+  if (*abort_flag) {
+    // After an abort, loads issued by the other CTA may still be landing here: give them time.
+    const uint64_t t0 = ptx::global_timer_ns();
+    while (ptx::global_timer_ns() - t0 < 200000ull) {
+    }
+  }
+  if (warp == kMmaWarp) {
+    ptx::tc_fence_after_sync();
+    ptx::tmem_dealloc_pair(tmem_base, L::kTmemCols);
+  }
+}
+
+}  // namespace gg

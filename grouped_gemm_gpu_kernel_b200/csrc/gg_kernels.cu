@@ -5,6 +5,7 @@
 
 #include "gg_internal.h"
 #include "gg_kernel.cuh"
+#include "gg_kernel_pair.cuh"
 
 namespace gg {
 
@@ -14,6 +15,12 @@ template <int BM, int BN>
 struct VariantTraits {
   static constexpr int kSmem = SmemLayout<BM, BN>::kDynamicSmem;
   static void* kernel() { return reinterpret_cast<void*>(&grouped_gemm_sm100_kernel<BM, BN>); }
+};
+
+template <int BN>
+struct PairTraits {
+  static constexpr int kSmem = PairLayout<BN>::kDynamicSmem;
+  static void* kernel() { return reinterpret_cast<void*>(&grouped_gemm_sm100_pair_kernel<BN>); }
 };
 
 // One bit per device: the dynamic shared-memory attribute has been raised there.
@@ -30,10 +37,30 @@ auto dispatch(Variant v, Fn&& fn) {
       return fn(VariantTraits<64, 128>{});
     case Variant::k128x128:
       return fn(VariantTraits<128, 128>{});
+    case Variant::k256x128:
+      return fn(PairTraits<128>{});
+    case Variant::k256x256:
+      return fn(PairTraits<256>{});
     case Variant::k128x256:
     default:
       return fn(VariantTraits<128, 256>{});
   }
+}
+
+// Launch configuration of a pair variant: clusters of two CTAs along x.
+cudaLaunchConfig_t pair_config(int grid, size_t smem, cudaStream_t stream, cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
 }
 
 bool valid(Variant v) { return static_cast<int>(v) >= 0 && static_cast<int>(v) < static_cast<int>(Variant::kCount); }
@@ -47,6 +74,8 @@ Variant resolve_variant(int cta_m, int cta_n, int cta_k, int threads) {
   if (cta_m == 128 && cta_n == 64 && cta_k == 32) return Variant::k128x64;
   if (cta_m == 64 && cta_n == 128 && cta_k == 32) return Variant::k64x128;
   // sm_100a-native shapes
+  if (cta_m == 256 && cta_n == 128 && cta_k == 64) return Variant::k256x128;
+  if (cta_m == 256 && cta_n == 256 && cta_k == 64) return Variant::k256x256;
   if (cta_m == 128 && cta_n == 128 && cta_k == 64) return Variant::k128x128;
   if (cta_m == 128 && cta_n == 256 && cta_k == 64) return Variant::k128x256;
   if (cta_m == 128 && cta_n == 64 && cta_k == 64) return Variant::k128x64;
@@ -54,7 +83,9 @@ Variant resolve_variant(int cta_m, int cta_n, int cta_k, int threads) {
 }
 
 int variant_bm(Variant v) {
-  return (v == Variant::k64x64 || v == Variant::k64x128) ? 64 : 128;
+  if (v == Variant::k64x64 || v == Variant::k64x128) return 64;
+  if (v == Variant::k256x128 || v == Variant::k256x256) return 256;
+  return 128;
 }
 
 int variant_bn(Variant v) {
@@ -64,11 +95,17 @@ int variant_bn(Variant v) {
       return 64;
     case Variant::k64x128:
     case Variant::k128x128:
+    case Variant::k256x128:
       return 128;
     default:
       return 256;
   }
 }
+
+bool variant_is_pair(Variant v) { return v == Variant::k256x128 || v == Variant::k256x256; }
+int variant_cta_rows(Variant v) { return variant_is_pair(v) ? 128 : variant_bm(v); }
+int variant_cta_cols(Variant v) { return variant_is_pair(v) ? variant_bn(v) / 2 : variant_bn(v); }
+int variant_ctas_per_tile(Variant v) { return variant_is_pair(v) ? 2 : 1; }
 
 int variant_dynamic_smem(Variant v) {
   if (!valid(v)) return 0;
@@ -110,10 +147,50 @@ cudaError_t launch_grouped_kernel(Variant v, const KernelParams& params, int gri
     case Variant::k128x256:
       grouped_gemm_sm100_kernel<128, 256><<<grid, kThreads, VariantTraits<128, 256>::kSmem, stream>>>(params);
       break;
+    case Variant::k256x128: {
+      if (grid % 2) return cudaErrorInvalidValue;
+      cudaLaunchAttribute attr[1];
+      const cudaLaunchConfig_t cfg = pair_config(grid, PairTraits<128>::kSmem, stream, attr);
+      return cudaLaunchKernelEx(&cfg, grouped_gemm_sm100_pair_kernel<128>, params);
+    }
+    case Variant::k256x256: {
+      if (grid % 2) return cudaErrorInvalidValue;
+      cudaLaunchAttribute attr[1];
+      const cudaLaunchConfig_t cfg = pair_config(grid, PairTraits<256>::kSmem, stream, attr);
+      return cudaLaunchKernelEx(&cfg, grouped_gemm_sm100_pair_kernel<256>, params);
+    }
     default:
       return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
+}
+
+cudaError_t kernel_resident_ctas(Variant v, int* ctas) {
+  cudaError_t st = prepare_kernel(v);
+  if (st != cudaSuccess) return st;
+  int dev = 0;
+  st = cudaGetDevice(&dev);
+  if (st != cudaSuccess) return st;
+  int sms = 0;
+  st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (st != cudaSuccess) return st;
+  if (!variant_is_pair(v)) {
+    int active = 0;
+    cudaFuncAttributes fa{};
+    st = kernel_occupancy(v, &active, &fa);
+    if (st != cudaSuccess) return st;
+    *ctas = sms * (active > 0 ? active : 1);
+    return cudaSuccess;
+  }
+  int clusters = 0;
+  st = dispatch(v, [&](auto t) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pair_config(2, decltype(t)::kSmem, nullptr, attr);
+    return cudaOccupancyMaxActiveClusters(&clusters, decltype(t)::kernel(), &cfg);
+  });
+  if (st != cudaSuccess) return st;
+  *ctas = 2 * (clusters > 0 ? clusters : 1);
+  return cudaSuccess;
 }
 
 cudaError_t kernel_occupancy(Variant v, int* active_blocks_per_sm, cudaFuncAttributes* attrs) {

@@ -44,7 +44,8 @@ struct ProblemDesc {
 };
 
 // Tile shape and launch shape. The defaults are the reference's; the sm_100a-native shapes
-// 128x128x64, 128x256x64 and 128x64x64 are also accepted (threads must be 256).
+// 128x128x64, 128x256x64, 128x64x64 and the CTA-pair shapes 256x128x64, 256x256x64 are also
+// accepted (threads must be 256).
 struct KernelConfig {
   int cta_m = 64;
   int cta_n = 64;

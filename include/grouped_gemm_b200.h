@@ -60,7 +60,9 @@ typedef struct gg_problem {
 
 /* Kernel configuration; the reference's KernelConfig (grouped_gemm.cuh:37-45) with the bool as
  * an int. Accepted (cta_m, cta_n, cta_k) with threads == 256:
- *   sm_100a-native tiles   128x128x64, 128x256x64, 128x64x64
+ *   sm_100a-native tiles   128x128x64, 128x256x64, 128x64x64 (one CTA per tile), and
+ *                          256x128x64, 256x256x64 (a cluster of two CTAs per tile,
+ *                          tcgen05 cta_group::2: 128 rows per CTA)
  *   the reference's tiles  64x64x16, 128x64x32, 64x128x32  (same tile decomposition, run on the
  *                          same tcgen05 kernel; cta_k only selects the variant)
  * use_tensor_cores is accepted either way: every variant runs on tcgen05 tensor cores. */

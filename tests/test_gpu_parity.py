@@ -139,6 +139,21 @@ def test_single_tile_tma_path(cuda):
     assert torch.allclose(D.double(), ref, rtol=1e-5, atol=1e-4)
 
 
+@pytest.mark.parametrize("bn", [128, 256])
+def test_single_tile_pair_path(cuda, bn):
+    """One 256 x BN tile on a CTA pair (cta_group::2): both halves of A and B, both TMEMs."""
+    torch = _torch()
+    g = torch.Generator(device=cuda).manual_seed(2)
+    A = torch.empty(256, 128, dtype=torch.float16, device=cuda).uniform_(-1, 1, generator=g)
+    B = torch.empty(128, bn, dtype=torch.float16, device=cuda).uniform_(-1, 1, generator=g)
+    D = torch.full((256, bn), float("nan"), device=cuda)
+    p = gg.problem_from_tensors(A, B, None, D)
+    ex = run_grouped([p], gg.KernelConfig(256, bn, 64), gg.SortMode.kNone)
+    assert ex.grid_ctas() == 2 and ex.total_tiles() == 1
+    ref = A.double() @ B.double()
+    assert torch.allclose(D.double(), ref, rtol=1e-5, atol=1e-4)
+
+
 def _fixture_problems(cuda):
     """The reference test's eight problems with its own inputs, on the device."""
     torch = _torch()
@@ -190,7 +205,8 @@ def test_reference_test_set_all_modes_and_baseline(cuda, cfg):
 
 
 @pytest.mark.parametrize("cfg", [gg.KernelConfig(128, 128, 64), gg.KernelConfig(64, 64, 16),
-                                 gg.KernelConfig(128, 256, 64)], ids=lambda c: f"{c.cta_m}x{c.cta_n}")
+                                 gg.KernelConfig(128, 256, 64), gg.KernelConfig(256, 128, 64),
+                                 gg.KernelConfig(256, 256, 64)], ids=lambda c: f"{c.cta_m}x{c.cta_n}")
 def test_small16_full(cuda, cfg):
     ps = W.allocate(W.make_shapes("small16"), cuda)
     for mode in MODES:
@@ -203,8 +219,8 @@ def test_small16_full(cuda, cfg):
     assert check_full(ps) <= 1.0
 
 
-@pytest.mark.parametrize("cfg", [gg.KernelConfig(128, 128, 64), gg.KernelConfig(64, 64, 16)],
-                         ids=lambda c: f"{c.cta_m}x{c.cta_n}")
+@pytest.mark.parametrize("cfg", [gg.KernelConfig(128, 128, 64), gg.KernelConfig(64, 64, 16),
+                                 gg.KernelConfig(256, 128, 64)], ids=lambda c: f"{c.cta_m}x{c.cta_n}")
 def test_tiny4096_full(cuda, cfg):
     ps = W.allocate(W.make_shapes("tiny4096"), cuda)
     run_grouped(ps.problems(), cfg, gg.SortMode.kByTiles)
@@ -217,9 +233,11 @@ def test_mixed512_all_modes_sampled(cuda):
         ps.d.fill_(float("nan"))
         run_grouped(ps.problems(), gg.KernelConfig(128, 128, 64), mode)
         assert check_sampled(ps, seed=int(mode)) <= 1.0
-    ps.d.fill_(float("nan"))
-    run_grouped(ps.problems(), gg.KernelConfig(128, 256, 64), gg.SortMode.kByTiles)
-    assert check_sampled(ps, seed=7) <= 1.0
+    for i, cfg in enumerate((gg.KernelConfig(128, 256, 64), gg.KernelConfig(256, 128, 64),
+                             gg.KernelConfig(256, 256, 64))):
+        ps.d.fill_(float("nan"))
+        run_grouped(ps.problems(), cfg, gg.SortMode.kByTiles)
+        assert check_sampled(ps, seed=7 + i) <= 1.0
     # canaries: the 256-byte alignment gaps between problems' D are never written
     d = ps.d.cpu().numpy()
     written = np.zeros(d.size, bool)
@@ -230,17 +248,21 @@ def test_mixed512_all_modes_sampled(cuda):
 
 
 @pytest.mark.slow
-def test_moe_full_size_sampled(cuda):
+@pytest.mark.parametrize("cfg", [gg.KernelConfig(128, 256, 64), gg.KernelConfig(256, 256, 64)],
+                         ids=lambda c: f"{c.cta_m}x{c.cta_n}")
+def test_moe_full_size_sampled(cuda, cfg):
     ps = W.allocate(W.make_shapes("moe"), cuda)
-    run_grouped(ps.problems(), gg.KernelConfig(128, 256, 64), gg.SortMode.kByTiles)
+    run_grouped(ps.problems(), cfg, gg.SortMode.kByTiles)
     assert check_sampled(ps, rows_per=3, cols_per=64) <= 1.0
     del ps
 
 
 @pytest.mark.slow
-def test_skew_full_size_sampled(cuda):
+@pytest.mark.parametrize("cfg", [gg.KernelConfig(128, 256, 64), gg.KernelConfig(256, 256, 64)],
+                         ids=lambda c: f"{c.cta_m}x{c.cta_n}")
+def test_skew_full_size_sampled(cuda, cfg):
     ps = W.allocate(W.make_shapes("skew"), cuda)
-    run_grouped(ps.problems(), gg.KernelConfig(128, 256, 64), gg.SortMode.kByTiles)
+    run_grouped(ps.problems(), cfg, gg.SortMode.kByTiles)
     assert check_sampled(ps, rows_per=6, cols_per=64) <= 1.0
 
 
@@ -317,7 +339,8 @@ EDGE_CASES = {
 
 
 @pytest.mark.parametrize("cfg", [gg.KernelConfig(128, 128, 64), gg.KernelConfig(64, 128, 32),
-                                 gg.KernelConfig(128, 64, 32)], ids=lambda c: f"{c.cta_m}x{c.cta_n}")
+                                 gg.KernelConfig(128, 64, 32), gg.KernelConfig(256, 128, 64),
+                                 gg.KernelConfig(256, 256, 64)], ids=lambda c: f"{c.cta_m}x{c.cta_n}")
 def test_edge_cases(cuda, cfg):
     cases = [(_edge_problem(cuda, seed=i, **kw)) for i, kw in enumerate(EDGE_CASES.values())]
     probs = [p for p, _ in cases]
@@ -379,6 +402,12 @@ def test_persistent_ctas_override(cuda):
         ps.d.fill_(float("nan"))
         ex = run_grouped(ps.problems(), cfg, gg.SortMode.kByK)
         assert ex.grid_ctas() == ctas
+        assert check_full(ps) <= 1.0
+    for ctas, want in ((1, 2), (3, 4), (6, 6)):  # pair configs round up to whole CTA pairs
+        cfg = gg.KernelConfig(256, 128, 64, persistent_ctas=ctas)
+        ps.d.fill_(float("nan"))
+        ex = run_grouped(ps.problems(), cfg, gg.SortMode.kByK)
+        assert ex.grid_ctas() == want
         assert check_full(ps) <= 1.0
 
 

@@ -119,8 +119,9 @@ def test_tile_count_entry_point():
 @pytest.mark.parametrize("cfg,ok", [
     (gg.KernelConfig(64, 64, 16), True), (gg.KernelConfig(128, 64, 32), True), (gg.KernelConfig(64, 128, 32), True),
     (gg.KernelConfig(128, 128, 64), True), (gg.KernelConfig(128, 256, 64), True), (gg.KernelConfig(128, 64, 64), True),
+    (gg.KernelConfig(256, 128, 64), True), (gg.KernelConfig(256, 256, 64), True), (gg.KernelConfig(256, 64, 64), False),
     (gg.KernelConfig(64, 64, 16, threads=128), False), (gg.KernelConfig(32, 32, 16), False),
-    (gg.KernelConfig(128, 128, 32), False), (gg.KernelConfig(256, 128, 64), False),
+    (gg.KernelConfig(128, 128, 32), False), (gg.KernelConfig(256, 128, 32), False),
 ])
 def test_build_config_validation(cfg, ok):
     """Unsupported configs fail with cudaErrorInvalidValue (reference src/grouped_gemm.cu:121-123)."""
