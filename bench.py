@@ -344,7 +344,7 @@ def main():
                 "frac": achieved / peaks["bf16_tflops"], "traffic": None, "peak_source": peaks["source"],
                 "algorithmic_flops_per_launch": local_flops}
     traffic_path = os.path.join(REPO, "profiles", "traffic.json")
-    if os.path.exists(traffic_path):
+    if os.path.exists(traffic_path) and world == 1:
         with open(traffic_path) as f:
             tr = json.load(f).get(f"{args.workload}/{cta[0]}x{cta[1]}x{cta[2]}")
         if tr:

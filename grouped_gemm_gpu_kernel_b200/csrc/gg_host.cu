@@ -166,7 +166,7 @@ DeviceProblemDesc make_device_problem(const gg_problem& p, Variant v, CUtensorMa
   }
   if (has_tiles &&
       encode_2d(&maps[kMapD], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.d, p.n, p.m, static_cast<int64_t>(p.ldd) * 4, 32,
-                cta_rows))
+                32))
     flags |= grouped_gemm::kFlagTmaD;
   if (p.c != nullptr && p.beta != 0.0f) flags |= grouped_gemm::kFlagReadC;
   if (aligned16(p.c) && (p.ldc % 4) == 0) flags |= grouped_gemm::kFlagCVec;

@@ -2,11 +2,11 @@
 //
 // One CTA per SM (shared memory > half an SM's), 256 threads in five warp roles:
 //
-//   warps 0-3  epilogue   TMEM -> registers (tcgen05.ld), D = alpha*acc + beta*C, then per 32-column
-//                         chunk one 128-byte-swizzled staging tile of all BM rows that a single
-//                         TMA store writes out (clipped at the problem edge), or masked direct
-//                         stores when D is not TMA-eligible. Warp w reads TMEM lanes
-//                         32w..32w+31 = tile rows 32w..32w+31.
+//   warps 0-3  epilogue   TMEM -> registers (tcgen05.ld), D = alpha*acc + beta*C. Warp w reads
+//                         TMEM lanes 32w..32w+31 = tile rows 32w..32w+31 and stores them on its
+//                         own: per 32-column chunk one 32x32 TMA store from a 128-byte-swizzled
+//                         staging tile (clipped at the problem edge), or, when D is not
+//                         TMA-eligible, coalesced masked stores read back from that tile.
 //   warp 4     MMA        allocates 2*BN TMEM columns (two accumulators, so the epilogue of one
 //                         tile overlaps the mainloop of the next); one thread issues
 //                         tcgen05.mma.kind::f16 (M=128, N=BN, K=16) and tcgen05.commit.
@@ -101,26 +101,349 @@ __device__ __forceinline__ void raster_tile(int local, int tiles_m, int tiles_n,
   tn = in_g / gm;
 }
 
-// ---- producer helpers ------------------------------------------------------------------------
-// Eight FP16 values of row `row`, columns col..col+7, with zero fill outside rows x cols.
-__device__ __forceinline__ uint4 load8_zero_fill(const __half* base, int ld, int row, int col, int rows, int cols) {
-  uint4 v = make_uint4(0u, 0u, 0u, 0u);
-  if (row < rows && col < cols) {
-    const unsigned short* src =
-        reinterpret_cast<const unsigned short*>(base) + static_cast<int64_t>(row) * ld + col;
-    if (col + 8 <= cols && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
-      v = __ldg(reinterpret_cast<const uint4*>(src));
-    } else {
-      uint32_t w[4] = {0u, 0u, 0u, 0u};
+// Scheduler state of one warp. Lane 0 keeps one tile claim in flight (the atomicAdd for the next
+// tile is issued before the current tile is searched), and every lane keeps its word of the last
+// problem's descriptor with that problem's tile range, so tiles claimed from the same problem skip
+// the search and the descriptor load.
+struct SchedState {
+  int cur;          // lane 0: claimed tile not yet handed out
+  int static_next;  // lane 0: next tile of the static order (baseline launches)
+  int q;            // problem of the cached descriptor, -1 when none
+  int q_first;      // its first tile
+  int q_end;        // one past its last tile
+  int w;            // this lane's 32-bit word of the cached descriptor
+};
+
+__device__ __forceinline__ int claim_tile(const KernelParams& p, SchedState& ss, int stride) {
+  if (p.single_mode) {
+    const int t = ss.static_next;
+    ss.static_next += stride;
+    return t;
+  }
+  return atomicAdd(p.tile_counter, 1);
+}
+
+__device__ __forceinline__ void sched_init(const KernelParams& p, SchedState& ss, int first_static, int stride,
+                                           int lane) {
+  ss.static_next = first_static;
+  ss.q = -1;
+  ss.q_first = 0;
+  ss.q_end = 0;
+  ss.w = 0;
+  ss.cur = 0;
+  if (lane == 0) ss.cur = claim_tile(p, ss, stride);
+}
+
+// Next tile of this CTA (warp-collective): returns false when the work is exhausted, else the
+// problem index, the tile coordinates, and leaves the problem's descriptor words in ss.w.
+__device__ __forceinline__ bool next_tile(const KernelParams& p, SchedState& ss, const DeviceProblemDesc* problems,
+                                          int lane, int stride, int& q_out, int& tile_m, int& tile_n) {
+  for (;;) {
+    const int tile = __shfl_sync(0xffffffffu, ss.cur, 0);
+    if (tile >= p.total_tiles) return false;
+    if (lane == 0) ss.cur = claim_tile(p, ss, stride);  // in flight while this tile is placed
+    if (!(ss.q >= 0 && tile >= ss.q_first && tile < ss.q_end)) {
+      const int q = p.single_mode ? 0 : find_problem_warp(p.tile_offsets, p.problem_count, tile, lane);
+      ss.q = q;
+      ss.q_first = p.single_mode ? 0 : __ldg(p.tile_offsets + q);
+      ss.q_end = p.single_mode ? p.total_tiles : __ldg(p.tile_offsets + q + 1);
+      const int* src = reinterpret_cast<const int*>(problems + q);
+      ss.w = lane < kDescWords ? src[lane] : 0;
+    }
+    const int local = tile - ss.q_first;
+    const int tiles_m = __shfl_sync(0xffffffffu, ss.w, static_cast<int>(offsetof(DeviceProblemDesc, tiles_m) / 4));
+    const int tiles_n = __shfl_sync(0xffffffffu, ss.w, static_cast<int>(offsetof(DeviceProblemDesc, tiles_n) / 4));
+    // A tile index outside its problem's tile grid (a prepared set inconsistent with the config)
+    // is skipped, as the reference kernel does (src/grouped_gemm.cu:662-672).
+    if (local < 0 || tiles_m <= 0 || tiles_n <= 0 || local >= tiles_m * tiles_n) continue;
+    raster_tile(local, tiles_m, tiles_n, p.raster_group, tile_m, tile_n);
+    q_out = ss.q;
+    return true;
+  }
+}
+
+// Warms the tensor maps a tile of this problem will use (only those that were encoded).
+__device__ __forceinline__ void prefetch_problem_maps(const CUtensorMap* maps, int q, unsigned flags, int lane) {
+  const bool map_valid = (lane == kMapA || lane == kMapB) ? (flags & grouped_gemm::kFlagTmaAB) != 0u
+                         : lane == kMapB3                 ? (flags & grouped_gemm::kFlagTmaB3) != 0u
+                         : lane == kMapD                  ? (flags & grouped_gemm::kFlagTmaD) != 0u
+                                                          : false;
+  if (map_valid) ptx::prefetch_tensormap(maps + kMapsPerProblem * q + lane);
+}
+
+// ---- epilogue helper ---------------------------------------------------------------------
+// One epilogue warp's share of a tile: rows row0..row0+31 (TMEM lanes of this warp's quarter) and
+// all nchunks 32-column chunks. D = alpha * acc + beta * C, C taken as 0 when it is not read
+// (reference src/grouped_gemm.cu:614-621). `stage` is this warp's 8 KB of shared memory: two
+// 4 KB staging tiles (32 rows x 128 bytes, 128-byte swizzle). The warp works alone, with no
+// barrier across warps inside the tile:
+//  - TMA-storable D: each chunk goes out in one 32x32 TMA store issued by lane 0; the staging
+//    tiles alternate, and lane 0's bulk groups say when a tile may be written again;
+//  - any other D: the chunk is read back from the staging tile so that 8 consecutive lanes hold
+//    one 128-byte row segment, and stored (and C loaded) with coalesced st.global / ld.global.
+// `release` hands the accumulator back to the MMA warp after the last TMEM read.
+template <typename Release>
+__device__ __forceinline__ void epilogue_warp(uint8_t* stage, uint32_t& store_count, uint32_t t_addr, int lane,
+                                              int row0, int m, int n, int col0, int nchunks, int kb_count,
+                                              unsigned flags, float alpha, float beta, const float* cptr, int ldc,
+                                              float* dptr, int ldd, const CUtensorMap* md, Release release) {
+  const bool warp_rows = row0 < m;  // warp-uniform
+  const bool read_c = (flags & grouped_gemm::kFlagReadC) != 0u;
+  const bool tma_d = (flags & grouped_gemm::kFlagTmaD) != 0u;
+  const int row = row0 + lane;
+  if (tma_d) {
+    // Two chunks per TMEM read (one 64-column tcgen05.ld and one wait), then one staging tile
+    // and one TMA store per chunk, so that a store is always in flight while the next chunk is
+    // prepared.
+    for (int c = 0; c < nchunks; c += 2) {
+      const int nsub = c + 1 < nchunks ? 2 : 1;
+      uint32_t r[64];
+      if (warp_rows && kb_count > 0) {
+        if (nsub == 2) {
+          ptx::tmem_load_64cols(t_addr + static_cast<uint32_t>(c * 32), r);
+        } else {
+          uint32_t h[32];
+          ptx::tmem_load_32cols(t_addr + static_cast<uint32_t>(c * 32), h);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = h[j];
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 64; ++j) r[j] = 0u;
+      }
+      if (c + nsub >= nchunks) {
+        // Last read of this accumulator: hand it back to the MMA warp before the stores.
+        ptx::tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) release();
+      }
+      if (!warp_rows) continue;
+#pragma unroll
+      for (int sub = 0; sub < 2; ++sub) {
+        if (sub >= nsub) break;
+        const int cc = col0 + (c + sub) * 32;
+        float cv[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) cv[j] = 0.0f;
+        if (read_c && row < m) {
+          const float* crow = cptr + static_cast<int64_t>(row) * ldc + cc;
+          if ((flags & grouped_gemm::kFlagCVec) && cc + 32 <= n) {
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+              const float4 v = __ldg(reinterpret_cast<const float4*>(crow + 4 * j4));
+              cv[4 * j4] = v.x;
+              cv[4 * j4 + 1] = v.y;
+              cv[4 * j4 + 2] = v.z;
+              cv[4 * j4 + 3] = v.w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (cc + j < n) cv[j] = __ldg(crow + j);
+          }
+        }
+        uint8_t* stile = stage + static_cast<int>(store_count & 1u) * 4096;
+        if (lane == 0) ptx::bulk_wait_read_le1();  // the store that used this tile two chunks ago
+        __syncwarp();
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
+          const int j = sub * 32 + 4 * j4;
+          float4 o;
+          o.x = alpha * __uint_as_float(r[j]) + beta * cv[4 * j4];
+          o.y = alpha * __uint_as_float(r[j + 1]) + beta * cv[4 * j4 + 1];
+          o.z = alpha * __uint_as_float(r[j + 2]) + beta * cv[4 * j4 + 2];
+          o.w = alpha * __uint_as_float(r[j + 3]) + beta * cv[4 * j4 + 3];
+          *reinterpret_cast<float4*>(stile + lane * 128 + ((j4 ^ (lane & 7)) << 4)) = o;
+        }
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          ptx::tma_store_2d(md, ptx::smem_addr(stile), cc, row0);  // rows past M are clipped
+          ptx::bulk_commit_group();
+        }
+        ++store_count;
+      }
+    }
+  } else {
+    // Any other D: each chunk is read back from the staging tile so that 8 consecutive lanes
+    // hold one 128-byte row segment, then C is loaded and D stored with coalesced accesses.
+    const int jj = lane & 7;
+    if (warp_rows && lane == 0) ptx::bulk_wait_all_read();  // staging tile 0 is free
+    for (int c = 0; c < nchunks; ++c) {
+      const int cc = col0 + c * 32;
+      const int gcol = cc + 4 * jj;
+      // C, issued before the TMEM read so that its latency overlaps it.
+      float cv[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) cv[j] = 0.0f;
+      if (read_c && warp_rows) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int grow = row0 + i * 4 + (lane >> 3);
+          if (grow < m && gcol < n) {
+            const float* crow = cptr + static_cast<int64_t>(grow) * ldc + gcol;
+            if ((flags & grouped_gemm::kFlagCVec) && gcol + 4 <= n) {
+              const float4 v = __ldg(reinterpret_cast<const float4*>(crow));
+              cv[4 * i] = v.x;
+              cv[4 * i + 1] = v.y;
+              cv[4 * i + 2] = v.z;
+              cv[4 * i + 3] = v.w;
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                if (gcol + e < n) cv[4 * i + e] = __ldg(crow + e);
+            }
+          }
+        }
+      }
+      uint32_t r[32];
+      if (warp_rows && kb_count > 0) {
+        ptx::tmem_load_32cols(t_addr + static_cast<uint32_t>(c * 32), r);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = 0u;
+      }
+      if (c == nchunks - 1) {
+        ptx::tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) release();
+      }
+      if (!warp_rows) continue;
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4)
+        *reinterpret_cast<uint4*>(stage + lane * 128 + ((j4 ^ (lane & 7)) << 4)) =
+            make_uint4(r[4 * j4], r[4 * j4 + 1], r[4 * j4 + 2], r[4 * j4 + 3]);
+      __syncwarp();
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const uint32_t h = (col + i < cols) ? static_cast<uint32_t>(__ldg(src + i)) : 0u;
-        w[i >> 1] |= h << ((i & 1) * 16);
+        const int rr = i * 4 + (lane >> 3);
+        const float4 a4 = *reinterpret_cast<const float4*>(stage + rr * 128 + ((jj ^ (rr & 7)) << 4));
+        const int grow = row0 + rr;
+        if (grow < m && gcol < n) {
+          float4 o;
+          o.x = alpha * a4.x + beta * cv[4 * i];
+          o.y = alpha * a4.y + beta * cv[4 * i + 1];
+          o.z = alpha * a4.z + beta * cv[4 * i + 2];
+          o.w = alpha * a4.w + beta * cv[4 * i + 3];
+          float* drow = dptr + static_cast<int64_t>(grow) * ldd + gcol;
+          if ((flags & grouped_gemm::kFlagDVec) && gcol + 4 <= n) {
+            *reinterpret_cast<float4*>(drow) = o;
+          } else {
+            drow[0] = o.x;
+            if (gcol + 1 < n) drow[1] = o.y;
+            if (gcol + 2 < n) drow[2] = o.z;
+            if (gcol + 3 < n) drow[3] = o.w;
+          }
+        }
       }
-      v = make_uint4(w[0], w[1], w[2], w[3]);
+      __syncwarp();
     }
   }
-  return v;
+  if (nchunks <= 0) {
+    ptx::tc_fence_before_sync();
+    __syncwarp();
+    if (lane == 0) release();
+  }
+}
+
+// ---- producer helpers ------------------------------------------------------------------------
+// Zero-fill loader for problems TMA cannot take (odd leading dimension or base alignment). Fills
+// one stage: A rows [row0, row0+ROWS) and B columns [col0, col0+COLS) of K block kb, in the same
+// 128-byte-swizzled layouts the TMA loads produce. Consecutive lanes read consecutive elements of
+// one row (coalesced), 2 bytes per lane, or 4 when every row of the operand starts on a 4-byte
+// boundary; each lane keeps up to 64 loads in flight before it stores them. Columns of A and rows of B
+// past K are written as zeros; rows of A past M and columns of B past N are not written at all:
+// they only reach accumulator rows and columns that are never stored.
+constexpr int kLsuBatch = 64;  // loads in flight per lane before their stores
+
+template <int V>
+__device__ __forceinline__ uint32_t lsu_load(const unsigned short* src, int c, int limit) {
+  if (V == 2 && c + 1 < limit) return __ldg(reinterpret_cast<const unsigned int*>(src + c));
+  return c < limit ? static_cast<uint32_t>(__ldg(src + c)) : 0u;
+}
+
+template <int V>
+__device__ __forceinline__ void lsu_store(uint8_t* dst, uint32_t v) {
+  if (V == 2) *reinterpret_cast<uint32_t*>(dst) = v;
+  else *reinterpret_cast<unsigned short*>(dst) = static_cast<unsigned short>(v);
+}
+
+template <int ROWS, int V>
+__device__ __forceinline__ void lsu_fill_a(uint8_t* as, const unsigned short* a16, int lda, int rows, int k, int row0,
+                                           int k0, int pw, int ln) {
+  constexpr int kW = kProdThreads / 32;
+  constexpr int kPer = 2 / V;  // loads per lane per row (a row is 64 elements)
+  constexpr int kB = (kLsuBatch / kPer) < (ROWS / kW) ? (kLsuBatch / kPer) : (ROWS / kW);  // rows per batch
+  const int klim = k - k0;            // columns of this K block inside K
+#pragma unroll 1
+  for (int rb = pw; rb < rows; rb += kW * kB) {
+    uint32_t v[kB][kPer];
+#pragma unroll
+    for (int i = 0; i < kB; ++i) {
+      const int r = rb + i * kW;
+      const unsigned short* src = a16 + static_cast<int64_t>(row0 + (r < rows ? r : 0)) * lda + k0;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) v[i][j] = r < rows ? lsu_load<V>(src, j * 32 + V * ln, klim) : 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < kB; ++i) {
+      const int r = rb + i * kW;
+      if (r < rows) {
+        const int sw = (r & 7) << 4;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) lsu_store<V>(as + r * 128 + (((j * 32 + V * ln) * 2) ^ sw), v[i][j]);
+      }
+    }
+  }
+}
+
+template <int COLS, int V>
+__device__ __forceinline__ void lsu_fill_b(uint8_t* bs, const unsigned short* b16, int ldb, int cols, int k, int col0,
+                                           int k0, int pw, int ln) {
+  constexpr int kW = kProdThreads / 32;
+  constexpr int kPer = COLS / (32 * V);  // loads per lane per K row
+  constexpr int kB = (kLsuBatch / kPer) < (kBK / kW) ? (kLsuBatch / kPer) : (kBK / kW);  // K rows per batch
+#pragma unroll 1
+  for (int rb = pw; rb < kBK; rb += kW * kB) {
+    uint32_t v[kB][kPer];
+#pragma unroll
+    for (int i = 0; i < kB; ++i) {
+      const int kr = rb + i * kW;
+      const bool kin = k0 + kr < k;
+      const unsigned short* src = b16 + static_cast<int64_t>(kin ? k0 + kr : 0) * ldb + col0;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) v[i][j] = kin ? lsu_load<V>(src, j * 32 * V + V * ln, cols) : 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < kB; ++i) {
+      const int kr = rb + i * kW;
+      const int sw = (kr & 7) << 4;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int c = j * 32 * V + V * ln;
+        if (c < cols) lsu_store<V>(bs + (c >> 6) * 8192 + kr * 128 + (((c & 63) * 2) ^ sw), v[i][j]);
+      }
+    }
+  }
+}
+
+template <int ROWS, int COLS>
+__device__ __forceinline__ void lsu_fill_stage(uint8_t* as, uint8_t* bs, const __half* a, int lda, const __half* b,
+                                               int ldb, int m, int n, int k, int row0, int col0, int kb, int ptid) {
+  const unsigned short* a16 = reinterpret_cast<const unsigned short*>(a);
+  const unsigned short* b16 = reinterpret_cast<const unsigned short*>(b);
+  const int pw = ptid >> 5, ln = ptid & 31;
+  const int k0 = kb * kBK;
+  const int rows = min(ROWS, m - row0);
+  const int cols = min(COLS, n - col0);
+  const bool a4 = ((lda & 1) == 0) && ((reinterpret_cast<uintptr_t>(a) & 3u) == 0u);
+  const bool b4 = ((ldb & 1) == 0) && ((reinterpret_cast<uintptr_t>(b) & 3u) == 0u);
+  if (a4) lsu_fill_a<ROWS, 2>(as, a16, lda, rows, k, row0, k0, pw, ln);
+  else lsu_fill_a<ROWS, 1>(as, a16, lda, rows, k, row0, k0, pw, ln);
+  if (cols > 0) {
+    if (b4) lsu_fill_b<COLS, 2>(bs, b16, ldb, cols, k, col0, k0, pw, ln);
+    else lsu_fill_b<COLS, 1>(bs, b16, ldb, cols, k, col0, k0, pw, ln);
+  }
 }
 
 // ---- the kernel --------------------------------------------------------------------------------
@@ -128,6 +451,7 @@ template <int BM, int BN>
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const __grid_constant__ KernelParams p) {
   using L = SmemLayout<BM, BN>;
   constexpr int S = L::kStages;
+  constexpr int kAcc = L::kAcc;
   static_assert(BM == 64 || BM == 128, "tile rows");
   static_assert(BN == 64 || BN == 128 || BN == 256, "tile columns");
 
@@ -141,10 +465,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
   auto empty_bar = [&](int s) { return bar0 + 8u * (S + s); };
   auto accf_bar = [&](int b) { return bar0 + 8u * (2 * S + b); };
-  auto acce_bar = [&](int b) { return bar0 + 8u * (2 * S + 2 + b); };
-  auto ringf_bar = [&](int r) { return bar0 + 8u * (2 * S + 4 + r); };
-  auto ringe_bar = [&](int r) { return bar0 + 8u * (2 * S + 4 + kRing + r); };
-  const uint32_t drain_bar = bar0 + 8u * (2 * S + 4 + 2 * kRing);
+  auto acce_bar = [&](int b) { return bar0 + 8u * (2 * S + kAcc + b); };
+  auto ringf_bar = [&](int r) { return bar0 + 8u * (2 * S + 2 * kAcc + r); };
+  auto ringe_bar = [&](int r) { return bar0 + 8u * (2 * S + 2 * kAcc + kRing + r); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * S + 2 * kAcc + 2 * kRing);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOffset);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 4);
   volatile int* prod_go = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 8);
@@ -158,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
       ptx::mbar_init(full_bar(s), 1);
       ptx::mbar_init(empty_bar(s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kAcc; ++b) {
       ptx::mbar_init(accf_bar(b), 1);
       ptx::mbar_init(acce_bar(b), kEpiWarps);
     }
@@ -188,7 +512,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
 
   if (warp == kSchedWarp) {
     // ======================= scheduler =======================
-    int static_next = static_cast<int>(blockIdx.x);
+    SchedState ss;
+    sched_init(p, ss, static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x), lane);
     for (int t = 0;; ++t) {
       const int slot = t % kRing;
       const uint32_t par = static_cast<uint32_t>(t / kRing) & 1u;
@@ -198,40 +523,13 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
       if (!ok) break;
       TileSlot* s = &ring[slot];
       int pidx = -1, tile_m = 0, tile_n = 0;
-      for (;;) {
-        int tile = 0;
-        if (lane == 0) {
-          if (p.single_mode) {
-            tile = static_next;
-            static_next += static_cast<int>(gridDim.x);
-          } else {
-            tile = atomicAdd(p.tile_counter, 1);
-          }
-        }
-        tile = __shfl_sync(0xffffffffu, tile, 0);
-        if (tile >= p.total_tiles) break;
-        const int q = p.single_mode ? 0 : find_problem_warp(p.tile_offsets, p.problem_count, tile, lane);
-        const int local = tile - (p.single_mode ? 0 : __ldg(p.tile_offsets + q));
-        const int* src = reinterpret_cast<const int*>(problems + q);
-        const int w = lane < kDescWords ? src[lane] : 0;
-        const int tiles_m = __shfl_sync(0xffffffffu, w, static_cast<int>(offsetof(DeviceProblemDesc, tiles_m) / 4));
-        const int tiles_n = __shfl_sync(0xffffffffu, w, static_cast<int>(offsetof(DeviceProblemDesc, tiles_n) / 4));
-        // A tile index outside its problem's tile grid (a prepared set inconsistent with the
-        // config) is skipped, as the reference kernel does (src/grouped_gemm.cu:662-672).
-        if (local < 0 || tiles_m <= 0 || tiles_n <= 0 || local >= tiles_m * tiles_n) continue;
-        raster_tile(local, tiles_m, tiles_n, p.raster_group, tile_m, tile_n);
-        if (lane < kDescWords) reinterpret_cast<int*>(&s->desc)[lane] = w;
-        // Warm the tensor maps this tile will use (only those that were encoded) while the tile
-        // waits in the ring.
+      if (next_tile(p, ss, problems, lane, static_cast<int>(gridDim.x), pidx, tile_m, tile_n)) {
+        if (lane < kDescWords) reinterpret_cast<int*>(&s->desc)[lane] = ss.w;
         const unsigned fl = static_cast<unsigned>(
-            __shfl_sync(0xffffffffu, w, static_cast<int>(offsetof(DeviceProblemDesc, flags) / 4)));
-        const bool map_valid = (lane == kMapA || lane == kMapB) ? (fl & grouped_gemm::kFlagTmaAB) != 0u
-                               : lane == kMapB3                 ? (fl & grouped_gemm::kFlagTmaB3) != 0u
-                               : lane == kMapD                  ? (fl & grouped_gemm::kFlagTmaD) != 0u
-                                                                : false;
-        if (map_valid) ptx::prefetch_tensormap(maps + kMapsPerProblem * q + lane);
-        pidx = q;
-        break;
+            __shfl_sync(0xffffffffu, ss.w, static_cast<int>(offsetof(DeviceProblemDesc, flags) / 4)));
+        prefetch_problem_maps(maps, pidx, fl, lane);
+      } else {
+        pidx = -1;
       }
       if (lane == 0) {
         s->problem = pidx;
@@ -317,18 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
           }
           uint8_t* as = smem + st * L::kStageBytes;
           uint8_t* bs = as + L::kABytes;
-          for (int idx = ptid; idx < BM * 8; idx += kProdThreads) {
-            const int r = idx >> 3, j = idx & 7;
-            const uint4 v = load8_zero_fill(a, lda, tile_m * BM + r, kb * kBK + j * 8, m, k);
-            *reinterpret_cast<uint4*>(as + r * 128 + ((j ^ (r & 7)) << 4)) = v;
-          }
-          constexpr int kChunksPerRow = BN / 8;
-          for (int idx = ptid; idx < kBK * kChunksPerRow; idx += kProdThreads) {
-            const int kr = idx / kChunksPerRow, jn = idx % kChunksPerRow;
-            const int c = jn >> 3, j = jn & 7;
-            const uint4 v = load8_zero_fill(b, ldb, kb * kBK + kr, tile_n * BN + jn * 8, k, n);
-            *reinterpret_cast<uint4*>(bs + c * 8192 + kr * 128 + ((j ^ (kr & 7)) << 4)) = v;
-          }
+          lsu_fill_stage<BM, BN>(as, bs, a, lda, b, ldb, m, n, k, tile_m * BM, tile_n * BN, kb, ptid);
           ptx::fence_proxy_async_smem();
           ptx::named_bar_sync(1, kProdThreads);
           if (ptid == 0) ptx::mbar_arrive(full_bar(st));
@@ -358,8 +645,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
         const int kb_count = ring[slot].desc.k_blocks;
         ptx::mbar_arrive(ringe_bar(slot));
         if (q < 0) break;
-        const int buf = t & 1;
-        if (!wait_phase(acce_bar(buf), (static_cast<uint32_t>(t >> 1) & 1u) ^ 1u, abort_flag, p.status, tmo,
+        const int buf = t % kAcc;
+        if (!wait_phase(acce_bar(buf), (static_cast<uint32_t>(t / kAcc) & 1u) ^ 1u, abort_flag, p.status, tmo,
                         GG_STATUS_TIMEOUT_MMA))
           break;
         ptx::tc_fence_after_sync();
@@ -428,111 +715,23 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(ringe_bar(slot));
       if (q < 0) break;
-      const int buf = t & 1;
+      const int buf = t % kAcc;
       if (et == 0)
-        epi_go[1] = wait_phase(accf_bar(buf), static_cast<uint32_t>(t >> 1) & 1u, abort_flag, p.status, tmo,
+        epi_go[1] = wait_phase(accf_bar(buf), static_cast<uint32_t>(t / kAcc) & 1u, abort_flag, p.status, tmo,
                                GG_STATUS_TIMEOUT_EPILOGUE) ? 1 : 0;
       ptx::named_bar_sync(2, kEpiThreads);
       if (!epi_go[1]) break;
       ptx::tc_fence_after_sync();
 
-      const int row0 = tile_m * BM + qw * 32;
-      const int row = row0 + lane;
-      const int col0 = tile_n * BN;
-      const bool warp_rows = qw * 32 < BM && row0 < m;  // warp-uniform
-      const int nchunks = min(BN / 32, (n - col0 + 31) / 32);  // tile-uniform
+      const int nchunks = min(BN / 32, (n - tile_n * BN + 31) / 32);  // tile-uniform
       const uint32_t t_addr = tmem_base + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(qw * 32) << 16);
-      const bool read_c = (flags & grouped_gemm::kFlagReadC) != 0u;
-      const bool tma_d = (flags & grouped_gemm::kFlagTmaD) != 0u;
-      const CUtensorMap* md = maps + kMapsPerProblem * q + kMapD;
-
-      for (int c = 0; c < nchunks; ++c) {
-        float acc[32];
-        if (warp_rows && kb_count > 0) {
-          uint32_t r[32];
-          ptx::tmem_load_32cols(t_addr + static_cast<uint32_t>(c * 32), r);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(r[j]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
-        }
-        if (c == nchunks - 1) {
-          // Last read of this accumulator: hand it back to the MMA warp before the stores.
-          ptx::tc_fence_before_sync();
-          __syncwarp();
-          if (lane == 0) ptx::mbar_arrive(acce_bar(buf));
-        }
-        const int cc = col0 + c * 32;
-        float cv[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) cv[j] = 0.0f;
-        if (read_c && warp_rows && row < m) {
-          const float* crow = cptr + static_cast<int64_t>(row) * ldc + cc;
-          if ((flags & grouped_gemm::kFlagCVec) && cc + 32 <= n) {
-#pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {
-              const float4 v = *reinterpret_cast<const float4*>(crow + 4 * j4);
-              cv[4 * j4] = v.x;
-              cv[4 * j4 + 1] = v.y;
-              cv[4 * j4 + 2] = v.z;
-              cv[4 * j4 + 3] = v.w;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (cc + j < n) cv[j] = crow[j];
-          }
-        }
-        // D = alpha * acc + beta * C, C taken as 0 when it is not read
-        // (reference src/grouped_gemm.cu:614-621).
-        float out[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) out[j] = alpha * acc[j] + beta * cv[j];
-
-        if (tma_d) {
-          // All BM rows of this 32-column chunk go out in one TMA store from a shared staging
-          // tile (two tiles alternate; the store that used this one two chunks ago must have
-          // finished reading it). Rows past M are clipped by the tensor map.
-          uint8_t* stile = smem + L::kEpiOffset + static_cast<int>(store_count & 1u) * kEpiTileBytes;
-          if (et == 0) ptx::bulk_wait_read_le1();
-          ptx::named_bar_sync(2, kEpiThreads);
-          if (qw * 32 < BM) {
-            const int r = qw * 32 + lane;
-#pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {
-              *reinterpret_cast<float4*>(stile + r * 128 + ((j4 ^ (r & 7)) << 4)) =
-                  make_float4(out[4 * j4], out[4 * j4 + 1], out[4 * j4 + 2], out[4 * j4 + 3]);
-            }
-          }
-          ptx::fence_proxy_async_smem();
-          ptx::named_bar_sync(2, kEpiThreads);
-          if (et == 0) {
-            ptx::tma_store_2d(md, ptx::smem_addr(stile), cc, tile_m * BM);
-            ptx::bulk_commit_group();
-          }
-          ++store_count;
-        } else if (warp_rows && row < m) {
-          float* drow = dptr + static_cast<int64_t>(row) * ldd + cc;
-          if ((flags & grouped_gemm::kFlagDVec) && cc + 32 <= n) {
-#pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4)
-              *reinterpret_cast<float4*>(drow + 4 * j4) =
-                  make_float4(out[4 * j4], out[4 * j4 + 1], out[4 * j4 + 2], out[4 * j4 + 3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (cc + j < n) drow[j] = out[j];
-          }
-        }
-      }
-      if (nchunks <= 0) {
-        ptx::tc_fence_before_sync();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(acce_bar(buf));
-      }
+      // Warps whose 32 rows lie past BM (64-row tiles) or past M store nothing.
+      const int row0 = qw * 32 < BM ? tile_m * BM + qw * 32 : m;
+      epilogue_warp(smem + L::kEpiOffset + qw * 8192, store_count, t_addr, lane, row0, m, n, tile_n * BN, nchunks,
+                    kb_count, flags, alpha, beta, cptr, ldc, dptr, ldd, maps + kMapsPerProblem * q + kMapD,
+                    [&] { ptx::mbar_arrive(acce_bar(buf)); });
     }
-    if (et == 0) ptx::bulk_wait_all();
+    if (lane == 0) ptx::bulk_wait_all();  // every warp issues its own TMA stores
     __syncwarp();
   }
 

@@ -30,6 +30,7 @@ template <int BN>
 struct PairLayout {
   static constexpr int kBHalf = BN / 2;
   static constexpr int kStages = BN >= 256 ? 6 : 8;
+  static constexpr int kAcc = AccCount<BN>::value;  // TMEM accumulators (BN columns each)
   static constexpr int kABytes = 128 * 128;     // 128 rows x 64 K
   static constexpr int kBBytes = kBHalf * 128;  // BN/2 columns (chunks of 64) x 64 K
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -37,12 +38,12 @@ struct PairLayout {
   static constexpr int kEpiBytes = 2 * kEpiTileBytes;
   static constexpr int kRingOffset = kEpiOffset + kEpiBytes;
   static constexpr int kBarOffset = kRingOffset + kRing * static_cast<int>(sizeof(TileSlot));
-  static constexpr int kNumBars = 2 * kStages + 4 + 2 * kRing + 1;
+  static constexpr int kNumBars = 2 * kStages + 2 * kAcc + 2 * kRing + 1;
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
   static constexpr int kBytes = kMiscOffset + 32;
   static constexpr int kDynamicSmem = kBytes + 1024;
   static constexpr uint32_t kStageTxPair = 2u * static_cast<uint32_t>(kStageBytes);  // both CTAs' halves
-  static constexpr uint32_t kTmemCols = 2 * BN;
+  static constexpr uint32_t kTmemCols = kAcc * BN;
   static_assert(kRingOffset % 1024 == 0, "stage and staging tiles stay 1024-byte aligned");
   static_assert(kDynamicSmem <= 232448, "fits the 227 KB opt-in shared memory of a CTA");
   static_assert(kDynamicSmem > 232448 / 2 + 1024, "one CTA per SM");
@@ -79,6 +80,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_sm100_pair_kernel(const __grid_constant__ KernelParams p) {
   using L = PairLayout<BN>;
   constexpr int S = L::kStages;
+  constexpr int kAcc = L::kAcc;
   constexpr int BM = 256;          // output rows per pair tile
   constexpr int HB = BN / 2;       // B columns per CTA
   static_assert(BN == 128 || BN == 256, "pair tile columns");
@@ -93,10 +95,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
   auto empty_bar = [&](int s) { return bar0 + 8u * (S + s); };
   auto accf_bar = [&](int b) { return bar0 + 8u * (2 * S + b); };
-  auto acce_bar = [&](int b) { return bar0 + 8u * (2 * S + 2 + b); };
-  auto ringf_bar = [&](int r) { return bar0 + 8u * (2 * S + 4 + r); };
-  auto ringe_bar = [&](int r) { return bar0 + 8u * (2 * S + 4 + kRing + r); };
-  const uint32_t drain_bar = bar0 + 8u * (2 * S + 4 + 2 * kRing);
+  auto acce_bar = [&](int b) { return bar0 + 8u * (2 * S + kAcc + b); };
+  auto ringf_bar = [&](int r) { return bar0 + 8u * (2 * S + 2 * kAcc + r); };
+  auto ringe_bar = [&](int r) { return bar0 + 8u * (2 * S + 2 * kAcc + kRing + r); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * S + 2 * kAcc + 2 * kRing);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOffset);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 4);
   volatile int* prod_go = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 8);
@@ -112,7 +114,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(full_bar(s), 2);   // leader producer (with the byte count) + peer producer
       ptx::mbar_init(empty_bar(s), 1);  // the MMA commit, multicast to both CTAs
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kAcc; ++b) {
       ptx::mbar_init(accf_bar(b), 1);
       ptx::mbar_init(acce_bar(b), 2 * kEpiWarps);  // epilogue warps of both CTAs (leader's copy used)
     }
@@ -151,7 +153,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (leader) {
       const int pair_id = static_cast<int>(blockIdx.x >> 1);
       const int pairs = static_cast<int>(gridDim.x >> 1);
-      int static_next = pair_id;
+      SchedState ss;
+      sched_init(p, ss, pair_id, pairs, lane);
       for (int t = 0;; ++t) {
         const int slot = t % kRing;
         const uint32_t par = static_cast<uint32_t>(t / kRing) & 1u;
@@ -162,36 +165,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         TileSlot* s = &ring[slot];
         int pidx = -1, tile_m = 0, tile_n = 0;
-        for (;;) {
-          int tile = 0;
-          if (lane == 0) {
-            if (p.single_mode) {
-              tile = static_next;
-              static_next += pairs;
-            } else {
-              tile = atomicAdd(p.tile_counter, 1);
-            }
-          }
-          tile = __shfl_sync(0xffffffffu, tile, 0);
-          if (tile >= p.total_tiles) break;
-          const int q = p.single_mode ? 0 : find_problem_warp(p.tile_offsets, p.problem_count, tile, lane);
-          const int local = tile - (p.single_mode ? 0 : __ldg(p.tile_offsets + q));
-          const int* src = reinterpret_cast<const int*>(problems + q);
-          const int w = lane < kDescWords ? src[lane] : 0;
-          const int tiles_m = __shfl_sync(0xffffffffu, w, static_cast<int>(offsetof(DeviceProblemDesc, tiles_m) / 4));
-          const int tiles_n = __shfl_sync(0xffffffffu, w, static_cast<int>(offsetof(DeviceProblemDesc, tiles_n) / 4));
-          if (local < 0 || tiles_m <= 0 || tiles_n <= 0 || local >= tiles_m * tiles_n) continue;
-          raster_tile(local, tiles_m, tiles_n, p.raster_group, tile_m, tile_n);
-          if (lane < kDescWords) reinterpret_cast<int*>(&s->desc)[lane] = w;
+        if (next_tile(p, ss, problems, lane, pairs, pidx, tile_m, tile_n)) {
+          if (lane < kDescWords) reinterpret_cast<int*>(&s->desc)[lane] = ss.w;
           const unsigned fl = static_cast<unsigned>(
-              __shfl_sync(0xffffffffu, w, static_cast<int>(offsetof(DeviceProblemDesc, flags) / 4)));
-          const bool map_valid = (lane == kMapA || lane == kMapB) ? (fl & grouped_gemm::kFlagTmaAB) != 0u
-                                 : lane == kMapB3                 ? (fl & grouped_gemm::kFlagTmaB3) != 0u
-                                 : lane == kMapD                  ? (fl & grouped_gemm::kFlagTmaD) != 0u
-                                                                  : false;
-          if (map_valid) ptx::prefetch_tensormap(maps + kMapsPerProblem * q + lane);
-          pidx = q;
-          break;
+              __shfl_sync(0xffffffffu, ss.w, static_cast<int>(offsetof(DeviceProblemDesc, flags) / 4)));
+          prefetch_problem_maps(maps, pidx, fl, lane);
+        } else {
+          pidx = -1;
         }
         if (lane == 0) {
           s->problem = pidx;
@@ -290,18 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* as = smem + st * L::kStageBytes;
           uint8_t* bs = as + L::kABytes;
-          for (int idx = ptid; idx < 128 * 8; idx += kProdThreads) {
-            const int r = idx >> 3, j = idx & 7;
-            const uint4 v = load8_zero_fill(a, lda, row_base + r, kb * kBK + j * 8, m, k);
-            *reinterpret_cast<uint4*>(as + r * 128 + ((j ^ (r & 7)) << 4)) = v;
-          }
-          constexpr int kChunksPerRow = HB / 8;
-          for (int idx = ptid; idx < kBK * kChunksPerRow; idx += kProdThreads) {
-            const int kr = idx / kChunksPerRow, jn = idx % kChunksPerRow;
-            const int c = jn >> 3, j = jn & 7;
-            const uint4 v = load8_zero_fill(b, ldb, kb * kBK + kr, col_base + jn * 8, k, n);
-            *reinterpret_cast<uint4*>(bs + c * 8192 + kr * 128 + ((j ^ (kr & 7)) << 4)) = v;
-          }
+          lsu_fill_stage<128, HB>(as, bs, a, lda, b, ldb, m, n, k, row_base, col_base, kb, ptid);
           ptx::fence_proxy_async_all();  // the leader's tensor cores read this CTA's shared memory
           ptx::named_bar_sync(1, kProdThreads);
           if (ptid == 0) {
@@ -337,8 +306,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool lsu_tile = (ring[slot].desc.flags & grouped_gemm::kFlagTmaAB) == 0u;
         ptx::mbar_arrive(ringe_bar(slot));
         if (q < 0) break;
-        const int buf = t & 1;
-        if (!wait_phase_cluster(acce_bar(buf), (static_cast<uint32_t>(t >> 1) & 1u) ^ 1u, abort_flag, p.status, tmo,
+        const int buf = t % kAcc;
+        if (!wait_phase_cluster(acce_bar(buf), (static_cast<uint32_t>(t / kAcc) & 1u) ^ 1u, abort_flag, p.status, tmo,
                                 GG_STATUS_TIMEOUT_MMA))
           break;
         ptx::tc_fence_after_sync();
@@ -403,112 +372,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) release_slot(slot);
       if (q < 0) break;
-      const int buf = t & 1;
+      const int buf = t % kAcc;
       if (et == 0)
-        epi_go[1] = wait_phase(accf_bar(buf), static_cast<uint32_t>(t >> 1) & 1u, abort_flag, p.status, tmo,
+        epi_go[1] = wait_phase(accf_bar(buf), static_cast<uint32_t>(t / kAcc) & 1u, abort_flag, p.status, tmo,
                                GG_STATUS_TIMEOUT_EPILOGUE) ? 1 : 0;
       ptx::named_bar_sync(2, kEpiThreads);
       if (!epi_go[1]) break;
       ptx::tc_fence_after_sync();
 
-      const int cta_row0 = tile_m * BM + static_cast<int>(rank) * 128;  // this CTA's first row
-      const int row0 = cta_row0 + qw * 32;
-      const int row = row0 + lane;
-      const int col0 = tile_n * BN;
-      const bool warp_rows = row0 < m;
-      const int nchunks = min(BN / 32, (n - col0 + 31) / 32);
+      const int nchunks = min(BN / 32, (n - tile_n * BN + 31) / 32);
       const uint32_t t_addr = tmem_base + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(qw * 32) << 16);
-      const bool read_c = (flags & grouped_gemm::kFlagReadC) != 0u;
-      const bool tma_d = (flags & grouped_gemm::kFlagTmaD) != 0u && cta_row0 < m;
-      const CUtensorMap* md = maps + kMapsPerProblem * q + kMapD;
-
-      for (int c = 0; c < nchunks; ++c) {
-        float acc[32];
-        if (warp_rows && kb_count > 0) {
-          uint32_t r[32];
-          ptx::tmem_load_32cols(t_addr + static_cast<uint32_t>(c * 32), r);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(r[j]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
-        }
-        if (c == nchunks - 1) {
-          ptx::tc_fence_before_sync();
-          __syncwarp();
-          if (lane == 0) {
-            if (leader) ptx::mbar_arrive(acce_bar(buf));
-            else ptx::mbar_arrive_cluster(ptx::mapa_shared(acce_bar(buf), 0));
-          }
-        }
-        const int cc = col0 + c * 32;
-        float cv[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) cv[j] = 0.0f;
-        if (read_c && warp_rows && row < m) {
-          const float* crow = cptr + static_cast<int64_t>(row) * ldc + cc;
-          if ((flags & grouped_gemm::kFlagCVec) && cc + 32 <= n) {
-#pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {
-              const float4 v = *reinterpret_cast<const float4*>(crow + 4 * j4);
-              cv[4 * j4] = v.x;
-              cv[4 * j4 + 1] = v.y;
-              cv[4 * j4 + 2] = v.z;
-              cv[4 * j4 + 3] = v.w;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (cc + j < n) cv[j] = crow[j];
-          }
-        }
-        float out[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) out[j] = alpha * acc[j] + beta * cv[j];
-
-        if (tma_d) {
-          uint8_t* stile = smem + L::kEpiOffset + static_cast<int>(store_count & 1u) * kEpiTileBytes;
-          if (et == 0) ptx::bulk_wait_read_le1();
-          ptx::named_bar_sync(2, kEpiThreads);
-          {
-            const int r = qw * 32 + lane;
-#pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {
-              *reinterpret_cast<float4*>(stile + r * 128 + ((j4 ^ (r & 7)) << 4)) =
-                  make_float4(out[4 * j4], out[4 * j4 + 1], out[4 * j4 + 2], out[4 * j4 + 3]);
-            }
-          }
-          ptx::fence_proxy_async_smem();
-          ptx::named_bar_sync(2, kEpiThreads);
-          if (et == 0) {
-            ptx::tma_store_2d(md, ptx::smem_addr(stile), cc, cta_row0);
-            ptx::bulk_commit_group();
-          }
-          ++store_count;
-        } else if (warp_rows && row < m) {
-          float* drow = dptr + static_cast<int64_t>(row) * ldd + cc;
-          if ((flags & grouped_gemm::kFlagDVec) && cc + 32 <= n) {
-#pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4)
-              *reinterpret_cast<float4*>(drow + 4 * j4) =
-                  make_float4(out[4 * j4], out[4 * j4 + 1], out[4 * j4 + 2], out[4 * j4 + 3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (cc + j < n) drow[j] = out[j];
-          }
-        }
-      }
-      if (nchunks <= 0) {
-        ptx::tc_fence_before_sync();
-        __syncwarp();
-        if (lane == 0) {
-          if (leader) ptx::mbar_arrive(acce_bar(buf));
-          else ptx::mbar_arrive_cluster(ptx::mapa_shared(acce_bar(buf), 0));
-        }
-      }
+      const int row0 = tile_m * BM + static_cast<int>(rank) * 128 + qw * 32;  // this warp's first row
+      epilogue_warp(smem + L::kEpiOffset + qw * 8192, store_count, t_addr, lane, row0, m, n, tile_n * BN, nchunks,
+                    kb_count, flags, alpha, beta, cptr, ldc, dptr, ldd, maps + kMapsPerProblem * q + kMapD, [&] {
+                      if (leader) ptx::mbar_arrive(acce_bar(buf));
+                      else ptx::mbar_arrive_cluster(ptx::mapa_shared(acce_bar(buf), 0));
+                    });
     }
-    if (et == 0) ptx::bulk_wait_all();
+    if (lane == 0) ptx::bulk_wait_all();  // every warp issues its own TMA stores
     __syncwarp();
   }
 

@@ -23,7 +23,7 @@ constexpr int kSchedWarp = 5;
 constexpr int kProdWarp0 = 6;
 constexpr int kProdThreads = 64;
 constexpr int kRingConsumerWarps = kEpiWarps + 1 + 2;  // arrivals that free one ring slot
-constexpr int kEpiTileBytes = 128 * 128;               // 128 rows x 32 FP32 columns of D
+constexpr int kEpiTileBytes = 128 * 128;               // 4 warps x 2 staging tiles of 32 x 32 FP32
 constexpr int kEpiThreads = kEpiWarps * 32;
 // Tensor maps per problem, in this order: A (64 K x BM rows), B by 64-column chunk (64 N x 64 K),
 // B as one 3-D box per stage (64 N x 64 K x BN/64 chunks; full chunks only), D (32 cols x BM rows).
@@ -47,9 +47,17 @@ struct StageCount {
   static constexpr int value = BN >= 256 ? 4 : 6;
 };
 
+// TMEM accumulators per CTA: BN FP32 columns each, 512 columns in all. More than two let the MMA
+// run several tiles ahead of an epilogue that is waiting on the SM's store bandwidth.
+template <int BN>
+struct AccCount {
+  static constexpr int value = BN <= 128 ? 4 : 2;
+};
+
 template <int BM, int BN>
 struct SmemLayout {
   static constexpr int kStages = StageCount<BN>::value;
+  static constexpr int kAcc = AccCount<BN>::value;
   static constexpr int kABytes = kMmaM * 128;
   static constexpr int kBBytes = BN * 128;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -57,13 +65,13 @@ struct SmemLayout {
   static constexpr int kEpiBytes = 2 * kEpiTileBytes;  // double-buffered staging tile
   static constexpr int kRingOffset = kEpiOffset + kEpiBytes;
   static constexpr int kBarOffset = kRingOffset + kRing * static_cast<int>(sizeof(TileSlot));
-  static constexpr int kNumBars = 2 * kStages + 4 + 2 * kRing + 1;
+  static constexpr int kNumBars = 2 * kStages + 2 * kAcc + 2 * kRing + 1;
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
   static constexpr int kBytes = kMiscOffset + 32;
   static constexpr int kDynamicSmem = kBytes + 1024;  // slack to align the base to 1024 bytes
   static constexpr uint32_t kATxBytes = static_cast<uint32_t>(BM) * 128;
   static constexpr uint32_t kBTxBytes = static_cast<uint32_t>(BN) * 128;
-  static constexpr uint32_t kTmemCols = 2 * BN;
+  static constexpr uint32_t kTmemCols = kAcc * BN;
   static_assert(kRingOffset % 1024 == 0, "stage and staging tiles stay 1024-byte aligned");
   static_assert(kBarOffset % 8 == 0, "mbarriers are 8-byte aligned");
   static_assert(kDynamicSmem <= 232448, "fits the 227 KB opt-in shared memory of a CTA");
