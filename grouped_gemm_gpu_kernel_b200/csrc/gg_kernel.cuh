@@ -184,9 +184,12 @@ __device__ __forceinline__ void prefetch_problem_maps(const CUtensorMap* maps, i
 // `release` hands the accumulator back to the MMA warp after the last TMEM read.
 template <typename Release>
 __device__ __forceinline__ void epilogue_warp(uint8_t* stage, uint32_t& store_count, uint32_t t_addr, int lane,
-                                              int row0, int m, int n, int col0, int nchunks, int kb_count,
-                                              unsigned flags, float alpha, float beta, const float* cptr, int ldc,
-                                              float* dptr, int ldd, const CUtensorMap* md, Release release) {
+                                              int row0, int m, int n, int col0, int c_begin, int c_end,
+                                              int kb_count, unsigned flags, float alpha, float beta,
+                                              const float* cptr, int ldc, float* dptr, int ldd,
+                                              const CUtensorMap* md, Release release) {
+  constexpr int kStageTiles = kEpiWarpBytes / 4096;  // staging tiles of this warp
+  static_assert(kStageTiles == 1 || kStageTiles == 2, "staging tiles per epilogue warp");
   const bool warp_rows = row0 < m;  // warp-uniform
   const bool read_c = (flags & grouped_gemm::kFlagReadC) != 0u;
   const bool tma_d = (flags & grouped_gemm::kFlagTmaD) != 0u;
@@ -195,8 +198,8 @@ __device__ __forceinline__ void epilogue_warp(uint8_t* stage, uint32_t& store_co
     // Two chunks per TMEM read (one 64-column tcgen05.ld and one wait), then one staging tile
     // and one TMA store per chunk, so that a store is always in flight while the next chunk is
     // prepared.
-    for (int c = 0; c < nchunks; c += 2) {
-      const int nsub = c + 1 < nchunks ? 2 : 1;
+    for (int c = c_begin; c < c_end; c += 2) {
+      const int nsub = c + 1 < c_end ? 2 : 1;
       uint32_t r[64];
       if (warp_rows && kb_count > 0) {
         if (nsub == 2) {
@@ -211,8 +214,8 @@ __device__ __forceinline__ void epilogue_warp(uint8_t* stage, uint32_t& store_co
 #pragma unroll
         for (int j = 0; j < 64; ++j) r[j] = 0u;
       }
-      if (c + nsub >= nchunks) {
-        // Last read of this accumulator: hand it back to the MMA warp before the stores.
+      if (c + nsub >= c_end) {
+        // This warp's last read of the accumulator: hand it back before the stores.
         ptx::tc_fence_before_sync();
         __syncwarp();
         if (lane == 0) release();
@@ -242,8 +245,11 @@ __device__ __forceinline__ void epilogue_warp(uint8_t* stage, uint32_t& store_co
               if (cc + j < n) cv[j] = __ldg(crow + j);
           }
         }
-        uint8_t* stile = stage + static_cast<int>(store_count & 1u) * 4096;
-        if (lane == 0) ptx::bulk_wait_read_le1();  // the store that used this tile two chunks ago
+        uint8_t* stile = stage + (kStageTiles == 2 ? static_cast<int>(store_count & 1u) * 4096 : 0);
+        if (lane == 0) {  // the store that last used this staging tile has read it
+          if (kStageTiles == 2) ptx::bulk_wait_read_le1();
+          else ptx::bulk_wait_all_read();
+        }
         __syncwarp();
 #pragma unroll
         for (int j4 = 0; j4 < 8; ++j4) {
@@ -269,7 +275,7 @@ __device__ __forceinline__ void epilogue_warp(uint8_t* stage, uint32_t& store_co
     // hold one 128-byte row segment, then C is loaded and D stored with coalesced accesses.
     const int jj = lane & 7;
     if (warp_rows && lane == 0) ptx::bulk_wait_all_read();  // staging tile 0 is free
-    for (int c = 0; c < nchunks; ++c) {
+    for (int c = c_begin; c < c_end; ++c) {
       const int cc = col0 + c * 32;
       const int gcol = cc + 4 * jj;
       // C, issued before the TMEM read so that its latency overlaps it.
@@ -303,7 +309,7 @@ __device__ __forceinline__ void epilogue_warp(uint8_t* stage, uint32_t& store_co
 #pragma unroll
         for (int j = 0; j < 32; ++j) r[j] = 0u;
       }
-      if (c == nchunks - 1) {
+      if (c == c_end - 1) {
         ptx::tc_fence_before_sync();
         __syncwarp();
         if (lane == 0) release();
@@ -339,11 +345,19 @@ __device__ __forceinline__ void epilogue_warp(uint8_t* stage, uint32_t& store_co
       __syncwarp();
     }
   }
-  if (nchunks <= 0) {
+  if (c_begin >= c_end) {
     ptx::tc_fence_before_sync();
     __syncwarp();
     if (lane == 0) release();
   }
+}
+
+// The chunk range [c_begin, c_end) of a tile's nchunks 32-column chunks that epilogue warp half
+// `half` stores: whole 64-column pairs, the first half taking the larger share.
+__device__ __forceinline__ void epilogue_chunk_range(int nchunks, int half, int& c_begin, int& c_end) {
+  const int split = min(nchunks, 2 * ((nchunks + 3) / 4));
+  c_begin = half ? split : 0;
+  c_end = half ? nchunks : split;
 }
 
 // ---- producer helpers ------------------------------------------------------------------------
@@ -351,10 +365,10 @@ __device__ __forceinline__ void epilogue_warp(uint8_t* stage, uint32_t& store_co
 // one stage: A rows [row0, row0+ROWS) and B columns [col0, col0+COLS) of K block kb, in the same
 // 128-byte-swizzled layouts the TMA loads produce. Consecutive lanes read consecutive elements of
 // one row (coalesced), 2 bytes per lane, or 4 when every row of the operand starts on a 4-byte
-// boundary; each lane keeps up to 64 loads in flight before it stores them. Columns of A and rows of B
+// boundary; each lane keeps up to 16 loads in flight before it stores them. Columns of A and rows of B
 // past K are written as zeros; rows of A past M and columns of B past N are not written at all:
 // they only reach accumulator rows and columns that are never stored.
-constexpr int kLsuBatch = 64;  // loads in flight per lane before their stores
+constexpr int kLsuBatch = 16;  // loads in flight per lane before their stores
 
 template <int V>
 __device__ __forceinline__ uint32_t lsu_load(const unsigned short* src, int c, int limit) {
@@ -688,11 +702,12 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
     }
     __syncwarp();
   } else {
-    // ======================= epilogue (warps 0-3) =======================
-    // The four warps move in step: thread 0 waits on the ring and accumulator barriers and
+    // ======================= epilogue (warps 0-7) =======================
+    // The eight warps move in step: thread 0 waits on the ring and accumulator barriers and
     // broadcasts the outcome through epi_go after a named barrier, so a timed-out wait ends
     // the loop in every warp at the same point (no warp is left inside a named barrier).
-    const int qw = warp;  // TMEM lane quarter = tile rows 32*qw .. 32*qw+31
+    const int qw = warp & 3;    // TMEM lane quarter = tile rows 32*qw .. 32*qw+31
+    const int half = warp >> 2;  // which half of the tile's columns this warp stores
     const int et = static_cast<int>(threadIdx.x);
     uint32_t store_count = 0;
     for (int t = 0;; ++t) {
@@ -724,12 +739,14 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
       ptx::tc_fence_after_sync();
 
       const int nchunks = min(BN / 32, (n - tile_n * BN + 31) / 32);  // tile-uniform
+      int c_begin, c_end;
+      epilogue_chunk_range(nchunks, half, c_begin, c_end);
       const uint32_t t_addr = tmem_base + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(qw * 32) << 16);
       // Warps whose 32 rows lie past BM (64-row tiles) or past M store nothing.
       const int row0 = qw * 32 < BM ? tile_m * BM + qw * 32 : m;
-      epilogue_warp(smem + L::kEpiOffset + qw * 8192, store_count, t_addr, lane, row0, m, n, tile_n * BN, nchunks,
-                    kb_count, flags, alpha, beta, cptr, ldc, dptr, ldd, maps + kMapsPerProblem * q + kMapD,
-                    [&] { ptx::mbar_arrive(acce_bar(buf)); });
+      epilogue_warp(smem + L::kEpiOffset + warp * kEpiWarpBytes, store_count, t_addr, lane, row0, m, n, tile_n * BN,
+                    c_begin, c_end, kb_count, flags, alpha, beta, cptr, ldc, dptr, ldd,
+                    maps + kMapsPerProblem * q + kMapD, [&] { ptx::mbar_arrive(acce_bar(buf)); });
     }
     if (lane == 0) ptx::bulk_wait_all();  // every warp issues its own TMA stores
     __syncwarp();

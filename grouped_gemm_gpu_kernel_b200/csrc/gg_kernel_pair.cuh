@@ -347,8 +347,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // ======================= epilogue (warps 0-3, both CTAs) =======================
-    const int qw = warp;
+    // ======================= epilogue (warps 0-7, both CTAs) =======================
+    const int qw = warp & 3;     // TMEM lane quarter
+    const int half = warp >> 2;  // half of the tile's columns
     const int et = static_cast<int>(threadIdx.x);
     uint32_t store_count = 0;
     for (int t = 0;; ++t) {
@@ -381,10 +382,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tc_fence_after_sync();
 
       const int nchunks = min(BN / 32, (n - tile_n * BN + 31) / 32);
+      int c_begin, c_end;
+      epilogue_chunk_range(nchunks, half, c_begin, c_end);
       const uint32_t t_addr = tmem_base + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(qw * 32) << 16);
       const int row0 = tile_m * BM + static_cast<int>(rank) * 128 + qw * 32;  // this warp's first row
-      epilogue_warp(smem + L::kEpiOffset + qw * 8192, store_count, t_addr, lane, row0, m, n, tile_n * BN, nchunks,
-                    kb_count, flags, alpha, beta, cptr, ldc, dptr, ldd, maps + kMapsPerProblem * q + kMapD, [&] {
+      epilogue_warp(smem + L::kEpiOffset + warp * kEpiWarpBytes, store_count, t_addr, lane, row0, m, n,
+                    tile_n * BN, c_begin, c_end, kb_count, flags, alpha, beta, cptr, ldc, dptr, ldd,
+                    maps + kMapsPerProblem * q + kMapD, [&] {
                       if (leader) ptx::mbar_arrive(acce_bar(buf));
                       else ptx::mbar_arrive_cluster(ptx::mapa_shared(acce_bar(buf), 0));
                     });

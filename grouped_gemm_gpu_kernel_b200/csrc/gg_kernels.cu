@@ -68,7 +68,7 @@ bool valid(Variant v) { return static_cast<int>(v) >= 0 && static_cast<int>(v) <
 }  // namespace
 
 Variant resolve_variant(int cta_m, int cta_n, int cta_k, int threads) {
-  if (threads != kThreads) return Variant::kUnsupported;
+  if (threads != kConfigThreads) return Variant::kUnsupported;
   // the reference's shapes (same tile decomposition, cta_k names the variant only)
   if (cta_m == 64 && cta_n == 64 && cta_k == 16) return Variant::k64x64;
   if (cta_m == 128 && cta_n == 64 && cta_k == 32) return Variant::k128x64;

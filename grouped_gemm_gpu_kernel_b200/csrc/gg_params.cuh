@@ -12,18 +12,20 @@ namespace gg {
 
 using grouped_gemm::DeviceProblemDesc;
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;  // 12 warps: 8 epilogue, MMA, scheduler, 2 producers
 constexpr int kBK = 64;     // K elements per pipeline stage: one 128-byte swizzle row of FP16
 constexpr int kMmaM = 128;  // tcgen05 M used by every variant
 constexpr int kMmaK = 16;   // tcgen05 K for 16-bit inputs
 constexpr int kRing = 4;    // scheduler ring depth
-constexpr int kEpiWarps = 4;
-constexpr int kMmaWarp = 4;
-constexpr int kSchedWarp = 5;
-constexpr int kProdWarp0 = 6;
+constexpr int kConfigThreads = 256;  // KernelConfig::threads accepted (the reference's default)
+constexpr int kEpiWarps = 8;         // two per TMEM lane quarter, each with half the tile's columns
+constexpr int kMmaWarp = 8;
+constexpr int kSchedWarp = 9;
+constexpr int kProdWarp0 = 10;
 constexpr int kProdThreads = 64;
 constexpr int kRingConsumerWarps = kEpiWarps + 1 + 2;  // arrivals that free one ring slot
-constexpr int kEpiTileBytes = 128 * 128;               // 4 warps x 2 staging tiles of 32 x 32 FP32
+constexpr int kEpiTileBytes = 128 * 128;               // 8 warps x one 4 KB staging tile (32 x 32 FP32)
+constexpr int kEpiWarpBytes = 2 * kEpiTileBytes / kEpiWarps;
 constexpr int kEpiThreads = kEpiWarps * 32;
 // Tensor maps per problem, in this order: A (64 K x BM rows), B by 64-column chunk (64 N x 64 K),
 // B as one 3-D box per stage (64 N x 64 K x BN/64 chunks; full chunks only), D (32 cols x BM rows).

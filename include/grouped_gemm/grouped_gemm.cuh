@@ -45,7 +45,8 @@ struct ProblemDesc {
 
 // Tile shape and launch shape. The defaults are the reference's; the sm_100a-native shapes
 // 128x128x64, 128x256x64, 128x64x64 and the CTA-pair shapes 256x128x64, 256x256x64 are also
-// accepted (threads must be 256).
+// accepted (threads must be 256, the reference default; the kernel itself launches 384-thread
+// blocks, which query_occupancy reports).
 struct KernelConfig {
   int cta_m = 64;
   int cta_n = 64;

@@ -120,11 +120,11 @@ def test_occupancy_report(cuda):
     for cfg in ALL_CONFIGS:
         st, info = gg.query_occupancy(cfg)
         assert st == 0
-        assert info.sm_count >= 100 and info.active_blocks_per_sm == 1 and info.threads_per_block == 256
-        assert info.warps_per_block == 8 and info.using_tensor_cores
+        assert info.sm_count >= 100 and info.active_blocks_per_sm == 1 and info.threads_per_block == 384
+        assert info.warps_per_block == 12 and info.using_tensor_cores
         assert 100_000 < info.dynamic_shared_bytes <= 232_448
-        assert 0 < info.registers_per_thread <= 255 and info.registers_per_block == info.registers_per_thread * 256
-        assert info.theoretical_occupancy == pytest.approx(8 / info.max_warps_per_sm)
+        assert 0 < info.registers_per_thread <= 168 and info.registers_per_block == info.registers_per_thread * 384
+        assert info.theoretical_occupancy == pytest.approx(12 / info.max_warps_per_sm)
 
 
 def test_single_tile_tma_path(cuda):
