@@ -40,6 +40,7 @@ import numpy as np
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
+L2_BYTES = 126 << 20
 METRIC = "aggregate TFLOP/s (2·ΣMNK/s) at 1/2/4/8 B200, % of dense FP16 peak"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 DEFAULT_CTA = {"small16": (128, 128, 64), "mixed512": (128, 256, 64), "moe": (128, 256, 64),
@@ -312,24 +313,43 @@ def main():
     clocks.start()
     for _ in range(max(args.warmup, 3)):
         assert ex.run(stream) == 0
+    alg_bytes = shapes.algorithmic_bytes()
+    # Inputs smaller than twice L2 would stay cache-resident from one step to the next: such
+    # workloads flush L2 (write a buffer larger than L2) before every step and time each step
+    # alone; larger ones run back to back.
+    flush = None
+    if alg_bytes < 2 * L2_BYTES:
+        flush = torch.empty(4 * L2_BYTES, dtype=torch.uint8, device=dev)
     barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks.mark(True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        ex.run(stream)
-    e1.record(stream)
-    barrier()
+    if flush is None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            ex.run(stream)
+        e1.record(stream)
+        barrier()
+        local_ms = e0.elapsed_time(e1) / args.steps
+    else:
+        evs = []
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
+                flush.zero_()
+                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a0.record(stream)
+                ex.run(stream)
+                a1.record(stream)
+                evs.append((a0, a1))
+        barrier()
+        local_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
     clocks.mark(False)
     clock_info = clocks.stop()
-    local_ms = e0.elapsed_time(e1) / args.steps
     if ex.status() != 0:
         raise RuntimeError("a bounded wait timed out inside the kernel during the timed region")
     ms = max_over_ranks(local_ms)
     value = global_flops / (ms * 1e-3) / 1e12
 
     peaks = load_peaks()
-    alg_bytes = shapes.algorithmic_bytes()
     local_flops = shapes.flops
     ai = local_flops / alg_bytes
     ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
@@ -411,6 +431,7 @@ def main():
                                              "grid": ex2.grid_ctas(), "tiles": ex2.total_tiles()}
             ex2.close()
         extras["sort_modes"] = sweep
+        extras["cuda_graph"] = graph_row(ex, stream, local_flops)
         extras["ref_gpu"] = reference_gpu_row(problems, stream, local_flops)
 
     cpu = None
@@ -425,8 +446,12 @@ def main():
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": args.workload, "problems_per_gpu": len(shapes.dims), "cta": "x".join(map(str, cta)),
                        "sort_mode": gg.sort_mode_name(args.sort_mode), "tiles": n_tiles, "grid_ctas": ex.grid_ctas(),
-                       "global_gflop": global_flops / 1e9, "l2": f"inputs larger than L2 ({alg_bytes / 1e9:.2f} GB "
-                       "algorithmic footprint per GPU > 126 MB), no flush", "accumulate": "f32",
+                       "global_gflop": global_flops / 1e9,
+                       "l2": (f"inputs larger than L2 ({alg_bytes / 1e9:.2f} GB algorithmic footprint per GPU "
+                              "> 2 x 126 MB), steps back to back, no flush") if flush is None else
+                             (f"footprint {alg_bytes / 1e6:.1f} MB < 2 x L2: L2 flushed ({4 * L2_BYTES >> 20} MB "
+                              "write) before every step, each step timed alone"),
+                       "accumulate": "f32",
                        "prep_build_ms": prep_ms, "parallelism": f"dp{world} (tile-balanced shards)"},
             "pct_dense_fp16_peak": 100.0 * value / (world * peaks["bf16_tflops"]),
             "peak_source": peaks["source"],
@@ -442,6 +467,33 @@ def main():
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def graph_row(ex, stream, flops, runs=20, replays=10):
+    """The same executor runs captured in one CUDA graph (counter reset + launch per run)."""
+    import torch
+
+    try:
+        g = torch.cuda.CUDAGraph()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=stream):
+            for _ in range(runs):
+                ex.run(torch.cuda.current_stream())
+        g.replay()
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(replays):
+                g.replay()
+        a1.record(stream)
+        torch.cuda.synchronize()
+        t = a0.elapsed_time(a1) / (runs * replays)
+        st = ex.status()
+        del g
+        return {"ms": t, "tflops": flops / (t * 1e-3) / 1e12, "runs_per_graph": runs, "status": st}
+    except Exception as e:  # capture is optional evidence; the timed line above does not use it
+        return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
 
 
 def reference_gpu_row(problems, stream, flops):

@@ -277,6 +277,33 @@ def test_determinism_bitwise(cuda):
     assert torch.equal(first, ps.d)
 
 
+def test_executor_run_captured_in_cuda_graph(cuda):
+    """gg_executor_run (counter reset + launch) replays from a CUDA graph with the same result."""
+    torch = _torch()
+    ps = W.allocate(W.make_shapes("small16"), cuda)
+    for cfg in (gg.KernelConfig(128, 256, 64), gg.KernelConfig(256, 128, 64)):
+        ex = gg.GroupedGemmExecutor()
+        assert ex.build(gg.prepare_problem_set(ps.problems(), cfg, gg.SortMode.kByK), cfg) == 0
+        s = torch.cuda.Stream(cuda)
+        torch.cuda.synchronize()
+        assert ex.run(s) == 0
+        torch.cuda.synchronize()
+        eager = ps.d.clone()
+        ps.d.fill_(float("nan"))
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(3):
+                assert ex.run(torch.cuda.current_stream()) == 0
+        g.replay()
+        torch.cuda.synchronize()
+        assert ex.status() == 0
+        # alignment gaps between the problems' D blocks hold NaN canaries in both copies
+        assert torch.equal(torch.nan_to_num(eager, nan=7.0), torch.nan_to_num(ps.d, nan=7.0))
+        del g
+        ex.close()
+
+
 def _edge_problem(cuda, m, n, k, lda=None, ldb=None, ldc=None, ldd=None, alpha=1.0, beta=0.0, a_shift=0,
                   b_shift=0, c_mode="rand", seed=0):
     """One problem with its own buffers; shifts misalign the base pointers by 2-byte steps."""
