@@ -59,6 +59,8 @@ def parse_args():
     ap.add_argument("--no-extras", action="store_true", help="skip the sort-mode sweep and the reference GPU row")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU work of the cpu_baseline sample")
+    ap.add_argument("--gather", action="store_true",
+                    help="N>1: after the timed region, gather every rank's D to rank 0 over NCCL and time it")
     return ap.parse_args()
 
 
@@ -411,6 +413,8 @@ def main():
                "path": "pinned host A/B(/C) -> cudaMemcpyAsync -> gg_executor_run -> D back to pinned host"}
 
     extras = {}
+    if args.gather and world > 1:
+        extras["gather"] = gather_row(args, cfg, ps, world, rank, dev, max_over_ranks, barrier)
     if not args.no_extras and world == 1:
         sweep = {}
         for mode in range(4):
@@ -467,6 +471,52 @@ def main():
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def gather_row(args, cfg, ps, world, rank, dev, max_over_ranks, barrier):
+    """Optional NCCL gather of every rank's D rectangles into rank 0's full D (not in `value`)."""
+    import torch
+
+    import grouped_gemm_gpu_kernel_b200 as gg
+    from grouped_gemm_gpu_kernel_b200 import workloads as W
+    from grouped_gemm_gpu_kernel_b200.gather import gather_pieces, piece_elems
+
+    reps = [W.make_shapes(args.workload, seed=42 + r) for r in range(world)]
+    dims = [d for s in reps for d in s.dims]
+    probs = [gg.ProblemDesc(m, n, k, 1, 1, None, 1, max(1, k), max(1, n), max(1, n), max(1, n)) for m, n, k in dims]
+    by_rank = [gg.partition(probs, cfg, world, r)[0] for r in range(world)]
+    local = []
+    for i, pc in enumerate(by_rank[rank]):
+        d = ps.views(i)[3]
+        local.append(d if d is not None else torch.empty((pc.rows, pc.cols), device=dev))
+    root_d = None
+    if rank == 0:
+        sizes = [max(m, 0) * max(n, 0) for m, n, k in dims]
+        slab = torch.empty(sum(sizes), dtype=torch.float32, device=dev)
+        root_d, off = {}, 0
+        for i, ((m, n, k), sz) in enumerate(zip(dims, sizes)):
+            root_d[i] = slab[off:off + sz].view(max(m, 0), max(n, 0))
+            off += sz
+    gather_pieces(by_rank, local, root_d)  # warm-up: NCCL P2P connections
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    got = gather_pieces(by_rank, local, root_d)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    into_root = sum(piece_elems(by_rank[r]) for r in range(1, world)) * 4
+    ok = True
+    if rank == 0:
+        pc0 = by_rank[0][0] if by_rank[0] else None
+        if pc0 is not None and pc0.rows and pc0.cols:
+            ok = bool(torch.equal(root_d[pc0.problem][pc0.row0:pc0.row0 + pc0.rows, pc0.col0:pc0.col0 + pc0.cols],
+                                  local[0]))
+    barrier()
+    return {"ms": ms, "bytes_into_root": into_root, "gbps_into_root": into_root / (ms * 1e-3) / 1e9,
+            "received_on_root": got if rank == 0 else None, "root_piece_check": ok,
+            "how": "after the timed region: one packed FP32 buffer per rank, NCCL send/recv to rank 0, "
+                   "unpacked into the full D of every global problem"}
 
 
 def graph_row(ex, stream, flops, runs=20, replays=10):

@@ -1,0 +1,92 @@
+"""Optional gather of D to one rank after a sharded grouped GEMM (multi-GPU only).
+
+The problems of a grouped GEMM are independent, so a problem set split across ranks by
+`partition` (gg_partition: tile-weighted rectangles of D) needs no collective while it computes.
+When the caller wants every D on one rank afterwards, `gather_pieces` moves each rank's D
+rectangles there: a non-root rank packs all its rectangles into one contiguous FP32 buffer and
+sends it with one point-to-point send (NCCL over NVLink/NVSwitch for CUDA tensors, gloo for CPU
+tensors); the root posts one matching receive per rank, all in flight together, and unpacks the
+rectangles into its full D matrices. The reference is single-GPU and has no counterpart.
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Sequence
+
+__all__ = ["gather_pieces", "piece_elems"]
+
+
+def piece_elems(pieces) -> int:
+    """FP32 elements a rank sends for these pieces (rows x cols each)."""
+    return sum(max(0, p.rows) * max(0, p.cols) for p in pieces)
+
+
+def gather_pieces(pieces_by_rank: Sequence[Sequence], local_d: Sequence, root_d: Dict[int, object] | None,
+                  group=None, root: int = 0) -> int:
+    """Collects every rank's D rectangles into the root's D matrices; returns bytes received.
+
+    pieces_by_rank[r] -- the ShardPiece list of rank r (problem, row0, rows, col0, cols), the same
+                         on every rank (gg_partition is deterministic)
+    local_d           -- on every rank, one 2-D FP32 tensor per piece of this rank (rows x cols,
+                         rows may be padded), in the order of pieces_by_rank[rank]
+    root_d            -- on the root, {problem index: full 2-D FP32 D tensor}; None elsewhere
+    The call is collective over `group`: every rank must enter it.
+    """
+    import torch
+    import torch.distributed as dist
+
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    mine = pieces_by_rank[rank]
+    if len(local_d) != len(mine):
+        raise ValueError("local_d must hold one tensor per piece of this rank")
+    for t, pc in zip(local_d, mine):
+        if tuple(t.shape) != (pc.rows, pc.cols) or t.dtype != torch.float32:
+            raise ValueError("each local D must be a rows x cols FP32 tensor")
+
+    def unpack(buf, pieces):
+        off = 0
+        for pc in pieces:
+            cnt = pc.rows * pc.cols
+            if cnt:
+                view = buf[off:off + cnt].view(pc.rows, pc.cols)
+                root_d[pc.problem][pc.row0:pc.row0 + pc.rows, pc.col0:pc.col0 + pc.cols].copy_(view)
+            off += cnt
+
+    if rank == root:
+        if root_d is None:
+            raise ValueError("the root needs its full D tensors")
+        for t, pc in zip(local_d, mine):
+            root_d[pc.problem][pc.row0:pc.row0 + pc.rows, pc.col0:pc.col0 + pc.cols].copy_(t)
+        device = next(iter(root_d.values())).device if root_d else torch.device("cpu")
+        bufs: List = []
+        ops = []
+        for r in range(world):
+            if r == root:
+                bufs.append(None)
+                continue
+            n = piece_elems(pieces_by_rank[r])
+            buf = torch.empty(n, dtype=torch.float32, device=device)
+            bufs.append(buf)
+            if n:
+                ops.append(dist.P2POp(dist.irecv, buf, r, group))
+        for w in dist.batch_isend_irecv(ops) if ops else []:
+            w.wait()
+        received = 0
+        for r in range(world):
+            if r != root and bufs[r] is not None and bufs[r].numel():
+                unpack(bufs[r], pieces_by_rank[r])
+                received += bufs[r].numel() * 4
+        return received
+    n = piece_elems(mine)
+    if n:
+        device = local_d[0].device
+        buf = torch.empty(n, dtype=torch.float32, device=device)
+        off = 0
+        for t, pc in zip(local_d, mine):
+            cnt = pc.rows * pc.cols
+            if cnt:
+                buf[off:off + cnt].view(pc.rows, pc.cols).copy_(t)
+            off += cnt
+        for w in dist.batch_isend_irecv([dist.P2POp(dist.isend, buf, root, group)]):
+            w.wait()
+    return 0
