@@ -18,7 +18,7 @@ EXPORTED_SYMBOLS = (
     "gg_executor_create", "gg_executor_destroy", "gg_executor_build", "gg_executor_run",
     "gg_executor_problem_count", "gg_executor_total_tiles", "gg_executor_grid_ctas", "gg_executor_status",
     "gg_run_grouped_gemm_once", "gg_run_baseline_per_problem", "gg_count_non_empty_problems",
-    "gg_partition", "gg_selftest_wait_timeout", "gg_run_grouped_gemm_noalloc",
+    "gg_partition", "gg_selftest_wait_timeout", "gg_run_grouped_gemm_noalloc", "gg_copy_rects",
 )
 GG_NOALLOC_MAX_PROBLEMS = 1024
 
@@ -60,6 +60,11 @@ class GGShardPiece(ctypes.Structure):
                 ("col0", ctypes.c_int), ("cols", ctypes.c_int)]
 
 
+class GGRectCopy(ctypes.Structure):
+    _fields_ = [("strided", ctypes.c_void_p), ("packed", ctypes.c_longlong), ("rows", ctypes.c_int),
+                ("cols", ctypes.c_int), ("ld", ctypes.c_int), ("reserved", ctypes.c_int)]
+
+
 _lib: Optional[ctypes.CDLL] = None
 
 
@@ -95,6 +100,7 @@ def load() -> ctypes.CDLL:
                           P(ctypes.c_double)], ctypes.c_int),
         "gg_selftest_wait_timeout": ([ctypes.c_ulonglong, i32p], ctypes.c_int),
         "gg_run_grouped_gemm_noalloc": ([pp, ctypes.c_int, ctypes.c_int, pc, vp], ctypes.c_int),
+        "gg_copy_rects": ([vp, vp, ctypes.c_int, ctypes.c_int, vp], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

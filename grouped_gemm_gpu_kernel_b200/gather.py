@@ -6,13 +6,57 @@ When the caller wants every D on one rank afterwards, `gather_pieces` moves each
 rectangles there: a non-root rank packs all its rectangles into one contiguous FP32 buffer and
 sends it with one point-to-point send (NCCL over NVLink/NVSwitch for CUDA tensors, gloo for CPU
 tensors); the root posts one matching receive per rank, all in flight together, and unpacks the
-rectangles into its full D matrices. The reference is single-GPU and has no counterpart.
+rectangles into its full D matrices. Packing and unpacking of CUDA tensors are one gg_copy_rects
+launch each. The reference is single-GPU and has no counterpart.
 """
 from __future__ import annotations
 
 from typing import Dict, List, Sequence
 
-__all__ = ["gather_pieces", "piece_elems"]
+__all__ = ["gather_pieces", "piece_elems", "copy_rects"]
+
+
+def copy_rects(packed, views, to_packed: bool) -> None:
+    """Moves 2-D FP32 tensors `views` (row pitch any, columns contiguous) to or from the 1-D
+    tensor `packed`, each view's rows x cols elements back to back in order. CUDA tensors take
+    one gg_copy_rects launch on the current stream; CPU tensors are copied view by view."""
+    import ctypes
+
+    import torch
+
+    if packed.device.type != "cuda":
+        off = 0
+        for v in views:
+            cnt = v.numel()
+            if cnt:
+                dst = packed[off:off + cnt].view(v.shape)
+                if to_packed:
+                    dst.copy_(v)
+                else:
+                    v.copy_(dst)
+            off += cnt
+        return
+    from . import capi
+
+    recs, off = [], 0
+    for v in views:
+        rows, cols = v.shape
+        if rows and cols:
+            if v.stride(1) != 1 and cols > 1:
+                raise ValueError("columns must be contiguous")
+            recs.append((v.data_ptr(), off, rows, cols, max(v.stride(0), cols) if rows > 1 else cols, 0))
+        off += rows * cols
+    if not recs:
+        return
+    arr = (capi.GGRectCopy * len(recs))(*[capi.GGRectCopy(*r) for r in recs])
+    host = torch.frombuffer(bytearray(ctypes.string_at(ctypes.addressof(arr), ctypes.sizeof(arr))), dtype=torch.uint8)
+    dev_recs = host.to(packed.device, non_blocking=False)
+    st = capi.load().gg_copy_rects(packed.data_ptr(), dev_recs.data_ptr(), len(recs), 1 if to_packed else 0,
+                                   torch.cuda.current_stream(packed.device).cuda_stream)
+    if st != 0:
+        raise RuntimeError(f"gg_copy_rects failed with status {st}")
+    # dev_recs was allocated on the stream the copy runs on, so the caching allocator reuses its
+    # memory only for work ordered after the copy.
 
 
 def piece_elems(pieces) -> int:
@@ -43,21 +87,16 @@ def gather_pieces(pieces_by_rank: Sequence[Sequence], local_d: Sequence, root_d:
         if tuple(t.shape) != (pc.rows, pc.cols) or t.dtype != torch.float32:
             raise ValueError("each local D must be a rows x cols FP32 tensor")
 
-    def unpack(buf, pieces):
-        off = 0
-        for pc in pieces:
-            cnt = pc.rows * pc.cols
-            if cnt:
-                view = buf[off:off + cnt].view(pc.rows, pc.cols)
-                root_d[pc.problem][pc.row0:pc.row0 + pc.rows, pc.col0:pc.col0 + pc.cols].copy_(view)
-            off += cnt
+    def root_views(pieces):
+        return [root_d[pc.problem][pc.row0:pc.row0 + pc.rows, pc.col0:pc.col0 + pc.cols] for pc in pieces]
 
     if rank == root:
         if root_d is None:
             raise ValueError("the root needs its full D tensors")
-        for t, pc in zip(local_d, mine):
-            root_d[pc.problem][pc.row0:pc.row0 + pc.rows, pc.col0:pc.col0 + pc.cols].copy_(t)
         device = next(iter(root_d.values())).device if root_d else torch.device("cpu")
+        own = torch.empty(piece_elems(mine), dtype=torch.float32, device=device)
+        copy_rects(own, list(local_d), to_packed=True)
+        copy_rects(own, root_views(mine), to_packed=False)
         bufs: List = []
         ops = []
         for r in range(world):
@@ -74,19 +113,14 @@ def gather_pieces(pieces_by_rank: Sequence[Sequence], local_d: Sequence, root_d:
         received = 0
         for r in range(world):
             if r != root and bufs[r] is not None and bufs[r].numel():
-                unpack(bufs[r], pieces_by_rank[r])
+                copy_rects(bufs[r], root_views(pieces_by_rank[r]), to_packed=False)
                 received += bufs[r].numel() * 4
         return received
     n = piece_elems(mine)
     if n:
         device = local_d[0].device
         buf = torch.empty(n, dtype=torch.float32, device=device)
-        off = 0
-        for t, pc in zip(local_d, mine):
-            cnt = pc.rows * pc.cols
-            if cnt:
-                buf[off:off + cnt].view(pc.rows, pc.cols).copy_(t)
-            off += cnt
+        copy_rects(buf, list(local_d), to_packed=True)
         for w in dist.batch_isend_irecv([dist.P2POp(dist.isend, buf, root, group)]):
             w.wait()
     return 0

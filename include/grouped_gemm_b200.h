@@ -207,6 +207,25 @@ int gg_selftest_wait_timeout(unsigned long long timeout_ns, int* status);
 int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count, int sort_mode,
                                 const gg_config* config, void* stream);
 
+/* No counterpart in the reference (which is single-GPU). One FP32 rectangle of a strided
+ * row-major matrix and its place in a packed buffer, for gg_copy_rects. */
+typedef struct gg_rect_copy {
+  float* strided;      /* first element of the rectangle in its matrix (device memory) */
+  long long packed;    /* element offset of the rectangle in the packed buffer */
+  int rows;            /* rectangle rows */
+  int cols;            /* rectangle columns */
+  int ld;              /* row pitch of the strided matrix, elements (>= cols) */
+  int reserved;
+} gg_rect_copy;
+
+/* No reference counterpart. Copies `count` FP32 rectangles between strided matrices and one packed
+ * buffer in a single kernel launch on `stream`: to_packed != 0 packs (strided -> packed, row-major,
+ * each rectangle at its `packed` offset), to_packed == 0 unpacks (packed -> strided). `rects` is an
+ * array of gg_rect_copy in DEVICE memory. Used by the optional multi-GPU gather of D (pack before
+ * the send, unpack after the receive). count == 0 launches nothing; count < 0, a null packed or
+ * rects pointer with count > 0 return cudaErrorInvalidValue. */
+int gg_copy_rects(float* packed, const gg_rect_copy* rects, int count, int to_packed, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -225,3 +225,11 @@ def test_cpp_dropin_header_compiles_and_links(tmp_path):
                    capture_output=True)
     out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout
     assert out.split() == ["sort_by_k", str(1 + 0 + 6), "2", "4"]
+
+
+def test_copy_rects_argument_checks_without_a_launch():
+    """gg_copy_rects rejects bad arguments before touching the GPU; count 0 is a no-op."""
+    lib = capi.load()
+    assert lib.gg_copy_rects(None, None, 0, 1, None) == 0
+    assert lib.gg_copy_rects(None, None, -1, 1, None) == 1
+    assert lib.gg_copy_rects(None, None, 3, 0, None) == 1
