@@ -269,6 +269,58 @@ def partition(problems: Sequence[ProblemDesc], config: KernelConfig, world_size:
     return [ShardPiece(o.problem, o.row0, o.rows, o.col0, o.cols) for o in out[:n.value]], w.value
 
 
+class MoePlan:
+    """Grouped GEMM whose per-problem row counts live on the device (gg_moe_plan_*).
+
+    Problems share n and k; their rows are packed back to back in A (capacity_rows x k FP16),
+    C and D (capacity_rows x n FP32); expert e multiplies its rows by its own B[e] (k x n FP16).
+    `run(rows)` takes an int32 device tensor of `experts` row counts and enqueues the device-side
+    preparation and the grouped kernel on the stream, with no host synchronisation.
+    """
+
+    def __init__(self, experts: int, n: int, k: int, capacity_rows: int, a: int, lda: int, b_ptrs: Sequence[int],
+                 ldb: int, d: int, ldd: int, c: Optional[int] = None, ldc: Optional[int] = None,
+                 alpha: float = 1.0, beta: float = 0.0, config: Optional[KernelConfig] = None):
+        self._lib = capi.load()
+        self._h = None
+        if len(b_ptrs) != experts:
+            raise ValueError("one B pointer per expert")
+        bs = (ctypes.c_void_p * max(1, experts))(*[ctypes.c_void_p(int(x) if x else None) for x in b_ptrs])
+        prob = capi.GGMoeProblem(a, ctypes.cast(bs, ctypes.POINTER(ctypes.c_void_p)), c, d, experts, n, k,
+                                 capacity_rows, lda, ldb, ldc if ldc is not None else max(1, n), ldd, alpha, beta)
+        cfg = (config or KernelConfig(128, 256, 64)).to_c()
+        h = ctypes.c_void_p()
+        st = self._lib.gg_moe_plan_create(ctypes.byref(prob), ctypes.byref(cfg), ctypes.byref(h))
+        if st != 0:
+            raise ValueError(f"gg_moe_plan_create failed with status {st}")
+        self._h = h
+        self.experts = experts
+
+    def run(self, rows, stream=None) -> int:
+        """rows: int32 device tensor (or device pointer) of `experts` row counts."""
+        ptr = rows if isinstance(rows, int) else rows.data_ptr()
+        return self._lib.gg_moe_plan_run(self._h, ctypes.c_void_p(ptr), _stream_ptr(stream))
+
+    def status(self):
+        """Synchronises; returns (GG_STATUS_* bits, then cleared; tile count of the last run)."""
+        st_bits, total = ctypes.c_int(0), ctypes.c_int(0)
+        st = self._lib.gg_moe_plan_status(self._h, ctypes.byref(st_bits), ctypes.byref(total))
+        if st != 0:
+            raise RuntimeError(f"gg_moe_plan_status failed with status {st}")
+        return st_bits.value, total.value
+
+    def close(self):
+        if self._h:
+            self._lib.gg_moe_plan_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def selftest_wait_timeout(timeout_ns: int = 20_000_000):
     """(status, device bits) of the bounded-wait self-test (see gg_selftest_wait_timeout)."""
     out = ctypes.c_int(0)

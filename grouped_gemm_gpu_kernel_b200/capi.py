@@ -19,7 +19,9 @@ EXPORTED_SYMBOLS = (
     "gg_executor_problem_count", "gg_executor_total_tiles", "gg_executor_grid_ctas", "gg_executor_status",
     "gg_run_grouped_gemm_once", "gg_run_baseline_per_problem", "gg_count_non_empty_problems",
     "gg_partition", "gg_selftest_wait_timeout", "gg_run_grouped_gemm_noalloc", "gg_copy_rects",
+    "gg_moe_plan_create", "gg_moe_plan_run", "gg_moe_plan_status", "gg_moe_plan_destroy",
 )
+GG_STATUS_BAD_ROWS = 0x100
 GG_NOALLOC_MAX_PROBLEMS = 1024
 
 GG_STATUS_TIMEOUT_PRODUCER = 0x1
@@ -65,6 +67,13 @@ class GGRectCopy(ctypes.Structure):
                 ("cols", ctypes.c_int), ("ld", ctypes.c_int), ("reserved", ctypes.c_int)]
 
 
+class GGMoeProblem(ctypes.Structure):
+    _fields_ = [("a", ctypes.c_void_p), ("b", ctypes.POINTER(ctypes.c_void_p)), ("c", ctypes.c_void_p),
+                ("d", ctypes.c_void_p), ("experts", ctypes.c_int), ("n", ctypes.c_int), ("k", ctypes.c_int),
+                ("capacity_rows", ctypes.c_int), ("lda", ctypes.c_int), ("ldb", ctypes.c_int), ("ldc", ctypes.c_int),
+                ("ldd", ctypes.c_int), ("alpha", ctypes.c_float), ("beta", ctypes.c_float)]
+
+
 _lib: Optional[ctypes.CDLL] = None
 
 
@@ -101,6 +110,10 @@ def load() -> ctypes.CDLL:
         "gg_selftest_wait_timeout": ([ctypes.c_ulonglong, i32p], ctypes.c_int),
         "gg_run_grouped_gemm_noalloc": ([pp, ctypes.c_int, ctypes.c_int, pc, vp], ctypes.c_int),
         "gg_copy_rects": ([vp, vp, ctypes.c_int, ctypes.c_int, vp], ctypes.c_int),
+        "gg_moe_plan_create": ([P(GGMoeProblem), pc, P(vp)], ctypes.c_int),
+        "gg_moe_plan_run": ([vp, vp, vp], ctypes.c_int),
+        "gg_moe_plan_status": ([vp, i32p, i32p], ctypes.c_int),
+        "gg_moe_plan_destroy": ([vp], None),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

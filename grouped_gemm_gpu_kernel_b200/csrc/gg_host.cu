@@ -600,7 +600,7 @@ int gg_selftest_wait_timeout(unsigned long long timeout_ns, int* status) {
 // must not grow its memory footprint after start-up. Everything the persistent kernel needs
 // besides the caller's A/B/C/D -- the problem table, the TMA descriptors, the tile offsets, the
 // tile counter and the status word -- lives in one fixed file-scope device array, sized for at
-// most GG_NOALLOC_MAX_PROBLEMS problems (608 KiB, held by every GPU that loads this library until
+// most GG_NOALLOC_MAX_PROBLEMS problems (616 KiB, held by every GPU that loads this library until
 // the process exits). Host-side preparation uses fixed static buffers as well.
 namespace gg {
 namespace {
@@ -613,7 +613,7 @@ constexpr size_t kNoAllocOffsOff =
 constexpr size_t kNoAllocCounterOff =
     (kNoAllocOffsOff + static_cast<size_t>(kNoAllocMaxProblems + 1) * sizeof(int) + 127) / 128 * 128;
 constexpr size_t kNoAllocBytes = (kNoAllocCounterOff + 128 + 4095) / 4096 * 4096;
-static_assert(kNoAllocBytes == 608 * 1024, "the documented size of the no-allocation scratch");
+static_assert(kNoAllocBytes == 616 * 1024, "the documented size of the no-allocation scratch");
 
 // The scratch itself. Host code must never pass this name to a kernel: on the host it only
 // names a stand-in, not device memory. Its device address comes from cudaGetSymbolAddress.
@@ -737,3 +737,265 @@ extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count
   kp.single_mode = 0;
   return gg::launch_grouped_kernel(v, kp, grid, s);
 }
+
+// ---- grouped GEMM with device-side preparation (mixture-of-experts routing) ---------------------
+// The problems share N and K and their rows are packed back to back in A, C and D; only the row
+// counts change from run to run, and they live on the device. Everything that does not depend on
+// them is built once on the host: one tensor map of the packed A and one of the packed D (each
+// spanning all capacity_rows rows; a problem addresses them from its first row, tma_row0), the B
+// maps of every expert, and a template problem record per expert. A run is a one-block
+// preparation kernel (prefix sums of rows and tiles, problem records, tile offsets, tile count,
+// counter reset) followed by the persistent kernel, which reads the tile count from the device.
+namespace gg {
+namespace {
+
+constexpr int kMoePrepThreads = 1024;
+
+// Exclusive prefix sum of v over the block (kMoePrepThreads threads); *total gets the sum.
+template <typename T>
+__device__ T block_exclusive_scan(T v, T* warp_sums, T* total) {
+  const int lane = static_cast<int>(threadIdx.x & 31), warp = static_cast<int>(threadIdx.x >> 5);
+  T x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const T y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    T w = lane < kMoePrepThreads / 32 ? warp_sums[lane] : T(0);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const T y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < kMoePrepThreads / 32) warp_sums[lane] = w;  // inclusive sums of the warps
+  }
+  __syncthreads();
+  const T before = warp > 0 ? warp_sums[warp - 1] : T(0);
+  *total = warp_sums[kMoePrepThreads / 32 - 1];
+  __syncthreads();  // warp_sums is reused by the next call
+  return before + x - v;
+}
+
+__global__ void __launch_bounds__(kMoePrepThreads) moe_prepare_kernel(
+    const int* __restrict__ rows, int experts, int capacity, int bm, int tiles_n,
+    const DeviceProblemDesc* __restrict__ templ, DeviceProblemDesc* __restrict__ descs, int* __restrict__ offsets,
+    int* total_tiles, int* counter, int* status, const __half* a, int lda, const float* c, int ldc, float* d,
+    int ldd) {
+  __shared__ long long s_rows[kMoePrepThreads / 32];
+  __shared__ int s_tiles[kMoePrepThreads / 32];
+  long long row_carry = 0;
+  int tile_carry = 0;
+  int bad = 0;
+  for (int base = 0; base < experts; base += kMoePrepThreads) {
+    const int e = base + static_cast<int>(threadIdx.x);
+    int r = e < experts ? rows[e] : 0;
+    if (r < 0) {
+      bad = 1;
+      r = 0;
+    }
+    const int tm = r > 0 ? (r + bm - 1) / bm : 0;
+    const int t = tiles_n > 0 ? tm * tiles_n : 0;
+    long long rows_total;
+    int tiles_total;
+    const long long row0 = row_carry + block_exclusive_scan<long long>(r, s_rows, &rows_total);
+    const int t0 = tile_carry + block_exclusive_scan<int>(t, s_tiles, &tiles_total);
+    if (e < experts) {
+      DeviceProblemDesc p = templ[e];
+      p.m = r;
+      p.a = a + row0 * lda;
+      p.c = c ? c + row0 * ldc : nullptr;
+      p.d = d + row0 * ldd;
+      p.tiles_m = t > 0 ? tm : 0;
+      p.tiles_n = t > 0 ? tiles_n : 0;
+      p.tma_row0 = static_cast<int>(row0 < capacity ? row0 : capacity);
+      descs[e] = p;
+      offsets[e] = t0;
+    }
+    row_carry += rows_total;
+    tile_carry += tiles_total;
+  }
+  bad = __syncthreads_or(bad);
+  if (threadIdx.x == 0) {
+    offsets[experts] = tile_carry;
+    const bool ok = !bad && row_carry <= static_cast<long long>(capacity);
+    *total_tiles = ok ? tile_carry : 0;
+    *counter = 0;
+    if (!ok) atomicOr(status, GG_STATUS_BAD_ROWS);
+  }
+}
+
+}  // namespace
+}  // namespace gg
+
+struct gg_moe_plan {
+  void* block = nullptr;  // maps | template records | records | offsets | total, counter, status
+  const DeviceProblemDesc* d_templ = nullptr;
+  DeviceProblemDesc* d_descs = nullptr;
+  int* d_offsets = nullptr;
+  int* d_total = nullptr;
+  int* d_counter = nullptr;
+  int* d_status = nullptr;
+  gg_moe_problem problem{};
+  gg::Variant variant = gg::Variant::kUnsupported;
+  int grid_ctas = 0;
+  int tiles_n = 0;
+  gg::KernelParams params{};
+};
+
+extern "C" {
+
+int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, gg_moe_plan** out) {
+  if (!out) return cudaErrorInvalidValue;
+  *out = nullptr;
+  const gg::Variant v = gg::variant_of(config);
+  if (!problem || v == gg::Variant::kUnsupported) return cudaErrorInvalidValue;
+  const gg_moe_problem& q = *problem;
+  if (q.experts < 1 || q.n < 0 || q.k < 0 || q.capacity_rows < 0 || !q.a || !q.b || !q.d) return cudaErrorInvalidValue;
+  if (q.lda < std::max(1, q.k) || q.ldb < std::max(1, q.n) || q.ldd < std::max(1, q.n) ||
+      (q.c && q.ldc < std::max(1, q.n)))
+    return cudaErrorInvalidValue;
+  for (int e = 0; e < q.experts; ++e)
+    if (!q.b[e]) return cudaErrorInvalidValue;
+
+  const int bn = gg::variant_bn(v);
+  const int cta_rows = gg::variant_cta_rows(v), cta_cols = gg::variant_cta_cols(v);
+  const size_t E = static_cast<size_t>(q.experts);
+  std::vector<CUtensorMap> maps(E * gg::kMapsPerProblem);
+  std::vector<DeviceProblemDesc> templ(E);
+  std::memset(maps.data(), 0, maps.size() * sizeof(CUtensorMap));
+  CUtensorMap map_a{}, map_d{};
+  const bool rows_exist = q.capacity_rows > 0 && q.n > 0;
+  const bool tma_a = rows_exist && q.k > 0 &&
+                     gg::encode_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, q.a, q.k, q.capacity_rows,
+                                   static_cast<int64_t>(q.lda) * 2, gg::kBK, cta_rows);
+  const bool tma_d = rows_exist && gg::encode_2d(&map_d, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, q.d, q.n, q.capacity_rows,
+                                                 static_cast<int64_t>(q.ldd) * 4, 32, 32);
+  for (size_t e = 0; e < E; ++e) {
+    CUtensorMap* m = &maps[e * gg::kMapsPerProblem];
+    DeviceProblemDesc& p = templ[e];
+    p.m = 0;
+    p.n = q.n;
+    p.k = q.k;
+    p.a = static_cast<const __half*>(q.a);
+    p.b = static_cast<const __half*>(q.b[e]);
+    p.c = q.c;
+    p.d = q.d;
+    p.lda = q.lda;
+    p.ldb = q.ldb;
+    p.ldc = q.ldc;
+    p.ldd = q.ldd;
+    p.alpha = q.alpha;
+    p.beta = q.beta;
+    p.k_blocks = q.k > 0 ? gg::ceil_div(q.k, gg::kBK) : 0;
+    unsigned flags = grouped_gemm::kFlagPackedRows;
+    if (tma_a && gg::encode_2d(&m[gg::kMapB], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, q.b[e], q.n, q.k,
+                               static_cast<int64_t>(q.ldb) * 2, 64, gg::kBK)) {
+      m[gg::kMapA] = map_a;
+      flags |= grouped_gemm::kFlagTmaAB;
+      if (gg::encode_b_chunks(&m[gg::kMapB3], q.b[e], q.k, q.n, static_cast<int64_t>(q.ldb) * 2, cta_cols / 64))
+        flags |= grouped_gemm::kFlagTmaB3;
+    }
+    if (tma_d) {
+      m[gg::kMapD] = map_d;
+      flags |= grouped_gemm::kFlagTmaD;
+    }
+    if (q.c != nullptr && q.beta != 0.0f) flags |= grouped_gemm::kFlagReadC;
+    if (gg::aligned16(q.c) && (q.ldc % 4) == 0) flags |= grouped_gemm::kFlagCVec;
+    if (gg::aligned16(q.d) && (q.ldd % 4) == 0) flags |= grouped_gemm::kFlagDVec;
+    p.flags = flags;
+  }
+
+  int grid = 0;
+  cudaError_t st = gg::persistent_grid(v, 1 << 30, config->persistent_ctas, &grid);
+  if (st != cudaSuccess) return st;
+
+  const size_t maps_bytes = maps.size() * sizeof(CUtensorMap);
+  const size_t templ_off = gg::round_up(maps_bytes, 128);
+  const size_t descs_off = gg::round_up(templ_off + E * sizeof(DeviceProblemDesc), 128);
+  const size_t offs_off = gg::round_up(descs_off + E * sizeof(DeviceProblemDesc), 128);
+  const size_t words_off = gg::round_up(offs_off + (E + 1) * sizeof(int), 128);
+  const size_t bytes = words_off + 128;
+  std::vector<unsigned char> image(bytes, 0);
+  std::memcpy(image.data(), maps.data(), maps_bytes);
+  std::memcpy(image.data() + templ_off, templ.data(), E * sizeof(DeviceProblemDesc));
+
+  gg_moe_plan* plan = new (std::nothrow) gg_moe_plan();
+  if (!plan) return cudaErrorMemoryAllocation;
+  st = cudaMalloc(&plan->block, bytes);
+  if (st != cudaSuccess) {
+    delete plan;
+    return st;
+  }
+  st = cudaMemcpy(plan->block, image.data(), bytes, cudaMemcpyHostToDevice);
+  if (st != cudaSuccess) {
+    cudaFree(plan->block);
+    delete plan;
+    return st;
+  }
+  unsigned char* base = static_cast<unsigned char*>(plan->block);
+  plan->d_templ = reinterpret_cast<const DeviceProblemDesc*>(base + templ_off);
+  plan->d_descs = reinterpret_cast<DeviceProblemDesc*>(base + descs_off);
+  plan->d_offsets = reinterpret_cast<int*>(base + offs_off);
+  plan->d_total = reinterpret_cast<int*>(base + words_off);
+  plan->d_counter = reinterpret_cast<int*>(base + words_off + 4);
+  plan->d_status = reinterpret_cast<int*>(base + words_off + 8);
+  plan->problem = q;
+  plan->problem.b = nullptr;  // the host array is not kept
+  plan->variant = v;
+  plan->grid_ctas = grid;
+  plan->tiles_n = q.n > 0 ? gg::ceil_div(q.n, bn) : 0;
+
+  gg::KernelParams& kp = plan->params;
+  std::memset(&kp, 0, sizeof(kp));
+  kp.problems = plan->d_descs;
+  kp.tmaps = reinterpret_cast<const CUtensorMap*>(base);
+  kp.tile_offsets = plan->d_offsets;
+  kp.tile_counter = plan->d_counter;
+  kp.total_tiles_dev = plan->d_total;
+  kp.status = plan->d_status;
+  kp.timeout_ns = gg::wait_timeout_ns();
+  kp.problem_count = q.experts;
+  kp.total_tiles = 0;
+  kp.raster_group = gg::raster_group();
+  kp.single_mode = 0;
+  *out = plan;
+  return cudaSuccess;
+}
+
+int gg_moe_plan_run(gg_moe_plan* plan, const int* rows, void* stream) {
+  if (!plan || !plan->block) return cudaErrorInvalidDevicePointer;
+  if (!rows) return cudaErrorInvalidValue;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const gg_moe_problem& q = plan->problem;
+  gg::moe_prepare_kernel<<<1, gg::kMoePrepThreads, 0, s>>>(
+      rows, q.experts, q.capacity_rows, gg::variant_bm(plan->variant), plan->tiles_n, plan->d_templ, plan->d_descs,
+      plan->d_offsets, plan->d_total, plan->d_counter, plan->d_status, static_cast<const __half*>(q.a), q.lda, q.c,
+      q.ldc, q.d, q.ldd);
+  cudaError_t st = cudaGetLastError();
+  if (st != cudaSuccess) return st;
+  return gg::launch_grouped_kernel(plan->variant, plan->params, plan->grid_ctas, s);
+}
+
+int gg_moe_plan_status(gg_moe_plan* plan, int* status, int* total_tiles) {
+  if (!plan || !plan->block) return cudaErrorInvalidDevicePointer;
+  if (!status) return cudaErrorInvalidValue;
+  cudaError_t st = cudaDeviceSynchronize();
+  if (st != cudaSuccess) return st;
+  int words[3] = {0, 0, 0};
+  st = cudaMemcpy(words, plan->d_total, sizeof(words), cudaMemcpyDeviceToHost);
+  if (st != cudaSuccess) return st;
+  *status = words[2];
+  if (total_tiles) *total_tiles = words[0];
+  return cudaMemset(plan->d_status, 0, sizeof(int));
+}
+
+void gg_moe_plan_destroy(gg_moe_plan* plan) {
+  if (!plan) return;
+  if (plan->block) cudaFree(plan->block);
+  delete plan;
+}
+
+}  // extern "C"

@@ -106,6 +106,7 @@ __device__ __forceinline__ void raster_tile(int local, int tiles_m, int tiles_n,
 // problem's descriptor with that problem's tile range, so tiles claimed from the same problem skip
 // the search and the descriptor load.
 struct SchedState {
+  int total;        // tiles of the launch
   int cur;          // lane 0: claimed tile not yet handed out
   int static_next;  // lane 0: next tile of the static order (baseline launches)
   int q;            // problem of the cached descriptor, -1 when none
@@ -125,6 +126,7 @@ __device__ __forceinline__ int claim_tile(const KernelParams& p, SchedState& ss,
 
 __device__ __forceinline__ void sched_init(const KernelParams& p, SchedState& ss, int first_static, int stride,
                                            int lane) {
+  ss.total = p.total_tiles_dev ? *p.total_tiles_dev : p.total_tiles;
   ss.static_next = first_static;
   ss.q = -1;
   ss.q_first = 0;
@@ -140,13 +142,13 @@ __device__ __forceinline__ bool next_tile(const KernelParams& p, SchedState& ss,
                                           int lane, int stride, int& q_out, int& tile_m, int& tile_n) {
   for (;;) {
     const int tile = __shfl_sync(0xffffffffu, ss.cur, 0);
-    if (tile >= p.total_tiles) return false;
+    if (tile >= ss.total) return false;
     if (lane == 0) ss.cur = claim_tile(p, ss, stride);  // in flight while this tile is placed
     if (!(ss.q >= 0 && tile >= ss.q_first && tile < ss.q_end)) {
       const int q = p.single_mode ? 0 : find_problem_warp(p.tile_offsets, p.problem_count, tile, lane);
       ss.q = q;
-      ss.q_first = p.single_mode ? 0 : __ldg(p.tile_offsets + q);
-      ss.q_end = p.single_mode ? p.total_tiles : __ldg(p.tile_offsets + q + 1);
+      ss.q_first = p.single_mode ? 0 : p.tile_offsets[q];
+      ss.q_end = p.single_mode ? ss.total : p.tile_offsets[q + 1];
       const int* src = reinterpret_cast<const int*>(problems + q);
       ss.w = lane < kDescWords ? src[lane] : 0;
     }
@@ -187,12 +189,14 @@ __device__ __forceinline__ void epilogue_warp(uint8_t* stage, uint32_t& store_co
                                               int row0, int m, int n, int col0, int c_begin, int c_end,
                                               int kb_count, unsigned flags, float alpha, float beta,
                                               const float* cptr, int ldc, float* dptr, int ldd,
-                                              const CUtensorMap* md, Release release) {
+                                              const CUtensorMap* md, int tma_row0, Release release) {
   constexpr int kStageTiles = kEpiWarpBytes / 4096;  // staging tiles of this warp
   static_assert(kStageTiles == 1 || kStageTiles == 2, "staging tiles per epilogue warp");
   const bool warp_rows = row0 < m;  // warp-uniform
   const bool read_c = (flags & grouped_gemm::kFlagReadC) != 0u;
-  const bool tma_d = (flags & grouped_gemm::kFlagTmaD) != 0u;
+  // With packed rows the D map spans every problem, so only a whole 32-row box may go out by TMA.
+  const bool tma_d = (flags & grouped_gemm::kFlagTmaD) != 0u &&
+                     ((flags & grouped_gemm::kFlagPackedRows) == 0u || row0 + 32 <= m);
   const int row = row0 + lane;
   if (tma_d) {
     // Two chunks per TMEM read (one 64-column tcgen05.ld and one wait), then one staging tile
@@ -264,7 +268,7 @@ __device__ __forceinline__ void epilogue_warp(uint8_t* stage, uint32_t& store_co
         ptx::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          ptx::tma_store_2d(md, ptx::smem_addr(stile), cc, row0);  // rows past M are clipped
+          ptx::tma_store_2d(md, ptx::smem_addr(stile), cc, tma_row0 + row0);  // rows past M are clipped
           ptx::bulk_commit_group();
         }
         ++store_count;
@@ -578,6 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
       const __half* a = s->desc.a;
       const __half* b = s->desc.b;
       const int lda = s->desc.lda, ldb = s->desc.ldb;
+      const int a_row = s->desc.tma_row0 + tile_m * BM;  // first A row of the tile in the A map
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(ringe_bar(slot));
       if (q < 0) break;
@@ -600,7 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
             const uint32_t a_dst = sbase + static_cast<uint32_t>(st * L::kStageBytes);
             const uint32_t b_dst = a_dst + L::kABytes;
             ptx::mbar_arrive_expect_tx(full_bar(st), L::kATxBytes + L::kBTxBytes);
-            ptx::tma_load_2d(a_dst, ma, full_bar(st), kb * kBK, tile_m * BM);
+            ptx::tma_load_2d(a_dst, ma, full_bar(st), kb * kBK, a_row);
             if (b_one_box) {
               ptx::tma_load_3d(b_dst, mb3, full_bar(st), 0, kb * kBK, tile_n * (BN / 64));
             } else {
@@ -727,6 +732,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
       const float* cptr = s->desc.c;
       float* dptr = s->desc.d;
       const int ldc = s->desc.ldc, ldd = s->desc.ldd;
+      const int tma_row0 = s->desc.tma_row0;
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(ringe_bar(slot));
       if (q < 0) break;
@@ -746,7 +752,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
       const int row0 = qw * 32 < BM ? tile_m * BM + qw * 32 : m;
       epilogue_warp(smem + L::kEpiOffset + warp * kEpiWarpBytes, store_count, t_addr, lane, row0, m, n, tile_n * BN,
                     c_begin, c_end, kb_count, flags, alpha, beta, cptr, ldc, dptr, ldd,
-                    maps + kMapsPerProblem * q + kMapD, [&] { ptx::mbar_arrive(acce_bar(buf)); });
+                    maps + kMapsPerProblem * q + kMapD, tma_row0, [&] { ptx::mbar_arrive(acce_bar(buf)); });
     }
     if (lane == 0) ptx::bulk_wait_all();  // every warp issues its own TMA stores
     __syncwarp();

@@ -220,6 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) release_slot(slot);
       if (q < 0) break;
       const int row_base = tile_m * BM + static_cast<int>(rank) * 128;  // this CTA's rows of A
+      const int a_row = s->desc.tma_row0 + row_base;                     // the same row in the A map
       const int col_base = tile_n * BN + static_cast<int>(rank) * HB;   // this CTA's columns of B
 
       if (flags & grouped_gemm::kFlagTmaAB) {
@@ -239,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t b_dst = a_dst + L::kABytes;
             const uint32_t bar_leader = ptx::mapa_shared(full_bar(st), 0);
             if (leader) ptx::mbar_arrive_expect_tx(full_bar(st), L::kStageTxPair);
-            ptx::tma_load_2d_pair(a_dst, ma, bar_leader, kb * kBK, row_base);
+            ptx::tma_load_2d_pair(a_dst, ma, bar_leader, kb * kBK, a_row);
             if (b_one_box) {
               ptx::tma_load_3d_pair(b_dst, mb3, bar_leader, 0, kb * kBK, col_base / 64);
             } else {
@@ -370,6 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* cptr = s->desc.c;
       float* dptr = s->desc.d;
       const int ldc = s->desc.ldc, ldd = s->desc.ldd;
+      const int tma_row0 = s->desc.tma_row0;
       __syncwarp();
       if (lane == 0) release_slot(slot);
       if (q < 0) break;
@@ -388,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row0 = tile_m * BM + static_cast<int>(rank) * 128 + qw * 32;  // this warp's first row
       epilogue_warp(smem + L::kEpiOffset + warp * kEpiWarpBytes, store_count, t_addr, lane, row0, m, n,
                     tile_n * BN, c_begin, c_end, kb_count, flags, alpha, beta, cptr, ldc, dptr, ldd,
-                    maps + kMapsPerProblem * q + kMapD, [&] {
+                    maps + kMapsPerProblem * q + kMapD, tma_row0, [&] {
                       if (leader) ptx::mbar_arrive(acce_bar(buf));
                       else ptx::mbar_arrive_cluster(ptx::mapa_shared(acce_bar(buf), 0));
                     });

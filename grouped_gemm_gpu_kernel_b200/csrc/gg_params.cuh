@@ -88,6 +88,8 @@ struct KernelParams {
   const CUtensorMap* tmaps;           // grouped launch: kMapsPerProblem maps per problem (64-byte aligned)
   const int* tile_offsets;            // grouped launch: problem_count + 1 prefix sums
   int* tile_counter;                  // grouped launch: claim counter, zero at launch
+  const int* total_tiles_dev;         // when set: the tile count, written on the device by an
+                                      // earlier launch (device-side preparation); else total_tiles
   int* status;                        // GG_STATUS_* bits
   unsigned long long timeout_ns;      // limit of every wait
   int problem_count;

@@ -2,8 +2,10 @@
 //
 // It extends the reference's DeviceProblemDesc (reference src/grouped_gemm.cu:25-45, internal
 // there) -- the ProblemDesc fields followed by tiles_m / tiles_n -- with the k-block count of
-// the kernel's K tiling and the problem's data-path flags, so the kernel never recomputes them
-// per tile. 88 bytes, a multiple of 4 so a warp can copy it word by word.
+// the kernel's K tiling, the problem's data-path flags and, for problem sets whose rows are
+// packed in one tensor (experts of a mixture-of-experts layer), the problem's first row in that
+// tensor, so the kernel never recomputes them per tile. 96 bytes, a multiple of 4 so a warp can
+// copy it word by word.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -17,6 +19,9 @@ enum DeviceProblemFlags : unsigned {
   kFlagCVec = 8u,    // C rows can be read as 16-byte vectors
   kFlagDVec = 16u,   // D rows can be written as 16-byte vectors (direct-store path)
   kFlagTmaB3 = 32u,  // B also has a 3-D map that loads a whole stage of full 64-column chunks at once
+  kFlagPackedRows = 64u,  // the A and D maps span the packed rows of every problem: TMA row
+                          // coordinates add tma_row0, and D goes out by TMA only in whole
+                          // 32-row boxes (a partial box would reach the next problem's rows)
 };
 
 struct DeviceProblemDesc {
@@ -41,9 +46,11 @@ struct DeviceProblemDesc {
   int tiles_n;   // ceil(n / cta_n), 0 when m <= 0 or n <= 0
   int k_blocks;  // ceil(k / 64): 64-deep K blocks of the tcgen05 mainloop
   unsigned flags;  // DeviceProblemFlags
+  int tma_row0;    // first row of this problem in the packed A/D maps (kFlagPackedRows), else 0
+  int reserved;
 };
 
-static_assert(sizeof(DeviceProblemDesc) == 88, "DeviceProblemDesc layout");
+static_assert(sizeof(DeviceProblemDesc) == 96, "DeviceProblemDesc layout");
 static_assert(sizeof(DeviceProblemDesc) % 4 == 0, "copied word by word");
 
 }  // namespace grouped_gemm

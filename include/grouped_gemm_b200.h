@@ -193,7 +193,7 @@ int gg_selftest_wait_timeout(unsigned long long timeout_ns, int* status);
  * synchronisation they imply are not acceptable, or processes that must not grow their device
  * footprint after start-up. It calls no cudaMalloc, cudaFree or other allocating routine, on
  * the device or the host: the problem table, TMA descriptors, tile offsets, tile counter and
- * status word live in one fixed device array of this library (608 KiB, held on every GPU that
+ * status word live in one fixed device array of this library (616 KiB, held on every GPU that
  * loads the library until the process exits). The caller still provides A, B, C and D.
  *   - At most GG_NOALLOC_MAX_PROBLEMS problems; more returns cudaErrorMemoryAllocation (2) and
  *     launches nothing. Other errors as for gg_run_grouped_gemm_once.
@@ -206,6 +206,51 @@ int gg_selftest_wait_timeout(unsigned long long timeout_ns, int* status);
 #define GG_NOALLOC_MAX_PROBLEMS 1024
 int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count, int sort_mode,
                                 const gg_config* config, void* stream);
+
+/* ---- grouped GEMM with device-side preparation (mixture-of-experts routing) ----------------
+ * No counterpart in the reference, whose problem set is prepared on the host. Here the number of
+ * rows of every problem lives in device memory -- as in a mixture-of-experts layer, where a
+ * router on the GPU decides how many tokens each expert gets -- and never travels to the host:
+ * the problems share N and K, their rows are packed back to back in A, C and D (expert 0's rows,
+ * then expert 1's, ...), and each has its own B. gg_moe_plan_create does the host work once per
+ * layer (tensor maps of the packed A and D and of every B, the device tables); gg_moe_plan_run
+ * launches a one-block preparation kernel that reads the row counts, prefix-sums rows and tiles,
+ * writes the problem records and tile offsets, and then the persistent grouped kernel, which reads
+ * the tile count from the device. No host synchronisation, no host copy per run, so a run can be
+ * captured in a CUDA graph and replayed with new row counts. */
+typedef struct gg_moe_problem {
+  const void* a;          /* FP16, capacity_rows x k, row pitch lda: the problems' rows packed */
+  const void* const* b;   /* host array of `experts` device pointers, each k x n FP16, row pitch ldb */
+  const float* c;         /* optional FP32, packed like A, row pitch ldc (read when beta != 0) */
+  float* d;               /* FP32, packed like A, row pitch ldd */
+  int experts;            /* problems, >= 1 */
+  int n;                  /* columns of every B and D, >= 0 */
+  int k;                  /* inner dimension, >= 0 */
+  int capacity_rows;      /* rows allocated in A, C and D; the row counts of a run must sum to at most this */
+  int lda;
+  int ldb;
+  int ldc;
+  int ldd;
+  float alpha;
+  float beta;
+} gg_moe_problem;
+
+typedef struct gg_moe_plan gg_moe_plan;
+
+/* Status bit set by gg_moe_plan_run's preparation when a row count is negative or their sum
+ * exceeds capacity_rows; that run computes nothing. */
+#define GG_STATUS_BAD_ROWS 0x100
+
+/* Builds the plan (allocates its device tables, encodes the tensor maps). Errors: invalid config,
+ * experts < 1, negative n/k/capacity, null a/b/d or a null B pointer -> cudaErrorInvalidValue
+ * (checked before any device work); CUDA errors passed through. */
+int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, gg_moe_plan** out);
+/* rows: `experts` ints in device memory. Enqueues preparation + grouped kernel on `stream`. */
+int gg_moe_plan_run(gg_moe_plan* plan, const int* rows, void* stream);
+/* Synchronises, returns (then clears) the GG_STATUS_* bits of the plan's runs, and the tile count
+ * of the last run in *total_tiles (nullable). */
+int gg_moe_plan_status(gg_moe_plan* plan, int* status, int* total_tiles);
+void gg_moe_plan_destroy(gg_moe_plan* plan);
 
 /* No counterpart in the reference (which is single-GPU). One FP32 rectangle of a strided
  * row-major matrix and its place in a packed buffer, for gg_copy_rects. */

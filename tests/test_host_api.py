@@ -233,3 +233,34 @@ def test_copy_rects_argument_checks_without_a_launch():
     assert lib.gg_copy_rects(None, None, 0, 1, None) == 0
     assert lib.gg_copy_rects(None, None, -1, 1, None) == 1
     assert lib.gg_copy_rects(None, None, 3, 0, None) == 1
+
+
+def test_moe_plan_create_rejects_bad_arguments_before_device_work():
+    """gg_moe_plan_create validates everything on the host first (no GPU needed for these)."""
+    import ctypes
+
+    lib = capi.load()
+    cfg = gg.KernelConfig(128, 256, 64).to_c()
+    b = (ctypes.c_void_p * 2)(ctypes.c_void_p(4096), ctypes.c_void_p(8192))
+    good = dict(a=4096, b=ctypes.cast(b, ctypes.POINTER(ctypes.c_void_p)), c=None, d=4096, experts=2, n=64, k=64,
+                capacity_rows=100, lda=64, ldb=64, ldc=64, ldd=64, alpha=1.0, beta=0.0)
+    h = ctypes.c_void_p()
+
+    def create(**kw):
+        args = dict(good)
+        args.update(kw)
+        prob = capi.GGMoeProblem(**args)
+        return lib.gg_moe_plan_create(ctypes.byref(prob), ctypes.byref(cfg), ctypes.byref(h))
+
+    assert lib.gg_moe_plan_create(None, ctypes.byref(cfg), ctypes.byref(h)) == 1
+    assert create(experts=0) == 1
+    assert create(a=None) == 1
+    assert create(d=None) == 1
+    assert create(lda=8) == 1
+    assert create(capacity_rows=-1) == 1
+    nullb = (ctypes.c_void_p * 2)(ctypes.c_void_p(4096), None)
+    assert create(b=ctypes.cast(nullb, ctypes.POINTER(ctypes.c_void_p))) == 1
+    bad_cfg = gg.KernelConfig(96, 96, 64).to_c()
+    prob = capi.GGMoeProblem(**good)
+    assert lib.gg_moe_plan_create(ctypes.byref(prob), ctypes.byref(bad_cfg), ctypes.byref(h)) == 1
+    assert lib.gg_moe_plan_run(None, None, None) == 17
