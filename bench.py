@@ -436,6 +436,8 @@ def main():
             ex2.close()
         extras["sort_modes"] = sweep
         extras["cuda_graph"] = graph_row(ex, stream, local_flops)
+        if args.workload == "moe":
+            extras["device_prep"] = moe_plan_row(ps, shapes, cfg, stream, local_flops, ms)
         extras["ref_gpu"] = reference_gpu_row(problems, stream, local_flops)
 
     cpu = None
@@ -517,6 +519,44 @@ def gather_row(args, cfg, ps, world, rank, dev, max_over_ranks, barrier):
             "received_on_root": got if rank == 0 else None, "root_piece_check": ok,
             "how": "after the timed region: one packed FP32 buffer per rank, NCCL send/recv to rank 0, "
                    "unpacked into the full D of every global problem"}
+
+
+def moe_plan_row(ps, shapes, cfg, stream, flops, executor_ms, runs=20):
+    """The same MoE problems through gg_moe_plan: row counts read from device memory, device-side
+    preparation kernel + grouped kernel per run (the workload's slabs are already row-packed)."""
+    import torch
+
+    import grouped_gemm_gpu_kernel_b200 as gg
+
+    rows = [m for m, n, k in shapes.dims]
+    n, k = shapes.dims[0][1], shapes.dims[0][2]
+    packed = all(ps.a_off[i + 1] == ps.a_off[i] + rows[i] * k and ps.d_off[i + 1] == ps.d_off[i] + rows[i] * n
+                 for i in range(len(rows) - 1))
+    if not packed or any(d[1] != n or d[2] != k for d in shapes.dims):
+        return {"unavailable": "problems do not share n, k or are not row-packed"}
+    b_ptrs = [ps.b.data_ptr() + 2 * off for off in ps.b_off]
+    plan = gg.MoePlan(len(rows), n, k, sum(rows), ps.a.data_ptr() + 2 * ps.a_off[0], k, b_ptrs, n,
+                      ps.d.data_ptr() + 4 * ps.d_off[0], n, None, n, 1.0, 0.0, cfg)
+    rows_t = torch.tensor(rows, dtype=torch.int32, device=ps.a.device)
+    ref = ps.d.clone()
+    torch.cuda.synchronize()
+    for _ in range(3):
+        plan.run(rows_t, stream)
+    torch.cuda.synchronize()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(runs):
+        plan.run(rows_t, stream)
+    a1.record(stream)
+    torch.cuda.synchronize()
+    t = a0.elapsed_time(a1) / runs
+    bits, total = plan.status()
+    same = bool(torch.equal(ps.d, ref))
+    plan.close()
+    return {"ms": t, "tflops": flops / (t * 1e-3) / 1e12, "executor_ms": executor_ms, "status": bits,
+            "tiles": total, "bitwise_equal_to_executor": same,
+            "how": "row counts in device memory; one-block prefix-scan kernel writes problem records and "
+                   "tile offsets, the persistent kernel reads the tile count from the device"}
 
 
 def graph_row(ex, stream, flops, runs=20, replays=10):
