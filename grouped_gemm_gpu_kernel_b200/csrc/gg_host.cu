@@ -131,7 +131,7 @@ bool encode_b_chunks(CUtensorMap* map, const void* base, int k, int n, int64_t r
 // Device record of one problem plus its kMapsPerProblem tensor maps. TMA is used for A/B only
 // when both operands qualify, for D when it qualifies; everything else takes the zero-fill load
 // path and masked direct stores.
-DeviceProblemDesc make_device_problem(const gg_problem& p, Variant v, CUtensorMap* maps) {
+DeviceProblemDesc make_device_problem(const gg_problem& p, Variant v, CUtensorMap* maps, int map_slot) {
   const int bm = variant_bm(v), bn = variant_bn(v);
   const int cta_rows = variant_cta_rows(v);  // A and D rows one CTA moves per tile
   const int cta_cols = variant_cta_cols(v);  // B columns one CTA loads per tile
@@ -149,6 +149,7 @@ DeviceProblemDesc make_device_problem(const gg_problem& p, Variant v, CUtensorMa
   d.ldd = p.ldd;
   d.alpha = p.alpha;
   d.beta = p.beta;
+  d.map_slot = map_slot;
   const bool has_tiles = p.m > 0 && p.n > 0;
   d.tiles_m = has_tiles ? ceil_div(p.m, bm) : 0;
   d.tiles_n = has_tiles ? ceil_div(p.n, bn) : 0;
@@ -365,7 +366,7 @@ int gg_executor_build(gg_executor* ex, const gg_problem* sorted_problems, int co
     const gg_problem& p = sorted_problems[i];
     if (p.m < 0 || p.n < 0 || p.k < 0) return cudaErrorInvalidValue;
     if (!p.a || !p.b || !p.d) return cudaErrorInvalidDevicePointer;
-    descs[static_cast<size_t>(i)] = gg::make_device_problem(p, v, &maps[static_cast<size_t>(i) * gg::kMapsPerProblem]);
+    descs[static_cast<size_t>(i)] = gg::make_device_problem(p, v, &maps[static_cast<size_t>(i) * gg::kMapsPerProblem], i);
   }
   if (count == 0 || total_tiles <= 0) {
     ex->problem_count = count;
@@ -483,7 +484,7 @@ int gg_run_baseline_per_problem(const gg_problem* problems, int count, const gg_
       if (!status) return cudaErrorMemoryAllocation;
     }
     std::memset(&kp, 0, sizeof(kp));
-    kp.single_desc = gg::make_device_problem(p, v, kp.single_maps);
+    kp.single_desc = gg::make_device_problem(p, v, kp.single_maps, 0);
     const int tiles = kp.single_desc.tiles_m * kp.single_desc.tiles_n;
     kp.status = status;
     kp.timeout_ns = gg::wait_timeout_ns();
@@ -694,7 +695,7 @@ extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count
   for (int s = 0; s < count; ++s) {
     const gg_problem& p = problems[gg::g_noalloc_order[s]];
     offs[s + 1] = offs[s] + gg::tile_count(p.m, p.n, config->cta_m, config->cta_n);
-    descs[s] = gg::make_device_problem(p, v, &maps[static_cast<size_t>(s) * gg::kMapsPerProblem]);
+    descs[s] = gg::make_device_problem(p, v, &maps[static_cast<size_t>(s) * gg::kMapsPerProblem], s);
   }
   const int total = offs[count];
   if (total == 0) return cudaSuccess;
@@ -779,6 +780,25 @@ __device__ T block_exclusive_scan(T v, T* warp_sums, T* total) {
   return before + x - v;
 }
 
+// Problem record of expert e whose rows start at row0 of the packed tensors.
+__device__ __forceinline__ DeviceProblemDesc moe_record(const DeviceProblemDesc* templ, int e, int r, long long row0,
+                                                        int tm, int tiles_n, int t, int capacity, const __half* a,
+                                                        int lda, const float* c, int ldc, float* d, int ldd) {
+  DeviceProblemDesc p = templ[e];
+  p.m = r;
+  p.a = a + row0 * lda;
+  p.c = c ? c + row0 * ldc : nullptr;
+  p.d = d + row0 * ldd;
+  p.tiles_m = t > 0 ? tm : 0;
+  p.tiles_n = t > 0 ? tiles_n : 0;
+  p.tma_row0 = static_cast<int>(row0 < capacity ? row0 : capacity);
+  return p;
+}
+
+// One block. Rows are packed in expert order, so the row offsets are a prefix sum in that order.
+// With at most kMoePrepThreads experts the problems are then ordered by tile count, largest
+// first (ties by expert index; the by-tiles rule of the host preparation), which shortens the
+// tail of the persistent schedule; larger sets keep expert order.
 __global__ void __launch_bounds__(kMoePrepThreads) moe_prepare_kernel(
     const int* __restrict__ rows, int experts, int capacity, int bm, int tiles_n,
     const DeviceProblemDesc* __restrict__ templ, DeviceProblemDesc* __restrict__ descs, int* __restrict__ offsets,
@@ -786,11 +806,14 @@ __global__ void __launch_bounds__(kMoePrepThreads) moe_prepare_kernel(
     int ldd) {
   __shared__ long long s_rows[kMoePrepThreads / 32];
   __shared__ int s_tiles[kMoePrepThreads / 32];
+  __shared__ long long s_key[kMoePrepThreads];
+  __shared__ long long s_row0[kMoePrepThreads];
+  const int tid = static_cast<int>(threadIdx.x);
   long long row_carry = 0;
   int tile_carry = 0;
   int bad = 0;
-  for (int base = 0; base < experts; base += kMoePrepThreads) {
-    const int e = base + static_cast<int>(threadIdx.x);
+  if (experts <= kMoePrepThreads) {
+    const int e = tid;
     int r = e < experts ? rows[e] : 0;
     if (r < 0) {
       bad = 1;
@@ -799,26 +822,62 @@ __global__ void __launch_bounds__(kMoePrepThreads) moe_prepare_kernel(
     const int tm = r > 0 ? (r + bm - 1) / bm : 0;
     const int t = tiles_n > 0 ? tm * tiles_n : 0;
     long long rows_total;
-    int tiles_total;
-    const long long row0 = row_carry + block_exclusive_scan<long long>(r, s_rows, &rows_total);
-    const int t0 = tile_carry + block_exclusive_scan<int>(t, s_tiles, &tiles_total);
-    if (e < experts) {
-      DeviceProblemDesc p = templ[e];
-      p.m = r;
-      p.a = a + row0 * lda;
-      p.c = c ? c + row0 * ldc : nullptr;
-      p.d = d + row0 * ldd;
-      p.tiles_m = t > 0 ? tm : 0;
-      p.tiles_n = t > 0 ? tiles_n : 0;
-      p.tma_row0 = static_cast<int>(row0 < capacity ? row0 : capacity);
-      descs[e] = p;
-      offsets[e] = t0;
+    const long long row0 = block_exclusive_scan<long long>(r, s_rows, &rows_total);
+    row_carry = rows_total;
+    s_row0[tid] = row0;
+    // descending sort key: tile count, then the lower expert index first; padding sorts last
+    s_key[tid] = e < experts ? (static_cast<long long>(t) << 32) | (0xffffffffll - e) : -1ll;
+    __syncthreads();
+    for (int k2 = 2; k2 <= kMoePrepThreads; k2 <<= 1) {
+      for (int j = k2 >> 1; j > 0; j >>= 1) {
+        const int ixj = tid ^ j;
+        if (ixj > tid) {
+          const long long x = s_key[tid], y = s_key[ixj];
+          const bool desc = (tid & k2) == 0;
+          if (desc ? (x < y) : (x > y)) {
+            s_key[tid] = y;
+            s_key[ixj] = x;
+          }
+        }
+        __syncthreads();
+      }
     }
-    row_carry += rows_total;
-    tile_carry += tiles_total;
+    const long long key = s_key[tid];
+    const int se = key < 0 ? -1 : static_cast<int>(0xffffffffll - (key & 0xffffffffll));
+    const int st = key < 0 ? 0 : static_cast<int>(key >> 32);
+    int tiles_total;
+    const int t0 = block_exclusive_scan<int>(st, s_tiles, &tiles_total);
+    tile_carry = tiles_total;
+    if (se >= 0) {
+      const int sr = max(rows[se], 0);
+      const int stm = sr > 0 ? (sr + bm - 1) / bm : 0;
+      descs[tid] = moe_record(templ, se, sr, s_row0[se], stm, tiles_n, st, capacity, a, lda, c, ldc, d, ldd);
+      offsets[tid] = t0;
+    }
+  } else {
+    for (int base = 0; base < experts; base += kMoePrepThreads) {
+      const int e = base + tid;
+      int r = e < experts ? rows[e] : 0;
+      if (r < 0) {
+        bad = 1;
+        r = 0;
+      }
+      const int tm = r > 0 ? (r + bm - 1) / bm : 0;
+      const int t = tiles_n > 0 ? tm * tiles_n : 0;
+      long long rows_total;
+      int tiles_total;
+      const long long row0 = row_carry + block_exclusive_scan<long long>(r, s_rows, &rows_total);
+      const int t0 = tile_carry + block_exclusive_scan<int>(t, s_tiles, &tiles_total);
+      if (e < experts) {
+        descs[e] = moe_record(templ, e, r, row0, tm, tiles_n, t, capacity, a, lda, c, ldc, d, ldd);
+        offsets[e] = t0;
+      }
+      row_carry += rows_total;
+      tile_carry += tiles_total;
+    }
   }
   bad = __syncthreads_or(bad);
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     offsets[experts] = tile_carry;
     const bool ok = !bad && row_carry <= static_cast<long long>(capacity);
     *total_tiles = ok ? tile_carry : 0;
@@ -890,6 +949,7 @@ int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, g
     p.alpha = q.alpha;
     p.beta = q.beta;
     p.k_blocks = q.k > 0 ? gg::ceil_div(q.k, gg::kBK) : 0;
+    p.map_slot = static_cast<int>(e);  // the maps stay in expert order; the records are reordered
     unsigned flags = grouped_gemm::kFlagPackedRows;
     if (tma_a && gg::encode_2d(&m[gg::kMapB], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, q.b[e], q.n, q.k,
                                static_cast<int64_t>(q.ldb) * 2, 64, gg::kBK)) {

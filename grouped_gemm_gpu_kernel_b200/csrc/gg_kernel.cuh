@@ -545,7 +545,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
         if (lane < kDescWords) reinterpret_cast<int*>(&s->desc)[lane] = ss.w;
         const unsigned fl = static_cast<unsigned>(
             __shfl_sync(0xffffffffu, ss.w, static_cast<int>(offsetof(DeviceProblemDesc, flags) / 4)));
-        prefetch_problem_maps(maps, pidx, fl, lane);
+        const int slot_maps = __shfl_sync(0xffffffffu, ss.w, static_cast<int>(offsetof(DeviceProblemDesc, map_slot) / 4));
+        prefetch_problem_maps(maps, slot_maps, fl, lane);
       } else {
         pidx = -1;
       }
@@ -583,15 +584,16 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
       const __half* b = s->desc.b;
       const int lda = s->desc.lda, ldb = s->desc.ldb;
       const int a_row = s->desc.tma_row0 + tile_m * BM;  // first A row of the tile in the A map
+      const int map_slot = s->desc.map_slot;
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(ringe_bar(slot));
       if (q < 0) break;
 
       if (flags & grouped_gemm::kFlagTmaAB) {
         if (ptid == 0) {
-          const CUtensorMap* ma = maps + kMapsPerProblem * q + kMapA;
-          const CUtensorMap* mb = maps + kMapsPerProblem * q + kMapB;
-          const CUtensorMap* mb3 = maps + kMapsPerProblem * q + kMapB3;
+          const CUtensorMap* ma = maps + kMapsPerProblem * map_slot + kMapA;
+          const CUtensorMap* mb = maps + kMapsPerProblem * map_slot + kMapB;
+          const CUtensorMap* mb3 = maps + kMapsPerProblem * map_slot + kMapB3;
           // One 3-D box loads the whole B stage when every 64-column chunk of the tile lies
           // inside N; an edge tile loads chunk by chunk so columns past N are zero-filled.
           const bool b_one_box = (flags & grouped_gemm::kFlagTmaB3) && (tile_n + 1) * BN <= n;
@@ -733,6 +735,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
       float* dptr = s->desc.d;
       const int ldc = s->desc.ldc, ldd = s->desc.ldd;
       const int tma_row0 = s->desc.tma_row0;
+      const int map_slot = s->desc.map_slot;
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(ringe_bar(slot));
       if (q < 0) break;
@@ -752,7 +755,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
       const int row0 = qw * 32 < BM ? tile_m * BM + qw * 32 : m;
       epilogue_warp(smem + L::kEpiOffset + warp * kEpiWarpBytes, store_count, t_addr, lane, row0, m, n, tile_n * BN,
                     c_begin, c_end, kb_count, flags, alpha, beta, cptr, ldc, dptr, ldd,
-                    maps + kMapsPerProblem * q + kMapD, tma_row0, [&] { ptx::mbar_arrive(acce_bar(buf)); });
+                    maps + kMapsPerProblem * map_slot + kMapD, tma_row0, [&] { ptx::mbar_arrive(acce_bar(buf)); });
     }
     if (lane == 0) ptx::bulk_wait_all();  // every warp issues its own TMA stores
     __syncwarp();

@@ -169,7 +169,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane < kDescWords) reinterpret_cast<int*>(&s->desc)[lane] = ss.w;
           const unsigned fl = static_cast<unsigned>(
               __shfl_sync(0xffffffffu, ss.w, static_cast<int>(offsetof(DeviceProblemDesc, flags) / 4)));
-          prefetch_problem_maps(maps, pidx, fl, lane);
+          const int slot_maps =
+              __shfl_sync(0xffffffffu, ss.w, static_cast<int>(offsetof(DeviceProblemDesc, map_slot) / 4));
+          prefetch_problem_maps(maps, slot_maps, fl, lane);
         } else {
           pidx = -1;
         }
@@ -221,13 +223,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (q < 0) break;
       const int row_base = tile_m * BM + static_cast<int>(rank) * 128;  // this CTA's rows of A
       const int a_row = s->desc.tma_row0 + row_base;                     // the same row in the A map
+      const int map_slot = s->desc.map_slot;
       const int col_base = tile_n * BN + static_cast<int>(rank) * HB;   // this CTA's columns of B
 
       if (flags & grouped_gemm::kFlagTmaAB) {
         if (ptid == 0) {
-          const CUtensorMap* ma = maps + kMapsPerProblem * q + kMapA;
-          const CUtensorMap* mb = maps + kMapsPerProblem * q + kMapB;
-          const CUtensorMap* mb3 = maps + kMapsPerProblem * q + kMapB3;
+          const CUtensorMap* ma = maps + kMapsPerProblem * map_slot + kMapA;
+          const CUtensorMap* mb = maps + kMapsPerProblem * map_slot + kMapB;
+          const CUtensorMap* mb3 = maps + kMapsPerProblem * map_slot + kMapB3;
           const bool b_one_box = HB > 64 && (flags & grouped_gemm::kFlagTmaB3) && col_base + HB <= n;
           for (int kb = 0; kb < kb_count; ++kb) {
             const int st = static_cast<int>(it % S);
@@ -372,6 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* dptr = s->desc.d;
       const int ldc = s->desc.ldc, ldd = s->desc.ldd;
       const int tma_row0 = s->desc.tma_row0;
+      const int map_slot = s->desc.map_slot;
       __syncwarp();
       if (lane == 0) release_slot(slot);
       if (q < 0) break;
@@ -390,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row0 = tile_m * BM + static_cast<int>(rank) * 128 + qw * 32;  // this warp's first row
       epilogue_warp(smem + L::kEpiOffset + warp * kEpiWarpBytes, store_count, t_addr, lane, row0, m, n,
                     tile_n * BN, c_begin, c_end, kb_count, flags, alpha, beta, cptr, ldc, dptr, ldd,
-                    maps + kMapsPerProblem * q + kMapD, tma_row0, [&] {
+                    maps + kMapsPerProblem * map_slot + kMapD, tma_row0, [&] {
                       if (leader) ptx::mbar_arrive(acce_bar(buf));
                       else ptx::mbar_arrive_cluster(ptx::mapa_shared(acce_bar(buf), 0));
                     });

@@ -47,7 +47,7 @@ struct DeviceProblemDesc {
   int k_blocks;  // ceil(k / 64): 64-deep K blocks of the tcgen05 mainloop
   unsigned flags;  // DeviceProblemFlags
   int tma_row0;    // first row of this problem in the packed A/D maps (kFlagPackedRows), else 0
-  int reserved;
+  int map_slot;    // index of this problem's group of tensor maps in the map table
 };
 
 static_assert(sizeof(DeviceProblemDesc) == 96, "DeviceProblemDesc layout");
