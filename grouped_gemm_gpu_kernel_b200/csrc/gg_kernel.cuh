@@ -1,26 +1,27 @@
 // gg_kernel.cuh -- the persistent grouped GEMM kernel for B200 (sm_100a).
 //
-// One CTA per SM (shared memory > half an SM's), 256 threads in five warp roles:
+// One CTA per SM (shared memory > half an SM's), 384 threads in five warp roles:
 //
-//   warps 0-3  epilogue   TMEM -> registers (tcgen05.ld), D = alpha*acc + beta*C. Warp w reads
-//                         TMEM lanes 32w..32w+31 = tile rows 32w..32w+31 and stores them on its
-//                         own: per 32-column chunk one 32x32 TMA store from a 128-byte-swizzled
-//                         staging tile (clipped at the problem edge), or, when D is not
-//                         TMA-eligible, coalesced masked stores read back from that tile.
-//   warp 4     MMA        allocates 2*BN TMEM columns (two accumulators, so the epilogue of one
-//                         tile overlaps the mainloop of the next); one thread issues
-//                         tcgen05.mma.kind::f16 (M=128, N=BN, K=16) and tcgen05.commit.
-//   warp 5     scheduler  claims global tile indices with atomicAdd (the reference's device
-//                         scheduler, src/grouped_gemm.cu:640-675), finds the owning problem with a
-//                         warp-parallel 32-ary search of tile_offsets (same answer as the
-//                         reference's binary search, src/grouped_gemm.cu:219-234), copies the
-//                         problem record into a 4-deep shared-memory ring read by every role.
-//   warps 6-7  producers  fill a multi-stage ring of A/B shared-memory tiles: one thread issues
-//                         TMA tensor loads for aligned problems (one box for A and, for tiles
-//                         inside N, one 3-D box for all of B); all 64 threads load with zero
-//                         fill for problems whose base or leading dimension TMA cannot take (the
-//                         reference's scalar zero-fill path, src/grouped_gemm.cu:273-371), writing
-//                         the same 128-byte-swizzled layout the TMA would.
+//   warps 0-7   epilogue   TMEM -> registers (tcgen05.ld), D = alpha*acc + beta*C. Warp w reads
+//                          TMEM lanes 32(w%4)..+31 = tile rows 32(w%4)..+31 and stores half of the
+//                          tile's columns (w/4 picks the half) on its own: per 32-column chunk one
+//                          32x32 TMA store from a 128-byte-swizzled staging tile (clipped at the
+//                          problem edge), or, when D is not TMA-eligible, coalesced masked stores
+//                          read back from that tile.
+//   warp 8      MMA        allocates 512 TMEM columns (2 accumulators of 256 columns or 4 of <= 128,
+//                          so the epilogue of one tile overlaps the mainloops of the next); one
+//                          thread issues tcgen05.mma.kind::f16 (M=128, N=BN, K=16) and tcgen05.commit.
+//   warp 9      scheduler  claims global tile indices with atomicAdd (the reference's device
+//                          scheduler, src/grouped_gemm.cu:640-675), finds the owning problem with a
+//                          warp-parallel 32-ary search of tile_offsets (same answer as the
+//                          reference's binary search, src/grouped_gemm.cu:219-234), copies the
+//                          problem record into a 4-deep shared-memory ring read by every role.
+//   warps 10-11 producers  fill a multi-stage ring of A/B shared-memory tiles: one thread issues
+//                          TMA tensor loads for aligned problems (one box for A and, for tiles
+//                          inside N, one 3-D box for all of B); all 64 threads load with zero
+//                          fill for problems whose base or leading dimension TMA cannot take (the
+//                          reference's scalar zero-fill path, src/grouped_gemm.cu:273-371),
+//                          writing the same 128-byte-swizzled layout the TMA would.
 //
 // Shared-memory layout per stage: A as 128 rows x 64 K (K-major, 128-byte rows, SW128) and B as
 // BN/64 column chunks of 64 K rows x 64 N (MN-major, SW128). A 64-row tile (reference shapes
