@@ -211,6 +211,25 @@ cudaError_t persistent_grid(Variant v, int total_tiles, int persistent_ctas, int
   return cudaSuccess;
 }
 
+// Grid and launch of the path a config selects: the tcgen05 kernel, or the CUDA-core kernel when
+// use_tensor_cores is 0 (persistent either way: at most one tile per CTA, at most what fits).
+cudaError_t path_grid(bool tc, Variant v, int total_tiles, int persistent_ctas, int* grid) {
+  if (tc) return persistent_grid(v, total_tiles, persistent_ctas, grid);
+  if (persistent_ctas > 0) {
+    *grid = persistent_ctas;
+    return cudaSuccess;
+  }
+  int resident = 0;
+  const cudaError_t st = simt_resident_ctas(&resident);
+  if (st != cudaSuccess) return st;
+  *grid = std::max(1, std::min(resident, total_tiles));
+  return cudaSuccess;
+}
+
+cudaError_t launch_path(bool tc, Variant v, const KernelParams& kp, int grid, cudaStream_t s) {
+  return tc ? launch_grouped_kernel(v, kp, grid, s) : launch_simt_kernel(v, kp, grid, s);
+}
+
 Variant variant_of(const gg_config* c) {
   if (!c) return Variant::kUnsupported;
   return resolve_variant(c->cta_m, c->cta_n, c->cta_k, c->threads);
@@ -233,6 +252,7 @@ struct gg_executor {
   int total_tiles = 0;
   int grid_ctas = 0;
   gg::Variant variant = gg::Variant::kUnsupported;
+  bool use_tc = true;  // tcgen05 kernel; false: the CUDA-core kernel
   gg::KernelParams params{};
 
   void release() {
@@ -308,17 +328,20 @@ int gg_query_occupancy(const gg_config* config, gg_occupancy* info) {
   o.max_registers_per_sm = attr(cudaDevAttrMaxRegistersPerMultiprocessor);
   o.max_registers_per_block = attr(cudaDevAttrMaxRegistersPerBlock);
   if (st != cudaSuccess) return st;
-  o.threads_per_block = gg::kThreads;
-  o.warps_per_block = gg::kThreads / (warp_size > 0 ? warp_size : 32);
+  const bool tc = config->use_tensor_cores != 0;
+  const int threads = tc ? gg::kThreads : gg::simt_threads();
+  o.threads_per_block = threads;
+  o.warps_per_block = threads / (warp_size > 0 ? warp_size : 32);
   o.max_warps_per_sm = o.max_threads_per_sm / (warp_size > 0 ? warp_size : 32);
   // Register model of the widest role, an epilogue thread: one 32-column TMEM chunk (32), the
   // matching C values (32) and ~24 for addresses, flags and loop state.
-  o.estimated_registers_per_thread = 32 + 32 + 24;
-  o.estimated_registers_per_block = o.estimated_registers_per_thread * gg::kThreads;
-  o.dynamic_shared_bytes = gg::variant_dynamic_smem(v);
-  o.using_tensor_cores = 1;
+  // (CUDA-core path: a 4 x 4 FP32 accumulator block (16), its 8 operands and ~24.)
+  o.estimated_registers_per_thread = tc ? 32 + 32 + 24 : 16 + 8 + 24;
+  o.estimated_registers_per_block = o.estimated_registers_per_thread * threads;
+  o.dynamic_shared_bytes = tc ? gg::variant_dynamic_smem(v) : 0;
+  o.using_tensor_cores = tc ? 1 : 0;
   cudaFuncAttributes fa{};
-  st = gg::kernel_occupancy(v, &o.active_blocks_per_sm, &fa);
+  st = tc ? gg::kernel_occupancy(v, &o.active_blocks_per_sm, &fa) : gg::simt_occupancy(&o.active_blocks_per_sm, &fa);
   if (st != cudaSuccess) return st;
   o.registers_per_thread = fa.numRegs;
   o.static_shared_bytes = static_cast<int>(fa.sharedSizeBytes);
@@ -359,6 +382,7 @@ int gg_executor_build(gg_executor* ex, const gg_problem* sorted_problems, int co
   ex->total_tiles = 0;
   ex->grid_ctas = 0;
   ex->variant = v;
+  ex->use_tc = config->use_tensor_cores != 0;
 
   std::vector<DeviceProblemDesc> descs(static_cast<size_t>(count));
   std::vector<CUtensorMap> maps(static_cast<size_t>(count) * gg::kMapsPerProblem);
@@ -375,7 +399,7 @@ int gg_executor_build(gg_executor* ex, const gg_problem* sorted_problems, int co
   }
 
   int grid = 0;
-  cudaError_t st = gg::persistent_grid(v, total_tiles, config->persistent_ctas, &grid);
+  cudaError_t st = gg::path_grid(ex->use_tc, v, total_tiles, config->persistent_ctas, &grid);
   if (st != cudaSuccess) return st;
 
   const size_t maps_bytes = maps.size() * sizeof(CUtensorMap);
@@ -431,7 +455,7 @@ int gg_executor_run(const gg_executor* ex, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t st = cudaMemsetAsync(ex->d_counter, 0, sizeof(int), s);
   if (st != cudaSuccess) return st;
-  return gg::launch_grouped_kernel(ex->variant, ex->params, ex->grid_ctas, s);
+  return gg::launch_path(ex->use_tc, ex->variant, ex->params, ex->grid_ctas, s);
 }
 
 int gg_executor_problem_count(const gg_executor* ex) { return ex ? ex->problem_count : 0; }
@@ -493,9 +517,10 @@ int gg_run_baseline_per_problem(const gg_problem* problems, int count, const gg_
     kp.raster_group = gg::raster_group();
     kp.single_mode = 1;
     int grid = 0;
-    cudaError_t st = gg::persistent_grid(v, tiles, 0, &grid);
+    const bool tc = config->use_tensor_cores != 0;
+    cudaError_t st = gg::path_grid(tc, v, tiles, 0, &grid);
     if (st != cudaSuccess) return st;
-    st = gg::launch_grouped_kernel(v, kp, grid, s);
+    st = gg::launch_path(tc, v, kp, grid, s);
     if (st != cudaSuccess) return st;
   }
   return cudaSuccess;
@@ -704,7 +729,7 @@ extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count
   cudaError_t st = gg::noalloc_scratch(&scratch);
   if (st != cudaSuccess) return st;
   int grid = 0;
-  st = gg::persistent_grid(v, total, config->persistent_ctas, &grid);
+  st = gg::path_grid(config->use_tensor_cores != 0, v, total, config->persistent_ctas, &grid);
   if (st != cudaSuccess) return st;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -736,7 +761,7 @@ extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count
   kp.total_tiles = total;
   kp.raster_group = gg::raster_group();
   kp.single_mode = 0;
-  return gg::launch_grouped_kernel(v, kp, grid, s);
+  return gg::launch_path(config->use_tensor_cores != 0, v, kp, grid, s);
 }
 
 // ---- grouped GEMM with device-side preparation (mixture-of-experts routing) ---------------------
@@ -899,6 +924,7 @@ struct gg_moe_plan {
   int* d_status = nullptr;
   gg_moe_problem problem{};
   gg::Variant variant = gg::Variant::kUnsupported;
+  bool use_tc = true;
   int grid_ctas = 0;
   int tiles_n = 0;
   gg::KernelParams params{};
@@ -969,7 +995,8 @@ int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, g
   }
 
   int grid = 0;
-  cudaError_t st = gg::persistent_grid(v, 1 << 30, config->persistent_ctas, &grid);
+  const bool use_tc = config->use_tensor_cores != 0;
+  cudaError_t st = gg::path_grid(use_tc, v, 1 << 30, config->persistent_ctas, &grid);
   if (st != cudaSuccess) return st;
 
   const size_t maps_bytes = maps.size() * sizeof(CUtensorMap);
@@ -1005,6 +1032,7 @@ int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, g
   plan->problem = q;
   plan->problem.b = nullptr;  // the host array is not kept
   plan->variant = v;
+  plan->use_tc = use_tc;
   plan->grid_ctas = grid;
   plan->tiles_n = q.n > 0 ? gg::ceil_div(q.n, bn) : 0;
 
@@ -1036,7 +1064,7 @@ int gg_moe_plan_run(gg_moe_plan* plan, const int* rows, void* stream) {
       q.ldc, q.d, q.ldd);
   cudaError_t st = cudaGetLastError();
   if (st != cudaSuccess) return st;
-  return gg::launch_grouped_kernel(plan->variant, plan->params, plan->grid_ctas, s);
+  return gg::launch_path(plan->use_tc, plan->variant, plan->params, plan->grid_ctas, s);
 }
 
 int gg_moe_plan_status(gg_moe_plan* plan, int* status, int* total_tiles) {

@@ -1,0 +1,174 @@
+// gg_simt.cu -- the CUDA-core path of the grouped GEMM, taken when KernelConfig::use_tensor_cores
+// is false: the reference's SIMT mainloop (compute_gemm_tile_simt, reference
+// src/grouped_gemm.cu:373-482) restated for this library's problem records and scheduler.
+//
+// Same contract as the tensor-core kernel: the same tile_offsets and tile numbering (the config's
+// cta_m x cta_n tiles), the same atomic tile claims and problem lookup (reference
+// src/grouped_gemm.cu:219-234, 640-675), the same epilogue D = alpha*acc + beta*C with C read only
+// when c != nullptr and beta != 0 (reference src/grouped_gemm.cu:460-481). FP16 operands are
+// widened to FP32 and accumulated with FP32 FMA (an FP16 x FP16 product is exact in FP32), so the
+// result differs from the tensor-core path only in the order of the FP32 additions.
+//
+// A CTA computes its tile as 64 x 64 sub-tiles: 256 threads, each 4 x 4 outputs; K in steps of 32
+// through shared memory (A stored k-major so a thread reads its 4 rows with one 16-byte load),
+// operands loaded with plain zero-filled loads (any leading dimension, any alignment). No
+// spin-waits: only atomics and block barriers.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "gg_internal.h"
+
+namespace gg {
+namespace {
+
+constexpr int kSimtThreads = 256;
+constexpr int kSub = 64;     // sub-tile edge
+constexpr int kSimtBK = 32;  // K per shared-memory step
+constexpr int kPad = 4;      // keeps 16-byte alignment of every row, spreads banks
+
+// Last q with offs[q] <= tile (offs has count + 1 entries, offs[count] = total > tile).
+__device__ int find_problem(const int* offs, int count, int tile) {
+  int lo = 0, hi = count;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (offs[mid] <= tile) lo = mid;
+    else hi = mid;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(kSimtThreads) grouped_gemm_simt_kernel(const __grid_constant__ KernelParams p,
+                                                                        int bm, int bn) {
+  __shared__ __align__(16) float As[kSimtBK][kSub + kPad];  // As[k][row]
+  __shared__ __align__(16) float Bs[kSimtBK][kSub + kPad];  // Bs[k][col]
+  __shared__ int s_work[3];                                 // problem, tile_m, tile_n
+
+  const DeviceProblemDesc* problems = p.single_mode ? &p.single_desc : p.problems;
+  const int total = p.total_tiles_dev ? *p.total_tiles_dev : p.total_tiles;
+  const int tid = static_cast<int>(threadIdx.x);
+  const int tx = tid & 15, ty = tid >> 4;
+  int static_next = static_cast<int>(blockIdx.x);
+
+  for (;;) {
+    if (tid == 0) {
+      int q = -1, tm = 0, tn = 0;
+      for (;;) {
+        int tile;
+        if (p.single_mode) {
+          tile = static_next;
+          static_next += static_cast<int>(gridDim.x);
+        } else {
+          tile = atomicAdd(p.tile_counter, 1);
+        }
+        if (tile >= total) break;
+        const int pq = p.single_mode ? 0 : find_problem(p.tile_offsets, p.problem_count, tile);
+        const int local = tile - (p.single_mode ? 0 : p.tile_offsets[pq]);
+        const int tiles_m = problems[pq].tiles_m, tiles_n = problems[pq].tiles_n;
+        // a tile outside its problem's grid (a prepared set inconsistent with the config) is
+        // skipped, as the reference kernel does (src/grouped_gemm.cu:662-672)
+        if (local < 0 || tiles_m <= 0 || tiles_n <= 0 || local >= tiles_m * tiles_n) continue;
+        q = pq;
+        tm = local / tiles_n;
+        tn = local % tiles_n;
+        break;
+      }
+      s_work[0] = q;
+      s_work[1] = tm;
+      s_work[2] = tn;
+    }
+    __syncthreads();
+    const int q = s_work[0], tile_m = s_work[1], tile_n = s_work[2];
+    __syncthreads();  // s_work is rewritten for the next tile only after every thread read it
+    if (q < 0) break;
+
+    const DeviceProblemDesc& d = problems[q];
+    const int m = d.m, n = d.n, k = d.k;
+    const __half* a = d.a;
+    const __half* b = d.b;
+    const int lda = d.lda, ldb = d.ldb;
+    const bool read_c = (d.flags & grouped_gemm::kFlagReadC) != 0u;
+    const float alpha = d.alpha, beta = d.beta;
+
+    for (int sm = 0; sm < bm; sm += kSub) {
+      const int row0 = tile_m * bm + sm;
+      if (row0 >= m) break;
+      for (int sn = 0; sn < bn; sn += kSub) {
+        const int col0 = tile_n * bn + sn;
+        if (col0 >= n) break;
+        float acc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+        for (int k0 = 0; k0 < k; k0 += kSimtBK) {
+          for (int i = tid; i < kSub * kSimtBK; i += kSimtThreads) {
+            const int r = i / kSimtBK, kk = i % kSimtBK;
+            const int gr = row0 + r, gk = k0 + kk;
+            As[kk][r] = (gr < m && gk < k) ? __half2float(a[static_cast<long long>(gr) * lda + gk]) : 0.0f;
+          }
+          for (int i = tid; i < kSimtBK * kSub; i += kSimtThreads) {
+            const int kk = i / kSub, c = i % kSub;
+            const int gk = k0 + kk, gc = col0 + c;
+            Bs[kk][c] = (gk < k && gc < n) ? __half2float(b[static_cast<long long>(gk) * ldb + gc]) : 0.0f;
+          }
+          __syncthreads();
+#pragma unroll 8
+          for (int kk = 0; kk < kSimtBK; ++kk) {
+            const float4 av = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+            const float4 bv = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+            const float ar[4] = {av.x, av.y, av.z, av.w};
+            const float br[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+              for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(ar[i], br[j], acc[i][j]);
+          }
+          __syncthreads();
+        }
+        // D = alpha * acc + beta * C, C taken as 0 when it is not read
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int gr = row0 + ty * 4 + i;
+          if (gr >= m) continue;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int gc = col0 + tx * 4 + j;
+            if (gc >= n) continue;
+            const float cv = read_c ? d.c[static_cast<long long>(gr) * d.ldc + gc] : 0.0f;
+            d.d[static_cast<long long>(gr) * d.ldd + gc] = alpha * acc[i][j] + beta * cv;
+          }
+        }
+      }
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t simt_resident_ctas(int* ctas) {
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaError_t st = cudaGetDevice(&dev);
+  if (st == cudaSuccess) st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (st == cudaSuccess)
+    st = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, grouped_gemm_simt_kernel, kSimtThreads, 0);
+  if (st != cudaSuccess) return st;
+  *ctas = sms * (per_sm > 0 ? per_sm : 1);
+  return cudaSuccess;
+}
+
+cudaError_t simt_occupancy(int* active_blocks_per_sm, cudaFuncAttributes* attrs) {
+  cudaError_t st = cudaFuncGetAttributes(attrs, grouped_gemm_simt_kernel);
+  if (st != cudaSuccess) return st;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(active_blocks_per_sm, grouped_gemm_simt_kernel, kSimtThreads,
+                                                       0);
+}
+
+int simt_threads() { return kSimtThreads; }
+
+cudaError_t launch_simt_kernel(Variant v, const KernelParams& params, int grid, cudaStream_t stream) {
+  if (grid <= 0) return cudaSuccess;
+  grouped_gemm_simt_kernel<<<grid, kSimtThreads, 0, stream>>>(params, variant_bm(v), variant_bn(v));
+  return cudaGetLastError();
+}
+
+}  // namespace gg

@@ -65,7 +65,8 @@ typedef struct gg_problem {
  *                          tcgen05 cta_group::2: 128 rows per CTA)
  *   the reference's tiles  64x64x16, 128x64x32, 64x128x32  (same tile decomposition, run on the
  *                          same tcgen05 kernel; cta_k only selects the variant)
- * use_tensor_cores is accepted either way: every variant runs on tcgen05 tensor cores. */
+ * use_tensor_cores != 0 runs the tcgen05 tensor-core kernel; 0 runs the CUDA-core kernel (FP16
+ * operands widened to FP32, FP32 FMA; the reference's SIMT path) with the same tile numbering. */
 typedef struct gg_config {
   int cta_m;
   int cta_n;

@@ -52,10 +52,11 @@ def _executor_reference(A, Bs, C, rows, n, k, cfg, alpha=1.0, beta=0.0):
     return D2
 
 
-CFGS = [gg.KernelConfig(128, 256, 64), gg.KernelConfig(128, 128, 64), gg.KernelConfig(256, 128, 64)]
+CFGS = [gg.KernelConfig(128, 256, 64), gg.KernelConfig(128, 128, 64), gg.KernelConfig(256, 128, 64),
+        gg.KernelConfig(128, 128, 64, use_tensor_cores=False)]
 
 
-@pytest.mark.parametrize("cfg", CFGS, ids=lambda c: f"{c.cta_m}x{c.cta_n}")
+@pytest.mark.parametrize("cfg", CFGS, ids=lambda c: f"{'' if c.use_tensor_cores else 'simt'}{c.cta_m}x{c.cta_n}")
 def test_plan_matches_executor_bitwise(cuda, cfg):
     import torch
 

@@ -379,6 +379,50 @@ def test_edge_cases(cuda, cfg):
             raise AssertionError(f"edge case {name}: {e}") from e
 
 
+SIMT_CONFIGS = [gg.KernelConfig(64, 64, 16, use_tensor_cores=False), gg.KernelConfig(128, 64, 32, use_tensor_cores=False),
+                gg.KernelConfig(128, 256, 64, use_tensor_cores=False), gg.KernelConfig(256, 128, 64, use_tensor_cores=False)]
+
+
+@pytest.mark.parametrize("cfg", SIMT_CONFIGS, ids=lambda c: f"simt{c.cta_m}x{c.cta_n}")
+def test_cuda_core_path_matches_oracle(cuda, cfg):
+    """use_tensor_cores = false (the reference's SIMT path): reference test set in every sort mode
+    and through the per-problem baseline, small16, tiny4096 and the edge cases, against FP64."""
+    torch = _torch()
+    probs, keep, refs = _fixture_problems(cuda)
+    for mode in MODES:
+        for _, d in refs:
+            d.fill_(float("nan"))
+        assert gg.run_grouped_gemm_once(probs, mode, cfg) == 0
+        torch.cuda.synchronize()
+        _check_fixture(refs)
+    for _, d in refs:
+        d.fill_(float("nan"))
+    assert gg.run_baseline_per_problem(probs, cfg) == 0
+    torch.cuda.synchronize()
+    _check_fixture(refs)
+    for wl in ("small16", "tiny4096"):
+        ps = W.allocate(W.make_shapes(wl), cuda)
+        run_grouped(ps.problems(), cfg, gg.SortMode.kByTiles)
+        assert check_full(ps) <= 1.0
+    cases = [(_edge_problem(cuda, seed=i, **kw)) for i, kw in enumerate(EDGE_CASES.values())]
+    run_grouped([p for p, _ in cases], cfg, gg.SortMode.kByK)
+    for (p, bufs), name in zip(cases, EDGE_CASES):
+        try:
+            _check_edge(p, bufs)
+        except AssertionError as e:
+            raise AssertionError(f"edge case {name}: {e}") from e
+
+
+def test_cuda_core_path_mixed512_sampled_and_occupancy(cuda):
+    cfg = gg.KernelConfig(128, 128, 64, use_tensor_cores=False)
+    ps = W.allocate(W.make_shapes("mixed512"), cuda)
+    run_grouped(ps.problems(), cfg, gg.SortMode.kByK)
+    assert check_sampled(ps) <= 1.0
+    st, info = gg.query_occupancy(cfg)
+    assert st == 0 and not info.using_tensor_cores and info.threads_per_block == 256
+    assert info.active_blocks_per_sm >= 1 and info.dynamic_shared_bytes == 0
+
+
 def test_zero_dim_problems_untouched(cuda):
     cases = [_edge_problem(cuda, m=0, n=64, k=16), _edge_problem(cuda, m=64, n=0, k=16),
              _edge_problem(cuda, m=64, n=64, k=16)]
