@@ -151,3 +151,24 @@ def test_plan_on_the_moe_workload_matches_executor(cuda):
     ref = _executor_reference(A, Bs, None, rows, n, k, cfg)
     assert torch.equal(D, ref)
     plan.close()
+
+
+def test_plan_with_more_experts_than_one_preparation_block(cuda):
+    """1500 problems: the preparation kernel scans in chunks of 1024 and keeps expert order."""
+    import torch
+
+    rng = np.random.default_rng(5)
+    rows = [int(x) for x in rng.integers(0, 40, size=1500)]
+    n, k = 96, 72
+    capacity = sum(rows) + 17
+    cfg = gg.KernelConfig(128, 128, 64)
+    A, Bs, C, D = _setup(cuda, rows, n, k, capacity, beta=0.25)
+    plan = _plan(A, Bs, C, D, n, k, capacity, cfg, beta=0.25)
+    assert plan.run(torch.tensor(rows, dtype=torch.int32, device=cuda)) == 0
+    bits, total = plan.status()
+    assert bits == 0 and total == sum(-(-r // 128) for r in rows)
+    ref = _executor_reference(A, Bs, C, rows, n, k, cfg, beta=0.25)
+    used = sum(rows)
+    assert torch.equal(D[:used], ref[:used])
+    assert torch.isnan(D[used:]).all()
+    plan.close()
