@@ -362,6 +362,8 @@ EDGE_CASES = {
     "lda_lt_8_mult": dict(m=64, n=64, k=64, lda=68),
     "n8": dict(m=300, n=8, k=96),
     "m_exact_tiles": dict(m=256, n=512, k=128, beta=0.25),
+    "packed_small_misaligned": dict(m=50, n=40, k=37, a_shift=1, b_shift=3, beta=0.5),
+    "packed_k64_misaligned": dict(m=70, n=200, k=64, a_shift=1, b_shift=1),
 }
 
 
