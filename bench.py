@@ -59,6 +59,8 @@ def parse_args():
     ap.add_argument("--no-extras", action="store_true", help="skip the sort-mode sweep and the reference GPU row")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU work of the cpu_baseline sample")
+    ap.add_argument("--input-type", choices=["f16", "bf16"], default="f16",
+                    help="A/B element type (bf16 is an extension; the reference is FP16 only)")
     ap.add_argument("--gather", action="store_true",
                     help="N>1: after the timed region, gather every rank's D to rank 0 over NCCL and time it")
     return ap.parse_args()
@@ -283,9 +285,11 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
     cta = tuple(int(x) for x in args.cta.split("x")) if args.cta else DEFAULT_CTA[args.workload]
-    cfg = gg.KernelConfig(*cta)
+    cfg = gg.KernelConfig(*cta, input_type=1 if args.input_type == "bf16" else 0)
     shapes, global_flops = rank_shapes(args.workload, world, rank, cfg)
     ps = W.allocate(shapes, dev, seed=42 + rank, d_fill=0.0)
+    if args.input_type == "bf16":
+        ps.to_bf16()
     problems = ps.problems()
     prep_t0 = time.perf_counter()
     prep = gg.prepare_problem_set(problems, cfg, args.sort_mode)
@@ -417,7 +421,7 @@ def main():
         # Streamed: two device buffer sets, copies in on one stream, the grouped GEMM on another,
         # copies out on a third, so step i+1's inputs cross PCIe while step i computes and step
         # i-1's D comes back. Every step still moves its own inputs in and its D out.
-        ps_b = W.allocate(shapes, dev, seed=42 + rank, d_fill=0.0)
+        ps_b = W.allocate(shapes, dev, seed=42 + rank, d_fill=0.0)  # overwritten by the copies in
         ex_b = gg.GroupedGemmExecutor()
         assert ex_b.build(gg.prepare_problem_set(ps_b.problems(), cfg, args.sort_mode), cfg) == 0
         sets = [(ps, ex), (ps_b, ex_b)]
@@ -496,7 +500,8 @@ def main():
         extras["cuda_graph"] = graph_row(ex, stream, local_flops)
         if args.workload == "moe":
             extras["device_prep"] = moe_plan_row(ps, shapes, cfg, stream, local_flops, ms)
-        extras["ref_gpu"] = reference_gpu_row(problems, stream, local_flops)
+        if args.input_type == "f16":  # the reference's kernels read FP16 only
+            extras["ref_gpu"] = reference_gpu_row(problems, stream, local_flops)
 
     cpu = None
     if rank == 0 and world == 1:
@@ -507,7 +512,7 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "vs_baseline": None, "dtype": args.input_type, "data": "synthetic",
             "config": {"workload": args.workload, "problems_per_gpu": len(shapes.dims), "cta": "x".join(map(str, cta)),
                        "sort_mode": gg.sort_mode_name(args.sort_mode), "tiles": n_tiles, "grid_ctas": ex.grid_ctas(),
                        "global_gflop": global_flops / 1e9,

@@ -71,10 +71,11 @@ class KernelConfig:
     threads: int = 256
     persistent_ctas: int = 0
     use_tensor_cores: bool = True
+    input_type: int = 0  # 0 = FP16 A/B (the reference's type), 1 = BF16
 
     def to_c(self) -> capi.GGConfig:
         return capi.GGConfig(self.cta_m, self.cta_n, self.cta_k, self.threads, self.persistent_ctas,
-                             1 if self.use_tensor_cores else 0)
+                             1 if self.use_tensor_cores else 0, int(self.input_type))
 
 
 # The reference's three tile shapes (reference src/grouped_gemm.cu:67-81) and the sm_100a ones.

@@ -22,6 +22,8 @@ EXPORTED_SYMBOLS = (
     "gg_moe_plan_create", "gg_moe_plan_run", "gg_moe_plan_status", "gg_moe_plan_destroy",
 )
 GG_STATUS_BAD_ROWS = 0x100
+GG_INPUT_F16 = 0
+GG_INPUT_BF16 = 1
 GG_NOALLOC_MAX_PROBLEMS = 1024
 
 GG_STATUS_TIMEOUT_PRODUCER = 0x1
@@ -45,7 +47,8 @@ class GGProblem(ctypes.Structure):
 
 class GGConfig(ctypes.Structure):
     _fields_ = [("cta_m", ctypes.c_int), ("cta_n", ctypes.c_int), ("cta_k", ctypes.c_int),
-                ("threads", ctypes.c_int), ("persistent_ctas", ctypes.c_int), ("use_tensor_cores", ctypes.c_int)]
+                ("threads", ctypes.c_int), ("persistent_ctas", ctypes.c_int), ("use_tensor_cores", ctypes.c_int),
+                ("input_type", ctypes.c_int)]
 
 
 class GGOccupancy(ctypes.Structure):

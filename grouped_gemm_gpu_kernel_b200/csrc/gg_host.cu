@@ -231,7 +231,7 @@ cudaError_t launch_path(bool tc, Variant v, const KernelParams& kp, int grid, cu
 }
 
 Variant variant_of(const gg_config* c) {
-  if (!c) return Variant::kUnsupported;
+  if (!c || (c->input_type != GG_INPUT_F16 && c->input_type != GG_INPUT_BF16)) return Variant::kUnsupported;
   return resolve_variant(c->cta_m, c->cta_n, c->cta_k, c->threads);
 }
 
@@ -445,6 +445,7 @@ int gg_executor_build(gg_executor* ex, const gg_problem* sorted_problems, int co
   kp.total_tiles = total_tiles;
   kp.raster_group = gg::raster_group();
   kp.single_mode = 0;
+  kp.input_format = config->input_type;
   return cudaSuccess;
 }
 
@@ -516,6 +517,7 @@ int gg_run_baseline_per_problem(const gg_problem* problems, int count, const gg_
     kp.total_tiles = tiles;
     kp.raster_group = gg::raster_group();
     kp.single_mode = 1;
+    kp.input_format = config->input_type;
     int grid = 0;
     const bool tc = config->use_tensor_cores != 0;
     cudaError_t st = gg::path_grid(tc, v, tiles, 0, &grid);
@@ -761,6 +763,7 @@ extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count
   kp.total_tiles = total;
   kp.raster_group = gg::raster_group();
   kp.single_mode = 0;
+  kp.input_format = config->input_type;
   return gg::launch_path(config->use_tensor_cores != 0, v, kp, grid, s);
 }
 
@@ -1049,6 +1052,7 @@ int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, g
   kp.total_tiles = 0;
   kp.raster_group = gg::raster_group();
   kp.single_mode = 0;
+  kp.input_format = config->input_type;
   *out = plan;
   return cudaSuccess;
 }

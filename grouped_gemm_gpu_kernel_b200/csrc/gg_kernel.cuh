@@ -657,7 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
   } else if (warp == kMmaWarp) {
     // ======================= MMA issuer =======================
     if (lane == 0) {
-      constexpr uint32_t kIdesc = ptx::idesc_f16_f32_kA_mnB(kMmaM, BN);
+      const uint32_t kIdesc = ptx::idesc_f16_f32_kA_mnB(kMmaM, BN, static_cast<uint32_t>(p.input_format));
       uint32_t it = 0;
       for (int t = 0;; ++t) {
         const int slot = t % kRing;

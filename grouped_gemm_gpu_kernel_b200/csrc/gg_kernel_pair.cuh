@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kMmaWarp) {
     // ======================= MMA issuer (leader only) =======================
     if (leader && lane == 0) {
-      constexpr uint32_t kIdesc = ptx::idesc_f16_f32_kA_mnB(256, BN);
+      const uint32_t kIdesc = ptx::idesc_f16_f32_kA_mnB(256, BN, static_cast<uint32_t>(p.input_format));
       uint32_t it = 0;
       for (int t = 0;; ++t) {
         const int slot = t % kRing;

@@ -96,6 +96,7 @@ struct KernelParams {
   int total_tiles;
   int raster_group;  // M-tiles per raster group inside a problem (L2 reuse of A and B panels)
   int single_mode;   // 1: baseline launch, tiles blockIdx.x + i*gridDim.x of single_desc
+  int input_format;  // A and B element type: 0 = FP16, 1 = BF16 (GG_INPUT_*)
 };
 
 }  // namespace gg

@@ -283,11 +283,12 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
-// Instruction descriptor for kind::f16 with FP16 A and B, FP32 D, A K-major, B MN-major:
-// D format in bits [4,6) (1 = F32), A/B formats [7,10) / [10,13) (0 = F16), A major bit 15
-// (0 = K), B major bit 16 (1 = MN), N >> 3 in [17,23), M >> 4 in [24,29).
-__host__ __device__ constexpr uint32_t idesc_f16_f32_kA_mnB(int m, int n) {
-  return (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | (1u << 16) |
+// Instruction descriptor for kind::f16 with 16-bit A and B (ab_format 0 = FP16, 1 = BF16, the
+// same for both), FP32 D, A K-major, B MN-major: D format in bits [4,6) (1 = F32), A/B formats
+// [7,10) / [10,13), A major bit 15 (0 = K), B major bit 16 (1 = MN), N >> 3 in [17,23), M >> 4 in
+// [24,29).
+__host__ __device__ constexpr uint32_t idesc_f16_f32_kA_mnB(int m, int n, uint32_t ab_format = 0u) {
+  return (1u << 4) | (ab_format << 7) | (ab_format << 10) | (0u << 15) | (1u << 16) |
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 

@@ -5,9 +5,9 @@
 // Same contract as the tensor-core kernel: the same tile_offsets and tile numbering (the config's
 // cta_m x cta_n tiles), the same atomic tile claims and problem lookup (reference
 // src/grouped_gemm.cu:219-234, 640-675), the same epilogue D = alpha*acc + beta*C with C read only
-// when c != nullptr and beta != 0 (reference src/grouped_gemm.cu:460-481). FP16 operands are
-// widened to FP32 and accumulated with FP32 FMA (an FP16 x FP16 product is exact in FP32), so the
-// result differs from the tensor-core path only in the order of the FP32 additions.
+// when c != nullptr and beta != 0 (reference src/grouped_gemm.cu:460-481). FP16 (or BF16) operands
+// are widened to FP32 and accumulated with FP32 FMA (a product of two 16-bit values is exact in
+// FP32), so the result differs from the tensor-core path only in the order of the FP32 additions.
 //
 // A CTA computes its tile as 64 x 64 sub-tiles: 256 threads, each 4 x 4 outputs; K in steps of 32
 // through shared memory (A stored k-major so a thread reads its 4 rows with one 16-byte load),
@@ -25,6 +25,12 @@ constexpr int kSimtThreads = 256;
 constexpr int kSub = 64;     // sub-tile edge
 constexpr int kSimtBK = 32;  // K per shared-memory step
 constexpr int kPad = 4;      // keeps 16-byte alignment of every row, spreads banks
+
+// One 16-bit operand element widened to FP32 (FP16, or BF16: its bits are the top half of an FP32).
+__device__ __forceinline__ float widen(const __half* x, long long i, bool bf16) {
+  if (bf16) return __uint_as_float(static_cast<unsigned>(reinterpret_cast<const unsigned short*>(x)[i]) << 16);
+  return __half2float(x[i]);
+}
 
 // Last q with offs[q] <= tile (offs has count + 1 entries, offs[count] = total > tile).
 __device__ int find_problem(const int* offs, int count, int tile) {
@@ -47,6 +53,7 @@ __global__ void __launch_bounds__(kSimtThreads) grouped_gemm_simt_kernel(const _
   const int total = p.total_tiles_dev ? *p.total_tiles_dev : p.total_tiles;
   const int tid = static_cast<int>(threadIdx.x);
   const int tx = tid & 15, ty = tid >> 4;
+  const bool bf16 = p.input_format == 1;
   int static_next = static_cast<int>(blockIdx.x);
 
   for (;;) {
@@ -104,12 +111,12 @@ __global__ void __launch_bounds__(kSimtThreads) grouped_gemm_simt_kernel(const _
           for (int i = tid; i < kSub * kSimtBK; i += kSimtThreads) {
             const int r = i / kSimtBK, kk = i % kSimtBK;
             const int gr = row0 + r, gk = k0 + kk;
-            As[kk][r] = (gr < m && gk < k) ? __half2float(a[static_cast<long long>(gr) * lda + gk]) : 0.0f;
+            As[kk][r] = (gr < m && gk < k) ? widen(a, static_cast<long long>(gr) * lda + gk, bf16) : 0.0f;
           }
           for (int i = tid; i < kSimtBK * kSub; i += kSimtThreads) {
             const int kk = i / kSub, c = i % kSub;
             const int gk = k0 + kk, gc = col0 + c;
-            Bs[kk][c] = (gk < k && gc < n) ? __half2float(b[static_cast<long long>(gk) * ldb + gc]) : 0.0f;
+            Bs[kk][c] = (gk < k && gc < n) ? widen(b, static_cast<long long>(gk) * ldb + gc, bf16) : 0.0f;
           }
           __syncthreads();
 #pragma unroll 8

@@ -31,6 +31,7 @@ gg_config to_c(const KernelConfig& c) {
   g.threads = c.threads;
   g.persistent_ctas = c.persistent_ctas;
   g.use_tensor_cores = c.use_tensor_cores ? 1 : 0;
+  g.input_type = GG_INPUT_F16;  // the reference's API is FP16 only; BF16 is a C-ABI extension
   return g;
 }
 

@@ -125,6 +125,17 @@ class DeviceProblemSet:
                                    max(1, k), max(1, n), max(1, n), max(1, n), al, be))
         return out
 
+    def to_bf16(self) -> "DeviceProblemSet":
+        """Re-encodes A and B in place as BF16 (each FP16 value rounded to the nearest BF16), for
+        runs with KernelConfig.input_type = 1. The slabs keep their torch dtype (float16) and now
+        hold BF16 bit patterns."""
+        import torch
+
+        for t in (self.a, self.b):
+            v = t.float()
+            t.view(torch.bfloat16).copy_(v)
+        return self
+
     def views(self, i: int):
         """(A, B, C or None, D) torch views of problem i."""
         m, n, k = self.shapes.dims[i]

@@ -66,7 +66,13 @@ typedef struct gg_problem {
  *   the reference's tiles  64x64x16, 128x64x32, 64x128x32  (same tile decomposition, run on the
  *                          same tcgen05 kernel; cta_k only selects the variant)
  * use_tensor_cores != 0 runs the tcgen05 tensor-core kernel; 0 runs the CUDA-core kernel (FP16
- * operands widened to FP32, FP32 FMA; the reference's SIMT path) with the same tile numbering. */
+ * operands widened to FP32, FP32 FMA; the reference's SIMT path) with the same tile numbering.
+ * input_type (no reference counterpart; the reference is FP16 only, and the C++ API of
+ * grouped_gemm/grouped_gemm.cuh keeps the reference's KernelConfig and always passes FP16): the
+ * element type of every A and B of the set, GG_INPUT_F16 (0) or GG_INPUT_BF16; any other value is
+ * an invalid config. C and D stay FP32 and the accumulation FP32 either way. */
+#define GG_INPUT_F16 0
+#define GG_INPUT_BF16 1
 typedef struct gg_config {
   int cta_m;
   int cta_n;
@@ -74,6 +80,7 @@ typedef struct gg_config {
   int threads;
   int persistent_ctas; /* > 0: fixed persistent grid size; 0: one CTA per SM slot, capped by tiles */
   int use_tensor_cores;
+  int input_type;      /* GG_INPUT_F16 or GG_INPUT_BF16 */
 } gg_config;
 
 /* Resource report; field-for-field the reference's OccupancyInfo (grouped_gemm.cuh:54-83). */

@@ -64,6 +64,10 @@ def load_oracle() -> ctypes.CDLL:
                                         _u16p, ctypes.c_int, _f32p, ctypes.c_int, ctypes.c_float,
                                         ctypes.c_float, _i32p, ctypes.c_int, _f64p, ctypes.c_int, _f64p]
         lib.oracle_gemm_f64.restype = None
+        lib.oracle_gemm_f64_fmt.argtypes = lib.oracle_gemm_f64.argtypes + [ctypes.c_int]
+        lib.oracle_gemm_f64_fmt.restype = None
+        lib.oracle_bf16_to_double.argtypes = [ctypes.c_uint16]
+        lib.oracle_bf16_to_double.restype = ctypes.c_double
         lib.oracle_gemm_f32_refloop.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, _u16p,
                                                 ctypes.c_int, _u16p, ctypes.c_int, _f32p, ctypes.c_int,
                                                 ctypes.c_float, ctypes.c_float, _f32p, ctypes.c_int]
@@ -151,8 +155,9 @@ def prepare(dims: Sequence[Sequence[int]], cta_m: int, cta_n: int, mode: int):
     return perm[:count], offs, int(total)
 
 
-def gemm_f64(m, n, k, a, lda, b, ldb, c, ldc, alpha, beta, rows=None):
-    """FP64 D (and the error scale) for one problem; `a`/`b` are uint16 FP16 bit arrays.
+def gemm_f64(m, n, k, a, lda, b, ldb, c, ldc, alpha, beta, rows=None, fmt=0):
+    """FP64 D (and the error scale) for one problem; `a`/`b` are uint16 bit arrays of FP16
+    (fmt 0) or BF16 (fmt 1) values.
 
     Returns (d, scale), each shaped (len(rows) or m, n).
     """
@@ -166,11 +171,11 @@ def gemm_f64(m, n, k, a, lda, b, ldb, c, ldc, alpha, beta, rows=None):
         return d[:nrows, :max(n, 0)], s[:nrows, :max(n, 0)]
     rows_arr = None if rows is None else np.ascontiguousarray(rows, dtype=np.int32)
     c_arr = None if c is None else np.ascontiguousarray(c, dtype=np.float32)
-    lib.oracle_gemm_f64(m, n, k, _ptr(a, ctypes.c_uint16), lda, _ptr(b, ctypes.c_uint16), ldb,
-                        None if c_arr is None else _ptr(c_arr, ctypes.c_float), ldc,
-                        float(alpha), float(beta),
-                        None if rows_arr is None else _ptr(rows_arr, ctypes.c_int), nrows,
-                        _ptr(d, ctypes.c_double), n, _ptr(s, ctypes.c_double))
+    lib.oracle_gemm_f64_fmt(m, n, k, _ptr(a, ctypes.c_uint16), lda, _ptr(b, ctypes.c_uint16), ldb,
+                            None if c_arr is None else _ptr(c_arr, ctypes.c_float), ldc,
+                            float(alpha), float(beta),
+                            None if rows_arr is None else _ptr(rows_arr, ctypes.c_int), nrows,
+                            _ptr(d, ctypes.c_double), n, _ptr(s, ctypes.c_double), int(fmt))
     return d, s
 
 

@@ -12,7 +12,8 @@
  *         D = alpha * (A x B) + beta * C, with C read only when c != NULL and beta != 0
  *   - the reference's host GEMM reference tests/test_correctness.cu:85-102 (FP32, natural k order,
  *         always reads C) -- restated as oracle_gemm_f32_refloop for the "port" CPU baseline.
- * The accuracy judge is oracle_gemm_f64: FP16 inputs decoded exactly, products and sums in FP64.
+ * The accuracy judge is oracle_gemm_f64: FP16 inputs decoded exactly, products and sums in FP64
+ * (oracle_gemm_f64_fmt also takes BF16 inputs, for the library's BF16 extension).
  *
  * Parity pin: tests/test_oracle.py checks every function here against the reference's own host
  * code compiled from its sources (oracle/Makefile -> oracle/_ref/libgg_ref.so) and against the
@@ -40,6 +41,16 @@ static double half_bits_to_double(uint16_t h) {
 }
 
 double oracle_half_to_double(uint16_t h) { return half_bits_to_double(h); }
+
+/* BF16 is the top half of an IEEE binary32: the value is exact as a float. */
+static double bf16_bits_to_double(uint16_t h) {
+  const uint32_t w = (uint32_t)h << 16;
+  float f;
+  memcpy(&f, &w, sizeof f);
+  return (double)f;
+}
+
+double oracle_bf16_to_double(uint16_t h) { return bf16_bits_to_double(h); }
 
 /* ---- tile counting: reference src/grouped_gemm.cu:54-65 ---------------------------------- */
 static int ceil_div_int(int x, int y) { return (x + y - 1) / y; }
@@ -126,9 +137,11 @@ int oracle_prepare(const int* m, const int* n, const int* k, int count, int cta_
  *   scale[r*ldd + j] = |alpha| * sqrt(sum_k (A[row,k]*B[k,j])^2) + |beta * C[row,j]|
  * 'r' indexes the output rows (0..nrows-1), 'row' the problem row. 'scale' (nullable) is the
  * magnitude that the relative-error metric of the tests divides by when |d| is small. */
-void oracle_gemm_f64(int m, int n, int k, const uint16_t* a, int lda, const uint16_t* b, int ldb,
-                     const float* c, int ldc, float alpha, float beta, const int* rows, int nrows,
-                     double* d, int ldd, double* scale) {
+/* As oracle_gemm_f64, with A and B in the 16-bit format `fmt` (0 = FP16, 1 = BF16). */
+void oracle_gemm_f64_fmt(int m, int n, int k, const uint16_t* a, int lda, const uint16_t* b, int ldb,
+                         const float* c, int ldc, float alpha, float beta, const int* rows, int nrows,
+                         double* d, int ldd, double* scale, int fmt) {
+  double (*decode)(uint16_t) = fmt == 1 ? bf16_bits_to_double : half_bits_to_double;
   if (m <= 0 || n <= 0) return;
   if (!rows) nrows = m;
   const int read_c = (c != NULL) && (beta != 0.0f);
@@ -141,9 +154,9 @@ void oracle_gemm_f64(int m, int n, int k, const uint16_t* a, int lda, const uint
     memset(acc, 0, (size_t)n * sizeof(double));
     memset(sq, 0, (size_t)n * sizeof(double));
     for (int kk = 0; kk < k; ++kk) {
-      const double av = half_bits_to_double(a[(int64_t)row * lda + kk]);
+      const double av = decode(a[(int64_t)row * lda + kk]);
       const uint16_t* bp = b + (int64_t)kk * ldb;
-      for (int j = 0; j < n; ++j) brow[j] = half_bits_to_double(bp[j]);
+      for (int j = 0; j < n; ++j) brow[j] = decode(bp[j]);
       for (int j = 0; j < n; ++j) {
         const double p = av * brow[j];
         acc[j] += p;
@@ -159,6 +172,12 @@ void oracle_gemm_f64(int m, int n, int k, const uint16_t* a, int lda, const uint
   free(acc);
   free(sq);
   free(brow);
+}
+
+void oracle_gemm_f64(int m, int n, int k, const uint16_t* a, int lda, const uint16_t* b, int ldb,
+                     const float* c, int ldc, float alpha, float beta, const int* rows, int nrows,
+                     double* d, int ldd, double* scale) {
+  oracle_gemm_f64_fmt(m, n, k, a, lda, b, ldb, c, ldc, alpha, beta, rows, nrows, d, ldd, scale, 0);
 }
 
 /* ---- the reference's host GEMM, restated (tests/test_correctness.cu:85-102) ---------------

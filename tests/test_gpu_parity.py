@@ -69,8 +69,9 @@ class HostSlabs:
         return a, b, c, d
 
 
-def check_full(ps: W.DeviceProblemSet, threads: int = 8) -> float:
-    """Every element of every problem against the FP64 oracle; returns the worst error/tolerance."""
+def check_full(ps: W.DeviceProblemSet, threads: int = 8, fmt: int = 0) -> float:
+    """Every element of every problem against the FP64 oracle; returns the worst error/tolerance.
+    fmt: the A/B element type of the run (0 FP16, 1 BF16)."""
     hs = HostSlabs(ps)
 
     def one(i):
@@ -78,7 +79,8 @@ def check_full(ps: W.DeviceProblemSet, threads: int = 8) -> float:
         if m <= 0 or n <= 0:
             return 0.0
         a, b, c, d = hs.problem(i)
-        ref, scale = O.gemm_f64(m, n, k, a, max(1, k), b, max(1, n), c, max(1, n), ps.shapes.alpha[i], ps.shapes.beta[i])
+        ref, scale = O.gemm_f64(m, n, k, a, max(1, k), b, max(1, n), c, max(1, n), ps.shapes.alpha[i], ps.shapes.beta[i],
+                                fmt=fmt)
         return O.rel_err(d.reshape(m, n), ref, scale) / O.tolerance(k)
 
     with ThreadPoolExecutor(threads) as pool:
@@ -86,7 +88,7 @@ def check_full(ps: W.DeviceProblemSet, threads: int = 8) -> float:
     return worst
 
 
-def check_sampled(ps: W.DeviceProblemSet, rows_per=4, cols_per=96, seed=0, threads=8) -> float:
+def check_sampled(ps: W.DeviceProblemSet, rows_per=4, cols_per=96, seed=0, threads=8, fmt=0) -> float:
     rng = np.random.default_rng(seed)
     jobs = []
     for i, (m, n, k) in enumerate(ps.shapes.dims):
@@ -99,7 +101,8 @@ def check_sampled(ps: W.DeviceProblemSet, rows_per=4, cols_per=96, seed=0, threa
 
     def one(job):
         i, r, c, k, h = job
-        ref, scale = O.gemm_f64(r, c, k, h["a"], max(1, k), h["b"], c, h["c"], c, ps.shapes.alpha[i], ps.shapes.beta[i])
+        ref, scale = O.gemm_f64(r, c, k, h["a"], max(1, k), h["b"], c, h["c"], c, ps.shapes.alpha[i], ps.shapes.beta[i],
+                                fmt=fmt)
         return O.rel_err(h["d"], ref, scale) / O.tolerance(k)
 
     with ThreadPoolExecutor(threads) as pool:
@@ -423,6 +426,43 @@ def test_cuda_core_path_mixed512_sampled_and_occupancy(cuda):
     st, info = gg.query_occupancy(cfg)
     assert st == 0 and not info.using_tensor_cores and info.threads_per_block == 256
     assert info.active_blocks_per_sm >= 1 and info.dynamic_shared_bytes == 0
+
+
+BF16_CONFIGS = [gg.KernelConfig(128, 256, 64, input_type=1), gg.KernelConfig(128, 128, 64, input_type=1),
+                gg.KernelConfig(256, 256, 64, input_type=1), gg.KernelConfig(64, 64, 16, input_type=1),
+                gg.KernelConfig(128, 128, 64, use_tensor_cores=False, input_type=1)]
+
+
+@pytest.mark.parametrize("cfg", BF16_CONFIGS,
+                         ids=lambda c: f"{'' if c.use_tensor_cores else 'simt'}{c.cta_m}x{c.cta_n}")
+def test_bf16_inputs_match_oracle(cuda, cfg):
+    """input_type = 1 (BF16 A and B; an extension, the reference is FP16 only): small16 and
+    tiny4096 in full (TMA-ineligible odd ld -> zero-fill loader), mixed512 sampled, and the
+    per-problem baseline, against the FP64 oracle decoding BF16."""
+    for wl in ("small16", "tiny4096"):
+        ps = W.allocate(W.make_shapes(wl), cuda).to_bf16()
+        run_grouped(ps.problems(), cfg, gg.SortMode.kByK)
+        assert check_full(ps, fmt=1) <= 1.0
+    ps = W.allocate(W.make_shapes("small16"), cuda).to_bf16()
+    assert gg.run_baseline_per_problem(ps.problems(), cfg) == 0
+    _torch().cuda.synchronize()
+    assert check_full(ps, fmt=1) <= 1.0
+    ps = W.allocate(W.make_shapes("mixed512"), cuda).to_bf16()
+    run_grouped(ps.problems(), cfg, gg.SortMode.kByK)
+    assert check_sampled(ps, fmt=1) <= 1.0
+
+
+def test_bf16_and_fp16_reads_differ(cuda):
+    """The same bits read as BF16 and as FP16 give different products: input_type reaches the MMA."""
+    torch = _torch()
+    ps = W.allocate(W.make_shapes("small16"), cuda).to_bf16()
+    run_grouped(ps.problems(), gg.KernelConfig(128, 128, 64, input_type=1), gg.SortMode.kNone)
+    as_bf16 = ps.d.clone()
+    run_grouped(ps.problems(), gg.KernelConfig(128, 128, 64, input_type=0), gg.SortMode.kNone)
+    finite = torch.isfinite(as_bf16) & torch.isfinite(ps.d)
+    assert not torch.equal(as_bf16[finite], ps.d[finite])
+    st, _ = gg.query_occupancy(gg.KernelConfig(128, 128, 64, input_type=2))
+    assert st == 1  # an unknown input type is an invalid config
 
 
 def test_zero_dim_problems_untouched(cuda):

@@ -264,3 +264,13 @@ def test_moe_plan_create_rejects_bad_arguments_before_device_work():
     prob = capi.GGMoeProblem(**good)
     assert lib.gg_moe_plan_create(ctypes.byref(prob), ctypes.byref(bad_cfg), ctypes.byref(h)) == 1
     assert lib.gg_moe_plan_run(None, None, None) == 17
+
+
+def test_input_type_is_validated_on_the_host():
+    """input_type must be GG_INPUT_F16 (0) or GG_INPUT_BF16 (1); anything else is an invalid config."""
+    for t, want in ((0, 0), (1, 0), (2, 1), (-1, 1)):
+        cfg = gg.KernelConfig(128, 128, 64, input_type=t)
+        ex = gg.GroupedGemmExecutor()
+        prep = gg.prepare_problem_set([], cfg, 0)
+        assert ex.build(prep, cfg) == want
+        ex.close()

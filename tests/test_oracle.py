@@ -172,3 +172,23 @@ def test_reference_host_gemm_matches_fixture():
         if p["m"] > 0 and p["n"] > 0:
             assert np.array_equal(d[:p["m"] * p["n"]], p["ref"][:p["m"] * p["n"]])
     assert secs >= 0.0
+
+
+def test_bf16_decode_and_gemm_against_numpy():
+    """oracle_gemm_f64 with BF16 inputs (fmt 1): exact decode (top half of a float32) and the same
+    FP64 result numpy gets from the decoded values."""
+    rng = np.random.default_rng(11)
+    m, n, k = 7, 5, 13
+    af = rng.uniform(-2, 2, size=(m, k)).astype(np.float32)
+    bf = rng.uniform(-2, 2, size=(k, n)).astype(np.float32)
+    a16 = (af.view(np.uint32) >> 16).astype(np.uint16)
+    b16 = (bf.view(np.uint32) >> 16).astype(np.uint16)
+    lib = O.load_oracle()
+    for bits in (0x3F80, 0xC000, 0x0001, 0x7F7F, 0x8000):
+        want = float(np.array([bits << 16], dtype=np.uint32).view(np.float32)[0])
+        assert lib.oracle_bf16_to_double(bits) == want
+    ad = (a16.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    bd = (b16.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    c = rng.uniform(-1, 1, size=(m, n)).astype(np.float32)
+    d, _ = O.gemm_f64(m, n, k, a16, k, b16, n, c, n, 1.5, -0.5, fmt=1)
+    assert np.allclose(d, 1.5 * ad @ bd - 0.5 * c.astype(np.float64), rtol=0, atol=1e-12)
