@@ -25,7 +25,8 @@ __all__ = [
     "SortMode", "ProblemDesc", "KernelConfig", "PreparedProblemSet", "OccupancyInfo", "GroupedGemmExecutor",
     "prepare_problem_set", "sort_mode_name", "query_occupancy", "run_grouped_gemm_once",
     "run_baseline_per_problem", "count_non_empty_problems", "partition", "ShardPiece", "problem_from_tensors",
-    "NATIVE_CONFIGS", "REFERENCE_CONFIGS", "PAIR_CONFIGS", "selftest_wait_timeout", "capi",
+    "NATIVE_CONFIGS", "REFERENCE_CONFIGS", "PAIR_CONFIGS", "selftest_wait_timeout", "capi", "MoePlan",
+    "InputType", "OutputType", "Activation",
 ]
 
 
@@ -34,6 +35,26 @@ class SortMode(enum.IntEnum):
     kByK = 1
     kByTiles = 2
     kByTilesThenK = 3
+
+
+class InputType(enum.IntEnum):
+    """Element type of every A and B (GG_INPUT_*); the reference's is FP16."""
+    kF16 = capi.GG_INPUT_F16
+    kBF16 = capi.GG_INPUT_BF16
+
+
+class OutputType(enum.IntEnum):
+    """Element type of every C and D (GG_OUTPUT_*); the reference's is FP32."""
+    kF32 = capi.GG_OUTPUT_F32
+    kF16 = capi.GG_OUTPUT_F16
+    kBF16 = capi.GG_OUTPUT_BF16
+
+
+class Activation(enum.IntEnum):
+    """Applied to D after the bias (GG_ACT_*); GELU is the tanh form."""
+    kNone = capi.GG_ACT_NONE
+    kReLU = capi.GG_ACT_RELU
+    kGELU = capi.GG_ACT_GELU
 
 
 @dataclass
@@ -71,11 +92,14 @@ class KernelConfig:
     threads: int = 256
     persistent_ctas: int = 0
     use_tensor_cores: bool = True
-    input_type: int = 0  # 0 = FP16 A/B (the reference's type), 1 = BF16
+    input_type: int = 0   # InputType: FP16 A/B (the reference's type) or BF16
+    output_type: int = 0  # OutputType: FP32 C/D (the reference's type), FP16 or BF16
+    activation: int = 0   # Activation applied after the bias
 
     def to_c(self) -> capi.GGConfig:
         return capi.GGConfig(self.cta_m, self.cta_n, self.cta_k, self.threads, self.persistent_ctas,
-                             1 if self.use_tensor_cores else 0, int(self.input_type))
+                             1 if self.use_tensor_cores else 0, int(self.input_type), int(self.output_type),
+                             int(self.activation))
 
 
 # The reference's three tile shapes (reference src/grouped_gemm.cu:67-81) and the sm_100a ones.
@@ -202,15 +226,24 @@ class GroupedGemmExecutor:
     def __exit__(self, *exc):
         self.close()
 
-    def build(self, prepared: PreparedProblemSet, config: KernelConfig) -> int:
+    def build(self, prepared: PreparedProblemSet, config: KernelConfig,
+              bias: Optional[Sequence[Optional[int]]] = None) -> int:
+        """bias (an extension; gg_executor_build_with_bias): one device pointer (or None) per sorted
+        problem, each to n FP32 values added to every row of that problem's D."""
         if not self._h:
             return capi.CUDA_ERROR_INVALID_DEVICE_POINTER
         count = len(prepared.sorted_problems)
         arr = _problems_array(prepared.sorted_problems)
         offs = (ctypes.c_int * max(1, len(prepared.tile_offsets)))(*prepared.tile_offsets)
         cfg = config.to_c()
-        return self._lib.gg_executor_build(self._h, arr, count, offs, len(prepared.tile_offsets),
-                                           int(prepared.total_tiles), ctypes.byref(cfg))
+        if bias is None:
+            return self._lib.gg_executor_build(self._h, arr, count, offs, len(prepared.tile_offsets),
+                                               int(prepared.total_tiles), ctypes.byref(cfg))
+        if len(bias) != count:
+            return capi.CUDA_ERROR_INVALID_VALUE
+        tbl = (ctypes.c_void_p * max(1, count))(*[ctypes.c_void_p(int(x) if x else None) for x in bias])
+        return self._lib.gg_executor_build_with_bias(self._h, arr, count, offs, len(prepared.tile_offsets),
+                                                     int(prepared.total_tiles), ctypes.byref(cfg), tbl)
 
     def run(self, stream=None) -> int:
         if not self._h:
@@ -274,21 +307,28 @@ class MoePlan:
     """Grouped GEMM whose per-problem row counts live on the device (gg_moe_plan_*).
 
     Problems share n and k; their rows are packed back to back in A (capacity_rows x k FP16),
-    C and D (capacity_rows x n FP32); expert e multiplies its rows by its own B[e] (k x n FP16).
+    C and D (capacity_rows x n FP32, or the config's output type); expert e multiplies its rows by
+    its own B[e] (k x n FP16) and, when bias_ptrs is given, adds its bias (n FP32 values, or None).
     `run(rows)` takes an int32 device tensor of `experts` row counts and enqueues the device-side
     preparation and the grouped kernel on the stream, with no host synchronisation.
     """
 
     def __init__(self, experts: int, n: int, k: int, capacity_rows: int, a: int, lda: int, b_ptrs: Sequence[int],
                  ldb: int, d: int, ldd: int, c: Optional[int] = None, ldc: Optional[int] = None,
-                 alpha: float = 1.0, beta: float = 0.0, config: Optional[KernelConfig] = None):
+                 alpha: float = 1.0, beta: float = 0.0, config: Optional[KernelConfig] = None,
+                 bias_ptrs: Optional[Sequence[Optional[int]]] = None):
         self._lib = capi.load()
         self._h = None
-        if len(b_ptrs) != experts:
-            raise ValueError("one B pointer per expert")
+        if len(b_ptrs) != experts or (bias_ptrs is not None and len(bias_ptrs) != experts):
+            raise ValueError("one B pointer (and bias pointer) per expert")
         bs = (ctypes.c_void_p * max(1, experts))(*[ctypes.c_void_p(int(x) if x else None) for x in b_ptrs])
+        bias_tbl = None
+        if bias_ptrs is not None:
+            bias_tbl = (ctypes.c_void_p * max(1, experts))(*[ctypes.c_void_p(int(x) if x else None)
+                                                             for x in bias_ptrs])
         prob = capi.GGMoeProblem(a, ctypes.cast(bs, ctypes.POINTER(ctypes.c_void_p)), c, d, experts, n, k,
-                                 capacity_rows, lda, ldb, ldc if ldc is not None else max(1, n), ldd, alpha, beta)
+                                 capacity_rows, lda, ldb, ldc if ldc is not None else max(1, n), ldd, alpha, beta,
+                                 ctypes.cast(bias_tbl, ctypes.POINTER(ctypes.c_void_p)) if bias_tbl else None)
         cfg = (config or KernelConfig(128, 256, 64)).to_c()
         h = ctypes.c_void_p()
         st = self._lib.gg_moe_plan_create(ctypes.byref(prob), ctypes.byref(cfg), ctypes.byref(h))
@@ -330,7 +370,8 @@ def selftest_wait_timeout(timeout_ns: int = 20_000_000):
 
 
 def problem_from_tensors(a, b, c, d, alpha: float = 1.0, beta: float = 0.0) -> ProblemDesc:
-    """ProblemDesc over torch tensors: a (m, k) fp16, b (k, n) fp16, c (m, n) fp32 or None, d (m, n) fp32.
+    """ProblemDesc over torch tensors: a (m, k) fp16, b (k, n) fp16, c (m, n) fp32 or None, d (m, n) fp32
+    (bf16 a/b and fp16/bf16 c/d with the matching KernelConfig input_type / output_type).
 
     Rows may be padded (row stride >= columns) but columns must be contiguous.
     """

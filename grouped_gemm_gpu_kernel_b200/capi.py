@@ -15,7 +15,8 @@ LIB_PATH = os.path.join(PKG, "libgrouped_gemm_b200.so")
 # Every declaration of include/grouped_gemm_b200.h; tests check the library exports each one.
 EXPORTED_SYMBOLS = (
     "gg_abi_version", "gg_sort_mode_name", "gg_tile_count", "gg_prepare", "gg_query_occupancy",
-    "gg_executor_create", "gg_executor_destroy", "gg_executor_build", "gg_executor_run",
+    "gg_executor_create", "gg_executor_destroy", "gg_executor_build", "gg_executor_build_with_bias",
+    "gg_executor_run",
     "gg_executor_problem_count", "gg_executor_total_tiles", "gg_executor_grid_ctas", "gg_executor_status",
     "gg_run_grouped_gemm_once", "gg_run_baseline_per_problem", "gg_count_non_empty_problems",
     "gg_partition", "gg_selftest_wait_timeout", "gg_run_grouped_gemm_noalloc", "gg_copy_rects",
@@ -24,6 +25,12 @@ EXPORTED_SYMBOLS = (
 GG_STATUS_BAD_ROWS = 0x100
 GG_INPUT_F16 = 0
 GG_INPUT_BF16 = 1
+GG_OUTPUT_F32 = 0
+GG_OUTPUT_F16 = 1
+GG_OUTPUT_BF16 = 2
+GG_ACT_NONE = 0
+GG_ACT_RELU = 1
+GG_ACT_GELU = 2
 GG_NOALLOC_MAX_PROBLEMS = 1024
 
 GG_STATUS_TIMEOUT_PRODUCER = 0x1
@@ -48,7 +55,7 @@ class GGProblem(ctypes.Structure):
 class GGConfig(ctypes.Structure):
     _fields_ = [("cta_m", ctypes.c_int), ("cta_n", ctypes.c_int), ("cta_k", ctypes.c_int),
                 ("threads", ctypes.c_int), ("persistent_ctas", ctypes.c_int), ("use_tensor_cores", ctypes.c_int),
-                ("input_type", ctypes.c_int)]
+                ("input_type", ctypes.c_int), ("output_type", ctypes.c_int), ("activation", ctypes.c_int)]
 
 
 class GGOccupancy(ctypes.Structure):
@@ -74,7 +81,8 @@ class GGMoeProblem(ctypes.Structure):
     _fields_ = [("a", ctypes.c_void_p), ("b", ctypes.POINTER(ctypes.c_void_p)), ("c", ctypes.c_void_p),
                 ("d", ctypes.c_void_p), ("experts", ctypes.c_int), ("n", ctypes.c_int), ("k", ctypes.c_int),
                 ("capacity_rows", ctypes.c_int), ("lda", ctypes.c_int), ("ldb", ctypes.c_int), ("ldc", ctypes.c_int),
-                ("ldd", ctypes.c_int), ("alpha", ctypes.c_float), ("beta", ctypes.c_float)]
+                ("ldd", ctypes.c_int), ("alpha", ctypes.c_float), ("beta", ctypes.c_float),
+                ("bias", ctypes.POINTER(ctypes.c_void_p))]
 
 
 _lib: Optional[ctypes.CDLL] = None
@@ -100,6 +108,8 @@ def load() -> ctypes.CDLL:
         "gg_executor_create": ([P(vp)], ctypes.c_int),
         "gg_executor_destroy": ([vp], None),
         "gg_executor_build": ([vp, pp, ctypes.c_int, i32p, ctypes.c_int, ctypes.c_int, pc], ctypes.c_int),
+        "gg_executor_build_with_bias": ([vp, pp, ctypes.c_int, i32p, ctypes.c_int, ctypes.c_int, pc, P(vp)],
+                                        ctypes.c_int),
         "gg_executor_run": ([vp, vp], ctypes.c_int),
         "gg_executor_problem_count": ([vp], ctypes.c_int),
         "gg_executor_total_tiles": ([vp], ctypes.c_int),

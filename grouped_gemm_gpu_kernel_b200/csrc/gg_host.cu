@@ -95,9 +95,11 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// 2-D row-major tensor (inner x outer elements, row pitch in bytes), 128-byte swizzled boxes.
+// 2-D row-major tensor (inner x outer elements, row pitch in bytes), swizzled boxes (128-byte
+// swizzle unless given).
 bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, int inner, int outer,
-               int64_t row_bytes, int box_inner, int box_outer) {
+               int64_t row_bytes, int box_inner, int box_outer,
+               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
   if (!enc || inner <= 0 || outer <= 0 || row_bytes <= 0 || (row_bytes % 16) != 0 || !aligned16(base)) return false;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
@@ -105,9 +107,33 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, int
   const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
   const cuuint32_t elem_strides[2] = {1, 1};
   const CUresult r = enc(map, type, 2, const_cast<void*>(base), dims, strides, box, elem_strides,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// Bytes of one C or D element in output format `fmt` (GG_OUTPUT_*).
+int out_bytes(int fmt) { return fmt == GG_OUTPUT_F32 ? 4 : 2; }
+
+bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
+
+// The D store map: 32 columns x 32 rows per box, in the staging layout of the epilogue (128-byte
+// rows with the 128-byte swizzle for FP32, 64-byte rows with the 64-byte swizzle for 16-bit D).
+bool encode_d(CUtensorMap* map, int fmt, const void* base, int n, int rows, int ldd) {
+  const CUtensorMapDataType t = fmt == GG_OUTPUT_F16    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                : fmt == GG_OUTPUT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  return encode_2d(map, t, base, n, rows, static_cast<int64_t>(ldd) * out_bytes(fmt), 32, 32,
+                   fmt == GG_OUTPUT_F32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
+// Vector-access flags of C and D in format fmt: C read 16 bytes at a time (so 16-bit C needs
+// rows a multiple of 8 elements apart), D written 4 elements at a time.
+unsigned vector_flags(int fmt, const void* c, int ldc, const void* d, int ldd) {
+  unsigned f = 0;
+  if (aligned16(c) && (ldc % (fmt == GG_OUTPUT_F32 ? 4 : 8)) == 0) f |= grouped_gemm::kFlagCVec;
+  if ((fmt == GG_OUTPUT_F32 ? aligned16(d) : aligned8(d)) && (ldd % 4) == 0) f |= grouped_gemm::kFlagDVec;
+  return f;
 }
 
 // B (k x n FP16, row pitch ldb) seen as 64 columns x k rows x (n / 64) full column chunks, the
@@ -131,7 +157,7 @@ bool encode_b_chunks(CUtensorMap* map, const void* base, int k, int n, int64_t r
 // Device record of one problem plus its kMapsPerProblem tensor maps. TMA is used for A/B only
 // when both operands qualify, for D when it qualifies; everything else takes the zero-fill load
 // path and masked direct stores.
-DeviceProblemDesc make_device_problem(const gg_problem& p, Variant v, CUtensorMap* maps, int map_slot) {
+DeviceProblemDesc make_device_problem(const gg_problem& p, Variant v, int out_fmt, CUtensorMap* maps, int map_slot) {
   const int bm = variant_bm(v), bn = variant_bn(v);
   const int cta_rows = variant_cta_rows(v);  // A and D rows one CTA moves per tile
   const int cta_cols = variant_cta_cols(v);  // B columns one CTA loads per tile
@@ -165,13 +191,9 @@ DeviceProblemDesc make_device_problem(const gg_problem& p, Variant v, CUtensorMa
     if (encode_b_chunks(&maps[kMapB3], p.b, p.k, p.n, static_cast<int64_t>(p.ldb) * 2, cta_cols / 64))
       flags |= grouped_gemm::kFlagTmaB3;
   }
-  if (has_tiles &&
-      encode_2d(&maps[kMapD], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.d, p.n, p.m, static_cast<int64_t>(p.ldd) * 4, 32,
-                32))
-    flags |= grouped_gemm::kFlagTmaD;
+  if (has_tiles && encode_d(&maps[kMapD], out_fmt, p.d, p.n, p.m, p.ldd)) flags |= grouped_gemm::kFlagTmaD;
   if (p.c != nullptr && p.beta != 0.0f) flags |= grouped_gemm::kFlagReadC;
-  if (aligned16(p.c) && (p.ldc % 4) == 0) flags |= grouped_gemm::kFlagCVec;
-  if (aligned16(p.d) && (p.ldd % 4) == 0) flags |= grouped_gemm::kFlagDVec;
+  flags |= vector_flags(out_fmt, p.c, p.ldc, p.d, p.ldd);
   d.flags = flags;
   return d;
 }
@@ -232,7 +254,18 @@ cudaError_t launch_path(bool tc, Variant v, const KernelParams& kp, int grid, cu
 
 Variant variant_of(const gg_config* c) {
   if (!c || (c->input_type != GG_INPUT_F16 && c->input_type != GG_INPUT_BF16)) return Variant::kUnsupported;
+  if (c->output_type != GG_OUTPUT_F32 && c->output_type != GG_OUTPUT_F16 && c->output_type != GG_OUTPUT_BF16)
+    return Variant::kUnsupported;
+  if (c->activation != GG_ACT_NONE && c->activation != GG_ACT_RELU && c->activation != GG_ACT_GELU)
+    return Variant::kUnsupported;
   return resolve_variant(c->cta_m, c->cta_n, c->cta_k, c->threads);
+}
+
+// The data-type and epilogue fields of a launch, from a validated config.
+void set_formats(KernelParams& kp, const gg_config* c) {
+  kp.input_format = c->input_type;
+  kp.output_format = c->output_type;
+  kp.activation = c->activation;
 }
 
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -370,6 +403,13 @@ void gg_executor_destroy(gg_executor* executor) {
 
 int gg_executor_build(gg_executor* ex, const gg_problem* sorted_problems, int count, const int* tile_offsets,
                       int offsets_len, int total_tiles, const gg_config* config) {
+  return gg_executor_build_with_bias(ex, sorted_problems, count, tile_offsets, offsets_len, total_tiles, config,
+                                     nullptr);
+}
+
+int gg_executor_build_with_bias(gg_executor* ex, const gg_problem* sorted_problems, int count,
+                                const int* tile_offsets, int offsets_len, int total_tiles, const gg_config* config,
+                                const float* const* bias) {
   if (!ex) return cudaErrorInvalidDevicePointer;
   const gg::Variant v = gg::variant_of(config);
   if (v == gg::Variant::kUnsupported) return cudaErrorInvalidValue;
@@ -390,7 +430,7 @@ int gg_executor_build(gg_executor* ex, const gg_problem* sorted_problems, int co
     const gg_problem& p = sorted_problems[i];
     if (p.m < 0 || p.n < 0 || p.k < 0) return cudaErrorInvalidValue;
     if (!p.a || !p.b || !p.d) return cudaErrorInvalidDevicePointer;
-    descs[static_cast<size_t>(i)] = gg::make_device_problem(p, v, &maps[static_cast<size_t>(i) * gg::kMapsPerProblem], i);
+    descs[static_cast<size_t>(i)] = gg::make_device_problem(p, v, config->output_type, &maps[static_cast<size_t>(i) * gg::kMapsPerProblem], i);
   }
   if (count == 0 || total_tiles <= 0) {
     ex->problem_count = count;
@@ -406,11 +446,13 @@ int gg_executor_build(gg_executor* ex, const gg_problem* sorted_problems, int co
   const size_t descs_off = gg::round_up(maps_bytes, 128);
   const size_t offs_off = gg::round_up(descs_off + descs.size() * sizeof(DeviceProblemDesc), 128);
   const size_t counter_off = gg::round_up(offs_off + static_cast<size_t>(offsets_len) * sizeof(int), 128);
-  const size_t bytes = counter_off + 128;
+  const size_t bias_off = counter_off + 128;  // bias table (one pointer per problem), when given
+  const size_t bytes = bias_off + (bias ? static_cast<size_t>(count) * sizeof(const float*) : 0);
   std::vector<unsigned char> image(bytes, 0);
   std::memcpy(image.data(), maps.data(), maps_bytes);
   std::memcpy(image.data() + descs_off, descs.data(), descs.size() * sizeof(DeviceProblemDesc));
   std::memcpy(image.data() + offs_off, tile_offsets, static_cast<size_t>(offsets_len) * sizeof(int));
+  if (bias) std::memcpy(image.data() + bias_off, bias, static_cast<size_t>(count) * sizeof(const float*));
 
   st = cudaMalloc(&ex->block, bytes);
   if (st != cudaSuccess) {
@@ -445,7 +487,8 @@ int gg_executor_build(gg_executor* ex, const gg_problem* sorted_problems, int co
   kp.total_tiles = total_tiles;
   kp.raster_group = gg::raster_group();
   kp.single_mode = 0;
-  kp.input_format = config->input_type;
+  gg::set_formats(kp, config);
+  kp.bias = bias ? reinterpret_cast<const float* const*>(base + bias_off) : nullptr;
   return cudaSuccess;
 }
 
@@ -509,7 +552,7 @@ int gg_run_baseline_per_problem(const gg_problem* problems, int count, const gg_
       if (!status) return cudaErrorMemoryAllocation;
     }
     std::memset(&kp, 0, sizeof(kp));
-    kp.single_desc = gg::make_device_problem(p, v, kp.single_maps, 0);
+    kp.single_desc = gg::make_device_problem(p, v, config->output_type, kp.single_maps, 0);
     const int tiles = kp.single_desc.tiles_m * kp.single_desc.tiles_n;
     kp.status = status;
     kp.timeout_ns = gg::wait_timeout_ns();
@@ -517,7 +560,7 @@ int gg_run_baseline_per_problem(const gg_problem* problems, int count, const gg_
     kp.total_tiles = tiles;
     kp.raster_group = gg::raster_group();
     kp.single_mode = 1;
-    kp.input_format = config->input_type;
+    gg::set_formats(kp, config);
     int grid = 0;
     const bool tc = config->use_tensor_cores != 0;
     cudaError_t st = gg::path_grid(tc, v, tiles, 0, &grid);
@@ -722,7 +765,7 @@ extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count
   for (int s = 0; s < count; ++s) {
     const gg_problem& p = problems[gg::g_noalloc_order[s]];
     offs[s + 1] = offs[s] + gg::tile_count(p.m, p.n, config->cta_m, config->cta_n);
-    descs[s] = gg::make_device_problem(p, v, &maps[static_cast<size_t>(s) * gg::kMapsPerProblem], s);
+    descs[s] = gg::make_device_problem(p, v, config->output_type, &maps[static_cast<size_t>(s) * gg::kMapsPerProblem], s);
   }
   const int total = offs[count];
   if (total == 0) return cudaSuccess;
@@ -763,7 +806,7 @@ extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count
   kp.total_tiles = total;
   kp.raster_group = gg::raster_group();
   kp.single_mode = 0;
-  kp.input_format = config->input_type;
+  gg::set_formats(kp, config);
   return gg::launch_path(config->use_tensor_cores != 0, v, kp, grid, s);
 }
 
@@ -811,12 +854,12 @@ __device__ T block_exclusive_scan(T v, T* warp_sums, T* total) {
 // Problem record of expert e whose rows start at row0 of the packed tensors.
 __device__ __forceinline__ DeviceProblemDesc moe_record(const DeviceProblemDesc* templ, int e, int r, long long row0,
                                                         int tm, int tiles_n, int t, int capacity, const __half* a,
-                                                        int lda, const float* c, int ldc, float* d, int ldd) {
+                                                        int lda, const void* c, int ldc, void* d, int ldd, int eb) {
   DeviceProblemDesc p = templ[e];
   p.m = r;
   p.a = a + row0 * lda;
-  p.c = c ? c + row0 * ldc : nullptr;
-  p.d = d + row0 * ldd;
+  p.c = c ? static_cast<const char*>(c) + row0 * ldc * eb : nullptr;
+  p.d = static_cast<char*>(d) + row0 * ldd * eb;
   p.tiles_m = t > 0 ? tm : 0;
   p.tiles_n = t > 0 ? tiles_n : 0;
   p.tma_row0 = static_cast<int>(row0 < capacity ? row0 : capacity);
@@ -830,8 +873,8 @@ __device__ __forceinline__ DeviceProblemDesc moe_record(const DeviceProblemDesc*
 __global__ void __launch_bounds__(kMoePrepThreads) moe_prepare_kernel(
     const int* __restrict__ rows, int experts, int capacity, int bm, int tiles_n,
     const DeviceProblemDesc* __restrict__ templ, DeviceProblemDesc* __restrict__ descs, int* __restrict__ offsets,
-    int* total_tiles, int* counter, int* status, const __half* a, int lda, const float* c, int ldc, float* d,
-    int ldd) {
+    int* total_tiles, int* counter, int* status, const __half* a, int lda, const void* c, int ldc, void* d,
+    int ldd, int eb) {
   __shared__ long long s_rows[kMoePrepThreads / 32];
   __shared__ int s_tiles[kMoePrepThreads / 32];
   __shared__ long long s_key[kMoePrepThreads];
@@ -879,7 +922,7 @@ __global__ void __launch_bounds__(kMoePrepThreads) moe_prepare_kernel(
     if (se >= 0) {
       const int sr = max(rows[se], 0);
       const int stm = sr > 0 ? (sr + bm - 1) / bm : 0;
-      descs[tid] = moe_record(templ, se, sr, s_row0[se], stm, tiles_n, st, capacity, a, lda, c, ldc, d, ldd);
+      descs[tid] = moe_record(templ, se, sr, s_row0[se], stm, tiles_n, st, capacity, a, lda, c, ldc, d, ldd, eb);
       offsets[tid] = t0;
     }
   } else {
@@ -897,7 +940,7 @@ __global__ void __launch_bounds__(kMoePrepThreads) moe_prepare_kernel(
       const long long row0 = row_carry + block_exclusive_scan<long long>(r, s_rows, &rows_total);
       const int t0 = tile_carry + block_exclusive_scan<int>(t, s_tiles, &tiles_total);
       if (e < experts) {
-        descs[e] = moe_record(templ, e, r, row0, tm, tiles_n, t, capacity, a, lda, c, ldc, d, ldd);
+        descs[e] = moe_record(templ, e, r, row0, tm, tiles_n, t, capacity, a, lda, c, ldc, d, ldd, eb);
         offsets[e] = t0;
       }
       row_carry += rows_total;
@@ -930,6 +973,7 @@ struct gg_moe_plan {
   bool use_tc = true;
   int grid_ctas = 0;
   int tiles_n = 0;
+  int out_bytes = 4;  // bytes of a C / D element
   gg::KernelParams params{};
 };
 
@@ -959,8 +1003,7 @@ int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, g
   const bool tma_a = rows_exist && q.k > 0 &&
                      gg::encode_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, q.a, q.k, q.capacity_rows,
                                    static_cast<int64_t>(q.lda) * 2, gg::kBK, cta_rows);
-  const bool tma_d = rows_exist && gg::encode_2d(&map_d, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, q.d, q.n, q.capacity_rows,
-                                                 static_cast<int64_t>(q.ldd) * 4, 32, 32);
+  const bool tma_d = rows_exist && gg::encode_d(&map_d, config->output_type, q.d, q.n, q.capacity_rows, q.ldd);
   for (size_t e = 0; e < E; ++e) {
     CUtensorMap* m = &maps[e * gg::kMapsPerProblem];
     DeviceProblemDesc& p = templ[e];
@@ -992,8 +1035,7 @@ int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, g
       flags |= grouped_gemm::kFlagTmaD;
     }
     if (q.c != nullptr && q.beta != 0.0f) flags |= grouped_gemm::kFlagReadC;
-    if (gg::aligned16(q.c) && (q.ldc % 4) == 0) flags |= grouped_gemm::kFlagCVec;
-    if (gg::aligned16(q.d) && (q.ldd % 4) == 0) flags |= grouped_gemm::kFlagDVec;
+    flags |= gg::vector_flags(config->output_type, q.c, q.ldc, q.d, q.ldd);
     p.flags = flags;
   }
 
@@ -1007,10 +1049,12 @@ int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, g
   const size_t descs_off = gg::round_up(templ_off + E * sizeof(DeviceProblemDesc), 128);
   const size_t offs_off = gg::round_up(descs_off + E * sizeof(DeviceProblemDesc), 128);
   const size_t words_off = gg::round_up(offs_off + (E + 1) * sizeof(int), 128);
-  const size_t bytes = words_off + 128;
+  const size_t bias_off = words_off + 128;  // bias table (one pointer per expert), when given
+  const size_t bytes = bias_off + (q.bias ? E * sizeof(const float*) : 0);
   std::vector<unsigned char> image(bytes, 0);
   std::memcpy(image.data(), maps.data(), maps_bytes);
   std::memcpy(image.data() + templ_off, templ.data(), E * sizeof(DeviceProblemDesc));
+  if (q.bias) std::memcpy(image.data() + bias_off, q.bias, E * sizeof(const float*));
 
   gg_moe_plan* plan = new (std::nothrow) gg_moe_plan();
   if (!plan) return cudaErrorMemoryAllocation;
@@ -1033,7 +1077,9 @@ int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, g
   plan->d_counter = reinterpret_cast<int*>(base + words_off + 4);
   plan->d_status = reinterpret_cast<int*>(base + words_off + 8);
   plan->problem = q;
-  plan->problem.b = nullptr;  // the host array is not kept
+  plan->problem.b = nullptr;  // the host arrays are not kept
+  plan->problem.bias = nullptr;
+  plan->out_bytes = gg::out_bytes(config->output_type);
   plan->variant = v;
   plan->use_tc = use_tc;
   plan->grid_ctas = grid;
@@ -1052,7 +1098,8 @@ int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, g
   kp.total_tiles = 0;
   kp.raster_group = gg::raster_group();
   kp.single_mode = 0;
-  kp.input_format = config->input_type;
+  gg::set_formats(kp, config);
+  kp.bias = q.bias ? reinterpret_cast<const float* const*>(base + bias_off) : nullptr;
   *out = plan;
   return cudaSuccess;
 }
@@ -1065,7 +1112,7 @@ int gg_moe_plan_run(gg_moe_plan* plan, const int* rows, void* stream) {
   gg::moe_prepare_kernel<<<1, gg::kMoePrepThreads, 0, s>>>(
       rows, q.experts, q.capacity_rows, gg::variant_bm(plan->variant), plan->tiles_n, plan->d_templ, plan->d_descs,
       plan->d_offsets, plan->d_total, plan->d_counter, plan->d_status, static_cast<const __half*>(q.a), q.lda, q.c,
-      q.ldc, q.d, q.ldd);
+      q.ldc, q.d, q.ldd, plan->out_bytes);
   cudaError_t st = cudaGetLastError();
   if (st != cudaSuccess) return st;
   return gg::launch_path(plan->use_tc, plan->variant, plan->params, plan->grid_ctas, s);

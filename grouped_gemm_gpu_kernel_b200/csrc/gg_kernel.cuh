@@ -37,6 +37,7 @@
 #include <cstddef>
 #include <cstdint>
 
+#include "gg_epilogue_ops.cuh"
 #include "gg_params.cuh"
 #include "gg_ptx.cuh"
 #include "grouped_gemm_b200.h"
@@ -175,38 +176,66 @@ __device__ __forceinline__ void prefetch_problem_maps(const CUtensorMap* maps, i
 }
 
 // ---- epilogue helper ---------------------------------------------------------------------
+// What one epilogue warp needs of its tile.
+struct EpiTile {
+  int row0;            // first of the warp's 32 rows (>= m: the warp stores nothing)
+  int m;
+  int n;
+  int col0;            // first column of the tile
+  int c_begin;         // the warp's 32-column chunks: [c_begin, c_end)
+  int c_end;
+  int kb_count;        // K blocks; 0: the accumulator is taken as zero
+  unsigned flags;      // DeviceProblemFlags
+  float alpha;
+  float beta;
+  const void* c;       // output format, row pitch ldc
+  int ldc;
+  void* d;             // output format, row pitch ldd
+  int ldd;
+  const float* bias;   // n FP32 values, or null
+  int act;             // GG_ACT_*
+  const CUtensorMap* md;  // D map (kFlagTmaD)
+  int tma_row0;
+};
+
 // One epilogue warp's share of a tile: rows row0..row0+31 (TMEM lanes of this warp's quarter) and
-// all nchunks 32-column chunks. D = alpha * acc + beta * C, C taken as 0 when it is not read
-// (reference src/grouped_gemm.cu:614-621). `stage` is this warp's 8 KB of shared memory: two
-// 4 KB staging tiles (32 rows x 128 bytes, 128-byte swizzle). The warp works alone, with no
-// barrier across warps inside the tile:
-//  - TMA-storable D: each chunk goes out in one 32x32 TMA store issued by lane 0; the staging
-//    tiles alternate, and lane 0's bulk groups say when a tile may be written again;
-//  - any other D: the chunk is read back from the staging tile so that 8 consecutive lanes hold
-//    one 128-byte row segment, and stored (and C loaded) with coalesced st.global / ld.global.
+// chunks [c_begin, c_end) of 32 columns. D = act(alpha * acc + (beta * C + bias)), C taken as 0
+// when it is not read (reference src/grouped_gemm.cu:614-621 for the FP32 form without bias and
+// activation), in output format `fmt` (GG_OUTPUT_*; one body serves all formats: three inlined
+// copies, one per format, would not fit the register budget together). `stage` is this warp's kEpiWarpBytes of shared memory: one
+// FP32 or two 16-bit staging tiles of 32 rows x 32 columns (128-byte rows with the 128-byte
+// swizzle for FP32, 64-byte rows with the 64-byte swizzle for 16-bit). The warp works alone, with
+// no barrier across warps inside the tile:
+//  - TMA-storable D: each chunk goes out in one 32x32 TMA store issued by lane 0; lane 0's bulk
+//    groups say when a staging tile may be written again;
+//  - any other D: the FP32 accumulator chunk is read back from the staging tile so that 8
+//    consecutive lanes hold one 32-column row segment, and C is loaded and D stored with
+//    coalesced accesses of 4 elements.
 // `release` hands the accumulator back to the MMA warp after the last TMEM read.
 template <typename Release>
-__device__ __forceinline__ void epilogue_warp(uint8_t* stage, uint32_t& store_count, uint32_t t_addr, int lane,
-                                              int row0, int m, int n, int col0, int c_begin, int c_end,
-                                              int kb_count, unsigned flags, float alpha, float beta,
-                                              const float* cptr, int ldc, float* dptr, int ldd,
-                                              const CUtensorMap* md, int tma_row0, Release release) {
-  constexpr int kStageTiles = kEpiWarpBytes / 4096;  // staging tiles of this warp
-  static_assert(kStageTiles == 1 || kStageTiles == 2, "staging tiles per epilogue warp");
+__device__ __forceinline__ void epilogue_warp(int fmt, uint8_t* stage, uint32_t& store_count, uint32_t t_addr,
+                                              int lane, const EpiTile& e, Release release) {
+  static_assert(kEpiWarpBytes == 4096, "one FP32 or two 16-bit staging tiles per epilogue warp");
+  const bool out32 = fmt == kOutF32;
+  const int eb = out32 ? 4 : 2;                // bytes per C / D element
+  const int tile_bytes = 32 * 32 * eb;         // one staged chunk
+  const bool two_tiles = !out32;               // 16-bit chunks: two staging tiles, alternating
+  const int m = e.m, n = e.n, row0 = e.row0;
   const bool warp_rows = row0 < m;  // warp-uniform
-  const bool read_c = (flags & grouped_gemm::kFlagReadC) != 0u;
+  const bool read_c = (e.flags & grouped_gemm::kFlagReadC) != 0u;
+  const bool cvec = (e.flags & grouped_gemm::kFlagCVec) != 0u;
   // With packed rows the D map spans every problem, so only a whole 32-row box may go out by TMA.
-  const bool tma_d = (flags & grouped_gemm::kFlagTmaD) != 0u &&
-                     ((flags & grouped_gemm::kFlagPackedRows) == 0u || row0 + 32 <= m);
+  const bool tma_d = (e.flags & grouped_gemm::kFlagTmaD) != 0u &&
+                     ((e.flags & grouped_gemm::kFlagPackedRows) == 0u || row0 + 32 <= m);
   const int row = row0 + lane;
   if (tma_d) {
     // Two chunks per TMEM read (one 64-column tcgen05.ld and one wait), then one staging tile
     // and one TMA store per chunk, so that a store is always in flight while the next chunk is
     // prepared.
-    for (int c = c_begin; c < c_end; c += 2) {
-      const int nsub = c + 1 < c_end ? 2 : 1;
+    for (int c = e.c_begin; c < e.c_end; c += 2) {
+      const int nsub = c + 1 < e.c_end ? 2 : 1;
       uint32_t r[64];
-      if (warp_rows && kb_count > 0) {
+      if (warp_rows && e.kb_count > 0) {
         if (nsub == 2) {
           ptx::tmem_load_64cols(t_addr + static_cast<uint32_t>(c * 32), r);
         } else {
@@ -219,7 +248,7 @@ __device__ __forceinline__ void epilogue_warp(uint8_t* stage, uint32_t& store_co
 #pragma unroll
         for (int j = 0; j < 64; ++j) r[j] = 0u;
       }
-      if (c + nsub >= c_end) {
+      if (c + nsub >= e.c_end) {
         // This warp's last read of the accumulator: hand it back before the stores.
         ptx::tc_fence_before_sync();
         __syncwarp();
@@ -229,47 +258,92 @@ __device__ __forceinline__ void epilogue_warp(uint8_t* stage, uint32_t& store_co
 #pragma unroll
       for (int sub = 0; sub < 2; ++sub) {
         if (sub >= nsub) break;
-        const int cc = col0 + (c + sub) * 32;
+        const int cc = e.col0 + (c + sub) * 32;
+        // cv = beta * C + bias, the addend of alpha * acc
         float cv[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) cv[j] = 0.0f;
         if (read_c && row < m) {
-          const float* crow = cptr + static_cast<int64_t>(row) * ldc + cc;
-          if ((flags & grouped_gemm::kFlagCVec) && cc + 32 <= n) {
+          const int64_t ci = static_cast<int64_t>(row) * e.ldc + cc;
+          if (cvec && cc + 32 <= n) {
+            const uint4* crow = reinterpret_cast<const uint4*>(static_cast<const char*>(e.c) + ci * eb);
+            if (out32) {
 #pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {
-              const float4 v = __ldg(reinterpret_cast<const float4*>(crow + 4 * j4));
-              cv[4 * j4] = v.x;
-              cv[4 * j4 + 1] = v.y;
-              cv[4 * j4 + 2] = v.z;
-              cv[4 * j4 + 3] = v.w;
+              for (int v = 0; v < 8; ++v) {
+                const uint4 u = __ldg(crow + v);
+                cv[4 * v] = __uint_as_float(u.x);
+                cv[4 * v + 1] = __uint_as_float(u.y);
+                cv[4 * v + 2] = __uint_as_float(u.z);
+                cv[4 * v + 3] = __uint_as_float(u.w);
+              }
+            } else {
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                const uint4 u = __ldg(crow + v);
+                const float2 f0 = unpack2_rt(fmt, u.x), f1 = unpack2_rt(fmt, u.y), f2 = unpack2_rt(fmt, u.z),
+                             f3 = unpack2_rt(fmt, u.w);
+                cv[8 * v] = f0.x;
+                cv[8 * v + 1] = f0.y;
+                cv[8 * v + 2] = f1.x;
+                cv[8 * v + 3] = f1.y;
+                cv[8 * v + 4] = f2.x;
+                cv[8 * v + 5] = f2.y;
+                cv[8 * v + 6] = f3.x;
+                cv[8 * v + 7] = f3.y;
+              }
             }
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (cc + j < n) cv[j] = __ldg(crow + j);
+              if (cc + j < n) cv[j] = load_out_rt(fmt, e.c, ci + j);
           }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) cv[j] *= e.beta;
         }
-        uint8_t* stile = stage + (kStageTiles == 2 ? static_cast<int>(store_count & 1u) * 4096 : 0);
+        // Lane j loads column cc + j's bias; the warp shares it by shuffles as the values are used.
+        const float bl = e.bias && cc + lane < n ? __ldg(e.bias + cc + lane) : 0.0f;
+        auto addend = [&](int j) { return e.bias ? cv[j] + __shfl_sync(0xffffffffu, bl, j) : cv[j]; };
+        uint8_t* stile = stage + (two_tiles ? static_cast<int>(store_count & 1u) * tile_bytes : 0);
         if (lane == 0) {  // the store that last used this staging tile has read it
-          if (kStageTiles == 2) ptx::bulk_wait_read_le1();
+          if (two_tiles) ptx::bulk_wait_read_le1();
           else ptx::bulk_wait_all_read();
         }
         __syncwarp();
+        if (out32) {
 #pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          const int j = sub * 32 + 4 * j4;
-          float4 o;
-          o.x = alpha * __uint_as_float(r[j]) + beta * cv[4 * j4];
-          o.y = alpha * __uint_as_float(r[j + 1]) + beta * cv[4 * j4 + 1];
-          o.z = alpha * __uint_as_float(r[j + 2]) + beta * cv[4 * j4 + 2];
-          o.w = alpha * __uint_as_float(r[j + 3]) + beta * cv[4 * j4 + 3];
-          *reinterpret_cast<float4*>(stile + lane * 128 + ((j4 ^ (lane & 7)) << 4)) = o;
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const int j = sub * 32 + 4 * j4;
+            float4 o = make_float4(fmaf(e.alpha, __uint_as_float(r[j]), addend(4 * j4)),
+                                   fmaf(e.alpha, __uint_as_float(r[j + 1]), addend(4 * j4 + 1)),
+                                   fmaf(e.alpha, __uint_as_float(r[j + 2]), addend(4 * j4 + 2)),
+                                   fmaf(e.alpha, __uint_as_float(r[j + 3]), addend(4 * j4 + 3)));
+            o = activate4(o, e.act);
+            *reinterpret_cast<float4*>(stile + lane * 128 + ((j4 ^ (lane & 7)) << 4)) = o;
+          }
+        } else {
+#pragma unroll
+          for (int j8 = 0; j8 < 4; ++j8) {
+            const int j = sub * 32 + 8 * j8;
+            float4 lo = make_float4(fmaf(e.alpha, __uint_as_float(r[j]), addend(8 * j8)),
+                                    fmaf(e.alpha, __uint_as_float(r[j + 1]), addend(8 * j8 + 1)),
+                                    fmaf(e.alpha, __uint_as_float(r[j + 2]), addend(8 * j8 + 2)),
+                                    fmaf(e.alpha, __uint_as_float(r[j + 3]), addend(8 * j8 + 3)));
+            float4 hi = make_float4(fmaf(e.alpha, __uint_as_float(r[j + 4]), addend(8 * j8 + 4)),
+                                    fmaf(e.alpha, __uint_as_float(r[j + 5]), addend(8 * j8 + 5)),
+                                    fmaf(e.alpha, __uint_as_float(r[j + 6]), addend(8 * j8 + 6)),
+                                    fmaf(e.alpha, __uint_as_float(r[j + 7]), addend(8 * j8 + 7)));
+            lo = activate4(lo, e.act);
+            hi = activate4(hi, e.act);
+            // 64-byte rows, 64-byte swizzle: 16-byte unit j8 of row `lane` sits at j8 ^ ((lane >> 1) & 3)
+            *reinterpret_cast<uint4*>(stile + lane * 64 + ((j8 ^ ((lane >> 1) & 3)) << 4)) =
+                make_uint4(pack2_rt(fmt, lo.x, lo.y), pack2_rt(fmt, lo.z, lo.w), pack2_rt(fmt, hi.x, hi.y),
+                           pack2_rt(fmt, hi.z, hi.w));
+          }
         }
         ptx::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          ptx::tma_store_2d(md, ptx::smem_addr(stile), cc, tma_row0 + row0);  // rows past M are clipped
+          ptx::tma_store_2d(e.md, ptx::smem_addr(stile), cc, e.tma_row0 + row0);  // rows past M are clipped
           ptx::bulk_commit_group();
         }
         ++store_count;
@@ -277,13 +351,14 @@ __device__ __forceinline__ void epilogue_warp(uint8_t* stage, uint32_t& store_co
     }
   } else {
     // Any other D: each chunk is read back from the staging tile so that 8 consecutive lanes
-    // hold one 128-byte row segment, then C is loaded and D stored with coalesced accesses.
+    // hold one 32-column row segment, then C is loaded and D stored with coalesced accesses.
     const int jj = lane & 7;
+    const bool dvec = (e.flags & grouped_gemm::kFlagDVec) != 0u;
     if (warp_rows && lane == 0) ptx::bulk_wait_all_read();  // staging tile 0 is free
-    for (int c = c_begin; c < c_end; ++c) {
-      const int cc = col0 + c * 32;
+    for (int c = e.c_begin; c < e.c_end; ++c) {
+      const int cc = e.col0 + c * 32;
       const int gcol = cc + 4 * jj;
-      // C, issued before the TMEM read so that its latency overlaps it.
+      // beta * C, issued before the TMEM read so that its latency overlaps it.
       float cv[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) cv[j] = 0.0f;
@@ -292,29 +367,31 @@ __device__ __forceinline__ void epilogue_warp(uint8_t* stage, uint32_t& store_co
         for (int i = 0; i < 8; ++i) {
           const int grow = row0 + i * 4 + (lane >> 3);
           if (grow < m && gcol < n) {
-            const float* crow = cptr + static_cast<int64_t>(grow) * ldc + gcol;
-            if ((flags & grouped_gemm::kFlagCVec) && gcol + 4 <= n) {
-              const float4 v = __ldg(reinterpret_cast<const float4*>(crow));
+            const int64_t ci = static_cast<int64_t>(grow) * e.ldc + gcol;
+            if (cvec && gcol + 4 <= n) {
+              const float4 v = load_out4_rt(fmt, static_cast<const char*>(e.c) + ci * eb);
               cv[4 * i] = v.x;
               cv[4 * i + 1] = v.y;
               cv[4 * i + 2] = v.z;
               cv[4 * i + 3] = v.w;
             } else {
 #pragma unroll
-              for (int e = 0; e < 4; ++e)
-                if (gcol + e < n) cv[4 * i + e] = __ldg(crow + e);
+              for (int q = 0; q < 4; ++q)
+                if (gcol + q < n) cv[4 * i + q] = load_out_rt(fmt, e.c, ci + q);
             }
           }
         }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) cv[j] *= e.beta;
       }
       uint32_t r[32];
-      if (warp_rows && kb_count > 0) {
+      if (warp_rows && e.kb_count > 0) {
         ptx::tmem_load_32cols(t_addr + static_cast<uint32_t>(c * 32), r);
       } else {
 #pragma unroll
         for (int j = 0; j < 32; ++j) r[j] = 0u;
       }
-      if (c == c_end - 1) {
+      if (c == e.c_end - 1) {
         ptx::tc_fence_before_sync();
         __syncwarp();
         if (lane == 0) release();
@@ -325,32 +402,36 @@ __device__ __forceinline__ void epilogue_warp(uint8_t* stage, uint32_t& store_co
         *reinterpret_cast<uint4*>(stage + lane * 128 + ((j4 ^ (lane & 7)) << 4)) =
             make_uint4(r[4 * j4], r[4 * j4 + 1], r[4 * j4 + 2], r[4 * j4 + 3]);
       __syncwarp();
+      float bv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      if (e.bias) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (gcol + q < n) bv[q] = __ldg(e.bias + gcol + q);
+      }
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int rr = i * 4 + (lane >> 3);
         const float4 a4 = *reinterpret_cast<const float4*>(stage + rr * 128 + ((jj ^ (rr & 7)) << 4));
         const int grow = row0 + rr;
         if (grow < m && gcol < n) {
-          float4 o;
-          o.x = alpha * a4.x + beta * cv[4 * i];
-          o.y = alpha * a4.y + beta * cv[4 * i + 1];
-          o.z = alpha * a4.z + beta * cv[4 * i + 2];
-          o.w = alpha * a4.w + beta * cv[4 * i + 3];
-          float* drow = dptr + static_cast<int64_t>(grow) * ldd + gcol;
-          if ((flags & grouped_gemm::kFlagDVec) && gcol + 4 <= n) {
-            *reinterpret_cast<float4*>(drow) = o;
+          float4 o = make_float4(fmaf(e.alpha, a4.x, cv[4 * i] + bv[0]), fmaf(e.alpha, a4.y, cv[4 * i + 1] + bv[1]),
+                                 fmaf(e.alpha, a4.z, cv[4 * i + 2] + bv[2]), fmaf(e.alpha, a4.w, cv[4 * i + 3] + bv[3]));
+          o = activate4(o, e.act);
+          const int64_t di = static_cast<int64_t>(grow) * e.ldd + gcol;
+          if (dvec && gcol + 4 <= n) {
+            store_out4_rt(fmt, static_cast<char*>(e.d) + di * eb, o);
           } else {
-            drow[0] = o.x;
-            if (gcol + 1 < n) drow[1] = o.y;
-            if (gcol + 2 < n) drow[2] = o.z;
-            if (gcol + 3 < n) drow[3] = o.w;
+            store_out_rt(fmt, e.d, di, o.x);
+            if (gcol + 1 < n) store_out_rt(fmt, e.d, di + 1, o.y);
+            if (gcol + 2 < n) store_out_rt(fmt, e.d, di + 2, o.z);
+            if (gcol + 3 < n) store_out_rt(fmt, e.d, di + 3, o.w);
           }
         }
       }
       __syncwarp();
     }
   }
-  if (c_begin >= c_end) {
+  if (e.c_begin >= e.c_end) {
     ptx::tc_fence_before_sync();
     __syncwarp();
     if (lane == 0) release();
@@ -731,11 +812,15 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
       const int m = s->desc.m, n = s->desc.n;
       const int kb_count = s->desc.k_blocks;
       const unsigned flags = s->desc.flags;
-      const float alpha = s->desc.alpha, beta = s->desc.beta;
-      const float* cptr = s->desc.c;
-      float* dptr = s->desc.d;
-      const int ldc = s->desc.ldc, ldd = s->desc.ldd;
-      const int tma_row0 = s->desc.tma_row0;
+      EpiTile e;
+      e.flags = flags;
+      e.alpha = s->desc.alpha;
+      e.beta = s->desc.beta;
+      e.c = s->desc.c;
+      e.ldc = s->desc.ldc;
+      e.d = s->desc.d;
+      e.ldd = s->desc.ldd;
+      e.tma_row0 = s->desc.tma_row0;
       const int map_slot = s->desc.map_slot;
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(ringe_bar(slot));
@@ -753,10 +838,18 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
       epilogue_chunk_range(nchunks, half, c_begin, c_end);
       const uint32_t t_addr = tmem_base + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(qw * 32) << 16);
       // Warps whose 32 rows lie past BM (64-row tiles) or past M store nothing.
-      const int row0 = qw * 32 < BM ? tile_m * BM + qw * 32 : m;
-      epilogue_warp(smem + L::kEpiOffset + warp * kEpiWarpBytes, store_count, t_addr, lane, row0, m, n, tile_n * BN,
-                    c_begin, c_end, kb_count, flags, alpha, beta, cptr, ldc, dptr, ldd,
-                    maps + kMapsPerProblem * map_slot + kMapD, tma_row0, [&] { ptx::mbar_arrive(acce_bar(buf)); });
+      e.row0 = qw * 32 < BM ? tile_m * BM + qw * 32 : m;
+      e.m = m;
+      e.n = n;
+      e.col0 = tile_n * BN;
+      e.c_begin = c_begin;
+      e.c_end = c_end;
+      e.kb_count = kb_count;
+      e.bias = p.bias ? p.bias[map_slot] : nullptr;
+      e.act = p.activation;
+      e.md = maps + kMapsPerProblem * map_slot + kMapD;
+      epilogue_warp(p.output_format, smem + L::kEpiOffset + warp * kEpiWarpBytes, store_count, t_addr, lane, e,
+                        [&] { ptx::mbar_arrive(acce_bar(buf)); });
     }
     if (lane == 0) ptx::bulk_wait_all();  // every warp issues its own TMA stores
     __syncwarp();

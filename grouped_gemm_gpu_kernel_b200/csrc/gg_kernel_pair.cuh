@@ -370,11 +370,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = s->desc.m, n = s->desc.n;
       const int kb_count = s->desc.k_blocks;
       const unsigned flags = s->desc.flags;
-      const float alpha = s->desc.alpha, beta = s->desc.beta;
-      const float* cptr = s->desc.c;
-      float* dptr = s->desc.d;
-      const int ldc = s->desc.ldc, ldd = s->desc.ldd;
-      const int tma_row0 = s->desc.tma_row0;
+      EpiTile e;
+      e.flags = flags;
+      e.alpha = s->desc.alpha;
+      e.beta = s->desc.beta;
+      e.c = s->desc.c;
+      e.ldc = s->desc.ldc;
+      e.d = s->desc.d;
+      e.ldd = s->desc.ldd;
+      e.tma_row0 = s->desc.tma_row0;
       const int map_slot = s->desc.map_slot;
       __syncwarp();
       if (lane == 0) release_slot(slot);
@@ -391,13 +395,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       int c_begin, c_end;
       epilogue_chunk_range(nchunks, half, c_begin, c_end);
       const uint32_t t_addr = tmem_base + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(qw * 32) << 16);
-      const int row0 = tile_m * BM + static_cast<int>(rank) * 128 + qw * 32;  // this warp's first row
-      epilogue_warp(smem + L::kEpiOffset + warp * kEpiWarpBytes, store_count, t_addr, lane, row0, m, n,
-                    tile_n * BN, c_begin, c_end, kb_count, flags, alpha, beta, cptr, ldc, dptr, ldd,
-                    maps + kMapsPerProblem * map_slot + kMapD, tma_row0, [&] {
-                      if (leader) ptx::mbar_arrive(acce_bar(buf));
-                      else ptx::mbar_arrive_cluster(ptx::mapa_shared(acce_bar(buf), 0));
-                    });
+      e.row0 = tile_m * BM + static_cast<int>(rank) * 128 + qw * 32;  // this warp's first row
+      e.m = m;
+      e.n = n;
+      e.col0 = tile_n * BN;
+      e.c_begin = c_begin;
+      e.c_end = c_end;
+      e.kb_count = kb_count;
+      e.bias = p.bias ? p.bias[map_slot] : nullptr;
+      e.act = p.activation;
+      e.md = maps + kMapsPerProblem * map_slot + kMapD;
+      epilogue_warp(p.output_format, smem + L::kEpiOffset + warp * kEpiWarpBytes, store_count, t_addr, lane, e,
+                        [&] {
+                          if (leader) ptx::mbar_arrive(acce_bar(buf));
+                          else ptx::mbar_arrive_cluster(ptx::mapa_shared(acce_bar(buf), 0));
+                        });
     }
     if (lane == 0) ptx::bulk_wait_all();  // every warp issues its own TMA stores
     __syncwarp();

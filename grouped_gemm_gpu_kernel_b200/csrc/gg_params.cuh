@@ -96,7 +96,10 @@ struct KernelParams {
   int total_tiles;
   int raster_group;  // M-tiles per raster group inside a problem (L2 reuse of A and B panels)
   int single_mode;   // 1: baseline launch, tiles blockIdx.x + i*gridDim.x of single_desc
-  int input_format;  // A and B element type: 0 = FP16, 1 = BF16 (GG_INPUT_*)
+  int input_format;   // A and B element type: 0 = FP16, 1 = BF16 (GG_INPUT_*)
+  int output_format;  // C and D element type: 0 = FP32, 1 = FP16, 2 = BF16 (GG_OUTPUT_*)
+  int activation;     // GG_ACT_* applied to D after the bias
+  const float* const* bias;  // per map slot: that problem's bias (n FP32 values) or null; null: none
 };
 
 }  // namespace gg

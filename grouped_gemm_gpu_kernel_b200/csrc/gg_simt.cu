@@ -5,7 +5,8 @@
 // Same contract as the tensor-core kernel: the same tile_offsets and tile numbering (the config's
 // cta_m x cta_n tiles), the same atomic tile claims and problem lookup (reference
 // src/grouped_gemm.cu:219-234, 640-675), the same epilogue D = alpha*acc + beta*C with C read only
-// when c != nullptr and beta != 0 (reference src/grouped_gemm.cu:460-481). FP16 (or BF16) operands
+// when c != nullptr and beta != 0 (reference src/grouped_gemm.cu:460-481), with the tensor-core
+// epilogue's extensions (output format, bias, activation; gg_epilogue_ops.cuh). FP16 (or BF16) operands
 // are widened to FP32 and accumulated with FP32 FMA (a product of two 16-bit values is exact in
 // FP32), so the result differs from the tensor-core path only in the order of the FP32 additions.
 //
@@ -16,6 +17,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "gg_epilogue_ops.cuh"
 #include "gg_internal.h"
 
 namespace gg {
@@ -30,6 +32,25 @@ constexpr int kPad = 4;      // keeps 16-byte alignment of every row, spreads ba
 __device__ __forceinline__ float widen(const __half* x, long long i, bool bf16) {
   if (bf16) return __uint_as_float(static_cast<unsigned>(reinterpret_cast<const unsigned short*>(x)[i]) << 16);
   return __half2float(x[i]);
+}
+
+// D = act(alpha * acc + (beta * C + bias)) for this thread's 4 x 4 outputs, C and D in format F.
+template <int F>
+__device__ __forceinline__ void store_block(const DeviceProblemDesc& d, const float* bias, int act, bool read_c,
+                                            const float (&acc)[4][4], int r0, int c0) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int gr = r0 + i;
+    if (gr >= d.m) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int gc = c0 + j;
+      if (gc >= d.n) continue;
+      float add = read_c ? d.beta * load_out<F>(d.c, static_cast<long long>(gr) * d.ldc + gc) : 0.0f;
+      if (bias) add += __ldg(bias + gc);
+      store_out<F>(d.d, static_cast<long long>(gr) * d.ldd + gc, activate(fmaf(d.alpha, acc[i][j], add), act));
+    }
+  }
 }
 
 // Last q with offs[q] <= tile (offs has count + 1 entries, offs[count] = total > tile).
@@ -94,7 +115,7 @@ __global__ void __launch_bounds__(kSimtThreads) grouped_gemm_simt_kernel(const _
     const __half* b = d.b;
     const int lda = d.lda, ldb = d.ldb;
     const bool read_c = (d.flags & grouped_gemm::kFlagReadC) != 0u;
-    const float alpha = d.alpha, beta = d.beta;
+    const float* bias = p.bias ? p.bias[d.map_slot] : nullptr;
 
     for (int sm = 0; sm < bm; sm += kSub) {
       const int row0 = tile_m * bm + sm;
@@ -132,19 +153,13 @@ __global__ void __launch_bounds__(kSimtThreads) grouped_gemm_simt_kernel(const _
           }
           __syncthreads();
         }
-        // D = alpha * acc + beta * C, C taken as 0 when it is not read
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int gr = row0 + ty * 4 + i;
-          if (gr >= m) continue;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int gc = col0 + tx * 4 + j;
-            if (gc >= n) continue;
-            const float cv = read_c ? d.c[static_cast<long long>(gr) * d.ldc + gc] : 0.0f;
-            d.d[static_cast<long long>(gr) * d.ldd + gc] = alpha * acc[i][j] + beta * cv;
-          }
-        }
+        // C taken as 0 when it is not read
+        if (p.output_format == kOutF16)
+          store_block<kOutF16>(d, bias, p.activation, read_c, acc, row0 + ty * 4, col0 + tx * 4);
+        else if (p.output_format == kOutBF16)
+          store_block<kOutBF16>(d, bias, p.activation, read_c, acc, row0 + ty * 4, col0 + tx * 4);
+        else
+          store_block<kOutF32>(d, bias, p.activation, read_c, acc, row0 + ty * 4, col0 + tx * 4);
       }
     }
   }

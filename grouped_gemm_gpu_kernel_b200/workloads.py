@@ -113,17 +113,65 @@ class DeviceProblemSet:
     b_off: List[int] = field(default_factory=list)
     c_off: List[int] = field(default_factory=list)
     d_off: List[int] = field(default_factory=list)
+    out_fmt: int = 0                  # C / D element type: 0 FP32, 1 FP16, 2 BF16 (KernelConfig.output_type)
+    bias: Optional["object"] = None   # FP32 slab of per-problem bias vectors (make_bias)
+    bias_off: List[Optional[int]] = field(default_factory=list)  # element offset, None = no bias
 
     def problems(self):
         from . import ProblemDesc
         out = []
+        eo = 4 if self.out_fmt == 0 else 2
         ab, bb, db = self.a.data_ptr(), self.b.data_ptr(), self.d.data_ptr()
         cb = self.c.data_ptr() if self.c is not None else None
         for i, ((m, n, k), al, be) in enumerate(zip(self.shapes.dims, self.shapes.alpha, self.shapes.beta)):
             out.append(ProblemDesc(m, n, k, ab + 2 * self.a_off[i], bb + 2 * self.b_off[i],
-                                   (cb + 4 * self.c_off[i]) if cb is not None else None, db + 4 * self.d_off[i],
+                                   (cb + eo * self.c_off[i]) if cb is not None else None, db + eo * self.d_off[i],
                                    max(1, k), max(1, n), max(1, n), max(1, n), al, be))
         return out
+
+    def to_output(self, out_fmt: int) -> "DeviceProblemSet":
+        """C and D in the 16-bit output type `out_fmt` (1 FP16, 2 BF16; KernelConfig.output_type):
+        C becomes its FP32 values rounded to that type, D a NaN-filled buffer of that type, both at
+        the same element offsets (which keeps every row start 16-byte aligned)."""
+        import torch
+
+        dt = {1: torch.float16, 2: torch.bfloat16}[int(out_fmt)]
+        if self.c is not None:
+            self.c = self.c.to(dt)
+        self.d = torch.full(self.d.shape, float("nan"), dtype=dt, device=self.d.device)
+        self.out_fmt = int(out_fmt)
+        return self
+
+    def make_bias(self, seed: int = 7, without: float = 0.25) -> List[Optional[int]]:
+        """One FP32 bias vector of n values ~ U[-1,1] per problem, a seeded fraction `without` of
+        the problems having none; returns the device pointers in problem order (None: no bias).
+        Each vector starts 4 bytes past a 256-byte boundary, so no vector is 16-byte aligned."""
+        import torch
+
+        rng = np.random.default_rng(seed)
+        offs: List[Optional[int]] = []
+        total = 0
+        for m, n, k in self.shapes.dims:
+            if rng.random() < without:
+                offs.append(None)
+                continue
+            offs.append(total + 1)
+            total += _aligned(max(n, 0) + 1, 4)
+        g = torch.Generator(device=self.a.device)
+        g.manual_seed(seed)
+        self.bias = torch.empty(max(total, 1), dtype=torch.float32, device=self.a.device).uniform_(-1.0, 1.0,
+                                                                                                  generator=g)
+        self.bias_off = offs
+        base = self.bias.data_ptr()
+        return [None if o is None else base + 4 * o for o in offs]
+
+    def bias_host(self, i: int, cols: Optional[np.ndarray] = None) -> Optional[np.ndarray]:
+        """Host copy (float32) of problem i's bias, or of its entries `cols`; None without bias."""
+        if self.bias is None or self.bias_off[i] is None:
+            return None
+        n = self.shapes.dims[i][1]
+        v = self.bias[self.bias_off[i]:self.bias_off[i] + n].cpu().numpy()
+        return v if cols is None else v[np.asarray(cols)]
 
     def to_bf16(self) -> "DeviceProblemSet":
         """Re-encodes A and B in place as BF16 (each FP16 value rounded to the nearest BF16), for
@@ -186,7 +234,8 @@ def allocate(shapes: Shapes, device="cuda", seed: int = 42, d_fill: float = floa
 
 def host_inputs(ps: DeviceProblemSet, i: int, rows: Optional[np.ndarray] = None,
                 cols: Optional[np.ndarray] = None) -> Dict[str, object]:
-    """Host copies (FP16 bits as uint16, C as float32) of problem i for the CPU oracle.
+    """Host copies (16-bit A/B bits as uint16, C and D widened to float32) of problem i for the
+    CPU oracle.
 
     With `rows`/`cols` only those rows of A (and C) and those columns of B (and C) are copied,
     so a full-size problem can be checked on a sample."""
@@ -207,6 +256,6 @@ def host_inputs(ps: DeviceProblemSet, i: int, rows: Optional[np.ndarray] = None,
     out = {}
     out["a"] = A.contiguous().view(torch.int16).cpu().numpy().view(np.uint16) if A is not None else np.zeros(1, np.uint16)
     out["b"] = B.contiguous().view(torch.int16).cpu().numpy().view(np.uint16) if B is not None else np.zeros(1, np.uint16)
-    out["c"] = C.contiguous().cpu().numpy() if C is not None else None
-    out["d"] = D.contiguous().cpu().numpy() if D is not None else None
+    out["c"] = C.contiguous().float().cpu().numpy() if C is not None else None
+    out["d"] = D.contiguous().float().cpu().numpy() if D is not None else None
     return out

@@ -14,10 +14,10 @@ namespace grouped_gemm {
 
 enum DeviceProblemFlags : unsigned {
   kFlagTmaAB = 1u,   // A and B are loaded by TMA (16-byte aligned bases, lda and ldb % 8 == 0)
-  kFlagTmaD = 2u,    // D is stored by TMA (16-byte aligned base, ldd % 4 == 0)
+  kFlagTmaD = 2u,    // D is stored by TMA (16-byte aligned base, rows a multiple of 16 bytes apart)
   kFlagReadC = 4u,   // c != nullptr && beta != 0: the epilogue reads C
-  kFlagCVec = 8u,    // C rows can be read as 16-byte vectors
-  kFlagDVec = 16u,   // D rows can be written as 16-byte vectors (direct-store path)
+  kFlagCVec = 8u,    // C rows can be read as 16-byte vectors (16-bit C: and row pitch % 8 == 0)
+  kFlagDVec = 16u,   // D rows can be written as 4-element vectors (direct-store path)
   kFlagTmaB3 = 32u,  // B also has a 3-D map that loads a whole stage of full 64-column chunks at once
   kFlagPackedRows = 64u,  // the A and D maps span the packed rows of every problem: TMA row
                           // coordinates add tma_row0, and D goes out by TMA only in whole
@@ -29,10 +29,10 @@ struct DeviceProblemDesc {
   int n;
   int k;
 
-  const __half* a;
+  const __half* a;  // FP16, or BF16 bits (the launch's input format)
   const __half* b;
-  const float* c;
-  float* d;
+  const void* c;    // FP32, or FP16 / BF16 (the launch's output format)
+  void* d;
 
   int lda;
   int ldb;

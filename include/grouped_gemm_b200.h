@@ -2,7 +2,10 @@
  * grouped_gemm_b200.h -- C-ABI of the B200 (sm_100a) grouped GEMM library libgrouped_gemm_b200.so.
  *
  * One launch runs many independent GEMMs  D_i = alpha_i * A_i x B_i + beta_i * C_i  with
- * A_i (m x k) and B_i (k x n) FP16 row-major, C_i and D_i FP32 row-major, FP32 accumulation.
+ * A_i (m x k) and B_i (k x n) FP16 row-major, C_i and D_i FP32 row-major, FP32 accumulation
+ * (the reference's contract). Extensions, all off by default: BF16 A/B (gg_config.input_type),
+ * FP16/BF16 C/D (gg_config.output_type), a per-column bias and an activation fused into the
+ * epilogue (gg_executor_build_with_bias, gg_config.activation).
  * This is the boundary a foreign-language caller binds (ctypes, cgo, JNI, ...): plain C types,
  * opaque handles, device pointers as void*, CUDA streams as void* (cudaStream_t; NULL = legacy
  * default stream). Every function that can fail returns an int holding a cudaError_t value:
@@ -41,15 +44,16 @@ extern "C" {
 #define GG_STATUS_TIMEOUT_SCHEDULER 0x8
 
 /* One GEMM problem. Layout-identical to the reference's ProblemDesc (grouped_gemm.cuh:18-35);
- * a and b point to FP16 (__half) device memory. */
+ * a and b point to FP16 (__half) device memory (BF16 with GG_INPUT_BF16), c and d to FP32 (FP16
+ * or BF16 with GG_OUTPUT_F16 / GG_OUTPUT_BF16). c may be NULL; it is read only when beta != 0. */
 typedef struct gg_problem {
   int m;
   int n;
   int k;
   const void* a;
   const void* b;
-  const float* c;
-  float* d;
+  const void* c;
+  void* d;
   int lda;
   int ldb;
   int ldc;
@@ -69,10 +73,25 @@ typedef struct gg_problem {
  * operands widened to FP32, FP32 FMA; the reference's SIMT path) with the same tile numbering.
  * input_type (no reference counterpart; the reference is FP16 only, and the C++ API of
  * grouped_gemm/grouped_gemm.cuh keeps the reference's KernelConfig and always passes FP16): the
- * element type of every A and B of the set, GG_INPUT_F16 (0) or GG_INPUT_BF16; any other value is
- * an invalid config. C and D stay FP32 and the accumulation FP32 either way. */
+ * element type of every A and B of the set, GG_INPUT_F16 (0) or GG_INPUT_BF16.
+ * output_type (no reference counterpart): the element type of every C and D of the set,
+ * GG_OUTPUT_F32 (0, the reference's), GG_OUTPUT_F16 or GG_OUTPUT_BF16. The accumulation and the
+ * epilogue arithmetic stay FP32; D is rounded to nearest even once, at the store.
+ * activation (no reference counterpart): applied to every element of D after the bias,
+ *   D = act(alpha * A x B + beta * C + bias):
+ *   GG_ACT_NONE (0), GG_ACT_RELU (max(x, 0)), GG_ACT_GELU (tanh form,
+ *   0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), the approximation of Hendrycks and Gimpel).
+ * Any other value of the three fields is an invalid config. The C++ API of
+ * grouped_gemm/grouped_gemm.cuh keeps the reference's KernelConfig and always passes 0 for all
+ * three. */
 #define GG_INPUT_F16 0
 #define GG_INPUT_BF16 1
+#define GG_OUTPUT_F32 0
+#define GG_OUTPUT_F16 1
+#define GG_OUTPUT_BF16 2
+#define GG_ACT_NONE 0
+#define GG_ACT_RELU 1
+#define GG_ACT_GELU 2
 typedef struct gg_config {
   int cta_m;
   int cta_n;
@@ -81,6 +100,8 @@ typedef struct gg_config {
   int persistent_ctas; /* > 0: fixed persistent grid size; 0: one CTA per SM slot, capped by tiles */
   int use_tensor_cores;
   int input_type;      /* GG_INPUT_F16 or GG_INPUT_BF16 */
+  int output_type;     /* GG_OUTPUT_F32, GG_OUTPUT_F16 or GG_OUTPUT_BF16 */
+  int activation;      /* GG_ACT_NONE, GG_ACT_RELU or GG_ACT_GELU */
 } gg_config;
 
 /* Resource report; field-for-field the reference's OccupancyInfo (grouped_gemm.cuh:54-83). */
@@ -149,6 +170,15 @@ void gg_executor_destroy(gg_executor* executor);
 int gg_executor_build(gg_executor* executor, const gg_problem* sorted_problems, int count,
                       const int* tile_offsets, int offsets_len, int total_tiles,
                       const gg_config* config);
+
+/* No reference counterpart. gg_executor_build plus a per-column bias fused into the epilogue:
+ * bias is a host array of `count` device pointers in the order of sorted_problems, entry i
+ * pointing to n_i FP32 values (any alignment) added to every row of D_i before the activation;
+ * a NULL entry means no bias for that problem, and bias == NULL is gg_executor_build. The
+ * pointers are copied into the executor's device table; the values are read at run time. */
+int gg_executor_build_with_bias(gg_executor* executor, const gg_problem* sorted_problems, int count,
+                                const int* tile_offsets, int offsets_len, int total_tiles,
+                                const gg_config* config, const float* const* bias);
 
 /* reference src/grouped_gemm.cu:1241-1265 (GroupedGemmExecutor::run): resets the tile counter
  * and launches the persistent kernel on `stream`. Runs of one executor on two streams at the
@@ -227,10 +257,10 @@ int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count, int sort_
  * the tile count from the device. No host synchronisation, no host copy per run, so a run can be
  * captured in a CUDA graph and replayed with new row counts. */
 typedef struct gg_moe_problem {
-  const void* a;          /* FP16, capacity_rows x k, row pitch lda: the problems' rows packed */
+  const void* a;          /* FP16 (config input_type), capacity_rows x k, row pitch lda: the problems' rows packed */
   const void* const* b;   /* host array of `experts` device pointers, each k x n FP16, row pitch ldb */
-  const float* c;         /* optional FP32, packed like A, row pitch ldc (read when beta != 0) */
-  float* d;               /* FP32, packed like A, row pitch ldd */
+  const void* c;          /* optional FP32 (config output_type), packed like A, row pitch ldc (read when beta != 0) */
+  void* d;                /* FP32 (config output_type), packed like A, row pitch ldd */
   int experts;            /* problems, >= 1 */
   int n;                  /* columns of every B and D, >= 0 */
   int k;                  /* inner dimension, >= 0 */
@@ -241,6 +271,8 @@ typedef struct gg_moe_problem {
   int ldd;
   float alpha;
   float beta;
+  const float* const* bias; /* optional host array of `experts` device pointers, each n FP32 values
+                               added to every row of that expert's D (NULL entries: none); NULL: no bias */
 } gg_moe_problem;
 
 typedef struct gg_moe_plan gg_moe_plan;

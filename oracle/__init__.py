@@ -66,6 +66,9 @@ def load_oracle() -> ctypes.CDLL:
         lib.oracle_gemm_f64.restype = None
         lib.oracle_gemm_f64_fmt.argtypes = lib.oracle_gemm_f64.argtypes + [ctypes.c_int]
         lib.oracle_gemm_f64_fmt.restype = None
+        lib.oracle_gemm_f64_epilogue.argtypes = lib.oracle_gemm_f64_fmt.argtypes + [
+            ctypes.POINTER(ctypes.c_float), ctypes.c_int]
+        lib.oracle_gemm_f64_epilogue.restype = None
         lib.oracle_bf16_to_double.argtypes = [ctypes.c_uint16]
         lib.oracle_bf16_to_double.restype = ctypes.c_double
         lib.oracle_gemm_f32_refloop.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, _u16p,
@@ -155,9 +158,11 @@ def prepare(dims: Sequence[Sequence[int]], cta_m: int, cta_n: int, mode: int):
     return perm[:count], offs, int(total)
 
 
-def gemm_f64(m, n, k, a, lda, b, ldb, c, ldc, alpha, beta, rows=None, fmt=0):
+def gemm_f64(m, n, k, a, lda, b, ldb, c, ldc, alpha, beta, rows=None, fmt=0, bias=None, act=0):
     """FP64 D (and the error scale) for one problem; `a`/`b` are uint16 bit arrays of FP16
-    (fmt 0) or BF16 (fmt 1) values.
+    (fmt 0) or BF16 (fmt 1) values. `bias` (n float32 values, one per output column, or None)
+    and `act` (0 none, 1 ReLU, 2 GELU tanh form) give the library's epilogue extensions:
+    D = act(alpha * A x B + beta * C + bias).
 
     Returns (d, scale), each shaped (len(rows) or m, n).
     """
@@ -171,11 +176,15 @@ def gemm_f64(m, n, k, a, lda, b, ldb, c, ldc, alpha, beta, rows=None, fmt=0):
         return d[:nrows, :max(n, 0)], s[:nrows, :max(n, 0)]
     rows_arr = None if rows is None else np.ascontiguousarray(rows, dtype=np.int32)
     c_arr = None if c is None else np.ascontiguousarray(c, dtype=np.float32)
-    lib.oracle_gemm_f64_fmt(m, n, k, _ptr(a, ctypes.c_uint16), lda, _ptr(b, ctypes.c_uint16), ldb,
-                            None if c_arr is None else _ptr(c_arr, ctypes.c_float), ldc,
-                            float(alpha), float(beta),
-                            None if rows_arr is None else _ptr(rows_arr, ctypes.c_int), nrows,
-                            _ptr(d, ctypes.c_double), n, _ptr(s, ctypes.c_double), int(fmt))
+    bias_arr = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    if bias_arr is not None and bias_arr.size < n:
+        raise ValueError("bias needs one value per output column")
+    lib.oracle_gemm_f64_epilogue(m, n, k, _ptr(a, ctypes.c_uint16), lda, _ptr(b, ctypes.c_uint16), ldb,
+                                 None if c_arr is None else _ptr(c_arr, ctypes.c_float), ldc,
+                                 float(alpha), float(beta),
+                                 None if rows_arr is None else _ptr(rows_arr, ctypes.c_int), nrows,
+                                 _ptr(d, ctypes.c_double), n, _ptr(s, ctypes.c_double), int(fmt),
+                                 None if bias_arr is None else _ptr(bias_arr, ctypes.c_float), int(act))
     return d, s
 
 
@@ -254,18 +263,26 @@ def tolerance(k: int) -> float:
     return 2e-3 * float(np.sqrt(max(int(k), 1) / 1024.0))
 
 
-def rel_err(d, ref, scale) -> float:
+# Rounding of D to a 16-bit output type (library output_type 1 = FP16, 2 = BF16): relative unit
+# roundoff, and the absolute half-spacing of the format's subnormals.
+OUTPUT_ROUNDING = {0: (0.0, 0.0), 1: (2.0 ** -11, 2.0 ** -25), 2: (2.0 ** -8, 2.0 ** -134)}
+
+
+def rel_err(d, ref, scale, out_fmt: int = 0) -> float:
     """max |d - ref| / max(|ref|, scale), with scale = |alpha|*sqrt(sum (a*b)^2) + |beta*c|.
 
     The scale is the magnitude of a random-sign sum of the K products, so outputs that cancel to
-    near zero are judged against the size of their terms rather than against ~0.
+    near zero are judged against the size of their terms rather than against ~0. For a 16-bit D
+    (out_fmt 1 or 2) the final rounding to that format, u*|ref| + the subnormal half-spacing, is
+    taken off the error first: the bound then applies to the FP32 result before its rounding.
     """
     d = np.asarray(d, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     if d.size == 0:
         return 0.0
+    u, floor = OUTPUT_ROUNDING[int(out_fmt)]
     denom = np.maximum(np.maximum(np.abs(ref), np.asarray(scale, dtype=np.float64)), 1e-30)
-    err = np.abs(d - ref) / denom
+    err = np.maximum(np.abs(d - ref) - u * np.abs(ref) - floor, 0.0) / denom
     if not np.all(np.isfinite(d)):
         return float("inf")
     return float(err.max())

@@ -13,7 +13,9 @@
  *   - the reference's host GEMM reference tests/test_correctness.cu:85-102 (FP32, natural k order,
  *         always reads C) -- restated as oracle_gemm_f32_refloop for the "port" CPU baseline.
  * The accuracy judge is oracle_gemm_f64: FP16 inputs decoded exactly, products and sums in FP64
- * (oracle_gemm_f64_fmt also takes BF16 inputs, for the library's BF16 extension).
+ * (oracle_gemm_f64_fmt also takes BF16 inputs, for the library's BF16 extension, and
+ * oracle_gemm_f64_epilogue adds the library's fused bias and activation; C given as float holds
+ * 16-bit C values exactly).
  *
  * Parity pin: tests/test_oracle.py checks every function here against the reference's own host
  * code compiled from its sources (oracle/Makefile -> oracle/_ref/libgg_ref.so) and against the
@@ -137,10 +139,25 @@ int oracle_prepare(const int* m, const int* n, const int* k, int count, int cta_
  *   scale[r*ldd + j] = |alpha| * sqrt(sum_k (A[row,k]*B[k,j])^2) + |beta * C[row,j]|
  * 'r' indexes the output rows (0..nrows-1), 'row' the problem row. 'scale' (nullable) is the
  * magnitude that the relative-error metric of the tests divides by when |d| is small. */
-/* As oracle_gemm_f64, with A and B in the 16-bit format `fmt` (0 = FP16, 1 = BF16). */
-void oracle_gemm_f64_fmt(int m, int n, int k, const uint16_t* a, int lda, const uint16_t* b, int ldb,
-                         const float* c, int ldc, float alpha, float beta, const int* rows, int nrows,
-                         double* d, int ldd, double* scale, int fmt) {
+/* The library's activations (GG_ACT_*): 1 = ReLU, max(z, 0) with NaN -> 0; 2 = GELU, tanh form
+ * 0.5 z (1 + tanh(sqrt(2/pi) (z + 0.044715 z^3))) (Hendrycks and Gimpel). act_lipschitz bounds
+ * |act'|, so an error e in z becomes at most act_lipschitz * e in act(z). */
+static double activate(double z, int act) {
+  if (act == 1) return z > 0.0 ? z : 0.0;
+  if (act == 2) return 0.5 * z * (1.0 + tanh(0.7978845608028654 * (z + 0.044715 * z * z * z)));
+  return z;
+}
+
+static double act_lipschitz(int act) { return act == 2 ? 1.13 : 1.0; } /* max GELU' = 1.1289... */
+
+/* As oracle_gemm_f64, with A and B in the 16-bit format `fmt` (0 = FP16, 1 = BF16), and the
+ * library's epilogue extensions: bias (nullable, one value per output column, bias[j] for column
+ * j) added after alpha*acc + beta*C, then activation `act`:
+ *   d     = act(alpha * acc + beta * C + bias[j])
+ *   scale = act_lipschitz(act) * (|alpha| * sqrt(sum (a*b)^2) + |beta * C| + |bias[j]|) */
+void oracle_gemm_f64_epilogue(int m, int n, int k, const uint16_t* a, int lda, const uint16_t* b, int ldb,
+                              const float* c, int ldc, float alpha, float beta, const int* rows, int nrows,
+                              double* d, int ldd, double* scale, int fmt, const float* bias, int act) {
   double (*decode)(uint16_t) = fmt == 1 ? bf16_bits_to_double : half_bits_to_double;
   if (m <= 0 || n <= 0) return;
   if (!rows) nrows = m;
@@ -165,13 +182,22 @@ void oracle_gemm_f64_fmt(int m, int n, int k, const uint16_t* a, int lda, const 
     }
     for (int j = 0; j < n; ++j) {
       const double cv = read_c ? (double)c[(int64_t)row * ldc + j] : 0.0;
-      d[(int64_t)r * ldd + j] = (double)alpha * acc[j] + (double)beta * cv;
-      if (scale) scale[(int64_t)r * ldd + j] = fabs((double)alpha) * sqrt(sq[j]) + fabs((double)beta * cv);
+      const double bv = bias ? (double)bias[j] : 0.0;
+      d[(int64_t)r * ldd + j] = activate((double)alpha * acc[j] + (double)beta * cv + bv, act);
+      if (scale)
+        scale[(int64_t)r * ldd + j] =
+            act_lipschitz(act) * (fabs((double)alpha) * sqrt(sq[j]) + fabs((double)beta * cv) + fabs(bv));
     }
   }
   free(acc);
   free(sq);
   free(brow);
+}
+
+void oracle_gemm_f64_fmt(int m, int n, int k, const uint16_t* a, int lda, const uint16_t* b, int ldb,
+                         const float* c, int ldc, float alpha, float beta, const int* rows, int nrows,
+                         double* d, int ldd, double* scale, int fmt) {
+  oracle_gemm_f64_epilogue(m, n, k, a, lda, b, ldb, c, ldc, alpha, beta, rows, nrows, d, ldd, scale, fmt, NULL, 0);
 }
 
 void oracle_gemm_f64(int m, int n, int k, const uint16_t* a, int lda, const uint16_t* b, int ldb,

@@ -34,11 +34,12 @@ def _plan(A, Bs, C, D, n, k, capacity, cfg, beta=0.0, alpha=1.0):
                       D.data_ptr(), n, C.data_ptr() if C is not None else None, n, alpha, beta, cfg)
 
 
-def _executor_reference(A, Bs, C, rows, n, k, cfg, alpha=1.0, beta=0.0):
-    """D of the same problems through the host-prepared executor (per-problem pointers)."""
+def _executor_reference(A, Bs, C, rows, n, k, cfg, alpha=1.0, beta=0.0, bias=None, dtype=None):
+    """D of the same problems through the host-prepared executor (per-problem pointers); bias:
+    one device pointer (or None) per expert; dtype: D's torch dtype (default FP32)."""
     import torch
 
-    D2 = torch.full((A.shape[0], n), float("nan"), device=A.device)
+    D2 = torch.full((A.shape[0], n), float("nan"), device=A.device, dtype=dtype or torch.float32)
     probs, r0 = [], 0
     for e, r in enumerate(rows):
         a = A[r0:r0 + max(r, 0)]
@@ -47,7 +48,14 @@ def _executor_reference(A, Bs, C, rows, n, k, cfg, alpha=1.0, beta=0.0):
                                     c.data_ptr() if c is not None and r > 0 else None,
                                     D2[r0:].data_ptr(), A.stride(0), n, n, n, alpha, beta))
         r0 += r
-    assert gg.run_grouped_gemm_once(probs, gg.SortMode.kNone, cfg) == 0
+    if bias is None:
+        assert gg.run_grouped_gemm_once(probs, gg.SortMode.kNone, cfg) == 0
+    else:
+        ex = gg.GroupedGemmExecutor()
+        assert ex.build(gg.prepare_problem_set(probs, cfg, gg.SortMode.kNone), cfg, bias=bias) == 0
+        assert ex.run() == 0
+        torch.cuda.synchronize()
+        ex.close()
     torch.cuda.synchronize()
     return D2
 
@@ -171,4 +179,45 @@ def test_plan_with_more_experts_than_one_preparation_block(cuda):
     used = sum(rows)
     assert torch.equal(D[:used], ref[:used])
     assert torch.isnan(D[used:]).all()
+    plan.close()
+
+
+@pytest.mark.parametrize("out", [gg.OutputType.kF16, gg.OutputType.kBF16], ids=["F16", "BF16"])
+@pytest.mark.parametrize("cfg", [gg.KernelConfig(128, 256, 64), gg.KernelConfig(256, 128, 64),
+                                 gg.KernelConfig(128, 128, 64, use_tensor_cores=False)],
+                         ids=["128x256", "256x128", "simt128x128"])
+def test_plan_output_type_bias_activation(cuda, cfg, out):
+    """16-bit packed C/D, per-expert bias (one expert without) and GELU: the plan matches the
+    executor bit for bit, rows past the problems stay untouched, and one expert meets the oracle."""
+    import torch
+
+    dt = torch.float16 if out == gg.OutputType.kF16 else torch.bfloat16
+    rows = [130, 0, 257, 31, 64, 7]
+    n, k, capacity = 200, 96, 600
+    A, Bs, C, _ = _setup(cuda, rows, n, k, capacity, beta=0.5, seed=4)
+    C = C.to(dt)
+    D = torch.full((capacity, n), float("nan"), device=cuda, dtype=dt)
+    g = torch.Generator(device=cuda).manual_seed(9)
+    biases = [None if e == 3 else torch.empty(n, device=cuda).uniform_(-1, 1, generator=g) for e in range(len(rows))]
+    ptrs = [None if t is None else t.data_ptr() for t in biases]
+    run_cfg = gg.KernelConfig(cfg.cta_m, cfg.cta_n, cfg.cta_k, use_tensor_cores=cfg.use_tensor_cores,
+                              output_type=out, activation=gg.Activation.kGELU)
+    plan = gg.MoePlan(len(rows), n, k, capacity, A.data_ptr(), k, [b.data_ptr() for b in Bs], n, D.data_ptr(), n,
+                      C.data_ptr(), n, 1.25, 0.5, run_cfg, bias_ptrs=ptrs)
+    assert plan.run(torch.tensor(rows, dtype=torch.int32, device=cuda)) == 0
+    assert plan.status()[0] == 0
+    ref = _executor_reference(A, Bs, C, rows, n, k, run_cfg, alpha=1.25, beta=0.5, bias=ptrs, dtype=dt)
+    used = sum(rows)
+    assert torch.equal(D[:used].float().nan_to_num(7.0), ref[:used].float().nan_to_num(7.0))
+    assert not torch.isnan(D[:used].float()).any()
+    assert torch.isnan(D[used:].float()).all()
+    for e in (2, 3):
+        r0 = sum(rows[:e])
+        a = A[r0:r0 + rows[e]].cpu().numpy()
+        c = C[r0:r0 + rows[e]].float().cpu().numpy()
+        bias = None if biases[e] is None else biases[e].cpu().numpy()
+        ref64, scale = O.gemm_f64(rows[e], n, k, a, k, Bs[e].cpu().numpy(), n, c, n, 1.25, 0.5, bias=bias,
+                                  act=int(gg.Activation.kGELU))
+        err = O.rel_err(D[r0:r0 + rows[e]].float().cpu().numpy(), ref64, scale, int(out))
+        assert err <= O.tolerance(k)
     plan.close()

@@ -274,3 +274,23 @@ def test_input_type_is_validated_on_the_host():
         prep = gg.prepare_problem_set([], cfg, 0)
         assert ex.build(prep, cfg) == want
         ex.close()
+
+
+def test_output_type_and_activation_are_validated_on_the_host():
+    """output_type must be GG_OUTPUT_F32/F16/BF16 (0..2) and activation GG_ACT_NONE/RELU/GELU
+    (0..2); anything else is an invalid config (status 1), checked before any device work."""
+    for out, act, want in ((0, 0, 0), (1, 2, 0), (2, 1, 0), (3, 0, 1), (-1, 0, 1), (0, 3, 1), (1, -1, 1)):
+        cfg = gg.KernelConfig(128, 128, 64, output_type=out, activation=act)
+        ex = gg.GroupedGemmExecutor()
+        prep = gg.prepare_problem_set([], cfg, 0)
+        assert ex.build(prep, cfg) == want
+        assert ex.build(prep, cfg, bias=[]) == want
+        ex.close()
+
+
+def test_bias_table_length_must_match_the_problem_count():
+    cfg = gg.KernelConfig(128, 128, 64)
+    ex = gg.GroupedGemmExecutor()
+    prep = gg.prepare_problem_set([], cfg, 0)
+    assert ex.build(prep, cfg, bias=[None]) == gg.capi.CUDA_ERROR_INVALID_VALUE
+    ex.close()

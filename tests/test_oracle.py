@@ -192,3 +192,37 @@ def test_bf16_decode_and_gemm_against_numpy():
     c = rng.uniform(-1, 1, size=(m, n)).astype(np.float32)
     d, _ = O.gemm_f64(m, n, k, a16, k, b16, n, c, n, 1.5, -0.5, fmt=1)
     assert np.allclose(d, 1.5 * ad @ bd - 0.5 * c.astype(np.float64), rtol=0, atol=1e-12)
+
+
+def test_epilogue_bias_and_activations_against_numpy():
+    """oracle_gemm_f64_epilogue: D = act(alpha*A*B + beta*C + bias) for ReLU and the tanh form of
+    GELU, scale = L * (|alpha| sqrt(sum p^2) + |beta c| + |bias|) with L = 1.13 for GELU; and the
+    16-bit output rounding allowance of rel_err."""
+    rng = np.random.default_rng(12)
+    m, n, k = 6, 9, 17
+    a = rng.uniform(-1, 1, size=(m, k)).astype(np.float16)
+    b = rng.uniform(-1, 1, size=(k, n)).astype(np.float16)
+    c = rng.uniform(-1, 1, size=(m, n)).astype(np.float32)
+    bias = rng.uniform(-1, 1, size=n).astype(np.float32)
+    p = a.astype(np.float64)[:, :, None] * b.astype(np.float64)[None, :, :]
+    z = 1.5 * p.sum(1) - 0.5 * c + bias
+    base_scale = 1.5 * np.sqrt((p * p).sum(1)) + np.abs(0.5 * c) + np.abs(bias)
+    gelu = 0.5 * z * (1.0 + np.tanh(np.sqrt(2.0 / np.pi) * (z + 0.044715 * z ** 3)))
+    for act, want, lip in ((0, z, 1.0), (1, np.maximum(z, 0.0), 1.0), (2, gelu, 1.13)):
+        d, s = O.gemm_f64(m, n, k, a.view(np.uint16), k, b.view(np.uint16), n, c, n, 1.5, -0.5, bias=bias, act=act)
+        assert np.allclose(d, want, rtol=0, atol=1e-12)
+        assert np.allclose(s, lip * base_scale, rtol=1e-12, atol=0)
+    # the selected-rows path indexes bias by output column
+    d_rows, _ = O.gemm_f64(m, n, k, a.view(np.uint16), k, b.view(np.uint16), n, c, n, 1.5, -0.5, rows=[4, 1],
+                           bias=bias, act=2)
+    assert np.allclose(d_rows, gelu[[4, 1]], rtol=0, atol=1e-12)
+    # rel_err: an FP16-rounded result is within its rounding allowance, an FP32 check is stricter
+    d16 = gelu.astype(np.float16).astype(np.float64)
+    s = np.full_like(gelu, 1e-9)
+    assert O.rel_err(d16, gelu, s, out_fmt=1) == 0.0
+    assert O.rel_err(d16, gelu, s, out_fmt=0) > 0.0
+    u = gelu.astype(np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000  # round to nearest even BF16
+    dbf = u.astype(np.uint32).view(np.float32).astype(np.float64)
+    assert O.rel_err(dbf, gelu, s, out_fmt=2) == 0.0
+    assert O.rel_err(dbf, gelu, s, out_fmt=1) > 0.0
