@@ -61,6 +61,11 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU work of the cpu_baseline sample")
     ap.add_argument("--input-type", choices=["f16", "bf16"], default="f16",
                     help="A/B element type (bf16 is an extension; the reference is FP16 only)")
+    ap.add_argument("--output-type", choices=["f32", "f16", "bf16"], default="f32",
+                    help="element type of C and D (f32: the reference's)")
+    ap.add_argument("--activation", choices=["none", "relu", "gelu"], default="none",
+                    help="activation fused into the epilogue")
+    ap.add_argument("--bias", action="store_true", help="a per-column FP32 bias on every problem")
     ap.add_argument("--gather", action="store_true",
                     help="N>1: after the timed region, gather every rank's D to rank 0 over NCCL and time it")
     return ap.parse_args()
@@ -285,16 +290,33 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
     cta = tuple(int(x) for x in args.cta.split("x")) if args.cta else DEFAULT_CTA[args.workload]
-    cfg = gg.KernelConfig(*cta, input_type=1 if args.input_type == "bf16" else 0)
+    out_type = {"f32": 0, "f16": 1, "bf16": 2}[args.output_type]
+    act = {"none": 0, "relu": 1, "gelu": 2}[args.activation]
+    if args.gather and out_type != 0:
+        raise SystemExit("--gather packs FP32 D only")
+    cfg = gg.KernelConfig(*cta, input_type=1 if args.input_type == "bf16" else 0, output_type=out_type,
+                          activation=act)
+    plain = out_type == 0 and act == 0 and not args.bias and args.input_type == "f16"
     shapes, global_flops = rank_shapes(args.workload, world, rank, cfg)
-    ps = W.allocate(shapes, dev, seed=42 + rank, d_fill=0.0)
-    if args.input_type == "bf16":
-        ps.to_bf16()
+
+    def make_set():
+        p = W.allocate(shapes, dev, seed=42 + rank, d_fill=0.0)
+        if args.input_type == "bf16":
+            p.to_bf16()
+        if out_type:
+            p.to_output(out_type)
+        return p, (p.make_bias(without=0.0, aligned=True) if args.bias else None)
+
+    def build(p_set, bias_ptrs, mode):
+        prepared = gg.prepare_problem_set(p_set.problems(), cfg, mode)
+        e = gg.GroupedGemmExecutor()
+        sb = None if bias_ptrs is None else [bias_ptrs[o] for o in prepared.sorted_to_original]
+        return e, e.build(prepared, cfg, bias=sb)
+
+    ps, bias_ptrs = make_set()
     problems = ps.problems()
     prep_t0 = time.perf_counter()
-    prep = gg.prepare_problem_set(problems, cfg, args.sort_mode)
-    ex = gg.GroupedGemmExecutor()
-    st = ex.build(prep, cfg)
+    ex, st = build(ps, bias_ptrs, args.sort_mode)
     prep_ms = 1e3 * (time.perf_counter() - prep_t0)
     if st != 0:
         raise RuntimeError(f"executor build failed: {st}")
@@ -319,7 +341,7 @@ def main():
     clocks.start()
     for _ in range(max(args.warmup, 3)):
         assert ex.run(stream) == 0
-    alg_bytes = shapes.algorithmic_bytes()
+    alg_bytes = shapes.algorithmic_bytes(4 if out_type == 0 else 2, args.bias)
     # Inputs smaller than twice L2 would stay cache-resident from one step to the next: such
     # workloads flush L2 (write a buffer larger than L2) before every step and time each step
     # alone; larger ones run back to back.
@@ -395,8 +417,8 @@ def main():
             h_c = torch.empty(ps.c.shape, dtype=ps.c.dtype, pin_memory=True)
             h_c.copy_(ps.c)
         h_d = torch.empty(ps.d.shape, dtype=ps.d.dtype, pin_memory=True)
-        h2d = h_a.numel() * 2 + h_b.numel() * 2 + (h_c.numel() * 4 if h_c is not None else 0)
-        d2h = h_d.numel() * 4
+        h2d = h_a.numel() * 2 + h_b.numel() * 2 + (h_c.numel() * h_c.element_size() if h_c is not None else 0)
+        d2h = h_d.numel() * h_d.element_size()
 
         def e2e_step():
             with torch.cuda.stream(stream):
@@ -421,9 +443,9 @@ def main():
         # Streamed: two device buffer sets, copies in on one stream, the grouped GEMM on another,
         # copies out on a third, so step i+1's inputs cross PCIe while step i computes and step
         # i-1's D comes back. Every step still moves its own inputs in and its D out.
-        ps_b = W.allocate(shapes, dev, seed=42 + rank, d_fill=0.0)  # overwritten by the copies in
-        ex_b = gg.GroupedGemmExecutor()
-        assert ex_b.build(gg.prepare_problem_set(ps_b.problems(), cfg, args.sort_mode), cfg) == 0
+        ps_b, bias_b = make_set()  # A/B/C overwritten by the copies in
+        ex_b, st_b = build(ps_b, bias_b, args.sort_mode)
+        assert st_b == 0
         sets = [(ps, ex), (ps_b, ex_b)]
         s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         in_done = [torch.cuda.Event() for _ in range(2)]
@@ -480,9 +502,8 @@ def main():
     if not args.no_extras and world == 1:
         sweep = {}
         for mode in range(4):
-            p2 = gg.prepare_problem_set(problems, cfg, mode)
-            ex2 = gg.GroupedGemmExecutor()
-            assert ex2.build(p2, cfg) == 0
+            ex2, st2 = build(ps, bias_ptrs, mode)
+            assert st2 == 0
             for _ in range(5):
                 ex2.run(stream)
             torch.cuda.synchronize()
@@ -499,8 +520,8 @@ def main():
         extras["sort_modes"] = sweep
         extras["cuda_graph"] = graph_row(ex, stream, local_flops)
         if args.workload == "moe":
-            extras["device_prep"] = moe_plan_row(ps, shapes, cfg, stream, local_flops, ms)
-        if args.input_type == "f16":  # the reference's kernels read FP16 only
+            extras["device_prep"] = moe_plan_row(ps, shapes, cfg, stream, local_flops, ms, bias_ptrs)
+        if plain:  # the reference's kernels: FP16 in, FP32 out, no fused bias or activation
             extras["ref_gpu"] = reference_gpu_row(problems, stream, local_flops)
 
     cpu = None
@@ -521,7 +542,8 @@ def main():
                              (f"footprint {alg_bytes / 1e6:.1f} MB < 2 x L2: L2 flushed ({4 * L2_BYTES >> 20} MB "
                               f"write, then a {2 * L2_BYTES >> 20} MB read so no dirty line is left) before every "
                               "step, each step timed alone"),
-                       "accumulate": "f32",
+                       "accumulate": "f32", "output_type": args.output_type, "activation": args.activation,
+                       "bias": bool(args.bias),
                        "prep_build_ms": prep_ms, "parallelism": f"dp{world} (tile-balanced shards)"},
             "pct_dense_fp16_peak": 100.0 * value / (world * peaks["bf16_tflops"]),
             "peak_source": peaks["source"],
@@ -585,7 +607,7 @@ def gather_row(args, cfg, ps, world, rank, dev, max_over_ranks, barrier):
                    "unpacked into the full D of every global problem"}
 
 
-def moe_plan_row(ps, shapes, cfg, stream, flops, executor_ms, runs=20):
+def moe_plan_row(ps, shapes, cfg, stream, flops, executor_ms, bias_ptrs=None, runs=20):
     """The same MoE problems through gg_moe_plan: row counts read from device memory, device-side
     preparation kernel + grouped kernel per run (the workload's slabs are already row-packed)."""
     import torch
@@ -600,7 +622,8 @@ def moe_plan_row(ps, shapes, cfg, stream, flops, executor_ms, runs=20):
         return {"unavailable": "problems do not share n, k or are not row-packed"}
     b_ptrs = [ps.b.data_ptr() + 2 * off for off in ps.b_off]
     plan = gg.MoePlan(len(rows), n, k, sum(rows), ps.a.data_ptr() + 2 * ps.a_off[0], k, b_ptrs, n,
-                      ps.d.data_ptr() + 4 * ps.d_off[0], n, None, n, 1.0, 0.0, cfg)
+                      ps.d.data_ptr() + ps.d.element_size() * ps.d_off[0], n, None, n, 1.0, 0.0, cfg,
+                      bias_ptrs=bias_ptrs)
     rows_t = torch.tensor(rows, dtype=torch.int32, device=ps.a.device)
     ref = ps.d.clone()
     torch.cuda.synchronize()

@@ -215,6 +215,8 @@ struct EpiTile {
 template <typename Release>
 __device__ __forceinline__ void epilogue_warp(int fmt, uint8_t* stage, uint32_t& store_count, uint32_t t_addr,
                                               int lane, const EpiTile& e, Release release) {
+  const float* bias = e.bias;
+  const int act = e.act;
   static_assert(kEpiWarpBytes == 4096, "one FP32 or two 16-bit staging tiles per epilogue warp");
   const bool out32 = fmt == kOutF32;
   const int eb = out32 ? 4 : 2;                // bytes per C / D element
@@ -300,9 +302,18 @@ __device__ __forceinline__ void epilogue_warp(int fmt, uint8_t* stage, uint32_t&
 #pragma unroll
           for (int j = 0; j < 32; ++j) cv[j] *= e.beta;
         }
-        // Lane j loads column cc + j's bias; the warp shares it by shuffles as the values are used.
-        const float bl = e.bias && cc + lane < n ? __ldg(e.bias + cc + lane) : 0.0f;
-        auto addend = [&](int j) { return e.bias ? cv[j] + __shfl_sync(0xffffffffu, bl, j) : cv[j]; };
+        if (bias) {  // lane j loads column cc + j's bias (an L1 hit: prefetched); shuffles share it
+          const float bl = cc + lane < n ? __ldg(bias + cc + lane) : 0.0f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) cv[j] += __shfl_sync(0xffffffffu, bl, j);
+        }
+        // the chunk's results, in cv: alpha * acc + (beta * C + bias), then the activation
+#pragma unroll
+        for (int j = 0; j < 32; ++j) cv[j] = fmaf(e.alpha, __uint_as_float(r[sub * 32 + j]), cv[j]);
+        if (act != GG_ACT_NONE) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) cv[j] = activate(cv[j], act);
+        }
         uint8_t* stile = stage + (two_tiles ? static_cast<int>(store_count & 1u) * tile_bytes : 0);
         if (lane == 0) {  // the store that last used this staging tile has read it
           if (two_tiles) ptx::bulk_wait_read_le1();
@@ -311,34 +322,17 @@ __device__ __forceinline__ void epilogue_warp(int fmt, uint8_t* stage, uint32_t&
         __syncwarp();
         if (out32) {
 #pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4) {
-            const int j = sub * 32 + 4 * j4;
-            float4 o = make_float4(fmaf(e.alpha, __uint_as_float(r[j]), addend(4 * j4)),
-                                   fmaf(e.alpha, __uint_as_float(r[j + 1]), addend(4 * j4 + 1)),
-                                   fmaf(e.alpha, __uint_as_float(r[j + 2]), addend(4 * j4 + 2)),
-                                   fmaf(e.alpha, __uint_as_float(r[j + 3]), addend(4 * j4 + 3)));
-            o = activate4(o, e.act);
-            *reinterpret_cast<float4*>(stile + lane * 128 + ((j4 ^ (lane & 7)) << 4)) = o;
-          }
+          for (int j4 = 0; j4 < 8; ++j4)
+            *reinterpret_cast<float4*>(stile + lane * 128 + ((j4 ^ (lane & 7)) << 4)) =
+                make_float4(cv[4 * j4], cv[4 * j4 + 1], cv[4 * j4 + 2], cv[4 * j4 + 3]);
         } else {
+          // 64-byte rows, 64-byte swizzle: 16-byte unit j8 of row `lane` sits at j8 ^ ((lane >> 1) & 3)
 #pragma unroll
-          for (int j8 = 0; j8 < 4; ++j8) {
-            const int j = sub * 32 + 8 * j8;
-            float4 lo = make_float4(fmaf(e.alpha, __uint_as_float(r[j]), addend(8 * j8)),
-                                    fmaf(e.alpha, __uint_as_float(r[j + 1]), addend(8 * j8 + 1)),
-                                    fmaf(e.alpha, __uint_as_float(r[j + 2]), addend(8 * j8 + 2)),
-                                    fmaf(e.alpha, __uint_as_float(r[j + 3]), addend(8 * j8 + 3)));
-            float4 hi = make_float4(fmaf(e.alpha, __uint_as_float(r[j + 4]), addend(8 * j8 + 4)),
-                                    fmaf(e.alpha, __uint_as_float(r[j + 5]), addend(8 * j8 + 5)),
-                                    fmaf(e.alpha, __uint_as_float(r[j + 6]), addend(8 * j8 + 6)),
-                                    fmaf(e.alpha, __uint_as_float(r[j + 7]), addend(8 * j8 + 7)));
-            lo = activate4(lo, e.act);
-            hi = activate4(hi, e.act);
-            // 64-byte rows, 64-byte swizzle: 16-byte unit j8 of row `lane` sits at j8 ^ ((lane >> 1) & 3)
+          for (int j8 = 0; j8 < 4; ++j8)
             *reinterpret_cast<uint4*>(stile + lane * 64 + ((j8 ^ ((lane >> 1) & 3)) << 4)) =
-                make_uint4(pack2_rt(fmt, lo.x, lo.y), pack2_rt(fmt, lo.z, lo.w), pack2_rt(fmt, hi.x, hi.y),
-                           pack2_rt(fmt, hi.z, hi.w));
-          }
+                make_uint4(pack2_rt(fmt, cv[8 * j8], cv[8 * j8 + 1]), pack2_rt(fmt, cv[8 * j8 + 2], cv[8 * j8 + 3]),
+                           pack2_rt(fmt, cv[8 * j8 + 4], cv[8 * j8 + 5]),
+                           pack2_rt(fmt, cv[8 * j8 + 6], cv[8 * j8 + 7]));
         }
         ptx::fence_proxy_async_smem();
         __syncwarp();
@@ -403,10 +397,10 @@ __device__ __forceinline__ void epilogue_warp(int fmt, uint8_t* stage, uint32_t&
             make_uint4(r[4 * j4], r[4 * j4 + 1], r[4 * j4 + 2], r[4 * j4 + 3]);
       __syncwarp();
       float bv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      if (e.bias) {
+      if (bias) {
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-          if (gcol + q < n) bv[q] = __ldg(e.bias + gcol + q);
+          if (gcol + q < n) bv[q] = __ldg(bias + gcol + q);
       }
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -416,7 +410,7 @@ __device__ __forceinline__ void epilogue_warp(int fmt, uint8_t* stage, uint32_t&
         if (grow < m && gcol < n) {
           float4 o = make_float4(fmaf(e.alpha, a4.x, cv[4 * i] + bv[0]), fmaf(e.alpha, a4.y, cv[4 * i + 1] + bv[1]),
                                  fmaf(e.alpha, a4.z, cv[4 * i + 2] + bv[2]), fmaf(e.alpha, a4.w, cv[4 * i + 3] + bv[3]));
-          o = activate4(o, e.act);
+          o = activate4(o, act);
           const int64_t di = static_cast<int64_t>(grow) * e.ldd + gcol;
           if (dvec && gcol + 4 <= n) {
             store_out4_rt(fmt, static_cast<char*>(e.d) + di * eb, o);
@@ -435,6 +429,17 @@ __device__ __forceinline__ void epilogue_warp(int fmt, uint8_t* stage, uint32_t&
     ptx::tc_fence_before_sync();
     __syncwarp();
     if (lane == 0) release();
+  }
+}
+
+// Brings the bias of this warp's chunks into L1 before the accumulator wait (lane j: column
+// col0 + c * 32 + j of each chunk c), so that the epilogue's loads of it hit L1 instead of waiting
+// on L2 or DRAM; holds no registers across the wait.
+__device__ __forceinline__ void epilogue_bias_prefetch(const EpiTile& e, int lane) {
+  if (!e.bias) return;
+  for (int c = e.c_begin; c < e.c_end; ++c) {
+    const int col = e.col0 + c * 32 + lane;
+    if (col < e.n) ptx::prefetch_l1(e.bias + col);
   }
 }
 
@@ -825,18 +830,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(ringe_bar(slot));
       if (q < 0) break;
-      const int buf = t % kAcc;
-      if (et == 0)
-        epi_go[1] = wait_phase(accf_bar(buf), static_cast<uint32_t>(t / kAcc) & 1u, abort_flag, p.status, tmo,
-                               GG_STATUS_TIMEOUT_EPILOGUE) ? 1 : 0;
-      ptx::named_bar_sync(2, kEpiThreads);
-      if (!epi_go[1]) break;
-      ptx::tc_fence_after_sync();
-
       const int nchunks = min(BN / 32, (n - tile_n * BN + 31) / 32);  // tile-uniform
       int c_begin, c_end;
       epilogue_chunk_range(nchunks, half, c_begin, c_end);
-      const uint32_t t_addr = tmem_base + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(qw * 32) << 16);
       // Warps whose 32 rows lie past BM (64-row tiles) or past M store nothing.
       e.row0 = qw * 32 < BM ? tile_m * BM + qw * 32 : m;
       e.m = m;
@@ -848,8 +844,18 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
       e.bias = p.bias ? p.bias[map_slot] : nullptr;
       e.act = p.activation;
       e.md = maps + kMapsPerProblem * map_slot + kMapD;
+      epilogue_bias_prefetch(e, lane);  // its latency hides behind the accumulator wait
+      const int buf = t % kAcc;
+      if (et == 0)
+        epi_go[1] = wait_phase(accf_bar(buf), static_cast<uint32_t>(t / kAcc) & 1u, abort_flag, p.status, tmo,
+                               GG_STATUS_TIMEOUT_EPILOGUE) ? 1 : 0;
+      ptx::named_bar_sync(2, kEpiThreads);
+      if (!epi_go[1]) break;
+      ptx::tc_fence_after_sync();
+
+      const uint32_t t_addr = tmem_base + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(qw * 32) << 16);
       epilogue_warp(p.output_format, smem + L::kEpiOffset + warp * kEpiWarpBytes, store_count, t_addr, lane, e,
-                        [&] { ptx::mbar_arrive(acce_bar(buf)); });
+                    [&] { ptx::mbar_arrive(acce_bar(buf)); });
     }
     if (lane == 0) ptx::bulk_wait_all();  // every warp issues its own TMA stores
     __syncwarp();

@@ -383,18 +383,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) release_slot(slot);
       if (q < 0) break;
-      const int buf = t % kAcc;
-      if (et == 0)
-        epi_go[1] = wait_phase(accf_bar(buf), static_cast<uint32_t>(t / kAcc) & 1u, abort_flag, p.status, tmo,
-                               GG_STATUS_TIMEOUT_EPILOGUE) ? 1 : 0;
-      ptx::named_bar_sync(2, kEpiThreads);
-      if (!epi_go[1]) break;
-      ptx::tc_fence_after_sync();
-
       const int nchunks = min(BN / 32, (n - tile_n * BN + 31) / 32);
       int c_begin, c_end;
       epilogue_chunk_range(nchunks, half, c_begin, c_end);
-      const uint32_t t_addr = tmem_base + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(qw * 32) << 16);
       e.row0 = tile_m * BM + static_cast<int>(rank) * 128 + qw * 32;  // this warp's first row
       e.m = m;
       e.n = n;
@@ -405,11 +396,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       e.bias = p.bias ? p.bias[map_slot] : nullptr;
       e.act = p.activation;
       e.md = maps + kMapsPerProblem * map_slot + kMapD;
+      epilogue_bias_prefetch(e, lane);  // its latency hides behind the accumulator wait
+      const int buf = t % kAcc;
+      if (et == 0)
+        epi_go[1] = wait_phase(accf_bar(buf), static_cast<uint32_t>(t / kAcc) & 1u, abort_flag, p.status, tmo,
+                               GG_STATUS_TIMEOUT_EPILOGUE) ? 1 : 0;
+      ptx::named_bar_sync(2, kEpiThreads);
+      if (!epi_go[1]) break;
+      ptx::tc_fence_after_sync();
+
+      const uint32_t t_addr = tmem_base + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(qw * 32) << 16);
       epilogue_warp(p.output_format, smem + L::kEpiOffset + warp * kEpiWarpBytes, store_count, t_addr, lane, e,
-                        [&] {
-                          if (leader) ptx::mbar_arrive(acce_bar(buf));
-                          else ptx::mbar_arrive_cluster(ptx::mapa_shared(acce_bar(buf), 0));
-                        });
+                    [&] {
+                      if (leader) ptx::mbar_arrive(acce_bar(buf));
+                      else ptx::mbar_arrive_cluster(ptx::mapa_shared(acce_bar(buf), 0));
+                    });
     }
     if (lane == 0) ptx::bulk_wait_all();  // every warp issues its own TMA stores
     __syncwarp();

@@ -75,6 +75,11 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 // ---- TMA ----------------------------------------------------------------------------------
+// Brings the line holding p into L1 (a hint: no register result, no fault on any address).
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p) : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

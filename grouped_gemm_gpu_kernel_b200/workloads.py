@@ -44,15 +44,18 @@ class Shapes:
     def flops(self) -> float:
         return float(sum(2.0 * m * n * k for m, n, k in self.dims))
 
-    def algorithmic_bytes(self) -> float:
-        """A and B read once, D written once, C read when beta != 0 (FP16 A/B, FP32 C/D)."""
+    def algorithmic_bytes(self, out_bytes: int = 4, bias: bool = False) -> float:
+        """A and B read once (16-bit), D written once, C read when beta != 0 (out_bytes per C/D
+        element: 4 for FP32, 2 for FP16/BF16), and, with `bias`, n FP32 bias values per problem."""
         tot = 0.0
         for (m, n, k), b in zip(self.dims, self.beta):
             if m <= 0 or n <= 0:
                 continue
-            tot += 2.0 * m * k + 2.0 * k * n + 4.0 * m * n
+            tot += 2.0 * m * k + 2.0 * k * n + out_bytes * m * n
             if self.has_c and b != 0.0:
-                tot += 4.0 * m * n
+                tot += out_bytes * m * n
+            if bias:
+                tot += 4.0 * n
         return tot
 
 
@@ -142,10 +145,11 @@ class DeviceProblemSet:
         self.out_fmt = int(out_fmt)
         return self
 
-    def make_bias(self, seed: int = 7, without: float = 0.25) -> List[Optional[int]]:
+    def make_bias(self, seed: int = 7, without: float = 0.25, aligned: bool = False) -> List[Optional[int]]:
         """One FP32 bias vector of n values ~ U[-1,1] per problem, a seeded fraction `without` of
         the problems having none; returns the device pointers in problem order (None: no bias).
-        Each vector starts 4 bytes past a 256-byte boundary, so no vector is 16-byte aligned."""
+        Each vector starts on a 256-byte boundary (`aligned`) or 4 bytes past one (no vector
+        16-byte aligned: the kernel's unaligned bias path)."""
         import torch
 
         rng = np.random.default_rng(seed)
@@ -155,7 +159,7 @@ class DeviceProblemSet:
             if rng.random() < without:
                 offs.append(None)
                 continue
-            offs.append(total + 1)
+            offs.append(total + (0 if aligned else 1))
             total += _aligned(max(n, 0) + 1, 4)
         g = torch.Generator(device=self.a.device)
         g.manual_seed(seed)

@@ -33,8 +33,9 @@ NONE, RELU, GELU = gg.Activation.kNone, gg.Activation.kReLU, gg.Activation.kGELU
 
 CONFIGS = [gg.KernelConfig(128, 256, 64), gg.KernelConfig(128, 128, 64), gg.KernelConfig(256, 256, 64),
            gg.KernelConfig(64, 64, 16), gg.KernelConfig(128, 128, 64, use_tensor_cores=False)]
-# (output type, activation, with bias)
-CASES = [(F16, GELU, True), (BF16, RELU, True), (F32, GELU, True), (F16, NONE, False), (BF16, NONE, True)]
+# (output type, activation, bias vectors: None, "aligned" (16-byte, vector loads) or "unaligned")
+CASES = [(F16, GELU, "unaligned"), (BF16, RELU, "aligned"), (F32, GELU, "aligned"), (F16, NONE, None),
+         (BF16, NONE, "unaligned"), (F32, RELU, "unaligned")]
 
 
 def _cfg_id(c):
@@ -43,7 +44,7 @@ def _cfg_id(c):
 
 def _case_id(case):
     out, act, bias = case
-    return f"{out.name[1:]}-{act.name[1:]}{'-bias' if bias else ''}"
+    return f"{out.name[1:]}-{act.name[1:]}{'-bias-' + bias if bias else ''}"
 
 
 def aligned_shapes(seed=3) -> W.Shapes:
@@ -135,7 +136,7 @@ def test_epilogue_extensions_match_oracle(cuda, cfg, case):
         ps = W.allocate(shapes, seed=11)
         if out != F32:
             ps.to_output(out)
-        bias = ps.make_bias() if with_bias else None
+        bias = ps.make_bias(aligned=with_bias == "aligned") if with_bias else None
         run_set(ps, run_cfg, bias)
         worst = check_full(ps, act)
         assert worst <= 1.0, f"{shapes.name}: error/tolerance {worst:.3f}"
@@ -147,7 +148,7 @@ def test_epilogue_mixed512_sampled(cuda, out):
     """The full-size benchmark set: TMA D stores of 16-bit tiles, GELU and bias on most problems."""
     ps = W.allocate(W.make_shapes("mixed512"), seed=42)
     ps.to_output(out)
-    bias = ps.make_bias()
+    bias = ps.make_bias(aligned=out == F16)
     run_set(ps, gg.KernelConfig(128, 256, 64, output_type=out, activation=GELU), bias)
     assert check_sampled(ps, GELU) <= 1.0
     assert padding_untouched(ps)
