@@ -59,8 +59,9 @@ def parse_args():
     ap.add_argument("--no-extras", action="store_true", help="skip the sort-mode sweep and the reference GPU row")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU work of the cpu_baseline sample")
-    ap.add_argument("--input-type", choices=["f16", "bf16"], default="f16",
-                    help="A/B element type (bf16 is an extension; the reference is FP16 only)")
+    ap.add_argument("--input-type", choices=["f16", "bf16", "e4m3", "e5m2"], default="f16",
+                    help="A/B element type (bf16 and the 8-bit floats are extensions; the reference is FP16 "
+                         "only); 8-bit runs pad the row pitches to 16 bytes")
     ap.add_argument("--output-type", choices=["f32", "f16", "bf16"], default="f32",
                     help="element type of C and D (f32: the reference's)")
     ap.add_argument("--activation", choices=["none", "relu", "gelu"], default="none",
@@ -294,15 +295,18 @@ def main():
     act = {"none": 0, "relu": 1, "gelu": 2}[args.activation]
     if args.gather and out_type != 0:
         raise SystemExit("--gather packs FP32 D only")
-    cfg = gg.KernelConfig(*cta, input_type=1 if args.input_type == "bf16" else 0, output_type=out_type,
+    in_type = {"f16": 0, "bf16": 1, "e4m3": 2, "e5m2": 3}[args.input_type]
+    cfg = gg.KernelConfig(*cta, input_type=in_type, output_type=out_type,
                           activation=act)
     plain = out_type == 0 and act == 0 and not args.bias and args.input_type == "f16"
     shapes, global_flops = rank_shapes(args.workload, world, rank, cfg)
 
     def make_set():
         p = W.allocate(shapes, dev, seed=42 + rank, d_fill=0.0)
-        if args.input_type == "bf16":
+        if in_type == 1:
             p.to_bf16()
+        elif in_type >= 2:
+            p.to_fp8(in_type)  # row pitches padded to 16 bytes (8-bit operands load by TMA only)
         if out_type:
             p.to_output(out_type)
         return p, (p.make_bias(without=0.0, aligned=True) if args.bias else None)
@@ -341,7 +345,7 @@ def main():
     clocks.start()
     for _ in range(max(args.warmup, 3)):
         assert ex.run(stream) == 0
-    alg_bytes = shapes.algorithmic_bytes(4 if out_type == 0 else 2, args.bias)
+    alg_bytes = shapes.algorithmic_bytes(4 if out_type == 0 else 2, args.bias, 1 if in_type >= 2 else 2)
     # Inputs smaller than twice L2 would stay cache-resident from one step to the next: such
     # workloads flush L2 (write a buffer larger than L2) before every step and time each step
     # alone; larger ones run back to back.
@@ -385,7 +389,10 @@ def main():
     peaks = load_peaks()
     local_flops = shapes.flops
     ai = local_flops / alg_bytes
-    ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    tensor_peak, tensor_src = peaks["bf16_tflops"], peaks["source"]
+    if in_type >= 2:  # no FP8 measurement: twice the measured dense BF16 rate (the FP8:BF16 ratio of B200)
+        tensor_peak, tensor_src = 2.0 * peaks["bf16_tflops"], "2 x " + peaks["source"] + " bf16"
+    ridge = tensor_peak * 1e12 / (peaks["hbm_gbs"] * 1e9)
     if ai < ridge:
         achieved = alg_bytes / (local_ms * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -393,8 +400,8 @@ def main():
                 "algorithmic_bytes_per_launch": alg_bytes}
     else:
         achieved = local_flops / (local_ms * 1e-3) / 1e12
-        roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": achieved / peaks["bf16_tflops"], "traffic": None, "peak_source": peaks["source"],
+        roof = {"bound": "tensor", "achieved": achieved, "peak": tensor_peak, "unit": "TFLOP/s",
+                "frac": achieved / tensor_peak, "traffic": None, "peak_source": tensor_src,
                 "algorithmic_flops_per_launch": local_flops}
     traffic_path = os.path.join(REPO, "profiles", "traffic.json")
     if os.path.exists(traffic_path) and world == 1:
@@ -417,7 +424,8 @@ def main():
             h_c = torch.empty(ps.c.shape, dtype=ps.c.dtype, pin_memory=True)
             h_c.copy_(ps.c)
         h_d = torch.empty(ps.d.shape, dtype=ps.d.dtype, pin_memory=True)
-        h2d = h_a.numel() * 2 + h_b.numel() * 2 + (h_c.numel() * h_c.element_size() if h_c is not None else 0)
+        h2d = (h_a.numel() * h_a.element_size() + h_b.numel() * h_b.element_size() +
+               (h_c.numel() * h_c.element_size() if h_c is not None else 0))
         d2h = h_d.numel() * h_d.element_size()
 
         def e2e_step():
@@ -620,8 +628,11 @@ def moe_plan_row(ps, shapes, cfg, stream, flops, executor_ms, bias_ptrs=None, ru
                  for i in range(len(rows) - 1))
     if not packed or any(d[1] != n or d[2] != k for d in shapes.dims):
         return {"unavailable": "problems do not share n, k or are not row-packed"}
-    b_ptrs = [ps.b.data_ptr() + 2 * off for off in ps.b_off]
-    plan = gg.MoePlan(len(rows), n, k, sum(rows), ps.a.data_ptr() + 2 * ps.a_off[0], k, b_ptrs, n,
+    ei = ps.a.element_size()
+    lda = ps.lda[0] if ps.lda else k
+    ldb = ps.ldb[0] if ps.ldb else n
+    b_ptrs = [ps.b.data_ptr() + ei * off for off in ps.b_off]
+    plan = gg.MoePlan(len(rows), n, k, sum(rows), ps.a.data_ptr() + ei * ps.a_off[0], lda, b_ptrs, ldb,
                       ps.d.data_ptr() + ps.d.element_size() * ps.d_off[0], n, None, n, 1.0, 0.0, cfg,
                       bias_ptrs=bias_ptrs)
     rows_t = torch.tensor(rows, dtype=torch.int32, device=ps.a.device)

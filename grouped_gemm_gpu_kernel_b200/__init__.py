@@ -41,6 +41,8 @@ class InputType(enum.IntEnum):
     """Element type of every A and B (GG_INPUT_*); the reference's is FP16."""
     kF16 = capi.GG_INPUT_F16
     kBF16 = capi.GG_INPUT_BF16
+    kE4M3 = capi.GG_INPUT_E4M3   # 8-bit float, 4 exponent bits, no infinities
+    kE5M2 = capi.GG_INPUT_E5M2   # 8-bit float, 5 exponent bits
 
 
 class OutputType(enum.IntEnum):
@@ -92,7 +94,7 @@ class KernelConfig:
     threads: int = 256
     persistent_ctas: int = 0
     use_tensor_cores: bool = True
-    input_type: int = 0   # InputType: FP16 A/B (the reference's type) or BF16
+    input_type: int = 0   # InputType: FP16 A/B (the reference's type), BF16, E4M3 or E5M2
     output_type: int = 0  # OutputType: FP32 C/D (the reference's type), FP16 or BF16
     activation: int = 0   # Activation applied after the bias
 

@@ -25,6 +25,8 @@ EXPORTED_SYMBOLS = (
 GG_STATUS_BAD_ROWS = 0x100
 GG_INPUT_F16 = 0
 GG_INPUT_BF16 = 1
+GG_INPUT_E4M3 = 2
+GG_INPUT_E5M2 = 3
 GG_OUTPUT_F32 = 0
 GG_OUTPUT_F16 = 1
 GG_OUTPUT_BF16 = 2

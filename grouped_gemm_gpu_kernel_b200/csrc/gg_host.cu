@@ -136,28 +136,51 @@ unsigned vector_flags(int fmt, const void* c, int ldc, const void* d, int ldd) {
   return f;
 }
 
-// B (k x n FP16, row pitch ldb) seen as 64 columns x k rows x (n / 64) full column chunks, the
-// chunk dimension 128 bytes apart: one box {64, 64, chunks} fills a whole B stage in the layout
-// the MMA reads (chunk-major, 8 KB per 64x64 chunk). Only full chunks are mapped, so no box can
-// read past a row end; tiles that reach past the last full chunk use the 2-D map instead.
-bool encode_b_chunks(CUtensorMap* map, const void* base, int k, int n, int64_t row_bytes, int chunks_per_box) {
+// Operand geometry of an input type: a 128-byte swizzle row holds 64 16-bit or 128 8-bit values,
+// so a K block is 64 or 128 deep and a B chunk 64 or 128 columns wide.
+struct InGeom {
+  bool f8;
+  int bytes;        // per element
+  int kblock;       // K elements per pipeline stage
+  int chunk;        // B columns per shared-memory chunk
+  CUtensorMapDataType type;
+};
+
+InGeom in_geom(int in_fmt) {
+  const bool f8 = in_fmt == GG_INPUT_E4M3 || in_fmt == GG_INPUT_E5M2;
+  return f8 ? InGeom{true, 1, 2 * kBK, 128, CU_TENSOR_MAP_DATA_TYPE_UINT8}
+            : InGeom{false, 2, kBK, 64, CU_TENSOR_MAP_DATA_TYPE_FLOAT16};
+}
+
+// B (k x n, row pitch ldb) seen as g.chunk columns x k rows x (n / g.chunk) full column chunks, the
+// chunk dimension 128 bytes apart: one box {chunk, kblock, chunks} fills a whole B stage in the
+// layout the MMA reads (chunk-major, 8 or 16 KB per chunk). Only full chunks are mapped, so no box
+// can read past a row end; tiles that reach past the last full chunk use the 2-D map instead.
+bool encode_b_chunks(CUtensorMap* map, const InGeom& g, const void* base, int k, int n, int64_t row_bytes,
+                     int chunks_per_box) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
-  const int full_chunks = n / 64;
-  if (!enc || k <= 0 || full_chunks <= 0 || row_bytes <= 0 || (row_bytes % 16) != 0 || !aligned16(base)) return false;
-  const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(full_chunks)};
+  const int full_chunks = n / g.chunk;
+  if (!enc || k <= 0 || full_chunks <= 0 || chunks_per_box <= 0 || row_bytes <= 0 || (row_bytes % 16) != 0 ||
+      !aligned16(base))
+    return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(g.chunk), static_cast<cuuint64_t>(k),
+                              static_cast<cuuint64_t>(full_chunks)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_bytes), 128};
-  const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(chunks_per_box)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(g.chunk), static_cast<cuuint32_t>(g.kblock),
+                             static_cast<cuuint32_t>(chunks_per_box)};
   const cuuint32_t elem_strides[3] = {1, 1, 1};
-  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box,
-                         elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r = enc(map, g.type, 3, const_cast<void*>(base), dims, strides, box, elem_strides,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
 // Device record of one problem plus its kMapsPerProblem tensor maps. TMA is used for A/B only
 // when both operands qualify, for D when it qualifies; everything else takes the zero-fill load
 // path and masked direct stores.
-DeviceProblemDesc make_device_problem(const gg_problem& p, Variant v, int out_fmt, CUtensorMap* maps, int map_slot) {
+DeviceProblemDesc make_device_problem(const gg_problem& p, Variant v, int in_fmt, int out_fmt, CUtensorMap* maps,
+                                      int map_slot) {
+  const InGeom g = in_geom(in_fmt);
   const int bm = variant_bm(v), bn = variant_bn(v);
   const int cta_rows = variant_cta_rows(v);  // A and D rows one CTA moves per tile
   const int cta_cols = variant_cta_cols(v);  // B columns one CTA loads per tile
@@ -179,16 +202,14 @@ DeviceProblemDesc make_device_problem(const gg_problem& p, Variant v, int out_fm
   const bool has_tiles = p.m > 0 && p.n > 0;
   d.tiles_m = has_tiles ? ceil_div(p.m, bm) : 0;
   d.tiles_n = has_tiles ? ceil_div(p.n, bn) : 0;
-  d.k_blocks = p.k > 0 ? ceil_div(p.k, kBK) : 0;
+  d.k_blocks = p.k > 0 ? ceil_div(p.k, g.kblock) : 0;
   unsigned flags = 0;
   std::memset(maps, 0, kMapsPerProblem * sizeof(CUtensorMap));
   if (has_tiles && p.k > 0 &&
-      encode_2d(&maps[kMapA], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, p.a, p.k, p.m, static_cast<int64_t>(p.lda) * 2, kBK,
-                cta_rows) &&
-      encode_2d(&maps[kMapB], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, p.b, p.n, p.k, static_cast<int64_t>(p.ldb) * 2, 64,
-                kBK)) {
+      encode_2d(&maps[kMapA], g.type, p.a, p.k, p.m, static_cast<int64_t>(p.lda) * g.bytes, g.kblock, cta_rows) &&
+      encode_2d(&maps[kMapB], g.type, p.b, p.n, p.k, static_cast<int64_t>(p.ldb) * g.bytes, g.chunk, g.kblock)) {
     flags |= grouped_gemm::kFlagTmaAB;
-    if (encode_b_chunks(&maps[kMapB3], p.b, p.k, p.n, static_cast<int64_t>(p.ldb) * 2, cta_cols / 64))
+    if (encode_b_chunks(&maps[kMapB3], g, p.b, p.k, p.n, static_cast<int64_t>(p.ldb) * g.bytes, cta_cols / g.chunk))
       flags |= grouped_gemm::kFlagTmaB3;
   }
   if (has_tiles && encode_d(&maps[kMapD], out_fmt, p.d, p.n, p.m, p.ldd)) flags |= grouped_gemm::kFlagTmaD;
@@ -253,12 +274,25 @@ cudaError_t launch_path(bool tc, Variant v, const KernelParams& kp, int grid, cu
 }
 
 Variant variant_of(const gg_config* c) {
-  if (!c || (c->input_type != GG_INPUT_F16 && c->input_type != GG_INPUT_BF16)) return Variant::kUnsupported;
+  if (!c || c->input_type < GG_INPUT_F16 || c->input_type > GG_INPUT_E5M2) return Variant::kUnsupported;
   if (c->output_type != GG_OUTPUT_F32 && c->output_type != GG_OUTPUT_F16 && c->output_type != GG_OUTPUT_BF16)
     return Variant::kUnsupported;
   if (c->activation != GG_ACT_NONE && c->activation != GG_ACT_RELU && c->activation != GG_ACT_GELU)
     return Variant::kUnsupported;
-  return resolve_variant(c->cta_m, c->cta_n, c->cta_k, c->threads);
+  const Variant v = resolve_variant(c->cta_m, c->cta_n, c->cta_k, c->threads);
+  // 8-bit B fills 128-column chunks: the tensor-core path needs per-CTA B widths of 128 or 256.
+  if (v != Variant::kUnsupported && c->use_tensor_cores && in_geom(c->input_type).f8 &&
+      variant_cta_cols(v) % 128 != 0)
+    return Variant::kUnsupported;
+  return v;
+}
+
+// False for an 8-bit problem with work on the tensor-core path that TMA cannot load (base not
+// 16-byte aligned, or a row pitch that is not a multiple of 16 bytes): the zero-fill loader is
+// 16-bit only, so such a problem is refused at build time.
+bool tensor_path_can_load(const DeviceProblemDesc& d, const gg_config* c) {
+  return !(c->use_tensor_cores && in_geom(c->input_type).f8 && d.tiles_m > 0 && d.k > 0 &&
+           (d.flags & grouped_gemm::kFlagTmaAB) == 0u);
 }
 
 // The data-type and epilogue fields of a launch, from a validated config.
@@ -430,7 +464,9 @@ int gg_executor_build_with_bias(gg_executor* ex, const gg_problem* sorted_proble
     const gg_problem& p = sorted_problems[i];
     if (p.m < 0 || p.n < 0 || p.k < 0) return cudaErrorInvalidValue;
     if (!p.a || !p.b || !p.d) return cudaErrorInvalidDevicePointer;
-    descs[static_cast<size_t>(i)] = gg::make_device_problem(p, v, config->output_type, &maps[static_cast<size_t>(i) * gg::kMapsPerProblem], i);
+    descs[static_cast<size_t>(i)] = gg::make_device_problem(p, v, config->input_type, config->output_type,
+                                                            &maps[static_cast<size_t>(i) * gg::kMapsPerProblem], i);
+    if (!gg::tensor_path_can_load(descs[static_cast<size_t>(i)], config)) return cudaErrorInvalidValue;
   }
   if (count == 0 || total_tiles <= 0) {
     ex->problem_count = count;
@@ -552,7 +588,8 @@ int gg_run_baseline_per_problem(const gg_problem* problems, int count, const gg_
       if (!status) return cudaErrorMemoryAllocation;
     }
     std::memset(&kp, 0, sizeof(kp));
-    kp.single_desc = gg::make_device_problem(p, v, config->output_type, kp.single_maps, 0);
+    kp.single_desc = gg::make_device_problem(p, v, config->input_type, config->output_type, kp.single_maps, 0);
+    if (!gg::tensor_path_can_load(kp.single_desc, config)) return cudaErrorInvalidValue;
     const int tiles = kp.single_desc.tiles_m * kp.single_desc.tiles_n;
     kp.status = status;
     kp.timeout_ns = gg::wait_timeout_ns();
@@ -765,7 +802,9 @@ extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count
   for (int s = 0; s < count; ++s) {
     const gg_problem& p = problems[gg::g_noalloc_order[s]];
     offs[s + 1] = offs[s] + gg::tile_count(p.m, p.n, config->cta_m, config->cta_n);
-    descs[s] = gg::make_device_problem(p, v, config->output_type, &maps[static_cast<size_t>(s) * gg::kMapsPerProblem], s);
+    descs[s] = gg::make_device_problem(p, v, config->input_type, config->output_type,
+                                       &maps[static_cast<size_t>(s) * gg::kMapsPerProblem], s);
+    if (!gg::tensor_path_can_load(descs[s], config)) return cudaErrorInvalidValue;
   }
   const int total = offs[count];
   if (total == 0) return cudaSuccess;
@@ -853,11 +892,12 @@ __device__ T block_exclusive_scan(T v, T* warp_sums, T* total) {
 
 // Problem record of expert e whose rows start at row0 of the packed tensors.
 __device__ __forceinline__ DeviceProblemDesc moe_record(const DeviceProblemDesc* templ, int e, int r, long long row0,
-                                                        int tm, int tiles_n, int t, int capacity, const __half* a,
-                                                        int lda, const void* c, int ldc, void* d, int ldd, int eb) {
+                                                        int tm, int tiles_n, int t, int capacity, const char* a,
+                                                        int lda, int a_eb, const void* c, int ldc, void* d, int ldd,
+                                                        int eb) {
   DeviceProblemDesc p = templ[e];
   p.m = r;
-  p.a = a + row0 * lda;
+  p.a = reinterpret_cast<const __half*>(a + row0 * lda * a_eb);
   p.c = c ? static_cast<const char*>(c) + row0 * ldc * eb : nullptr;
   p.d = static_cast<char*>(d) + row0 * ldd * eb;
   p.tiles_m = t > 0 ? tm : 0;
@@ -873,8 +913,8 @@ __device__ __forceinline__ DeviceProblemDesc moe_record(const DeviceProblemDesc*
 __global__ void __launch_bounds__(kMoePrepThreads) moe_prepare_kernel(
     const int* __restrict__ rows, int experts, int capacity, int bm, int tiles_n,
     const DeviceProblemDesc* __restrict__ templ, DeviceProblemDesc* __restrict__ descs, int* __restrict__ offsets,
-    int* total_tiles, int* counter, int* status, const __half* a, int lda, const void* c, int ldc, void* d,
-    int ldd, int eb) {
+    int* total_tiles, int* counter, int* status, const char* a, int lda, int a_eb, const void* c, int ldc,
+    void* d, int ldd, int eb) {
   __shared__ long long s_rows[kMoePrepThreads / 32];
   __shared__ int s_tiles[kMoePrepThreads / 32];
   __shared__ long long s_key[kMoePrepThreads];
@@ -922,7 +962,8 @@ __global__ void __launch_bounds__(kMoePrepThreads) moe_prepare_kernel(
     if (se >= 0) {
       const int sr = max(rows[se], 0);
       const int stm = sr > 0 ? (sr + bm - 1) / bm : 0;
-      descs[tid] = moe_record(templ, se, sr, s_row0[se], stm, tiles_n, st, capacity, a, lda, c, ldc, d, ldd, eb);
+      descs[tid] =
+          moe_record(templ, se, sr, s_row0[se], stm, tiles_n, st, capacity, a, lda, a_eb, c, ldc, d, ldd, eb);
       offsets[tid] = t0;
     }
   } else {
@@ -940,7 +981,7 @@ __global__ void __launch_bounds__(kMoePrepThreads) moe_prepare_kernel(
       const long long row0 = row_carry + block_exclusive_scan<long long>(r, s_rows, &rows_total);
       const int t0 = tile_carry + block_exclusive_scan<int>(t, s_tiles, &tiles_total);
       if (e < experts) {
-        descs[e] = moe_record(templ, e, r, row0, tm, tiles_n, t, capacity, a, lda, c, ldc, d, ldd, eb);
+        descs[e] = moe_record(templ, e, r, row0, tm, tiles_n, t, capacity, a, lda, a_eb, c, ldc, d, ldd, eb);
         offsets[e] = t0;
       }
       row_carry += rows_total;
@@ -973,6 +1014,7 @@ struct gg_moe_plan {
   bool use_tc = true;
   int grid_ctas = 0;
   int tiles_n = 0;
+  int in_bytes = 2;   // bytes of an A / B element
   int out_bytes = 4;  // bytes of a C / D element
   gg::KernelParams params{};
 };
@@ -1000,9 +1042,13 @@ int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, g
   std::memset(maps.data(), 0, maps.size() * sizeof(CUtensorMap));
   CUtensorMap map_a{}, map_d{};
   const bool rows_exist = q.capacity_rows > 0 && q.n > 0;
+  const gg::InGeom g = gg::in_geom(config->input_type);
+  // 8-bit operands on the tensor-core path go through TMA only (see tensor_path_can_load).
+  const bool f8_tc = g.f8 && config->use_tensor_cores;
   const bool tma_a = rows_exist && q.k > 0 &&
-                     gg::encode_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, q.a, q.k, q.capacity_rows,
-                                   static_cast<int64_t>(q.lda) * 2, gg::kBK, cta_rows);
+                     gg::encode_2d(&map_a, g.type, q.a, q.k, q.capacity_rows, static_cast<int64_t>(q.lda) * g.bytes,
+                                   g.kblock, cta_rows);
+  if (f8_tc && rows_exist && q.k > 0 && !tma_a) return cudaErrorInvalidValue;
   const bool tma_d = rows_exist && gg::encode_d(&map_d, config->output_type, q.d, q.n, q.capacity_rows, q.ldd);
   for (size_t e = 0; e < E; ++e) {
     CUtensorMap* m = &maps[e * gg::kMapsPerProblem];
@@ -1020,15 +1066,18 @@ int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, g
     p.ldd = q.ldd;
     p.alpha = q.alpha;
     p.beta = q.beta;
-    p.k_blocks = q.k > 0 ? gg::ceil_div(q.k, gg::kBK) : 0;
+    p.k_blocks = q.k > 0 ? gg::ceil_div(q.k, g.kblock) : 0;
     p.map_slot = static_cast<int>(e);  // the maps stay in expert order; the records are reordered
     unsigned flags = grouped_gemm::kFlagPackedRows;
-    if (tma_a && gg::encode_2d(&m[gg::kMapB], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, q.b[e], q.n, q.k,
-                               static_cast<int64_t>(q.ldb) * 2, 64, gg::kBK)) {
+    if (tma_a && gg::encode_2d(&m[gg::kMapB], g.type, q.b[e], q.n, q.k, static_cast<int64_t>(q.ldb) * g.bytes,
+                               g.chunk, g.kblock)) {
       m[gg::kMapA] = map_a;
       flags |= grouped_gemm::kFlagTmaAB;
-      if (gg::encode_b_chunks(&m[gg::kMapB3], q.b[e], q.k, q.n, static_cast<int64_t>(q.ldb) * 2, cta_cols / 64))
+      if (gg::encode_b_chunks(&m[gg::kMapB3], g, q.b[e], q.k, q.n, static_cast<int64_t>(q.ldb) * g.bytes,
+                              cta_cols / g.chunk))
         flags |= grouped_gemm::kFlagTmaB3;
+    } else if (f8_tc && rows_exist && q.k > 0) {
+      return cudaErrorInvalidValue;
     }
     if (tma_d) {
       m[gg::kMapD] = map_d;
@@ -1080,6 +1129,7 @@ int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, g
   plan->problem.b = nullptr;  // the host arrays are not kept
   plan->problem.bias = nullptr;
   plan->out_bytes = gg::out_bytes(config->output_type);
+  plan->in_bytes = g.bytes;
   plan->variant = v;
   plan->use_tc = use_tc;
   plan->grid_ctas = grid;
@@ -1111,8 +1161,8 @@ int gg_moe_plan_run(gg_moe_plan* plan, const int* rows, void* stream) {
   const gg_moe_problem& q = plan->problem;
   gg::moe_prepare_kernel<<<1, gg::kMoePrepThreads, 0, s>>>(
       rows, q.experts, q.capacity_rows, gg::variant_bm(plan->variant), plan->tiles_n, plan->d_templ, plan->d_descs,
-      plan->d_offsets, plan->d_total, plan->d_counter, plan->d_status, static_cast<const __half*>(q.a), q.lda, q.c,
-      q.ldc, q.d, q.ldd, plan->out_bytes);
+      plan->d_offsets, plan->d_total, plan->d_counter, plan->d_status, static_cast<const char*>(q.a), q.lda, plan->in_bytes,
+      q.c, q.ldc, q.d, q.ldd, plan->out_bytes);
   cudaError_t st = cudaGetLastError();
   if (st != cudaSuccess) return st;
   return gg::launch_path(plan->use_tc, plan->variant, plan->params, plan->grid_ctas, s);

@@ -24,7 +24,8 @@
 //                          writing the same 128-byte-swizzled layout the TMA would.
 //
 // Shared-memory layout per stage: A as 128 rows x 64 K (K-major, 128-byte rows, SW128) and B as
-// BN/64 column chunks of 64 K rows x 64 N (MN-major, SW128). A 64-row tile (reference shapes
+// BN/64 column chunks of 64 K rows x 64 N (MN-major, SW128); with 8-bit A/B (kind::f8f6f4) the
+// same bytes hold 128 rows x 128 K of A and BN/128 chunks of 128 K rows x 128 N of B. A 64-row tile (reference shapes
 // 64xN) still runs an M=128 MMA; rows 64..127 of the accumulator are never stored.
 //
 // Every wait is bounded (timeout_ns from %globaltimer): a wait that runs out sets a status bit
@@ -551,6 +552,58 @@ __device__ __forceinline__ void lsu_fill_stage(uint8_t* as, uint8_t* bs, const _
   }
 }
 
+// ---- mainloop helpers ------------------------------------------------------------------------
+// The four MMAs of one K block (one shared-memory stage). F8: 8-bit A/B (kind::f8f6f4, K = 32 per
+// MMA), else 16-bit (kind::f16, K = 16); either way one MMA's K step of A is 32 bytes of the
+// 128-byte K-major row, and the element geometry is a compile-time constant here so the
+// descriptors fold.
+//   A: K-major SW128, 8-row groups 1024 bytes apart.
+//   B: MN-major SW128, one MMA's K rows = 2048 (16-bit) or 4096 (8-bit) bytes; column chunks
+//      8192 / 16384 bytes apart (leading byte offset), 8-row K groups 1024 bytes apart (stride).
+template <bool F8, bool kPair>
+__device__ __forceinline__ void mma_kblock(uint32_t d_tmem, uint32_t a0, uint32_t b0, uint32_t idesc, bool first) {
+  constexpr uint32_t kBStep = F8 ? 4096u : 2048u;
+  constexpr uint32_t kBLbo = F8 ? 16384u : 8192u;
+#pragma unroll
+  for (int kk = 0; kk < kBK / kMmaK; ++kk) {
+    const uint64_t adesc = ptx::smem_desc_sw128(a0 + kk * 32u, 16u, 1024u);
+    const uint64_t bdesc = ptx::smem_desc_sw128(b0 + kk * kBStep, kBLbo, 1024u);
+    const uint32_t acc = (!first || kk != 0) ? 1u : 0u;
+    if constexpr (kPair) {
+      if constexpr (F8) ptx::tc_mma_f8_pair(d_tmem, adesc, bdesc, idesc, acc);
+      else ptx::tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, acc);
+    } else {
+      if constexpr (F8) ptx::tc_mma_f8(d_tmem, adesc, bdesc, idesc, acc);
+      else ptx::tc_mma_f16(d_tmem, adesc, bdesc, idesc, acc);
+    }
+  }
+}
+
+// The TMA loads of one stage: A (one box of kblock K x rows) and B (one 3-D box of the whole
+// stage when b_one_box, else one 2-D box per column chunk), completing on `bar`. COLS: B columns
+// this CTA loads; F8: 8-bit operands (128-deep K blocks, 128-column chunks of 16 KB) or 16-bit
+// (64, 64, 8 KB); kPair: the cta_group::2 form whose bytes complete on the leader's barrier.
+template <int COLS, bool F8, bool kPair>
+__device__ __forceinline__ void load_stage_tma(uint32_t a_dst, uint32_t b_dst, const CUtensorMap* ma,
+                                               const CUtensorMap* mb, const CUtensorMap* mb3, uint32_t bar, int kb,
+                                               int a_row, int col0, bool b_one_box) {
+  constexpr int kKb = F8 ? 2 * kBK : kBK;
+  constexpr int kCw = F8 ? 128 : 64;
+  constexpr uint32_t kChunk = F8 ? 16384u : 8192u;
+  if constexpr (kPair) ptx::tma_load_2d_pair(a_dst, ma, bar, kb * kKb, a_row);
+  else ptx::tma_load_2d(a_dst, ma, bar, kb * kKb, a_row);
+  if (b_one_box) {
+    if constexpr (kPair) ptx::tma_load_3d_pair(b_dst, mb3, bar, 0, kb * kKb, col0 / kCw);
+    else ptx::tma_load_3d(b_dst, mb3, bar, 0, kb * kKb, col0 / kCw);
+  } else {
+#pragma unroll
+    for (int j = 0; j < COLS / kCw; ++j) {
+      if constexpr (kPair) ptx::tma_load_2d_pair(b_dst + j * kChunk, mb, bar, col0 + j * kCw, kb * kKb);
+      else ptx::tma_load_2d(b_dst + j * kChunk, mb, bar, col0 + j * kCw, kb * kKb);
+    }
+  }
+}
+
 // ---- the kernel --------------------------------------------------------------------------------
 template <int BM, int BN>
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const __grid_constant__ KernelParams p) {
@@ -652,6 +705,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
   } else if (warp >= kProdWarp0) {
     // ======================= producers =======================
     const int ptid = static_cast<int>(threadIdx.x) - kProdWarp0 * 32;
+    // Stage geometry: a 128-byte swizzle row holds 64 16-bit or 128 8-bit values, so a K block
+    // is 64 (FP16/BF16) or 128 (FP8) deep and a B chunk 64 or 128 columns wide (load_stage_tma);
+    // the stage's bytes are the same either way.
+    const bool f8 = p.input_format >= GG_INPUT_E4M3;
     uint32_t it = 0;  // global k-block counter: stage = it % S, phase = (it / S) & 1
     bool aborted = false;
     for (int t = 0;; ++t) {
@@ -681,8 +738,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
           const CUtensorMap* ma = maps + kMapsPerProblem * map_slot + kMapA;
           const CUtensorMap* mb = maps + kMapsPerProblem * map_slot + kMapB;
           const CUtensorMap* mb3 = maps + kMapsPerProblem * map_slot + kMapB3;
-          // One 3-D box loads the whole B stage when every 64-column chunk of the tile lies
-          // inside N; an edge tile loads chunk by chunk so columns past N are zero-filled.
+          // One 3-D box loads the whole B stage when every column chunk of the tile lies inside N;
+          // an edge tile loads chunk by chunk so columns past N are zero-filled.
           const bool b_one_box = (flags & grouped_gemm::kFlagTmaB3) && (tile_n + 1) * BN <= n;
           for (int kb = 0; kb < kb_count; ++kb) {
             const int st = static_cast<int>(it % S);
@@ -694,14 +751,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
             const uint32_t a_dst = sbase + static_cast<uint32_t>(st * L::kStageBytes);
             const uint32_t b_dst = a_dst + L::kABytes;
             ptx::mbar_arrive_expect_tx(full_bar(st), L::kATxBytes + L::kBTxBytes);
-            ptx::tma_load_2d(a_dst, ma, full_bar(st), kb * kBK, a_row);
-            if (b_one_box) {
-              ptx::tma_load_3d(b_dst, mb3, full_bar(st), 0, kb * kBK, tile_n * (BN / 64));
-            } else {
-#pragma unroll
-              for (int j = 0; j < BN / 64; ++j)
-                ptx::tma_load_2d(b_dst + j * 8192u, mb, full_bar(st), tile_n * BN + j * 64, kb * kBK);
-            }
+            if (f8) load_stage_tma<BN, true, false>(
+                a_dst, b_dst, ma, mb, mb3, full_bar(st), kb, a_row, tile_n * BN, b_one_box);
+            else load_stage_tma<BN, false, false>(
+                a_dst, b_dst, ma, mb, mb3, full_bar(st), kb, a_row, tile_n * BN, b_one_box);
             ++it;
           }
         } else {
@@ -723,7 +776,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
           }
           uint8_t* as = smem + st * L::kStageBytes;
           uint8_t* bs = as + L::kABytes;
-          lsu_fill_stage<BM, BN>(as, bs, a, lda, b, ldb, m, n, k, tile_m * BM, tile_n * BN, kb, ptid);
+          // 16-bit operands only: the host sends every 8-bit problem with work through TMA.
+          if (!f8) lsu_fill_stage<BM, BN>(as, bs, a, lda, b, ldb, m, n, k, tile_m * BM, tile_n * BN, kb, ptid);
           ptx::fence_proxy_async_smem();
           ptx::named_bar_sync(1, kProdThreads);
           if (ptid == 0) ptx::mbar_arrive(full_bar(st));
@@ -743,7 +797,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
   } else if (warp == kMmaWarp) {
     // ======================= MMA issuer =======================
     if (lane == 0) {
-      const uint32_t kIdesc = ptx::idesc_f16_f32_kA_mnB(kMmaM, BN, static_cast<uint32_t>(p.input_format));
+      const bool f8 = p.input_format >= GG_INPUT_E4M3;
+      const uint32_t kIdesc = ptx::idesc_f16_f32_kA_mnB(
+          kMmaM, BN, static_cast<uint32_t>(f8 ? p.input_format - GG_INPUT_E4M3 : p.input_format));
       uint32_t it = 0;
       for (int t = 0;; ++t) {
         const int slot = t % kRing;
@@ -774,16 +830,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
           ptx::tc_fence_after_sync();
           const uint32_t a0 = sbase + static_cast<uint32_t>(st * L::kStageBytes);
           const uint32_t b0 = a0 + L::kABytes;
-#pragma unroll
-          for (int kk = 0; kk < kBK / kMmaK; ++kk) {
-            // A: K-major SW128, 16-element K step = 32 bytes inside the 128-byte row;
-            //    8-row groups 1024 bytes apart.
-            // B: MN-major SW128, 16-row K step = 2048 bytes; 64-column chunks 8192 bytes
-            //    apart (leading byte offset), 8-row K groups 1024 bytes apart (stride offset).
-            const uint64_t adesc = ptx::smem_desc_sw128(a0 + kk * 32u, 16u, 1024u);
-            const uint64_t bdesc = ptx::smem_desc_sw128(b0 + kk * 2048u, 8192u, 1024u);
-            ptx::tc_mma_f16(d_tmem, adesc, bdesc, kIdesc, (kb | kk) != 0 ? 1u : 0u);
-          }
+          if (f8) mma_kblock<true, false>(d_tmem, a0, b0, kIdesc, kb == 0);
+          else mma_kblock<false, false>(d_tmem, a0, b0, kIdesc, kb == 0);
           ptx::tc_commit(empty_bar(st));  // stage is free once these MMAs have read it
           ++it;
         }

@@ -199,6 +199,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= kProdWarp0) {
     // ======================= producers (both CTAs) =======================
     const int ptid = static_cast<int>(threadIdx.x) - kProdWarp0 * 32;
+    // 16-bit operands: 64-deep K blocks, 64-column B chunks; 8-bit: 128 and 128 (same bytes).
+    const bool f8 = p.input_format >= GG_INPUT_E4M3;
+    const int cw = f8 ? 128 : 64;
     uint32_t it = 0;
     bool aborted = false;
     for (int t = 0;; ++t) {
@@ -231,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const CUtensorMap* ma = maps + kMapsPerProblem * map_slot + kMapA;
           const CUtensorMap* mb = maps + kMapsPerProblem * map_slot + kMapB;
           const CUtensorMap* mb3 = maps + kMapsPerProblem * map_slot + kMapB3;
-          const bool b_one_box = HB > 64 && (flags & grouped_gemm::kFlagTmaB3) && col_base + HB <= n;
+          const bool b_one_box = HB > cw && (flags & grouped_gemm::kFlagTmaB3) && col_base + HB <= n;
           for (int kb = 0; kb < kb_count; ++kb) {
             const int st = static_cast<int>(it % S);
             const uint32_t ph = (it / S) & 1u;
@@ -243,14 +246,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t b_dst = a_dst + L::kABytes;
             const uint32_t bar_leader = ptx::mapa_shared(full_bar(st), 0);
             if (leader) ptx::mbar_arrive_expect_tx(full_bar(st), L::kStageTxPair);
-            ptx::tma_load_2d_pair(a_dst, ma, bar_leader, kb * kBK, a_row);
-            if (b_one_box) {
-              ptx::tma_load_3d_pair(b_dst, mb3, bar_leader, 0, kb * kBK, col_base / 64);
-            } else {
-#pragma unroll
-              for (int j = 0; j < HB / 64; ++j)
-                ptx::tma_load_2d_pair(b_dst + j * 8192u, mb, bar_leader, col_base + j * 64, kb * kBK);
-            }
+            if (f8) load_stage_tma<HB, true, true>(
+                a_dst, b_dst, ma, mb, mb3, bar_leader, kb, a_row, col_base, b_one_box);
+            else load_stage_tma<HB, false, true>(
+                a_dst, b_dst, ma, mb, mb3, bar_leader, kb, a_row, col_base, b_one_box);
             // The peer's arrival only counts: its TMA bytes are tracked by complete_tx.
             if (!leader) ptx::mbar_arrive_cluster_relaxed(bar_leader);
             ++it;
@@ -274,7 +273,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* as = smem + st * L::kStageBytes;
           uint8_t* bs = as + L::kABytes;
-          lsu_fill_stage<128, HB>(as, bs, a, lda, b, ldb, m, n, k, row_base, col_base, kb, ptid);
+          // 16-bit operands only: the host sends every 8-bit problem with work through TMA.
+          if (!f8) lsu_fill_stage<128, HB>(as, bs, a, lda, b, ldb, m, n, k, row_base, col_base, kb, ptid);
           ptx::fence_proxy_async_all();  // the leader's tensor cores read this CTA's shared memory
           ptx::named_bar_sync(1, kProdThreads);
           if (ptid == 0) {
@@ -297,7 +297,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kMmaWarp) {
     // ======================= MMA issuer (leader only) =======================
     if (leader && lane == 0) {
-      const uint32_t kIdesc = ptx::idesc_f16_f32_kA_mnB(256, BN, static_cast<uint32_t>(p.input_format));
+      const bool f8 = p.input_format >= GG_INPUT_E4M3;
+      const uint32_t kIdesc = ptx::idesc_f16_f32_kA_mnB(
+          256, BN, static_cast<uint32_t>(f8 ? p.input_format - GG_INPUT_E4M3 : p.input_format));
       uint32_t it = 0;
       for (int t = 0;; ++t) {
         const int slot = t % kRing;
@@ -334,12 +336,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tc_fence_after_sync();
           const uint32_t a0 = sbase + static_cast<uint32_t>(st * L::kStageBytes);
           const uint32_t b0 = a0 + L::kABytes;
-#pragma unroll
-          for (int kk = 0; kk < kBK / kMmaK; ++kk) {
-            const uint64_t adesc = ptx::smem_desc_sw128(a0 + kk * 32u, 16u, 1024u);
-            const uint64_t bdesc = ptx::smem_desc_sw128(b0 + kk * 2048u, 8192u, 1024u);
-            ptx::tc_mma_f16_pair(d_tmem, adesc, bdesc, kIdesc, (kb | kk) != 0 ? 1u : 0u);
-          }
+          if (f8) mma_kblock<true, true>(d_tmem, a0, b0, kIdesc, kb == 0);
+          else mma_kblock<false, true>(d_tmem, a0, b0, kIdesc, kb == 0);
           ptx::tc_commit_pair_mc(empty_bar(st), 0x3);  // both CTAs' stage is free
           ++it;
         }

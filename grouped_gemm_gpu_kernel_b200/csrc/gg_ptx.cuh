@@ -153,6 +153,17 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
+// The same MMA for 8-bit A and B (E4M3 / E5M2, selected by the instruction descriptor), K = 32.
+__device__ __forceinline__ void tc_mma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  const uint32_t mask0 = 0, mask1 = 0, mask2 = 0, mask3 = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(mask0), "r"(mask1), "r"(mask2), "r"(mask3)
+      : "memory");
+}
+
 // 32 lanes x 32 consecutive FP32 columns of TMEM into 32 registers per thread (thread i gets
 // lane base+i), followed by the wait so the registers are valid when the statement ends.
 // 64 consecutive FP32 columns of the warp's 32 TMEM lanes (lane i of the warp gets row i), load
@@ -262,6 +273,16 @@ __device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t a_desc
       "r"(z)
       : "memory");
 }
+__device__ __forceinline__ void tc_mma_f8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z), "r"(z), "r"(z), "r"(z),
+      "r"(z)
+      : "memory");
+}
 // Arrive once on the mbarrier at `bar` (same offset) in every CTA of `cta_mask` when the pair's
 // tensor-core work issued so far by this thread has completed.
 __device__ __forceinline__ void tc_commit_pair_mc(uint32_t bar, uint16_t cta_mask) {
@@ -288,10 +309,10 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
-// Instruction descriptor for kind::f16 with 16-bit A and B (ab_format 0 = FP16, 1 = BF16, the
-// same for both), FP32 D, A K-major, B MN-major: D format in bits [4,6) (1 = F32), A/B formats
-// [7,10) / [10,13), A major bit 15 (0 = K), B major bit 16 (1 = MN), N >> 3 in [17,23), M >> 4 in
-// [24,29).
+// Instruction descriptor, FP32 D, A K-major, B MN-major: D format in bits [4,6) (1 = F32), A/B
+// formats [7,10) / [10,13) (the same for both; kind::f16: 0 = FP16, 1 = BF16; kind::f8f6f4:
+// 0 = E4M3, 1 = E5M2), A major bit 15 (0 = K), B major bit 16 (1 = MN), N >> 3 in [17,23),
+// M >> 4 in [24,29). The same layout serves both kinds.
 __host__ __device__ constexpr uint32_t idesc_f16_f32_kA_mnB(int m, int n, uint32_t ab_format = 0u) {
   return (1u << 4) | (ab_format << 7) | (ab_format << 10) | (0u << 15) | (1u << 16) |
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);

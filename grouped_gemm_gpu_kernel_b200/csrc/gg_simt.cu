@@ -15,6 +15,7 @@
 // operands loaded with plain zero-filled loads (any leading dimension, any alignment). No
 // spin-waits: only atomics and block barriers.
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
 #include "gg_epilogue_ops.cuh"
@@ -28,9 +29,15 @@ constexpr int kSub = 64;     // sub-tile edge
 constexpr int kSimtBK = 32;  // K per shared-memory step
 constexpr int kPad = 4;      // keeps 16-byte alignment of every row, spreads banks
 
-// One 16-bit operand element widened to FP32 (FP16, or BF16: its bits are the top half of an FP32).
-__device__ __forceinline__ float widen(const __half* x, long long i, bool bf16) {
-  if (bf16) return __uint_as_float(static_cast<unsigned>(reinterpret_cast<const unsigned short*>(x)[i]) << 16);
+// Operand element i widened to FP32, exactly: FP16; BF16 (its bits are the top half of an FP32);
+// E4M3 / E5M2 (one byte per element; every value of both is an FP16 value).
+__device__ __forceinline__ float widen(const __half* x, long long i, int fmt) {
+  if (fmt == GG_INPUT_BF16)
+    return __uint_as_float(static_cast<unsigned>(reinterpret_cast<const unsigned short*>(x)[i]) << 16);
+  if (fmt == GG_INPUT_E4M3 || fmt == GG_INPUT_E5M2) {
+    const __nv_fp8_storage_t v = reinterpret_cast<const unsigned char*>(x)[i];
+    return __half2float(__half(__nv_cvt_fp8_to_halfraw(v, fmt == GG_INPUT_E4M3 ? __NV_E4M3 : __NV_E5M2)));
+  }
   return __half2float(x[i]);
 }
 
@@ -74,7 +81,7 @@ __global__ void __launch_bounds__(kSimtThreads) grouped_gemm_simt_kernel(const _
   const int total = p.total_tiles_dev ? *p.total_tiles_dev : p.total_tiles;
   const int tid = static_cast<int>(threadIdx.x);
   const int tx = tid & 15, ty = tid >> 4;
-  const bool bf16 = p.input_format == 1;
+  const int in_fmt = p.input_format;
   int static_next = static_cast<int>(blockIdx.x);
 
   for (;;) {
@@ -132,12 +139,12 @@ __global__ void __launch_bounds__(kSimtThreads) grouped_gemm_simt_kernel(const _
           for (int i = tid; i < kSub * kSimtBK; i += kSimtThreads) {
             const int r = i / kSimtBK, kk = i % kSimtBK;
             const int gr = row0 + r, gk = k0 + kk;
-            As[kk][r] = (gr < m && gk < k) ? widen(a, static_cast<long long>(gr) * lda + gk, bf16) : 0.0f;
+            As[kk][r] = (gr < m && gk < k) ? widen(a, static_cast<long long>(gr) * lda + gk, in_fmt) : 0.0f;
           }
           for (int i = tid; i < kSimtBK * kSub; i += kSimtThreads) {
             const int kk = i / kSub, c = i % kSub;
             const int gk = k0 + kk, gc = col0 + c;
-            Bs[kk][c] = (gk < k && gc < n) ? widen(b, static_cast<long long>(gk) * ldb + gc, bf16) : 0.0f;
+            Bs[kk][c] = (gk < k && gc < n) ? widen(b, static_cast<long long>(gk) * ldb + gc, in_fmt) : 0.0f;
           }
           __syncthreads();
 #pragma unroll 8

@@ -44,14 +44,15 @@ class Shapes:
     def flops(self) -> float:
         return float(sum(2.0 * m * n * k for m, n, k in self.dims))
 
-    def algorithmic_bytes(self, out_bytes: int = 4, bias: bool = False) -> float:
-        """A and B read once (16-bit), D written once, C read when beta != 0 (out_bytes per C/D
-        element: 4 for FP32, 2 for FP16/BF16), and, with `bias`, n FP32 bias values per problem."""
+    def algorithmic_bytes(self, out_bytes: int = 4, bias: bool = False, in_bytes: int = 2) -> float:
+        """A and B read once (in_bytes per element: 2 for FP16/BF16, 1 for FP8), D written once, C
+        read when beta != 0 (out_bytes per C/D element: 4 for FP32, 2 for FP16/BF16), and, with
+        `bias`, n FP32 bias values per problem."""
         tot = 0.0
         for (m, n, k), b in zip(self.dims, self.beta):
             if m <= 0 or n <= 0:
                 continue
-            tot += 2.0 * m * k + 2.0 * k * n + out_bytes * m * n
+            tot += in_bytes * (m * k + k * n) + out_bytes * m * n
             if self.has_c and b != 0.0:
                 tot += out_bytes * m * n
             if bias:
@@ -117,6 +118,9 @@ class DeviceProblemSet:
     c_off: List[int] = field(default_factory=list)
     d_off: List[int] = field(default_factory=list)
     out_fmt: int = 0                  # C / D element type: 0 FP32, 1 FP16, 2 BF16 (KernelConfig.output_type)
+    in_fmt: int = 0                   # A / B element type: 0 FP16, 1 BF16, 2 E4M3, 3 E5M2 (KernelConfig.input_type)
+    lda: Optional[List[int]] = None   # row pitches of A and B per problem (None: packed, k and n)
+    ldb: Optional[List[int]] = None
     bias: Optional["object"] = None   # FP32 slab of per-problem bias vectors (make_bias)
     bias_off: List[Optional[int]] = field(default_factory=list)  # element offset, None = no bias
 
@@ -124,13 +128,49 @@ class DeviceProblemSet:
         from . import ProblemDesc
         out = []
         eo = 4 if self.out_fmt == 0 else 2
+        ei = self.a.element_size()
         ab, bb, db = self.a.data_ptr(), self.b.data_ptr(), self.d.data_ptr()
         cb = self.c.data_ptr() if self.c is not None else None
         for i, ((m, n, k), al, be) in enumerate(zip(self.shapes.dims, self.shapes.alpha, self.shapes.beta)):
-            out.append(ProblemDesc(m, n, k, ab + 2 * self.a_off[i], bb + 2 * self.b_off[i],
+            lda = self.lda[i] if self.lda else max(1, k)
+            ldb = self.ldb[i] if self.ldb else max(1, n)
+            out.append(ProblemDesc(m, n, k, ab + ei * self.a_off[i], bb + ei * self.b_off[i],
                                    (cb + eo * self.c_off[i]) if cb is not None else None, db + eo * self.d_off[i],
-                                   max(1, k), max(1, n), max(1, n), max(1, n), al, be))
+                                   lda, ldb, max(1, n), max(1, n), al, be))
         return out
+
+    def to_fp8(self, fmt: int) -> "DeviceProblemSet":
+        """A and B re-encoded as 8-bit floats for runs with KernelConfig.input_type = fmt (2 E4M3,
+        3 E5M2): each FP16 value rounded to the nearest 8-bit value by torch, one byte per element,
+        in new uint8 slabs whose row pitches are padded to multiples of 16 elements and whose
+        operands start on 256-byte boundaries (the tensor-core path loads 8-bit operands by TMA,
+        which needs 16-byte-aligned rows)."""
+        import torch
+
+        dt = {2: torch.float8_e4m3fn, 3: torch.float8_e5m2}[int(fmt)]
+
+        def pad16(x):
+            return (max(x, 1) + 15) // 16 * 16
+
+        lda = [pad16(k) for m, n, k in self.shapes.dims]
+        ldb = [pad16(n) for m, n, k in self.shapes.dims]
+        a_off, b_off, na, nb = [], [], 0, 0
+        for (m, n, k), la, lb in zip(self.shapes.dims, lda, ldb):
+            a_off.append(na)
+            na += _aligned(max(m, 0) * la, 1)
+            b_off.append(nb)
+            nb += _aligned(max(k, 0) * lb, 1)
+        a8 = torch.zeros(max(na, 1), dtype=torch.uint8, device=self.a.device)
+        b8 = torch.zeros(max(nb, 1), dtype=torch.uint8, device=self.b.device)
+        for i, (m, n, k) in enumerate(self.shapes.dims):
+            A, B, _, _ = self.views(i)
+            if A is not None:
+                a8[a_off[i]:a_off[i] + m * lda[i]].view(m, lda[i])[:, :k].copy_(A.to(dt).view(torch.uint8))
+            if B is not None:
+                b8[b_off[i]:b_off[i] + k * ldb[i]].view(k, ldb[i])[:, :n].copy_(B.to(dt).view(torch.uint8))
+        self.a, self.b, self.a_off, self.b_off, self.lda, self.ldb = a8, b8, a_off, b_off, lda, ldb
+        self.in_fmt = int(fmt)
+        return self
 
     def to_output(self, out_fmt: int) -> "DeviceProblemSet":
         """C and D in the 16-bit output type `out_fmt` (1 FP16, 2 BF16; KernelConfig.output_type):
@@ -191,8 +231,10 @@ class DeviceProblemSet:
     def views(self, i: int):
         """(A, B, C or None, D) torch views of problem i."""
         m, n, k = self.shapes.dims[i]
-        A = self.a[self.a_off[i]:self.a_off[i] + max(m * k, 0)].view(max(m, 0), max(k, 0)) if m * k > 0 else None
-        B = self.b[self.b_off[i]:self.b_off[i] + max(k * n, 0)].view(k, n) if k * n > 0 else None
+        la = self.lda[i] if self.lda else k
+        lb = self.ldb[i] if self.ldb else n
+        A = self.a[self.a_off[i]:self.a_off[i] + m * la].view(m, la)[:, :k] if m * k > 0 else None
+        B = self.b[self.b_off[i]:self.b_off[i] + k * lb].view(k, lb)[:, :n] if k * n > 0 else None
         C = None
         if self.c is not None and m * n > 0:
             C = self.c[self.c_off[i]:self.c_off[i] + m * n].view(m, n)
@@ -258,8 +300,14 @@ def host_inputs(ps: DeviceProblemSet, i: int, rows: Optional[np.ndarray] = None,
         C = C.index_select(1, cidx) if C is not None else None
         D = D.index_select(1, cidx) if D is not None else None
     out = {}
-    out["a"] = A.contiguous().view(torch.int16).cpu().numpy().view(np.uint16) if A is not None else np.zeros(1, np.uint16)
-    out["b"] = B.contiguous().view(torch.int16).cpu().numpy().view(np.uint16) if B is not None else np.zeros(1, np.uint16)
+    def bits(t):  # the operand's raw bits: uint16 for 16-bit types, uint8 for 8-bit ones
+        if t is None:
+            return np.zeros(1, np.uint8 if ps.a.element_size() == 1 else np.uint16)
+        t = t.contiguous()
+        return t.cpu().numpy() if t.element_size() == 1 else t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+    out["a"] = bits(A)
+    out["b"] = bits(B)
     out["c"] = C.contiguous().float().cpu().numpy() if C is not None else None
     out["d"] = D.contiguous().float().cpu().numpy() if D is not None else None
     return out

@@ -3,7 +3,7 @@
  *
  * One launch runs many independent GEMMs  D_i = alpha_i * A_i x B_i + beta_i * C_i  with
  * A_i (m x k) and B_i (k x n) FP16 row-major, C_i and D_i FP32 row-major, FP32 accumulation
- * (the reference's contract). Extensions, all off by default: BF16 A/B (gg_config.input_type),
+ * (the reference's contract). Extensions, all off by default: BF16 or FP8 A/B (gg_config.input_type),
  * FP16/BF16 C/D (gg_config.output_type), a per-column bias and an activation fused into the
  * epilogue (gg_executor_build_with_bias, gg_config.activation).
  * This is the boundary a foreign-language caller binds (ctypes, cgo, JNI, ...): plain C types,
@@ -44,7 +44,7 @@ extern "C" {
 #define GG_STATUS_TIMEOUT_SCHEDULER 0x8
 
 /* One GEMM problem. Layout-identical to the reference's ProblemDesc (grouped_gemm.cuh:18-35);
- * a and b point to FP16 (__half) device memory (BF16 with GG_INPUT_BF16), c and d to FP32 (FP16
+ * a and b point to FP16 (__half) device memory (BF16 / FP8 with input_type), c and d to FP32 (FP16
  * or BF16 with GG_OUTPUT_F16 / GG_OUTPUT_BF16). c may be NULL; it is read only when beta != 0. */
 typedef struct gg_problem {
   int m;
@@ -73,7 +73,14 @@ typedef struct gg_problem {
  * operands widened to FP32, FP32 FMA; the reference's SIMT path) with the same tile numbering.
  * input_type (no reference counterpart; the reference is FP16 only, and the C++ API of
  * grouped_gemm/grouped_gemm.cuh keeps the reference's KernelConfig and always passes FP16): the
- * element type of every A and B of the set, GG_INPUT_F16 (0) or GG_INPUT_BF16.
+ * element type of every A and B of the set: GG_INPUT_F16 (0), GG_INPUT_BF16, or the 8-bit floats
+ * GG_INPUT_E4M3 (1 sign, 4 exponent bits with bias 7, 3 mantissa bits; no infinities, S.1111.111
+ * is NaN) and GG_INPUT_E5M2 (1-5-2, bias 15, IEEE-style infinities and NaNs), one byte per element,
+ * multiplied exactly and accumulated in FP32 (tcgen05 kind::f8f6f4). With 8-bit inputs the tensor
+ * -core path needs tiles whose per-CTA B width is a multiple of 128 (128x128, 128x256, 64x128,
+ * 256x256; others are an invalid config) and, for every problem with work, A and B bases that are
+ * 16-byte aligned with lda and ldb multiples of 16 (else the build returns 1); the CUDA-core path
+ * takes any tile and any alignment.
  * output_type (no reference counterpart): the element type of every C and D of the set,
  * GG_OUTPUT_F32 (0, the reference's), GG_OUTPUT_F16 or GG_OUTPUT_BF16. The accumulation and the
  * epilogue arithmetic stay FP32; D is rounded to nearest even once, at the store.
@@ -86,6 +93,8 @@ typedef struct gg_problem {
  * three. */
 #define GG_INPUT_F16 0
 #define GG_INPUT_BF16 1
+#define GG_INPUT_E4M3 2
+#define GG_INPUT_E5M2 3
 #define GG_OUTPUT_F32 0
 #define GG_OUTPUT_F16 1
 #define GG_OUTPUT_BF16 2
@@ -99,7 +108,7 @@ typedef struct gg_config {
   int threads;
   int persistent_ctas; /* > 0: fixed persistent grid size; 0: one CTA per SM slot, capped by tiles */
   int use_tensor_cores;
-  int input_type;      /* GG_INPUT_F16 or GG_INPUT_BF16 */
+  int input_type;      /* GG_INPUT_F16, GG_INPUT_BF16, GG_INPUT_E4M3 or GG_INPUT_E5M2 */
   int output_type;     /* GG_OUTPUT_F32, GG_OUTPUT_F16 or GG_OUTPUT_BF16 */
   int activation;      /* GG_ACT_NONE, GG_ACT_RELU or GG_ACT_GELU */
 } gg_config;

@@ -66,9 +66,13 @@ def load_oracle() -> ctypes.CDLL:
         lib.oracle_gemm_f64.restype = None
         lib.oracle_gemm_f64_fmt.argtypes = lib.oracle_gemm_f64.argtypes + [ctypes.c_int]
         lib.oracle_gemm_f64_fmt.restype = None
-        lib.oracle_gemm_f64_epilogue.argtypes = lib.oracle_gemm_f64_fmt.argtypes + [
-            ctypes.POINTER(ctypes.c_float), ctypes.c_int]
+        lib.oracle_gemm_f64_epilogue.argtypes = [
+            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+            _f32p, ctypes.c_int, ctypes.c_float, ctypes.c_float, _i32p, ctypes.c_int, _f64p, ctypes.c_int, _f64p,
+            ctypes.c_int, ctypes.POINTER(ctypes.c_float), ctypes.c_int]
         lib.oracle_gemm_f64_epilogue.restype = None
+        lib.oracle_fp8_to_double.argtypes = [ctypes.c_uint8, ctypes.c_int]
+        lib.oracle_fp8_to_double.restype = ctypes.c_double
         lib.oracle_bf16_to_double.argtypes = [ctypes.c_uint16]
         lib.oracle_bf16_to_double.restype = ctypes.c_double
         lib.oracle_gemm_f32_refloop.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, _u16p,
@@ -159,16 +163,17 @@ def prepare(dims: Sequence[Sequence[int]], cta_m: int, cta_n: int, mode: int):
 
 
 def gemm_f64(m, n, k, a, lda, b, ldb, c, ldc, alpha, beta, rows=None, fmt=0, bias=None, act=0):
-    """FP64 D (and the error scale) for one problem; `a`/`b` are uint16 bit arrays of FP16
-    (fmt 0) or BF16 (fmt 1) values. `bias` (n float32 values, one per output column, or None)
+    """FP64 D (and the error scale) for one problem; `a`/`b` are bit arrays of FP16 (fmt 0) or
+    BF16 (fmt 1) values (2 bytes each), or of E4M3 (fmt 2) or E5M2 (fmt 3) values (1 byte). `bias` (n float32 values, one per output column, or None)
     and `act` (0 none, 1 ReLU, 2 GELU tanh form) give the library's epilogue extensions:
     D = act(alpha * A x B + beta * C + bias).
 
     Returns (d, scale), each shaped (len(rows) or m, n).
     """
     lib = load_oracle()
-    a = np.ascontiguousarray(a).view(np.uint16)
-    b = np.ascontiguousarray(b).view(np.uint16)
+    elem = np.uint8 if int(fmt) in (2, 3) else np.uint16
+    a = np.ascontiguousarray(a).view(elem)
+    b = np.ascontiguousarray(b).view(elem)
     nrows = m if rows is None else len(rows)
     d = np.zeros((max(nrows, 1), max(n, 1)), dtype=np.float64)
     s = np.zeros_like(d)
@@ -179,7 +184,7 @@ def gemm_f64(m, n, k, a, lda, b, ldb, c, ldc, alpha, beta, rows=None, fmt=0, bia
     bias_arr = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
     if bias_arr is not None and bias_arr.size < n:
         raise ValueError("bias needs one value per output column")
-    lib.oracle_gemm_f64_epilogue(m, n, k, _ptr(a, ctypes.c_uint16), lda, _ptr(b, ctypes.c_uint16), ldb,
+    lib.oracle_gemm_f64_epilogue(m, n, k, a.ctypes.data, lda, b.ctypes.data, ldb,
                                  None if c_arr is None else _ptr(c_arr, ctypes.c_float), ldc,
                                  float(alpha), float(beta),
                                  None if rows_arr is None else _ptr(rows_arr, ctypes.c_int), nrows,

@@ -54,6 +54,42 @@ static double bf16_bits_to_double(uint16_t h) {
 
 double oracle_bf16_to_double(uint16_t h) { return bf16_bits_to_double(h); }
 
+/* ---- 8-bit float decode (exact), the library's GG_INPUT_E4M3 / GG_INPUT_E5M2 -------------------
+ * E4M3: sign, 4 exponent bits (bias 7), 3 mantissa bits; no infinities, S.1111.111 is NaN;
+ *       exponent 0 is subnormal, m * 2^-9.
+ * E5M2: sign, 5 exponent bits (bias 15), 2 mantissa bits; exponent 31 is inf (m = 0) or NaN;
+ *       exponent 0 is subnormal, m * 2^-16. */
+static double e4m3_bits_to_double(uint8_t v) {
+  const int e = (v >> 3) & 0xf, m = v & 7;
+  double x;
+  if (e == 15 && m == 7) x = NAN;
+  else if (e == 0) x = ldexp((double)m, -9);
+  else x = ldexp((double)(8 + m), e - 10);
+  return (v & 0x80) ? -x : x;
+}
+
+static double e5m2_bits_to_double(uint8_t v) {
+  const int e = (v >> 2) & 0x1f, m = v & 3;
+  double x;
+  if (e == 31) x = m ? NAN : INFINITY;
+  else if (e == 0) x = ldexp((double)m, -16);
+  else x = ldexp((double)(4 + m), e - 17);
+  return (v & 0x80) ? -x : x;
+}
+
+/* fmt 2 = E4M3, 3 = E5M2 */
+double oracle_fp8_to_double(uint8_t v, int fmt) { return fmt == 3 ? e5m2_bits_to_double(v) : e4m3_bits_to_double(v); }
+
+/* Element i of an operand array in input format fmt (0 FP16, 1 BF16: 2 bytes; 2 E4M3, 3 E5M2: 1). */
+static double decode_elem(const void* p, int64_t i, int fmt) {
+  switch (fmt) {
+    case 1: return bf16_bits_to_double(((const uint16_t*)p)[i]);
+    case 2: return e4m3_bits_to_double(((const uint8_t*)p)[i]);
+    case 3: return e5m2_bits_to_double(((const uint8_t*)p)[i]);
+    default: return half_bits_to_double(((const uint16_t*)p)[i]);
+  }
+}
+
 /* ---- tile counting: reference src/grouped_gemm.cu:54-65 ---------------------------------- */
 static int ceil_div_int(int x, int y) { return (x + y - 1) / y; }
 
@@ -150,15 +186,15 @@ static double activate(double z, int act) {
 
 static double act_lipschitz(int act) { return act == 2 ? 1.13 : 1.0; } /* max GELU' = 1.1289... */
 
-/* As oracle_gemm_f64, with A and B in the 16-bit format `fmt` (0 = FP16, 1 = BF16), and the
+/* As oracle_gemm_f64, with A and B in input format `fmt` (0 = FP16, 1 = BF16, 2 = E4M3, 3 = E5M2;
+ * `a` and `b` point to 2-byte or 1-byte elements accordingly), and the
  * library's epilogue extensions: bias (nullable, one value per output column, bias[j] for column
  * j) added after alpha*acc + beta*C, then activation `act`:
  *   d     = act(alpha * acc + beta * C + bias[j])
  *   scale = act_lipschitz(act) * (|alpha| * sqrt(sum (a*b)^2) + |beta * C| + |bias[j]|) */
-void oracle_gemm_f64_epilogue(int m, int n, int k, const uint16_t* a, int lda, const uint16_t* b, int ldb,
+void oracle_gemm_f64_epilogue(int m, int n, int k, const void* a, int lda, const void* b, int ldb,
                               const float* c, int ldc, float alpha, float beta, const int* rows, int nrows,
                               double* d, int ldd, double* scale, int fmt, const float* bias, int act) {
-  double (*decode)(uint16_t) = fmt == 1 ? bf16_bits_to_double : half_bits_to_double;
   if (m <= 0 || n <= 0) return;
   if (!rows) nrows = m;
   const int read_c = (c != NULL) && (beta != 0.0f);
@@ -171,9 +207,8 @@ void oracle_gemm_f64_epilogue(int m, int n, int k, const uint16_t* a, int lda, c
     memset(acc, 0, (size_t)n * sizeof(double));
     memset(sq, 0, (size_t)n * sizeof(double));
     for (int kk = 0; kk < k; ++kk) {
-      const double av = decode(a[(int64_t)row * lda + kk]);
-      const uint16_t* bp = b + (int64_t)kk * ldb;
-      for (int j = 0; j < n; ++j) brow[j] = decode(bp[j]);
+      const double av = decode_elem(a, (int64_t)row * lda + kk, fmt);
+      for (int j = 0; j < n; ++j) brow[j] = decode_elem(b, (int64_t)kk * ldb + j, fmt);
       for (int j = 0; j < n; ++j) {
         const double p = av * brow[j];
         acc[j] += p;

@@ -185,3 +185,98 @@ def test_relu_output_is_nonnegative_and_gelu_differs(cuda):
     assert (outs[RELU][valid] >= 0).all()
     assert torch.equal(outs[RELU][valid], torch.clamp(outs[NONE][valid], min=0))
     assert not torch.equal(outs[GELU][valid], outs[RELU][valid])
+
+
+# ---- 8-bit inputs (KernelConfig.input_type E4M3 / E5M2; kind::f8f6f4 on the tensor cores) -------
+E4M3, E5M2 = gg.InputType.kE4M3, gg.InputType.kE5M2
+FP8_CONFIGS = [gg.KernelConfig(128, 256, 64), gg.KernelConfig(128, 128, 64), gg.KernelConfig(64, 128, 32),
+               gg.KernelConfig(256, 256, 64), gg.KernelConfig(128, 128, 64, use_tensor_cores=False)]
+
+
+def check_problems(ps: W.DeviceProblemSet, act: int = 0, sample: bool = False, threads: int = 8) -> float:
+    """Worst error / tolerance of every problem (all elements, or sampled rows and columns) against
+    the oracle, for any input format (host_inputs copies the operands' raw bits)."""
+    rng = np.random.default_rng(0)
+    jobs = []
+    for i, (m, n, k) in enumerate(ps.shapes.dims):
+        if m <= 0 or n <= 0:
+            continue
+        rows = cols = None
+        if sample:
+            rows = np.unique(np.concatenate([[0, m - 1], rng.integers(0, m, size=4)])).astype(np.int64)
+            cols = np.unique(np.concatenate([[0, n - 1], rng.integers(0, n, size=96)])).astype(np.int64)
+        h = W.host_inputs(ps, i, rows, cols)
+        jobs.append((i, m if rows is None else len(rows), n if cols is None else len(cols), k, h,
+                     ps.bias_host(i, cols)))
+
+    def one(job):
+        i, r, c, k, h, bias = job
+        ref, scale = O.gemm_f64(r, c, k, h["a"], max(1, k), h["b"], c, h["c"], c, ps.shapes.alpha[i],
+                                ps.shapes.beta[i], fmt=ps.in_fmt, bias=bias, act=act)
+        return O.rel_err(h["d"].reshape(r, c), ref, scale, ps.out_fmt) / O.tolerance(k)
+
+    with ThreadPoolExecutor(threads) as pool:
+        return max(pool.map(one, jobs), default=0.0)
+
+
+@pytest.mark.parametrize("fmt", [E4M3, E5M2], ids=["E4M3", "E5M2"])
+@pytest.mark.parametrize("cfg", FP8_CONFIGS, ids=_cfg_id)
+def test_fp8_inputs_match_oracle(cuda, cfg, fmt):
+    run_cfg = gg.KernelConfig(cfg.cta_m, cfg.cta_n, cfg.cta_k, use_tensor_cores=cfg.use_tensor_cores,
+                              input_type=fmt)
+    for shapes in (W.make_shapes("small16", seed=5), aligned_shapes(), W.make_shapes("tiny4096", seed=6)):
+        ps = W.allocate(shapes, seed=11).to_fp8(fmt)
+        run_set(ps, run_cfg, None)
+        worst = check_problems(ps)
+        assert worst <= 1.0, f"{shapes.name}: error/tolerance {worst:.3f}"
+        assert padding_untouched(ps)
+
+
+@pytest.mark.parametrize("fmt", [E4M3, E5M2], ids=["E4M3", "E5M2"])
+def test_fp8_mixed512_sampled_with_epilogue(cuda, fmt):
+    """The benchmark set with 8-bit A/B, FP16 D, bias and GELU: every extension at once."""
+    ps = W.allocate(W.make_shapes("mixed512"), seed=42).to_fp8(fmt)
+    ps.to_output(F16)
+    bias = ps.make_bias(aligned=True)
+    run_set(ps, gg.KernelConfig(128, 256, 64, input_type=fmt, output_type=F16, activation=GELU), bias)
+    assert check_problems(ps, act=GELU, sample=True) <= 1.0
+    assert padding_untouched(ps)
+
+
+def test_fp8_and_fp16_decode_differ(cuda):
+    """The same bytes read as E4M3 and as E5M2 give different products (the format field reaches
+    the tensor cores), and each matches its own oracle."""
+    import torch
+
+    outs = []
+    for fmt in (E4M3, E5M2):
+        ps = W.allocate(aligned_shapes(), seed=11).to_fp8(E4M3)  # the same E4M3 bytes both times
+        ps.in_fmt = int(fmt)
+        run_set(ps, gg.KernelConfig(128, 128, 64, input_type=fmt), None)
+        assert check_problems(ps) <= 1.0
+        outs.append(ps.d.clone())
+    valid = ~torch.isnan(outs[0])
+    assert not torch.equal(outs[0][valid], outs[1][valid])
+
+
+def test_fp8_problem_that_tma_cannot_load_is_refused(cuda):
+    """8-bit operands on the tensor-core path go through TMA only: a row pitch that is not a
+    multiple of 16 bytes makes the build fail with cudaErrorInvalidValue (1); the CUDA-core path
+    takes the same problem."""
+    import torch
+
+    m, n, k = 40, 48, 37  # lda = 37 bytes
+    A = torch.zeros((m, k), dtype=torch.uint8, device=cuda)
+    B = torch.zeros((k, n), dtype=torch.uint8, device=cuda)
+    D = torch.zeros((m, n), device=cuda)
+    p = gg.ProblemDesc(m, n, k, A.data_ptr(), B.data_ptr(), None, D.data_ptr(), k, n, n, n)
+    for tc, want in ((True, 1), (False, 0)):
+        cfg = gg.KernelConfig(128, 128, 64, use_tensor_cores=tc, input_type=E4M3)
+        ex = gg.GroupedGemmExecutor()
+        assert ex.build(gg.prepare_problem_set([p], cfg, 0), cfg) == want
+        if want == 0:
+            assert ex.run() == 0
+            torch.cuda.synchronize()
+            assert ex.status() == 0
+        ex.close()
+    assert torch.equal(D, torch.zeros_like(D))  # zero inputs: zero products

@@ -461,7 +461,7 @@ def test_bf16_and_fp16_reads_differ(cuda):
     run_grouped(ps.problems(), gg.KernelConfig(128, 128, 64, input_type=0), gg.SortMode.kNone)
     finite = torch.isfinite(as_bf16) & torch.isfinite(ps.d)
     assert not torch.equal(as_bf16[finite], ps.d[finite])
-    st, _ = gg.query_occupancy(gg.KernelConfig(128, 128, 64, input_type=2))
+    st, _ = gg.query_occupancy(gg.KernelConfig(128, 128, 64, input_type=4))
     assert st == 1  # an unknown input type is an invalid config
 
 

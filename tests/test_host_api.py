@@ -267,8 +267,9 @@ def test_moe_plan_create_rejects_bad_arguments_before_device_work():
 
 
 def test_input_type_is_validated_on_the_host():
-    """input_type must be GG_INPUT_F16 (0) or GG_INPUT_BF16 (1); anything else is an invalid config."""
-    for t, want in ((0, 0), (1, 0), (2, 1), (-1, 1)):
+    """input_type must be GG_INPUT_F16 (0), GG_INPUT_BF16 (1), GG_INPUT_E4M3 (2) or GG_INPUT_E5M2 (3);
+    anything else is an invalid config."""
+    for t, want in ((0, 0), (1, 0), (2, 0), (3, 0), (4, 1), (-1, 1)):
         cfg = gg.KernelConfig(128, 128, 64, input_type=t)
         ex = gg.GroupedGemmExecutor()
         prep = gg.prepare_problem_set([], cfg, 0)
@@ -293,4 +294,22 @@ def test_bias_table_length_must_match_the_problem_count():
     ex = gg.GroupedGemmExecutor()
     prep = gg.prepare_problem_set([], cfg, 0)
     assert ex.build(prep, cfg, bias=[None]) == gg.capi.CUDA_ERROR_INVALID_VALUE
+    ex.close()
+
+
+def test_fp8_inputs_need_128_column_b_tiles_on_the_tensor_cores():
+    """8-bit B fills 128-column shared-memory chunks: tensor-core tiles whose per-CTA B width is not a
+    multiple of 128 are an invalid config with E4M3 / E5M2 inputs; the CUDA-core path takes them."""
+    ok = [(128, 256, 64), (128, 128, 64), (64, 128, 32), (256, 256, 64)]
+    bad = [(64, 64, 16), (128, 64, 32), (128, 64, 64), (256, 128, 64)]
+    for fmt in (2, 3):
+        for shape, want in [(s, 0) for s in ok] + [(s, 1) for s in bad]:
+            for tc in (True, False):
+                cfg = gg.KernelConfig(*shape, use_tensor_cores=tc, input_type=fmt)
+                ex = gg.GroupedGemmExecutor()
+                assert ex.build(gg.prepare_problem_set([], cfg, 0), cfg) == (want if tc else 0), (shape, tc)
+                ex.close()
+    cfg = gg.KernelConfig(128, 128, 64, input_type=4)
+    ex = gg.GroupedGemmExecutor()
+    assert ex.build(gg.prepare_problem_set([], cfg, 0), cfg) == 1
     ex.close()

@@ -226,3 +226,27 @@ def test_epilogue_bias_and_activations_against_numpy():
     dbf = u.astype(np.uint32).view(np.float32).astype(np.float64)
     assert O.rel_err(dbf, gelu, s, out_fmt=2) == 0.0
     assert O.rel_err(dbf, gelu, s, out_fmt=1) > 0.0
+
+
+def test_fp8_decode_and_gemm_against_torch():
+    """E4M3 and E5M2 decode (every one of the 256 codes against torch's float8 types) and an FP8
+    oracle GEMM against numpy on the decoded values."""
+    import torch
+
+    lib = O.load_oracle()
+    codes = torch.arange(256, dtype=torch.int32).to(torch.uint8)
+    for fmt, dt in ((2, torch.float8_e4m3fn), (3, torch.float8_e5m2)):
+        want = codes.view(dt).to(torch.float64).numpy()
+        got = np.array([lib.oracle_fp8_to_double(int(v), fmt) for v in range(256)])
+        assert np.array_equal(np.isnan(got), np.isnan(want))
+        ok = ~np.isnan(want)
+        assert np.array_equal(got[ok], want[ok])
+    rng = np.random.default_rng(13)
+    m, n, k = 5, 6, 40
+    for fmt, dt in ((2, torch.float8_e4m3fn), (3, torch.float8_e5m2)):
+        a8 = torch.from_numpy(rng.uniform(-2, 2, size=(m, k)).astype(np.float32)).to(dt)
+        b8 = torch.from_numpy(rng.uniform(-2, 2, size=(k, n)).astype(np.float32)).to(dt)
+        ad, bd = a8.to(torch.float64).numpy(), b8.to(torch.float64).numpy()
+        d, _ = O.gemm_f64(m, n, k, a8.view(torch.uint8).numpy(), k, b8.view(torch.uint8).numpy(), n, None, n, 0.5,
+                          0.0, fmt=fmt)
+        assert np.allclose(d, 0.5 * ad @ bd, rtol=0, atol=1e-12)
