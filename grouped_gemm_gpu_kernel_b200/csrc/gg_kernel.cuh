@@ -10,7 +10,8 @@
 //                          read back from that tile.
 //   warp 8      MMA        allocates 512 TMEM columns (2 accumulators of 256 columns or 4 of <= 128,
 //                          so the epilogue of one tile overlaps the mainloops of the next); one
-//                          thread issues tcgen05.mma.kind::f16 (M=128, N=BN, K=16) and tcgen05.commit.
+//                          thread issues tcgen05.mma.kind::f16 (M=128, N=BN, K=16; kind::f8f6f4,
+//                          K=32, for 8-bit A/B) and tcgen05.commit.
 //   warp 9      scheduler  claims global tile indices with atomicAdd (the reference's device
 //                          scheduler, src/grouped_gemm.cu:640-675), finds the owning problem with a
 //                          warp-parallel 32-ary search of tile_offsets (same answer as the
