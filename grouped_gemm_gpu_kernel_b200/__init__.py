@@ -26,7 +26,7 @@ __all__ = [
     "prepare_problem_set", "sort_mode_name", "query_occupancy", "run_grouped_gemm_once",
     "run_baseline_per_problem", "count_non_empty_problems", "partition", "ShardPiece", "problem_from_tensors",
     "NATIVE_CONFIGS", "REFERENCE_CONFIGS", "PAIR_CONFIGS", "selftest_wait_timeout", "capi", "MoePlan",
-    "InputType", "OutputType", "Activation",
+    "InputType", "OutputType", "Activation", "Layout",
 ]
 
 
@@ -50,6 +50,13 @@ class OutputType(enum.IntEnum):
     kF32 = capi.GG_OUTPUT_F32
     kF16 = capi.GG_OUTPUT_F16
     kBF16 = capi.GG_OUTPUT_BF16
+
+
+class Layout(enum.IntEnum):
+    """Storage of A or B (GG_LAYOUT_*): row-major (the reference's: A m x k, B k x n) or
+    column-major (A stored k x m with lda >= m, B stored n x k with ldb >= k)."""
+    kRowMajor = capi.GG_LAYOUT_ROW_MAJOR
+    kColMajor = capi.GG_LAYOUT_COL_MAJOR
 
 
 class Activation(enum.IntEnum):
@@ -97,11 +104,13 @@ class KernelConfig:
     input_type: int = 0   # InputType: FP16 A/B (the reference's type), BF16, E4M3 or E5M2
     output_type: int = 0  # OutputType: FP32 C/D (the reference's type), FP16 or BF16
     activation: int = 0   # Activation applied after the bias
+    a_layout: int = 0     # Layout of every A (row-major: the reference's)
+    b_layout: int = 0     # Layout of every B
 
     def to_c(self) -> capi.GGConfig:
         return capi.GGConfig(self.cta_m, self.cta_n, self.cta_k, self.threads, self.persistent_ctas,
                              1 if self.use_tensor_cores else 0, int(self.input_type), int(self.output_type),
-                             int(self.activation))
+                             int(self.activation), int(self.a_layout), int(self.b_layout))
 
 
 # The reference's three tile shapes (reference src/grouped_gemm.cu:67-81) and the sm_100a ones.

@@ -178,9 +178,11 @@ bool encode_b_chunks(CUtensorMap* map, const InGeom& g, const void* base, int k,
 // Device record of one problem plus its kMapsPerProblem tensor maps. TMA is used for A/B only
 // when both operands qualify, for D when it qualifies; everything else takes the zero-fill load
 // path and masked direct stores.
-DeviceProblemDesc make_device_problem(const gg_problem& p, Variant v, int in_fmt, int out_fmt, CUtensorMap* maps,
+DeviceProblemDesc make_device_problem(const gg_problem& p, Variant v, const gg_config* cfg, CUtensorMap* maps,
                                       int map_slot) {
-  const InGeom g = in_geom(in_fmt);
+  const InGeom g = in_geom(cfg->input_type);
+  const int out_fmt = cfg->output_type;
+  const bool a_col = cfg->a_layout == GG_LAYOUT_COL_MAJOR, b_col = cfg->b_layout == GG_LAYOUT_COL_MAJOR;
   const int bm = variant_bm(v), bn = variant_bn(v);
   const int cta_rows = variant_cta_rows(v);  // A and D rows one CTA moves per tile
   const int cta_cols = variant_cta_cols(v);  // B columns one CTA loads per tile
@@ -205,11 +207,17 @@ DeviceProblemDesc make_device_problem(const gg_problem& p, Variant v, int in_fmt
   d.k_blocks = p.k > 0 ? ceil_div(p.k, g.kblock) : 0;
   unsigned flags = 0;
   std::memset(maps, 0, kMapsPerProblem * sizeof(CUtensorMap));
-  if (has_tiles && p.k > 0 &&
-      encode_2d(&maps[kMapA], g.type, p.a, p.k, p.m, static_cast<int64_t>(p.lda) * g.bytes, g.kblock, cta_rows) &&
-      encode_2d(&maps[kMapB], g.type, p.b, p.n, p.k, static_cast<int64_t>(p.ldb) * g.bytes, g.chunk, g.kblock)) {
+  // A row-major: boxes of kblock K x cta_rows rows; column-major (k x m): chunk M x kblock K per
+  // box. B row-major: chunk N x kblock K per box (+ the 3-D whole-stage map); column-major (n x k):
+  // kblock K x cta_cols rows, the whole stage in one box.
+  const int64_t a_pitch = static_cast<int64_t>(p.lda) * g.bytes, b_pitch = static_cast<int64_t>(p.ldb) * g.bytes;
+  const bool a_ok = a_col ? encode_2d(&maps[kMapA], g.type, p.a, p.m, p.k, a_pitch, g.chunk, g.kblock)
+                          : encode_2d(&maps[kMapA], g.type, p.a, p.k, p.m, a_pitch, g.kblock, cta_rows);
+  if (has_tiles && p.k > 0 && a_ok &&
+      (b_col ? encode_2d(&maps[kMapB], g.type, p.b, p.k, p.n, b_pitch, g.kblock, cta_cols)
+             : encode_2d(&maps[kMapB], g.type, p.b, p.n, p.k, b_pitch, g.chunk, g.kblock))) {
     flags |= grouped_gemm::kFlagTmaAB;
-    if (encode_b_chunks(&maps[kMapB3], g, p.b, p.k, p.n, static_cast<int64_t>(p.ldb) * g.bytes, cta_cols / g.chunk))
+    if (!b_col && encode_b_chunks(&maps[kMapB3], g, p.b, p.k, p.n, b_pitch, cta_cols / g.chunk))
       flags |= grouped_gemm::kFlagTmaB3;
   }
   if (has_tiles && encode_d(&maps[kMapD], out_fmt, p.d, p.n, p.m, p.ldd)) flags |= grouped_gemm::kFlagTmaD;
@@ -279,10 +287,14 @@ Variant variant_of(const gg_config* c) {
     return Variant::kUnsupported;
   if (c->activation != GG_ACT_NONE && c->activation != GG_ACT_RELU && c->activation != GG_ACT_GELU)
     return Variant::kUnsupported;
+  const auto layout_ok = [](int l) { return l == GG_LAYOUT_ROW_MAJOR || l == GG_LAYOUT_COL_MAJOR; };
+  if (!layout_ok(c->a_layout) || !layout_ok(c->b_layout)) return Variant::kUnsupported;
   const Variant v = resolve_variant(c->cta_m, c->cta_n, c->cta_k, c->threads);
-  // 8-bit B fills 128-column chunks: the tensor-core path needs per-CTA B widths of 128 or 256.
+  // 8-bit MN-major operands fill 128-wide chunks: on the tensor cores a row-major B needs per-CTA
+  // B widths of 128 or 256, a column-major A 128 rows per CTA.
   if (v != Variant::kUnsupported && c->use_tensor_cores && in_geom(c->input_type).f8 &&
-      variant_cta_cols(v) % 128 != 0)
+      ((c->b_layout == GG_LAYOUT_ROW_MAJOR && variant_cta_cols(v) % 128 != 0) ||
+       (c->a_layout == GG_LAYOUT_COL_MAJOR && variant_cta_rows(v) % 128 != 0)))
     return Variant::kUnsupported;
   return v;
 }
@@ -300,6 +312,7 @@ void set_formats(KernelParams& kp, const gg_config* c) {
   kp.input_format = c->input_type;
   kp.output_format = c->output_type;
   kp.activation = c->activation;
+  kp.layout = (c->a_layout == GG_LAYOUT_COL_MAJOR ? 1 : 0) | (c->b_layout == GG_LAYOUT_COL_MAJOR ? 2 : 0);
 }
 
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -464,8 +477,7 @@ int gg_executor_build_with_bias(gg_executor* ex, const gg_problem* sorted_proble
     const gg_problem& p = sorted_problems[i];
     if (p.m < 0 || p.n < 0 || p.k < 0) return cudaErrorInvalidValue;
     if (!p.a || !p.b || !p.d) return cudaErrorInvalidDevicePointer;
-    descs[static_cast<size_t>(i)] = gg::make_device_problem(p, v, config->input_type, config->output_type,
-                                                            &maps[static_cast<size_t>(i) * gg::kMapsPerProblem], i);
+    descs[static_cast<size_t>(i)] = gg::make_device_problem(p, v, config, &maps[static_cast<size_t>(i) * gg::kMapsPerProblem], i);
     if (!gg::tensor_path_can_load(descs[static_cast<size_t>(i)], config)) return cudaErrorInvalidValue;
   }
   if (count == 0 || total_tiles <= 0) {
@@ -588,7 +600,7 @@ int gg_run_baseline_per_problem(const gg_problem* problems, int count, const gg_
       if (!status) return cudaErrorMemoryAllocation;
     }
     std::memset(&kp, 0, sizeof(kp));
-    kp.single_desc = gg::make_device_problem(p, v, config->input_type, config->output_type, kp.single_maps, 0);
+    kp.single_desc = gg::make_device_problem(p, v, config, kp.single_maps, 0);
     if (!gg::tensor_path_can_load(kp.single_desc, config)) return cudaErrorInvalidValue;
     const int tiles = kp.single_desc.tiles_m * kp.single_desc.tiles_n;
     kp.status = status;
@@ -802,8 +814,7 @@ extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count
   for (int s = 0; s < count; ++s) {
     const gg_problem& p = problems[gg::g_noalloc_order[s]];
     offs[s + 1] = offs[s] + gg::tile_count(p.m, p.n, config->cta_m, config->cta_n);
-    descs[s] = gg::make_device_problem(p, v, config->input_type, config->output_type,
-                                       &maps[static_cast<size_t>(s) * gg::kMapsPerProblem], s);
+    descs[s] = gg::make_device_problem(p, v, config, &maps[static_cast<size_t>(s) * gg::kMapsPerProblem], s);
     if (!gg::tensor_path_can_load(descs[s], config)) return cudaErrorInvalidValue;
   }
   const int total = offs[count];
@@ -1028,7 +1039,10 @@ int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, g
   if (!problem || v == gg::Variant::kUnsupported) return cudaErrorInvalidValue;
   const gg_moe_problem& q = *problem;
   if (q.experts < 1 || q.n < 0 || q.k < 0 || q.capacity_rows < 0 || !q.a || !q.b || !q.d) return cudaErrorInvalidValue;
-  if (q.lda < std::max(1, q.k) || q.ldb < std::max(1, q.n) || q.ldd < std::max(1, q.n) ||
+  // The packed rows are rows of a row-major A; B may be either layout (column-major: n x k).
+  if (config->a_layout != GG_LAYOUT_ROW_MAJOR) return cudaErrorInvalidValue;
+  const bool b_col = config->b_layout == GG_LAYOUT_COL_MAJOR;
+  if (q.lda < std::max(1, q.k) || q.ldb < std::max(1, b_col ? q.k : q.n) || q.ldd < std::max(1, q.n) ||
       (q.c && q.ldc < std::max(1, q.n)))
     return cudaErrorInvalidValue;
   for (int e = 0; e < q.experts; ++e)
@@ -1069,12 +1083,12 @@ int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, g
     p.k_blocks = q.k > 0 ? gg::ceil_div(q.k, g.kblock) : 0;
     p.map_slot = static_cast<int>(e);  // the maps stay in expert order; the records are reordered
     unsigned flags = grouped_gemm::kFlagPackedRows;
-    if (tma_a && gg::encode_2d(&m[gg::kMapB], g.type, q.b[e], q.n, q.k, static_cast<int64_t>(q.ldb) * g.bytes,
-                               g.chunk, g.kblock)) {
+    const int64_t b_pitch = static_cast<int64_t>(q.ldb) * g.bytes;
+    if (tma_a && (b_col ? gg::encode_2d(&m[gg::kMapB], g.type, q.b[e], q.k, q.n, b_pitch, g.kblock, cta_cols)
+                        : gg::encode_2d(&m[gg::kMapB], g.type, q.b[e], q.n, q.k, b_pitch, g.chunk, g.kblock))) {
       m[gg::kMapA] = map_a;
       flags |= grouped_gemm::kFlagTmaAB;
-      if (gg::encode_b_chunks(&m[gg::kMapB3], g, q.b[e], q.k, q.n, static_cast<int64_t>(q.ldb) * g.bytes,
-                              cta_cols / g.chunk))
+      if (!b_col && gg::encode_b_chunks(&m[gg::kMapB3], g, q.b[e], q.k, q.n, b_pitch, cta_cols / g.chunk))
         flags |= grouped_gemm::kFlagTmaB3;
     } else if (f8_tc && rows_exist && q.k > 0) {
       return cudaErrorInvalidValue;

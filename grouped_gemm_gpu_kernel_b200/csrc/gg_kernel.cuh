@@ -534,9 +534,12 @@ __device__ __forceinline__ void lsu_fill_b(uint8_t* bs, const unsigned short* b1
   }
 }
 
+// `col_a` / `col_b`: the operand is stored column-major, so A (k x m) fills the MN-major chunk
+// layout of row-major B and B (n x k) the K-major row layout of row-major A.
 template <int ROWS, int COLS>
 __device__ __forceinline__ void lsu_fill_stage(uint8_t* as, uint8_t* bs, const __half* a, int lda, const __half* b,
-                                               int ldb, int m, int n, int k, int row0, int col0, int kb, int ptid) {
+                                               int ldb, int m, int n, int k, int row0, int col0, int kb, int ptid,
+                                               bool col_a, bool col_b) {
   const unsigned short* a16 = reinterpret_cast<const unsigned short*>(a);
   const unsigned short* b16 = reinterpret_cast<const unsigned short*>(b);
   const int pw = ptid >> 5, ln = ptid & 31;
@@ -545,30 +548,54 @@ __device__ __forceinline__ void lsu_fill_stage(uint8_t* as, uint8_t* bs, const _
   const int cols = min(COLS, n - col0);
   const bool a4 = ((lda & 1) == 0) && ((reinterpret_cast<uintptr_t>(a) & 3u) == 0u);
   const bool b4 = ((ldb & 1) == 0) && ((reinterpret_cast<uintptr_t>(b) & 3u) == 0u);
-  if (a4) lsu_fill_a<ROWS, 2>(as, a16, lda, rows, k, row0, k0, pw, ln);
-  else lsu_fill_a<ROWS, 1>(as, a16, lda, rows, k, row0, k0, pw, ln);
+  if (col_a) {
+    if (a4) lsu_fill_b<ROWS, 2>(as, a16, lda, rows, k, row0, k0, pw, ln);
+    else lsu_fill_b<ROWS, 1>(as, a16, lda, rows, k, row0, k0, pw, ln);
+  } else {
+    if (a4) lsu_fill_a<ROWS, 2>(as, a16, lda, rows, k, row0, k0, pw, ln);
+    else lsu_fill_a<ROWS, 1>(as, a16, lda, rows, k, row0, k0, pw, ln);
+  }
   if (cols > 0) {
-    if (b4) lsu_fill_b<COLS, 2>(bs, b16, ldb, cols, k, col0, k0, pw, ln);
-    else lsu_fill_b<COLS, 1>(bs, b16, ldb, cols, k, col0, k0, pw, ln);
+    if (col_b) {
+      if (b4) lsu_fill_a<COLS, 2>(bs, b16, ldb, cols, k, col0, k0, pw, ln);
+      else lsu_fill_a<COLS, 1>(bs, b16, ldb, cols, k, col0, k0, pw, ln);
+    } else {
+      if (b4) lsu_fill_b<COLS, 2>(bs, b16, ldb, cols, k, col0, k0, pw, ln);
+      else lsu_fill_b<COLS, 1>(bs, b16, ldb, cols, k, col0, k0, pw, ln);
+    }
   }
 }
 
 // ---- mainloop helpers ------------------------------------------------------------------------
-// The four MMAs of one K block (one shared-memory stage). F8: 8-bit A/B (kind::f8f6f4, K = 32 per
-// MMA), else 16-bit (kind::f16, K = 16); either way one MMA's K step of A is 32 bytes of the
-// 128-byte K-major row, and the element geometry is a compile-time constant here so the
-// descriptors fold.
-//   A: K-major SW128, 8-row groups 1024 bytes apart.
-//   B: MN-major SW128, one MMA's K rows = 2048 (16-bit) or 4096 (8-bit) bytes; column chunks
-//      8192 / 16384 bytes apart (leading byte offset), 8-row K groups 1024 bytes apart (stride).
-template <bool F8, bool kPair>
+// Operand modes of a launch, one bit each: 8-bit A/B, A stored column-major (k x m: MN-major in
+// shared memory), B stored column-major (n x k: K-major in shared memory). The per-stage helpers
+// below take them as template parameters so that the geometry folds; the roles pick the
+// instantiation once per K block.
+constexpr int kModeF8 = 1;
+constexpr int kModeACol = 2;
+constexpr int kModeBCol = 4;
+
+__device__ __forceinline__ int operand_mode(const KernelParams& p) {
+  return (p.input_format >= GG_INPUT_E4M3 ? kModeF8 : 0) | ((p.layout & 1) ? kModeACol : 0) |
+         ((p.layout & 2) ? kModeBCol : 0);
+}
+
+// The four MMAs of one K block (one shared-memory stage). F8: kind::f8f6f4, K = 32 per MMA, else
+// kind::f16, K = 16. A K-major operand (row-major A, column-major B) is 128-byte rows of K, SW128,
+// one MMA's K step = 32 bytes inside the row, 8-row groups 1024 bytes apart. An MN-major operand
+// (row-major B, column-major A) is column chunks of 64 (16-bit) or 128 (8-bit) values x K rows,
+// SW128: one MMA's K rows = 2048 / 4096 bytes, chunks 8192 / 16384 bytes apart (leading byte
+// offset), 8-row K groups 1024 bytes apart (stride offset).
+template <bool F8, bool ACol, bool BCol, bool kPair>
 __device__ __forceinline__ void mma_kblock(uint32_t d_tmem, uint32_t a0, uint32_t b0, uint32_t idesc, bool first) {
-  constexpr uint32_t kBStep = F8 ? 4096u : 2048u;
-  constexpr uint32_t kBLbo = F8 ? 16384u : 8192u;
+  constexpr uint32_t kMnStep = F8 ? 4096u : 2048u;
+  constexpr uint32_t kMnLbo = F8 ? 16384u : 8192u;
 #pragma unroll
   for (int kk = 0; kk < kBK / kMmaK; ++kk) {
-    const uint64_t adesc = ptx::smem_desc_sw128(a0 + kk * 32u, 16u, 1024u);
-    const uint64_t bdesc = ptx::smem_desc_sw128(b0 + kk * kBStep, kBLbo, 1024u);
+    const uint64_t adesc = ACol ? ptx::smem_desc_sw128(a0 + kk * kMnStep, kMnLbo, 1024u)
+                                : ptx::smem_desc_sw128(a0 + kk * 32u, 16u, 1024u);
+    const uint64_t bdesc = BCol ? ptx::smem_desc_sw128(b0 + kk * 32u, 16u, 1024u)
+                                : ptx::smem_desc_sw128(b0 + kk * kMnStep, kMnLbo, 1024u);
     const uint32_t acc = (!first || kk != 0) ? 1u : 0u;
     if constexpr (kPair) {
       if constexpr (F8) ptx::tc_mma_f8_pair(d_tmem, adesc, bdesc, idesc, acc);
@@ -580,29 +607,72 @@ __device__ __forceinline__ void mma_kblock(uint32_t d_tmem, uint32_t a0, uint32_
   }
 }
 
-// The TMA loads of one stage: A (one box of kblock K x rows) and B (one 3-D box of the whole
-// stage when b_one_box, else one 2-D box per column chunk), completing on `bar`. COLS: B columns
-// this CTA loads; F8: 8-bit operands (128-deep K blocks, 128-column chunks of 16 KB) or 16-bit
-// (64, 64, 8 KB); kPair: the cta_group::2 form whose bytes complete on the leader's barrier.
-template <int COLS, bool F8, bool kPair>
+template <bool kPair>
+__device__ __forceinline__ void mma_kblock_any(int mode, uint32_t d_tmem, uint32_t a0, uint32_t b0, uint32_t idesc,
+                                               bool first) {
+  switch (mode) {
+    case 0: mma_kblock<false, false, false, kPair>(d_tmem, a0, b0, idesc, first); break;
+    case 1: mma_kblock<true, false, false, kPair>(d_tmem, a0, b0, idesc, first); break;
+    case 2: mma_kblock<false, true, false, kPair>(d_tmem, a0, b0, idesc, first); break;
+    case 3: mma_kblock<true, true, false, kPair>(d_tmem, a0, b0, idesc, first); break;
+    case 4: mma_kblock<false, false, true, kPair>(d_tmem, a0, b0, idesc, first); break;
+    case 5: mma_kblock<true, false, true, kPair>(d_tmem, a0, b0, idesc, first); break;
+    case 6: mma_kblock<false, true, true, kPair>(d_tmem, a0, b0, idesc, first); break;
+    default: mma_kblock<true, true, true, kPair>(d_tmem, a0, b0, idesc, first); break;
+  }
+}
+
+// The TMA loads of one stage, completing on `bar`: ROWS rows of A starting at a_row and COLS
+// columns of B starting at col0, K block kb. F8: 128-deep K blocks and 128-wide MN chunks of 16 KB,
+// else 64 and 64 (8 KB). A row-major: one box {kblock, ROWS}; column-major: one box {chunk, kblock}
+// per chunk of rows. B row-major: one 3-D box of the whole stage when b_one_box, else one box per
+// column chunk; column-major: one box {kblock, COLS}. kPair: the cta_group::2 form whose bytes
+// complete on the leader's barrier.
+template <int ROWS, int COLS, bool F8, bool ACol, bool BCol, bool kPair>
 __device__ __forceinline__ void load_stage_tma(uint32_t a_dst, uint32_t b_dst, const CUtensorMap* ma,
                                                const CUtensorMap* mb, const CUtensorMap* mb3, uint32_t bar, int kb,
                                                int a_row, int col0, bool b_one_box) {
   constexpr int kKb = F8 ? 2 * kBK : kBK;
   constexpr int kCw = F8 ? 128 : 64;
   constexpr uint32_t kChunk = F8 ? 16384u : 8192u;
-  if constexpr (kPair) ptx::tma_load_2d_pair(a_dst, ma, bar, kb * kKb, a_row);
-  else ptx::tma_load_2d(a_dst, ma, bar, kb * kKb, a_row);
-  if (b_one_box) {
+  auto load2 = [&](uint32_t dst, const CUtensorMap* map, int x, int y) {
+    if constexpr (kPair) ptx::tma_load_2d_pair(dst, map, bar, x, y);
+    else ptx::tma_load_2d(dst, map, bar, x, y);
+  };
+  if constexpr (ACol) {
+#pragma unroll
+    for (int j = 0; j < ROWS / kCw; ++j) load2(a_dst + j * kChunk, ma, a_row + j * kCw, kb * kKb);
+  } else {
+    load2(a_dst, ma, kb * kKb, a_row);
+  }
+  if constexpr (BCol) {
+    load2(b_dst, mb, kb * kKb, col0);
+  } else if (b_one_box) {
     if constexpr (kPair) ptx::tma_load_3d_pair(b_dst, mb3, bar, 0, kb * kKb, col0 / kCw);
     else ptx::tma_load_3d(b_dst, mb3, bar, 0, kb * kKb, col0 / kCw);
   } else {
 #pragma unroll
-    for (int j = 0; j < COLS / kCw; ++j) {
-      if constexpr (kPair) ptx::tma_load_2d_pair(b_dst + j * kChunk, mb, bar, col0 + j * kCw, kb * kKb);
-      else ptx::tma_load_2d(b_dst + j * kChunk, mb, bar, col0 + j * kCw, kb * kKb);
-    }
+    for (int j = 0; j < COLS / kCw; ++j) load2(b_dst + j * kChunk, mb, col0 + j * kCw, kb * kKb);
   }
+}
+
+template <int ROWS, int COLS, bool kPair>
+__device__ __forceinline__ void load_stage_tma_any(int mode, uint32_t a_dst, uint32_t b_dst, const CUtensorMap* ma,
+                                                   const CUtensorMap* mb, const CUtensorMap* mb3, uint32_t bar,
+                                                   int kb, int a_row, int col0, bool b_one_box) {
+#define GG_LOAD_STAGE(F8, AC, BC) \
+  load_stage_tma<ROWS, COLS, F8, AC, BC, kPair>(a_dst, b_dst, ma, mb, mb3, bar, kb, a_row, col0, b_one_box)
+  switch (mode) {
+    case 0: GG_LOAD_STAGE(false, false, false); break;
+    case 1: GG_LOAD_STAGE(true, false, false); break;
+    case 2: GG_LOAD_STAGE(false, true, false); break;
+    case 3: GG_LOAD_STAGE(true, true, false); break;
+    case 4: GG_LOAD_STAGE(false, false, true); break;
+    case 5: GG_LOAD_STAGE(true, false, true); break;
+    case 6: GG_LOAD_STAGE(false, true, true); break;
+    default: GG_LOAD_STAGE(true, true, true); break;
+  }
+#undef GG_LOAD_STAGE
 }
 
 // ---- the kernel --------------------------------------------------------------------------------
@@ -707,9 +777,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
     // ======================= producers =======================
     const int ptid = static_cast<int>(threadIdx.x) - kProdWarp0 * 32;
     // Stage geometry: a 128-byte swizzle row holds 64 16-bit or 128 8-bit values, so a K block
-    // is 64 (FP16/BF16) or 128 (FP8) deep and a B chunk 64 or 128 columns wide (load_stage_tma);
-    // the stage's bytes are the same either way.
-    const bool f8 = p.input_format >= GG_INPUT_E4M3;
+    // is 64 (FP16/BF16) or 128 (FP8) deep and an MN chunk 64 or 128 wide (load_stage_tma); the
+    // stage's bytes are the same either way.
+    const int mode = operand_mode(p);
+    const bool f8 = (mode & kModeF8) != 0;
     uint32_t it = 0;  // global k-block counter: stage = it % S, phase = (it / S) & 1
     bool aborted = false;
     for (int t = 0;; ++t) {
@@ -752,10 +823,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
             const uint32_t a_dst = sbase + static_cast<uint32_t>(st * L::kStageBytes);
             const uint32_t b_dst = a_dst + L::kABytes;
             ptx::mbar_arrive_expect_tx(full_bar(st), L::kATxBytes + L::kBTxBytes);
-            if (f8) load_stage_tma<BN, true, false>(
-                a_dst, b_dst, ma, mb, mb3, full_bar(st), kb, a_row, tile_n * BN, b_one_box);
-            else load_stage_tma<BN, false, false>(
-                a_dst, b_dst, ma, mb, mb3, full_bar(st), kb, a_row, tile_n * BN, b_one_box);
+            load_stage_tma_any<BM, BN, false>(mode, a_dst, b_dst, ma, mb, mb3, full_bar(st), kb, a_row, tile_n * BN,
+                                              b_one_box);
             ++it;
           }
         } else {
@@ -778,7 +847,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
           uint8_t* as = smem + st * L::kStageBytes;
           uint8_t* bs = as + L::kABytes;
           // 16-bit operands only: the host sends every 8-bit problem with work through TMA.
-          if (!f8) lsu_fill_stage<BM, BN>(as, bs, a, lda, b, ldb, m, n, k, tile_m * BM, tile_n * BN, kb, ptid);
+          if (!f8)
+            lsu_fill_stage<BM, BN>(as, bs, a, lda, b, ldb, m, n, k, tile_m * BM, tile_n * BN, kb, ptid,
+                                   (mode & kModeACol) != 0, (mode & kModeBCol) != 0);
           ptx::fence_proxy_async_smem();
           ptx::named_bar_sync(1, kProdThreads);
           if (ptid == 0) ptx::mbar_arrive(full_bar(st));
@@ -798,9 +869,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
   } else if (warp == kMmaWarp) {
     // ======================= MMA issuer =======================
     if (lane == 0) {
-      const bool f8 = p.input_format >= GG_INPUT_E4M3;
-      const uint32_t kIdesc = ptx::idesc_f16_f32_kA_mnB(
-          kMmaM, BN, static_cast<uint32_t>(f8 ? p.input_format - GG_INPUT_E4M3 : p.input_format));
+      const int mode = operand_mode(p);
+      const uint32_t kIdesc = ptx::idesc_f32acc(
+          kMmaM, BN, static_cast<uint32_t>((mode & kModeF8) ? p.input_format - GG_INPUT_E4M3 : p.input_format),
+          (mode & kModeACol) != 0, (mode & kModeBCol) == 0);
       uint32_t it = 0;
       for (int t = 0;; ++t) {
         const int slot = t % kRing;
@@ -831,8 +903,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
           ptx::tc_fence_after_sync();
           const uint32_t a0 = sbase + static_cast<uint32_t>(st * L::kStageBytes);
           const uint32_t b0 = a0 + L::kABytes;
-          if (f8) mma_kblock<true, false>(d_tmem, a0, b0, kIdesc, kb == 0);
-          else mma_kblock<false, false>(d_tmem, a0, b0, kIdesc, kb == 0);
+          mma_kblock_any<false>(mode, d_tmem, a0, b0, kIdesc, kb == 0);
           ptx::tc_commit(empty_bar(st));  // stage is free once these MMAs have read it
           ++it;
         }

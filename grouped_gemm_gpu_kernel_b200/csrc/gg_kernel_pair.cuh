@@ -199,8 +199,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= kProdWarp0) {
     // ======================= producers (both CTAs) =======================
     const int ptid = static_cast<int>(threadIdx.x) - kProdWarp0 * 32;
-    // 16-bit operands: 64-deep K blocks, 64-column B chunks; 8-bit: 128 and 128 (same bytes).
-    const bool f8 = p.input_format >= GG_INPUT_E4M3;
+    // 16-bit operands: 64-deep K blocks, 64-wide MN chunks; 8-bit: 128 and 128 (same bytes).
+    const int mode = operand_mode(p);
+    const bool f8 = (mode & kModeF8) != 0;
     const int cw = f8 ? 128 : 64;
     uint32_t it = 0;
     bool aborted = false;
@@ -246,10 +247,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t b_dst = a_dst + L::kABytes;
             const uint32_t bar_leader = ptx::mapa_shared(full_bar(st), 0);
             if (leader) ptx::mbar_arrive_expect_tx(full_bar(st), L::kStageTxPair);
-            if (f8) load_stage_tma<HB, true, true>(
-                a_dst, b_dst, ma, mb, mb3, bar_leader, kb, a_row, col_base, b_one_box);
-            else load_stage_tma<HB, false, true>(
-                a_dst, b_dst, ma, mb, mb3, bar_leader, kb, a_row, col_base, b_one_box);
+            load_stage_tma_any<128, HB, true>(mode, a_dst, b_dst, ma, mb, mb3, bar_leader, kb, a_row, col_base,
+                                              b_one_box);
             // The peer's arrival only counts: its TMA bytes are tracked by complete_tx.
             if (!leader) ptx::mbar_arrive_cluster_relaxed(bar_leader);
             ++it;
@@ -274,7 +273,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* as = smem + st * L::kStageBytes;
           uint8_t* bs = as + L::kABytes;
           // 16-bit operands only: the host sends every 8-bit problem with work through TMA.
-          if (!f8) lsu_fill_stage<128, HB>(as, bs, a, lda, b, ldb, m, n, k, row_base, col_base, kb, ptid);
+          if (!f8)
+            lsu_fill_stage<128, HB>(as, bs, a, lda, b, ldb, m, n, k, row_base, col_base, kb, ptid,
+                                    (mode & kModeACol) != 0, (mode & kModeBCol) != 0);
           ptx::fence_proxy_async_all();  // the leader's tensor cores read this CTA's shared memory
           ptx::named_bar_sync(1, kProdThreads);
           if (ptid == 0) {
@@ -297,9 +298,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kMmaWarp) {
     // ======================= MMA issuer (leader only) =======================
     if (leader && lane == 0) {
-      const bool f8 = p.input_format >= GG_INPUT_E4M3;
-      const uint32_t kIdesc = ptx::idesc_f16_f32_kA_mnB(
-          256, BN, static_cast<uint32_t>(f8 ? p.input_format - GG_INPUT_E4M3 : p.input_format));
+      const int mode = operand_mode(p);
+      const uint32_t kIdesc = ptx::idesc_f32acc(
+          256, BN, static_cast<uint32_t>((mode & kModeF8) ? p.input_format - GG_INPUT_E4M3 : p.input_format),
+          (mode & kModeACol) != 0, (mode & kModeBCol) == 0);
       uint32_t it = 0;
       for (int t = 0;; ++t) {
         const int slot = t % kRing;
@@ -336,8 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tc_fence_after_sync();
           const uint32_t a0 = sbase + static_cast<uint32_t>(st * L::kStageBytes);
           const uint32_t b0 = a0 + L::kABytes;
-          if (f8) mma_kblock<true, true>(d_tmem, a0, b0, kIdesc, kb == 0);
-          else mma_kblock<false, true>(d_tmem, a0, b0, kIdesc, kb == 0);
+          mma_kblock_any<true>(mode, d_tmem, a0, b0, kIdesc, kb == 0);
           ptx::tc_commit_pair_mc(empty_bar(st), 0x3);  // both CTAs' stage is free
           ++it;
         }

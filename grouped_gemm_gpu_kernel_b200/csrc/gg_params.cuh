@@ -99,6 +99,7 @@ struct KernelParams {
   int input_format;   // A and B element type: 0 = FP16, 1 = BF16 (GG_INPUT_*)
   int output_format;  // C and D element type: 0 = FP32, 1 = FP16, 2 = BF16 (GG_OUTPUT_*)
   int activation;     // GG_ACT_* applied to D after the bias
+  int layout;         // bit 0: every A stored column-major (k x m); bit 1: every B column-major (n x k)
   const float* const* bias;  // per map slot: that problem's bias (n FP32 values) or null; null: none
 };
 

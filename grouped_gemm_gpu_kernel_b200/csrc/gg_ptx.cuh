@@ -318,5 +318,11 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32_kA_mnB(int m, int n, uint32
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// The same with the operand majors given: a_mn = A MN-major (bit 15), b_mn = B MN-major (bit 16).
+__host__ __device__ constexpr uint32_t idesc_f32acc(int m, int n, uint32_t ab_format, bool a_mn, bool b_mn) {
+  return (1u << 4) | (ab_format << 7) | (ab_format << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
 }  // namespace ptx
 }  // namespace gg

@@ -6,7 +6,8 @@
 // cta_m x cta_n tiles), the same atomic tile claims and problem lookup (reference
 // src/grouped_gemm.cu:219-234, 640-675), the same epilogue D = alpha*acc + beta*C with C read only
 // when c != nullptr and beta != 0 (reference src/grouped_gemm.cu:460-481), with the tensor-core
-// epilogue's extensions (output format, bias, activation; gg_epilogue_ops.cuh). FP16 (or BF16) operands
+// epilogue's extensions (output format, bias, activation; gg_epilogue_ops.cuh) and the operand
+// layouts (row- or column-major A and B). FP16 (or BF16, FP8) operands
 // are widened to FP32 and accumulated with FP32 FMA (a product of two 16-bit values is exact in
 // FP32), so the result differs from the tensor-core path only in the order of the FP32 additions.
 //
@@ -82,6 +83,8 @@ __global__ void __launch_bounds__(kSimtThreads) grouped_gemm_simt_kernel(const _
   const int tid = static_cast<int>(threadIdx.x);
   const int tx = tid & 15, ty = tid >> 4;
   const int in_fmt = p.input_format;
+  const bool a_col = (p.layout & 1) != 0;  // A stored k x m
+  const bool b_col = (p.layout & 2) != 0;  // B stored n x k
   int static_next = static_cast<int>(blockIdx.x);
 
   for (;;) {
@@ -136,15 +139,18 @@ __global__ void __launch_bounds__(kSimtThreads) grouped_gemm_simt_kernel(const _
 #pragma unroll
           for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
         for (int k0 = 0; k0 < k; k0 += kSimtBK) {
+          // consecutive threads take consecutive elements of the stored layout (coalesced reads)
           for (int i = tid; i < kSub * kSimtBK; i += kSimtThreads) {
-            const int r = i / kSimtBK, kk = i % kSimtBK;
+            const int r = a_col ? i % kSub : i / kSimtBK, kk = a_col ? i / kSub : i % kSimtBK;
             const int gr = row0 + r, gk = k0 + kk;
-            As[kk][r] = (gr < m && gk < k) ? widen(a, static_cast<long long>(gr) * lda + gk, in_fmt) : 0.0f;
+            const long long ai = a_col ? static_cast<long long>(gk) * lda + gr : static_cast<long long>(gr) * lda + gk;
+            As[kk][r] = (gr < m && gk < k) ? widen(a, ai, in_fmt) : 0.0f;
           }
           for (int i = tid; i < kSimtBK * kSub; i += kSimtThreads) {
-            const int kk = i / kSub, c = i % kSub;
+            const int kk = b_col ? i % kSimtBK : i / kSub, c = b_col ? i / kSimtBK : i % kSub;
             const int gk = k0 + kk, gc = col0 + c;
-            Bs[kk][c] = (gk < k && gc < n) ? widen(b, static_cast<long long>(gk) * ldb + gc, in_fmt) : 0.0f;
+            const long long bi = b_col ? static_cast<long long>(gc) * ldb + gk : static_cast<long long>(gk) * ldb + gc;
+            Bs[kk][c] = (gk < k && gc < n) ? widen(b, bi, in_fmt) : 0.0f;
           }
           __syncthreads();
 #pragma unroll 8

@@ -31,10 +31,13 @@ gg_config to_c(const KernelConfig& c) {
   g.threads = c.threads;
   g.persistent_ctas = c.persistent_ctas;
   g.use_tensor_cores = c.use_tensor_cores ? 1 : 0;
-  // the reference's API is FP16 in, FP32 out, no fused bias or activation; the rest are C-ABI extensions
+  // the reference's API is FP16 in, FP32 out, row-major, no fused bias or activation; the rest are
+  // C-ABI extensions
   g.input_type = GG_INPUT_F16;
   g.output_type = GG_OUTPUT_F32;
   g.activation = GG_ACT_NONE;
+  g.a_layout = GG_LAYOUT_ROW_MAJOR;
+  g.b_layout = GG_LAYOUT_ROW_MAJOR;
   return g;
 }
 

@@ -121,6 +121,8 @@ class DeviceProblemSet:
     in_fmt: int = 0                   # A / B element type: 0 FP16, 1 BF16, 2 E4M3, 3 E5M2 (KernelConfig.input_type)
     lda: Optional[List[int]] = None   # row pitches of A and B per problem (None: packed, k and n)
     ldb: Optional[List[int]] = None
+    a_col: bool = False               # A stored column-major (k x m, lda >= m; KernelConfig.a_layout)
+    b_col: bool = False               # B stored column-major (n x k, ldb >= k; KernelConfig.b_layout)
     bias: Optional["object"] = None   # FP32 slab of per-problem bias vectors (make_bias)
     bias_off: List[Optional[int]] = field(default_factory=list)  # element offset, None = no bias
 
@@ -139,37 +141,58 @@ class DeviceProblemSet:
                                    lda, ldb, max(1, n), max(1, n), al, be))
         return out
 
+    def _relayout(self, convert, out_dtype, a_col: bool, b_col: bool, pad: int) -> None:
+        """New A and B slabs holding convert(logical operand) in the given storage layouts, each
+        operand starting on a 256-byte boundary, row pitches padded to multiples of `pad`."""
+        import torch
+
+        def up(x):
+            return (max(x, 1) + pad - 1) // pad * pad
+
+        esz = torch.empty(0, dtype=out_dtype).element_size()
+        lda = [up(m if a_col else k) for m, n, k in self.shapes.dims]
+        ldb = [up(k if b_col else n) for m, n, k in self.shapes.dims]
+        a_off, b_off, na, nb = [], [], 0, 0
+        for (m, n, k), la, lb in zip(self.shapes.dims, lda, ldb):
+            a_off.append(na)
+            na += _aligned(max(k if a_col else m, 0) * la, esz)
+            b_off.append(nb)
+            nb += _aligned(max(n if b_col else k, 0) * lb, esz)
+        a2 = torch.zeros(max(na, 1), dtype=out_dtype, device=self.a.device)
+        b2 = torch.zeros(max(nb, 1), dtype=out_dtype, device=self.b.device)
+        for i, (m, n, k) in enumerate(self.shapes.dims):
+            A, B, _, _ = self.views(i)  # logical m x k and k x n
+            if A is not None:
+                if a_col:
+                    a2[a_off[i]:a_off[i] + k * lda[i]].view(k, lda[i])[:, :m].copy_(convert(A.t()))
+                else:
+                    a2[a_off[i]:a_off[i] + m * lda[i]].view(m, lda[i])[:, :k].copy_(convert(A))
+            if B is not None:
+                if b_col:
+                    b2[b_off[i]:b_off[i] + n * ldb[i]].view(n, ldb[i])[:, :k].copy_(convert(B.t()))
+                else:
+                    b2[b_off[i]:b_off[i] + k * ldb[i]].view(k, ldb[i])[:, :n].copy_(convert(B))
+        self.a, self.b, self.a_off, self.b_off, self.lda, self.ldb = a2, b2, a_off, b_off, lda, ldb
+        self.a_col, self.b_col = a_col, b_col
+
     def to_fp8(self, fmt: int) -> "DeviceProblemSet":
         """A and B re-encoded as 8-bit floats for runs with KernelConfig.input_type = fmt (2 E4M3,
         3 E5M2): each FP16 value rounded to the nearest 8-bit value by torch, one byte per element,
         in new uint8 slabs whose row pitches are padded to multiples of 16 elements and whose
         operands start on 256-byte boundaries (the tensor-core path loads 8-bit operands by TMA,
-        which needs 16-byte-aligned rows)."""
+        which needs 16-byte-aligned rows). The storage layouts are kept."""
         import torch
 
         dt = {2: torch.float8_e4m3fn, 3: torch.float8_e5m2}[int(fmt)]
-
-        def pad16(x):
-            return (max(x, 1) + 15) // 16 * 16
-
-        lda = [pad16(k) for m, n, k in self.shapes.dims]
-        ldb = [pad16(n) for m, n, k in self.shapes.dims]
-        a_off, b_off, na, nb = [], [], 0, 0
-        for (m, n, k), la, lb in zip(self.shapes.dims, lda, ldb):
-            a_off.append(na)
-            na += _aligned(max(m, 0) * la, 1)
-            b_off.append(nb)
-            nb += _aligned(max(k, 0) * lb, 1)
-        a8 = torch.zeros(max(na, 1), dtype=torch.uint8, device=self.a.device)
-        b8 = torch.zeros(max(nb, 1), dtype=torch.uint8, device=self.b.device)
-        for i, (m, n, k) in enumerate(self.shapes.dims):
-            A, B, _, _ = self.views(i)
-            if A is not None:
-                a8[a_off[i]:a_off[i] + m * lda[i]].view(m, lda[i])[:, :k].copy_(A.to(dt).view(torch.uint8))
-            if B is not None:
-                b8[b_off[i]:b_off[i] + k * ldb[i]].view(k, ldb[i])[:, :n].copy_(B.to(dt).view(torch.uint8))
-        self.a, self.b, self.a_off, self.b_off, self.lda, self.ldb = a8, b8, a_off, b_off, lda, ldb
+        self._relayout(lambda t: t.to(dt).view(torch.uint8), torch.uint8, self.a_col, self.b_col, 16)
         self.in_fmt = int(fmt)
+        return self
+
+    def to_layout(self, a_col: bool, b_col: bool, pad: int = 1) -> "DeviceProblemSet":
+        """A and/or B stored column-major (A as k x m, B as n x k: KernelConfig.a_layout / b_layout
+        = 1) with the same values; row pitches padded to multiples of `pad` elements (1: packed,
+        so odd sizes reach the zero-fill loader; 8: every 16-bit row 16-byte aligned, for TMA)."""
+        self._relayout(lambda t: t, self.a.dtype, a_col, b_col, pad)
         return self
 
     def to_output(self, out_fmt: int) -> "DeviceProblemSet":
@@ -229,12 +252,18 @@ class DeviceProblemSet:
         return self
 
     def views(self, i: int):
-        """(A, B, C or None, D) torch views of problem i."""
+        """(A, B, C or None, D) torch views of problem i; A and B are the logical m x k and k x n
+        operands whatever their storage layout."""
         m, n, k = self.shapes.dims[i]
         la = self.lda[i] if self.lda else k
         lb = self.ldb[i] if self.ldb else n
-        A = self.a[self.a_off[i]:self.a_off[i] + m * la].view(m, la)[:, :k] if m * k > 0 else None
-        B = self.b[self.b_off[i]:self.b_off[i] + k * lb].view(k, lb)[:, :n] if k * n > 0 else None
+        A = B = None
+        if m * k > 0:  # logical m x k (a transposed view of a column-major store)
+            A = (self.a[self.a_off[i]:self.a_off[i] + k * la].view(k, la)[:, :m].t() if self.a_col else
+                 self.a[self.a_off[i]:self.a_off[i] + m * la].view(m, la)[:, :k])
+        if k * n > 0:  # logical k x n
+            B = (self.b[self.b_off[i]:self.b_off[i] + n * lb].view(n, lb)[:, :k].t() if self.b_col else
+                 self.b[self.b_off[i]:self.b_off[i] + k * lb].view(k, lb)[:, :n])
         C = None
         if self.c is not None and m * n > 0:
             C = self.c[self.c_off[i]:self.c_off[i] + m * n].view(m, n)

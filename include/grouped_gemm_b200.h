@@ -5,7 +5,8 @@
  * A_i (m x k) and B_i (k x n) FP16 row-major, C_i and D_i FP32 row-major, FP32 accumulation
  * (the reference's contract). Extensions, all off by default: BF16 or FP8 A/B (gg_config.input_type),
  * FP16/BF16 C/D (gg_config.output_type), a per-column bias and an activation fused into the
- * epilogue (gg_executor_build_with_bias, gg_config.activation).
+ * epilogue (gg_executor_build_with_bias, gg_config.activation), column-major A and/or B
+ * (gg_config.a_layout / b_layout).
  * This is the boundary a foreign-language caller binds (ctypes, cgo, JNI, ...): plain C types,
  * opaque handles, device pointers as void*, CUDA streams as void* (cudaStream_t; NULL = legacy
  * default stream). Every function that can fail returns an int holding a cudaError_t value:
@@ -88,9 +89,16 @@ typedef struct gg_problem {
  *   D = act(alpha * A x B + beta * C + bias):
  *   GG_ACT_NONE (0), GG_ACT_RELU (max(x, 0)), GG_ACT_GELU (tanh form,
  *   0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), the approximation of Hendrycks and Gimpel).
- * Any other value of the three fields is an invalid config. The C++ API of
+ * a_layout / b_layout (no reference counterpart, whose operands are row-major): GG_LAYOUT_ROW_MAJOR
+ *   (0: A is m x k with row pitch lda >= k, B is k x n with ldb >= n) or GG_LAYOUT_COL_MAJOR
+ *   (A stored as its transpose, k x m with lda >= m; B stored as n x k with ldb >= k, the layout of
+ *   a [out_features][in_features] weight). The tensor cores read either form directly (K-major or
+ *   MN-major shared-memory operands). With 8-bit inputs a column-major A needs 128-row tiles
+ *   per CTA (not 64x128), and a column-major B lifts the 128-column rule. The mixture-of-experts
+ *   plan takes a row-major A only.
+ * Any other value of these fields is an invalid config. The C++ API of
  * grouped_gemm/grouped_gemm.cuh keeps the reference's KernelConfig and always passes 0 for all
- * three. */
+ * of them. */
 #define GG_INPUT_F16 0
 #define GG_INPUT_BF16 1
 #define GG_INPUT_E4M3 2
@@ -101,6 +109,8 @@ typedef struct gg_problem {
 #define GG_ACT_NONE 0
 #define GG_ACT_RELU 1
 #define GG_ACT_GELU 2
+#define GG_LAYOUT_ROW_MAJOR 0
+#define GG_LAYOUT_COL_MAJOR 1
 typedef struct gg_config {
   int cta_m;
   int cta_n;
@@ -111,6 +121,8 @@ typedef struct gg_config {
   int input_type;      /* GG_INPUT_F16, GG_INPUT_BF16, GG_INPUT_E4M3 or GG_INPUT_E5M2 */
   int output_type;     /* GG_OUTPUT_F32, GG_OUTPUT_F16 or GG_OUTPUT_BF16 */
   int activation;      /* GG_ACT_NONE, GG_ACT_RELU or GG_ACT_GELU */
+  int a_layout;        /* GG_LAYOUT_ROW_MAJOR or GG_LAYOUT_COL_MAJOR */
+  int b_layout;        /* GG_LAYOUT_ROW_MAJOR or GG_LAYOUT_COL_MAJOR */
 } gg_config;
 
 /* Resource report; field-for-field the reference's OccupancyInfo (grouped_gemm.cuh:54-83). */

@@ -313,3 +313,20 @@ def test_fp8_inputs_need_128_column_b_tiles_on_the_tensor_cores():
     ex = gg.GroupedGemmExecutor()
     assert ex.build(gg.prepare_problem_set([], cfg, 0), cfg) == 1
     ex.close()
+
+
+def test_layouts_are_validated_on_the_host():
+    """a_layout / b_layout must be GG_LAYOUT_ROW_MAJOR (0) or GG_LAYOUT_COL_MAJOR (1); with 8-bit
+    inputs on the tensor cores a column-major A needs 128-row tiles per CTA and a column-major B
+    lifts the 128-column rule of a row-major B."""
+    cases = [((128, 128, 64), 0, 0, 1, 0, 0), ((128, 128, 64), 0, 1, 1, 0, 0), ((128, 128, 64), 0, 2, 0, 0, 1),
+             ((128, 128, 64), 0, 0, -1, 0, 1),
+             ((128, 64, 64), 2, 0, 1, 0, 0), ((128, 64, 64), 2, 0, 0, 0, 1),     # 8-bit B: K-major lifts the rule
+             ((64, 128, 32), 2, 1, 0, 0, 1), ((64, 128, 32), 2, 1, 0, 1, 1),     # 8-bit MN-major A needs 128 rows
+             ((64, 128, 32), 2, 0, 0, 0, 0), ((256, 128, 64), 3, 1, 1, 0, 0)]
+    for shape, in_t, a_l, b_l, simt, want in cases:
+        cfg = gg.KernelConfig(*shape, input_type=in_t, a_layout=a_l, b_layout=b_l, use_tensor_cores=not simt)
+        ex = gg.GroupedGemmExecutor()
+        got = ex.build(gg.prepare_problem_set([], cfg, 0), cfg)
+        ex.close()
+        assert got == (0 if simt and a_l in (0, 1) and b_l in (0, 1) else want), (shape, in_t, a_l, b_l, simt)
