@@ -67,6 +67,10 @@ def parse_args():
     ap.add_argument("--activation", choices=["none", "relu", "gelu"], default="none",
                     help="activation fused into the epilogue")
     ap.add_argument("--bias", action="store_true", help="a per-column FP32 bias on every problem")
+    ap.add_argument("--a-layout", choices=["row", "col"], default="row",
+                    help="storage of every A (col: k x m, an extension; row pitches padded to 16 bytes)")
+    ap.add_argument("--b-layout", choices=["row", "col"], default="row",
+                    help="storage of every B (col: n x k, the [out][in] weight layout; pitches padded to 16 bytes)")
     ap.add_argument("--gather", action="store_true",
                     help="N>1: after the timed region, gather every rank's D to rank 0 over NCCL and time it")
     return ap.parse_args()
@@ -296,13 +300,16 @@ def main():
     if args.gather and out_type != 0:
         raise SystemExit("--gather packs FP32 D only")
     in_type = {"f16": 0, "bf16": 1, "e4m3": 2, "e5m2": 3}[args.input_type]
-    cfg = gg.KernelConfig(*cta, input_type=in_type, output_type=out_type,
-                          activation=act)
-    plain = out_type == 0 and act == 0 and not args.bias and args.input_type == "f16"
+    a_col, b_col = args.a_layout == "col", args.b_layout == "col"
+    cfg = gg.KernelConfig(*cta, input_type=in_type, output_type=out_type, activation=act, a_layout=int(a_col),
+                          b_layout=int(b_col))
+    plain = out_type == 0 and act == 0 and not args.bias and args.input_type == "f16" and not (a_col or b_col)
     shapes, global_flops = rank_shapes(args.workload, world, rank, cfg)
 
     def make_set():
         p = W.allocate(shapes, dev, seed=42 + rank, d_fill=0.0)
+        if a_col or b_col:
+            p.to_layout(a_col, b_col, 8)
         if in_type == 1:
             p.to_bf16()
         elif in_type >= 2:
@@ -551,7 +558,7 @@ def main():
                               f"write, then a {2 * L2_BYTES >> 20} MB read so no dirty line is left) before every "
                               "step, each step timed alone"),
                        "accumulate": "f32", "output_type": args.output_type, "activation": args.activation,
-                       "bias": bool(args.bias),
+                       "bias": bool(args.bias), "a_layout": args.a_layout, "b_layout": args.b_layout,
                        "prep_build_ms": prep_ms, "parallelism": f"dp{world} (tile-balanced shards)"},
             "pct_dense_fp16_peak": 100.0 * value / (world * peaks["bf16_tflops"]),
             "peak_source": peaks["source"],
@@ -628,6 +635,8 @@ def moe_plan_row(ps, shapes, cfg, stream, flops, executor_ms, bias_ptrs=None, ru
                  for i in range(len(rows) - 1))
     if not packed or any(d[1] != n or d[2] != k for d in shapes.dims):
         return {"unavailable": "problems do not share n, k or are not row-packed"}
+    if ps.a_col:
+        return {"unavailable": "the plan takes a row-major A"}
     ei = ps.a.element_size()
     lda = ps.lda[0] if ps.lda else k
     ldb = ps.ldb[0] if ps.ldb else n
