@@ -616,10 +616,61 @@ def gather_row(args, cfg, ps, world, rank, dev, max_over_ranks, barrier):
             ok = bool(torch.equal(root_d[pc0.problem][pc0.row0:pc0.row0 + pc0.rows, pc0.col0:pc0.col0 + pc0.cols],
                                   local[0]))
     barrier()
-    return {"ms": ms, "bytes_into_root": into_root, "gbps_into_root": into_root / (ms * 1e-3) / 1e9,
-            "received_on_root": got if rank == 0 else None, "root_piece_check": ok,
-            "how": "after the timed region: one packed FP32 buffer per rank, NCCL send/recv to rank 0, "
-                   "unpacked into the full D of every global problem"}
+    row = {"ms": ms, "bytes_into_root": into_root, "gbps_into_root": into_root / (ms * 1e-3) / 1e9,
+           "received_on_root": got if rank == 0 else None, "root_piece_check": ok,
+           "how": "after the timed region: one packed FP32 buffer per rank, NCCL send/recv to rank 0, "
+                  "unpacked into the full D of every global problem"}
+    row["fused"] = fused_gather_row(cfg, ps, by_rank, dims, world, rank, dev, max_over_ranks, barrier,
+                                    slab if rank == 0 else None)
+    return row
+
+
+def fused_gather_row(cfg, ps, by_rank, dims, world, rank, dev, max_over_ranks, barrier, gathered, runs=5):
+    """The same gather fused into the kernel: the root exports a D buffer (CUDA IPC), every other
+    rank maps it and runs its pieces with D pointers into it, so the epilogue stores each tile into
+    the root's memory over NVLink (plain stores) while later tiles compute. Timed per run as the max
+    over ranks; the root then checks the buffer against the NCCL-gathered D bit for bit."""
+    import dataclasses
+
+    import torch
+    import torch.distributed as dist
+
+    import grouped_gemm_gpu_kernel_b200 as gg
+    from grouped_gemm_gpu_kernel_b200.gather import close_buffer, export_buffer, fused_targets, open_buffer
+
+    total = sum(max(m, 0) * max(n, 0) for m, n, k in dims)
+    fbuf = torch.full((max(total, 1),), float("nan"), device=dev) if rank == 0 else None
+    obj = [export_buffer(fbuf) if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    base = fbuf.data_ptr() if rank == 0 else open_buffer(obj[0])
+    mine = by_rank[rank]
+    probs = [dataclasses.replace(p, d=t[0], ldd=t[1]) for p, t in zip(ps.problems(), fused_targets(mine, dims, base))]
+    ex = gg.GroupedGemmExecutor()
+    st = ex.build(gg.prepare_problem_set(probs, cfg, gg.SortMode.kByK), cfg)
+    if st != 0:
+        raise RuntimeError(f"fused-gather executor build failed: {st}")
+    stream = torch.cuda.Stream(dev)
+    assert ex.run(stream) == 0
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(runs):
+        ex.run(stream)
+    e1.record(stream)
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / runs)
+    status = ex.status()
+    ex.close()
+    barrier()  # every rank's stores into the root's buffer have completed
+    same = bool(torch.equal(fbuf[:total], gathered[:total])) if rank == 0 else None
+    if rank != 0:
+        close_buffer(base)
+    barrier()  # the root frees its buffer only after every mapping is closed
+    into_root = 4 * sum(pc.rows * pc.cols for r in range(1, world) for pc in by_rank[r])
+    return {"ms": ms, "status": status, "bitwise_equal_to_nccl_gather": same,
+            "gbps_into_root": into_root / (ms * 1e-3) / 1e9,
+            "how": "one grouped-kernel launch per rank whose D pointers lie in rank 0's buffer (CUDA IPC "
+                   "mapping, peer access): compute and the NVLink transfer of D in the same kernel"}
 
 
 def moe_plan_row(ps, shapes, cfg, stream, flops, executor_ms, bias_ptrs=None, runs=20):

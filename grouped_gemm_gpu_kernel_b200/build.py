@@ -26,7 +26,7 @@ BUILD_DIR = os.path.join(PKG, "_build")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
               "--expt-relaxed-constexpr", "-I" + INCLUDE, "-I" + CSRC]
-SOURCES = ["gg_kernels.cu", "gg_host.cu", "gg_copy.cu", "gg_simt.cu", "grouped_gemm_api.cpp"]
+SOURCES = ["gg_kernels.cu", "gg_host.cu", "gg_copy.cu", "gg_simt.cu", "gg_ipc.cu", "grouped_gemm_api.cpp"]
 
 
 def nvcc() -> str:

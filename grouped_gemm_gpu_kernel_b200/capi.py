@@ -21,6 +21,7 @@ EXPORTED_SYMBOLS = (
     "gg_run_grouped_gemm_once", "gg_run_baseline_per_problem", "gg_count_non_empty_problems",
     "gg_partition", "gg_selftest_wait_timeout", "gg_run_grouped_gemm_noalloc", "gg_copy_rects",
     "gg_moe_plan_create", "gg_moe_plan_run", "gg_moe_plan_status", "gg_moe_plan_destroy",
+    "gg_ipc_export", "gg_ipc_open", "gg_ipc_close",
 )
 GG_STATUS_BAD_ROWS = 0x100
 GG_INPUT_F16 = 0
@@ -90,6 +91,10 @@ class GGMoeProblem(ctypes.Structure):
                 ("bias", ctypes.POINTER(ctypes.c_void_p))]
 
 
+class GGIpcHandle(ctypes.Structure):
+    _fields_ = [("handle", ctypes.c_ubyte * 64), ("offset", ctypes.c_ulonglong), ("bytes", ctypes.c_ulonglong)]
+
+
 _lib: Optional[ctypes.CDLL] = None
 
 
@@ -132,6 +137,9 @@ def load() -> ctypes.CDLL:
         "gg_moe_plan_run": ([vp, vp, vp], ctypes.c_int),
         "gg_moe_plan_status": ([vp, i32p, i32p], ctypes.c_int),
         "gg_moe_plan_destroy": ([vp], None),
+        "gg_ipc_export": ([vp, P(GGIpcHandle)], ctypes.c_int),
+        "gg_ipc_open": ([P(GGIpcHandle), P(vp)], ctypes.c_int),
+        "gg_ipc_close": ([vp], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

@@ -112,6 +112,43 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, int
   return r == CUDA_SUCCESS;
 }
 
+// False when p is device memory of another GPU (a peer buffer mapped into this process, e.g. the
+// root's D of a gather fused into the kernel): such a D is written with plain stores, never TMA.
+// Everything else counts as this device's. The last allocation range looked up is cached, so a
+// problem set whose D matrices share one buffer costs one query.
+bool on_this_device(const void* p) {
+  static thread_local uintptr_t lo = 0, hi = 0;
+  static thread_local int cached_dev = -1;
+  static thread_local bool cached_local = true;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return true;
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  if (dev == cached_dev && a >= lo && a < hi) return cached_local;
+  cudaPointerAttributes attr{};
+  if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return true;
+  }
+  const bool local = !(attr.type == cudaMemoryTypeDevice && attr.device != dev);
+  static PFN_cuMemGetAddressRange_v3020 range = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<PFN_cuMemGetAddressRange_v3020>(nullptr);
+    return reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(f);
+  }();
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range && range(&base, &size, static_cast<CUdeviceptr>(a)) == CUDA_SUCCESS) {
+    lo = static_cast<uintptr_t>(base);
+    hi = lo + size;
+    cached_dev = dev;
+    cached_local = local;
+  }
+  return local;
+}
+
 // Bytes of one C or D element in output format `fmt` (GG_OUTPUT_*).
 int out_bytes(int fmt) { return fmt == GG_OUTPUT_F32 ? 4 : 2; }
 
@@ -220,7 +257,8 @@ DeviceProblemDesc make_device_problem(const gg_problem& p, Variant v, const gg_c
     if (!b_col && encode_b_chunks(&maps[kMapB3], g, p.b, p.k, p.n, b_pitch, cta_cols / g.chunk))
       flags |= grouped_gemm::kFlagTmaB3;
   }
-  if (has_tiles && encode_d(&maps[kMapD], out_fmt, p.d, p.n, p.m, p.ldd)) flags |= grouped_gemm::kFlagTmaD;
+  if (has_tiles && on_this_device(p.d) && encode_d(&maps[kMapD], out_fmt, p.d, p.n, p.m, p.ldd))
+    flags |= grouped_gemm::kFlagTmaD;
   if (p.c != nullptr && p.beta != 0.0f) flags |= grouped_gemm::kFlagReadC;
   flags |= vector_flags(out_fmt, p.c, p.ldc, p.d, p.ldd);
   d.flags = flags;
@@ -1063,7 +1101,8 @@ int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, g
                      gg::encode_2d(&map_a, g.type, q.a, q.k, q.capacity_rows, static_cast<int64_t>(q.lda) * g.bytes,
                                    g.kblock, cta_rows);
   if (f8_tc && rows_exist && q.k > 0 && !tma_a) return cudaErrorInvalidValue;
-  const bool tma_d = rows_exist && gg::encode_d(&map_d, config->output_type, q.d, q.n, q.capacity_rows, q.ldd);
+  const bool tma_d = rows_exist && gg::on_this_device(q.d) &&
+                     gg::encode_d(&map_d, config->output_type, q.d, q.n, q.capacity_rows, q.ldd);
   for (size_t e = 0; e < E; ++e) {
     CUtensorMap* m = &maps[e * gg::kMapsPerProblem];
     DeviceProblemDesc& p = templ[e];

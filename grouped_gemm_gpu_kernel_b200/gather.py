@@ -13,7 +13,8 @@ from __future__ import annotations
 
 from typing import Dict, List, Sequence
 
-__all__ = ["gather_pieces", "piece_elems", "copy_rects"]
+__all__ = ["gather_pieces", "piece_elems", "copy_rects", "export_buffer", "open_buffer", "close_buffer",
+           "root_offsets", "fused_targets"]
 
 
 def copy_rects(packed, views, to_packed: bool) -> None:
@@ -124,3 +125,72 @@ def gather_pieces(pieces_by_rank: Sequence[Sequence], local_d: Sequence, root_d:
         for w in dist.batch_isend_irecv([dist.P2POp(dist.isend, buf, root, group)]):
             w.wait()
     return 0
+
+
+# ---- the gather fused into the grouped kernel ---------------------------------------------------
+# Instead of computing D locally and moving it afterwards, every rank builds its executor with D
+# pointers inside the root's D buffer (mapped into the rank's process with CUDA IPC): the kernel's
+# epilogue then stores each tile straight into the root's memory over NVLink, overlapped with the
+# tiles still being computed, and no separate gather runs. A D on another GPU is written with the
+# kernel's plain coalesced stores (never TMA).
+
+def export_buffer(t) -> bytes:
+    """CUDA IPC handle (gg_ipc_handle bytes) of device tensor t's memory, for open_buffer in
+    another process of this node."""
+    import ctypes
+
+    from . import capi
+
+    h = capi.GGIpcHandle()
+    st = capi.load().gg_ipc_export(ctypes.c_void_p(t.data_ptr()), ctypes.byref(h))
+    if st != 0:
+        raise RuntimeError(f"gg_ipc_export failed with status {st}")
+    return bytes(ctypes.string_at(ctypes.addressof(h), ctypes.sizeof(h)))
+
+
+def open_buffer(handle: bytes) -> int:
+    """Maps another process's exported buffer; returns the device pointer of its first byte."""
+    import ctypes
+
+    from . import capi
+
+    h = capi.GGIpcHandle.from_buffer_copy(handle)
+    ptr = ctypes.c_void_p()
+    st = capi.load().gg_ipc_open(ctypes.byref(h), ctypes.byref(ptr))
+    if st != 0:
+        raise RuntimeError(f"gg_ipc_open failed with status {st}")
+    return int(ptr.value)
+
+
+def close_buffer(ptr: int) -> None:
+    import ctypes
+
+    from . import capi
+
+    st = capi.load().gg_ipc_close(ctypes.c_void_p(ptr))
+    if st != 0:
+        raise RuntimeError(f"gg_ipc_close failed with status {st}")
+
+
+def root_offsets(dims) -> List[int]:
+    """Element offsets of the global problems' D matrices (m x n, row-major, packed) back to back
+    in the root's buffer."""
+    offs, off = [], 0
+    for m, n, k in dims:
+        offs.append(off)
+        off += max(m, 0) * max(n, 0)
+    return offs
+
+
+def fused_targets(pieces, dims, base: int, elem_bytes: int = 4):
+    """(d pointer, ldd) of each piece of a rank inside the root's D buffer at device address
+    `base` (layout of root_offsets): the piece's first element is row row0, column col0 of its
+    global problem, whose row pitch is that problem's n."""
+    offs = root_offsets(dims)
+    out = []
+    for pc in pieces:
+        m, n, k = dims[pc.problem]
+        if not (0 <= pc.row0 and pc.row0 + pc.rows <= m and 0 <= pc.col0 and pc.col0 + pc.cols <= n):
+            raise ValueError("piece outside its problem")
+        out.append((base + elem_bytes * (offs[pc.problem] + pc.row0 * n + pc.col0), max(1, n)))
+    return out

@@ -332,6 +332,31 @@ typedef struct gg_rect_copy {
  * rects pointer with count > 0 return cudaErrorInvalidValue. */
 int gg_copy_rects(float* packed, const gg_rect_copy* rects, int count, int to_packed, void* stream);
 
+/* ---- device memory shared between processes (the gather fused into the kernel) ---------------
+ * No reference counterpart. A multi-GPU run that wants every D on one root GPU can skip the
+ * separate gather: the root exports its D buffer, every other rank opens it and builds its
+ * executor with d pointers (and ldd) into the root's matrices, so that the grouped kernel's
+ * epilogue stores each D tile straight into the root's memory over NVLink while later tiles are
+ * still computing. A D that lies on another GPU is always written with plain coalesced stores (the
+ * kernel's direct-store path), never with TMA. The handle is CUDA IPC: the exporting allocation
+ * must be cudaMalloc memory (the PyTorch caching allocator's default), and the handle is valid
+ * only on the same node while the allocation lives. */
+typedef struct gg_ipc_handle {
+  unsigned char handle[64];   /* cudaIpcMemHandle_t of the allocation that holds the pointer */
+  unsigned long long offset;  /* byte offset of the pointer in that allocation */
+  unsigned long long bytes;   /* bytes of the allocation from the pointer on */
+} gg_ipc_handle;
+
+/* Fills *out for device pointer ptr (current device). cudaErrorInvalidValue for a null pointer or
+ * argument; CUDA errors pass through. */
+int gg_ipc_export(const void* ptr, gg_ipc_handle* out);
+/* Maps an exported allocation into this process (peer access enabled lazily) and returns the
+ * pointer that corresponds to the exported one. Opening a handle of this very process fails
+ * (CUDA IPC is between processes). */
+int gg_ipc_open(const gg_ipc_handle* handle, void** ptr);
+/* Unmaps what gg_ipc_open mapped; ptr is the pointer it returned. */
+int gg_ipc_close(void* ptr);
+
 #ifdef __cplusplus
 }
 #endif

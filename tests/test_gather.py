@@ -81,3 +81,28 @@ def test_piece_elems_counts_rectangles():
 
     assert piece_elems([gg.ShardPiece(0, 0, 3, 0, 4), gg.ShardPiece(1, 2, 0, 0, 9)]) == 12
     assert piece_elems([]) == 0
+
+
+def test_fused_targets_cover_the_root_buffer_exactly_once():
+    """The D pointers that the fused gather gives each rank's pieces tile the root's buffer: every
+    element of every global problem is written by exactly one piece of one rank, and no piece
+    reaches outside its problem's matrix."""
+    import numpy as np
+
+    from grouped_gemm_gpu_kernel_b200.gather import fused_targets, root_offsets
+
+    cfg = gg.KernelConfig(128, 256, 64)
+    probs = [gg.ProblemDesc(m, n, k, 1, 1, None, 1, max(1, k), max(1, n), max(1, n), max(1, n)) for m, n, k in DIMS]
+    total = sum(max(m, 0) * max(n, 0) for m, n, k in DIMS)
+    for world in (1, 2, 3, 8):
+        hits = np.zeros(total, dtype=np.int64)
+        for r in range(world):
+            pieces = gg.partition(probs, cfg, world, r)[0]
+            for pc, (ptr, ldd) in zip(pieces, fused_targets(pieces, DIMS, base=0, elem_bytes=4)):
+                first = ptr // 4
+                for i in range(pc.rows):
+                    hits[first + i * ldd:first + i * ldd + pc.cols] += 1
+        assert (hits == 1).all(), world
+    assert root_offsets([(2, 3, 1), (0, 5, 1), (4, 1, 1)]) == [0, 6, 6]
+    with pytest.raises(ValueError):
+        fused_targets([gg.ShardPiece(0, 1, 2, 0, 3)], [(2, 3, 1)], base=0)
