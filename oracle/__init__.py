@@ -8,7 +8,7 @@ Two native libraries back it:
 
 * ``oracle/liboracle.so`` -- ``gg_oracle.c``, the C restatement of the reference's host algorithm
   (reference ``src/grouped_gemm.cu:54-65,967-1022`` and ``tests/test_correctness.cu:85-102``) and
-  the FP64 accuracy judge.
+  the FP64 accuracy reference.
 * ``oracle/_ref/libgg_ref.so`` -- the reference's own sources compiled unmodified (see
   ``oracle/Makefile``) plus ``ref_shim.cu``; used to pin the restatement and as the
   ``"reference"`` CPU baseline. Absent when the reference tree was not available at build time.

@@ -12,7 +12,7 @@
  *         D = alpha * (A x B) + beta * C, with C read only when c != NULL and beta != 0
  *   - the reference's host GEMM reference tests/test_correctness.cu:85-102 (FP32, natural k order,
  *         always reads C) -- restated as oracle_gemm_f32_refloop for the "port" CPU baseline.
- * The accuracy judge is oracle_gemm_f64: FP16 inputs decoded exactly, products and sums in FP64
+ * The accuracy reference is oracle_gemm_f64: FP16 inputs decoded exactly, products and sums in FP64
  * (oracle_gemm_f64_fmt also takes BF16 inputs, for the library's BF16 extension, and
  * oracle_gemm_f64_epilogue adds the library's fused bias and activation; C given as float holds
  * 16-bit C values exactly).
@@ -169,7 +169,7 @@ int oracle_prepare(const int* m, const int* n, const int* k, int count, int cta_
   return offsets[count];
 }
 
-/* ---- FP64 GEMM (the accuracy judge) --------------------------------------------------------
+/* ---- FP64 GEMM (the accuracy reference) --------------------------------------------------------
  * Computes, for the selected rows (rows == NULL -> all m rows, in order) and all n columns:
  *   d[r*ldd + j]     = alpha * sum_k A[row,k]*B[k,j] + beta * C[row,j]   (C only if c && beta != 0)
  *   scale[r*ldd + j] = |alpha| * sqrt(sum_k (A[row,k]*B[k,j])^2) + |beta * C[row,j]|

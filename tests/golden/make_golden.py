@@ -67,7 +67,7 @@ def problem_sets():
     rng = np.random.default_rng(7)
     sets = {
         "ref_test_shapes": REF_TEST_SHAPES,
-        "survey_kat": [(64, 64, 64), (128, 64, 96), (45, 81, 37), (17, 23, 9), (0, 64, 16), (192, 32, 64)],
+        "host_kat": [(64, 64, 64), (128, 64, 96), (45, 81, 37), (17, 23, 9), (0, 64, 16), (192, 32, 64)],
         "empty": [],
         "all_empty_problems": [(0, 5, 5), (5, 0, 5), (0, 0, 0)],
         "k_zero": [(64, 64, 0), (1, 1, 0), (130, 70, 0)],

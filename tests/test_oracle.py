@@ -52,7 +52,7 @@ def test_fp16_decode_exhaustive():
     assert np.array_equal(np.isinf(got), np.isinf(w))
 
 
-def test_survey_known_answers():
+def test_host_known_answers():
     # reference src/grouped_gemm.cu:967-1022 on the six shapes with 64x64 tiles
     dims = [(64, 64, 64), (128, 64, 96), (45, 81, 37), (17, 23, 9), (0, 64, 16), (192, 32, 64)]
     perm, offs, total = O.prepare(dims, 64, 64, 0)
@@ -94,7 +94,7 @@ def test_f32_port_bit_exact_against_reference_fixture():
 
 
 def test_f64_oracle_against_reference_fixture():
-    """The FP64 judge agrees with the reference's FP32 host GEMM far inside the accuracy bound."""
+    """The FP64 oracle agrees with the reference's FP32 host GEMM far inside the accuracy bound."""
     for p in ref_test_problems():
         m, n, k = p["m"], p["n"], p["k"]
         if m <= 0 or n <= 0:
