@@ -337,14 +337,6 @@ Variant variant_of(const gg_config* c) {
   return v;
 }
 
-// False for an 8-bit problem with work on the tensor-core path that TMA cannot load (base not
-// 16-byte aligned, or a row pitch that is not a multiple of 16 bytes): the zero-fill loader is
-// 16-bit only, so such a problem is refused at build time.
-bool tensor_path_can_load(const DeviceProblemDesc& d, const gg_config* c) {
-  return !(c->use_tensor_cores && in_geom(c->input_type).f8 && d.tiles_m > 0 && d.k > 0 &&
-           (d.flags & grouped_gemm::kFlagTmaAB) == 0u);
-}
-
 // The data-type and epilogue fields of a launch, from a validated config.
 void set_formats(KernelParams& kp, const gg_config* c) {
   kp.input_format = c->input_type;
@@ -516,7 +508,6 @@ int gg_executor_build_with_bias(gg_executor* ex, const gg_problem* sorted_proble
     if (p.m < 0 || p.n < 0 || p.k < 0) return cudaErrorInvalidValue;
     if (!p.a || !p.b || !p.d) return cudaErrorInvalidDevicePointer;
     descs[static_cast<size_t>(i)] = gg::make_device_problem(p, v, config, &maps[static_cast<size_t>(i) * gg::kMapsPerProblem], i);
-    if (!gg::tensor_path_can_load(descs[static_cast<size_t>(i)], config)) return cudaErrorInvalidValue;
   }
   if (count == 0 || total_tiles <= 0) {
     ex->problem_count = count;
@@ -639,7 +630,6 @@ int gg_run_baseline_per_problem(const gg_problem* problems, int count, const gg_
     }
     std::memset(&kp, 0, sizeof(kp));
     kp.single_desc = gg::make_device_problem(p, v, config, kp.single_maps, 0);
-    if (!gg::tensor_path_can_load(kp.single_desc, config)) return cudaErrorInvalidValue;
     const int tiles = kp.single_desc.tiles_m * kp.single_desc.tiles_n;
     kp.status = status;
     kp.timeout_ns = gg::wait_timeout_ns();
@@ -853,7 +843,6 @@ extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count
     const gg_problem& p = problems[gg::g_noalloc_order[s]];
     offs[s + 1] = offs[s] + gg::tile_count(p.m, p.n, config->cta_m, config->cta_n);
     descs[s] = gg::make_device_problem(p, v, config, &maps[static_cast<size_t>(s) * gg::kMapsPerProblem], s);
-    if (!gg::tensor_path_can_load(descs[s], config)) return cudaErrorInvalidValue;
   }
   const int total = offs[count];
   if (total == 0) return cudaSuccess;
@@ -1095,12 +1084,9 @@ int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, g
   CUtensorMap map_a{}, map_d{};
   const bool rows_exist = q.capacity_rows > 0 && q.n > 0;
   const gg::InGeom g = gg::in_geom(config->input_type);
-  // 8-bit operands on the tensor-core path go through TMA only (see tensor_path_can_load).
-  const bool f8_tc = g.f8 && config->use_tensor_cores;
   const bool tma_a = rows_exist && q.k > 0 &&
                      gg::encode_2d(&map_a, g.type, q.a, q.k, q.capacity_rows, static_cast<int64_t>(q.lda) * g.bytes,
                                    g.kblock, cta_rows);
-  if (f8_tc && rows_exist && q.k > 0 && !tma_a) return cudaErrorInvalidValue;
   const bool tma_d = rows_exist && gg::on_this_device(q.d) &&
                      gg::encode_d(&map_d, config->output_type, q.d, q.n, q.capacity_rows, q.ldd);
   for (size_t e = 0; e < E; ++e) {
@@ -1129,8 +1115,6 @@ int gg_moe_plan_create(const gg_moe_problem* problem, const gg_config* config, g
       flags |= grouped_gemm::kFlagTmaAB;
       if (!b_col && gg::encode_b_chunks(&m[gg::kMapB3], g, q.b[e], q.k, q.n, b_pitch, cta_cols / g.chunk))
         flags |= grouped_gemm::kFlagTmaB3;
-    } else if (f8_tc && rows_exist && q.k > 0) {
-      return cudaErrorInvalidValue;
     }
     if (tma_d) {
       m[gg::kMapD] = map_d;

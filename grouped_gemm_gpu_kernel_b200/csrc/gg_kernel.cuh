@@ -455,42 +455,63 @@ __device__ __forceinline__ void epilogue_chunk_range(int nchunks, int half, int&
 
 // ---- producer helpers ------------------------------------------------------------------------
 // Zero-fill loader for problems TMA cannot take (odd leading dimension or base alignment). Fills
-// one stage: A rows [row0, row0+ROWS) and B columns [col0, col0+COLS) of K block kb, in the same
-// 128-byte-swizzled layouts the TMA loads produce. Consecutive lanes read consecutive elements of
-// one row (coalesced), 2 bytes per lane, or 4 when every row of the operand starts on a 4-byte
-// boundary; each lane keeps up to 16 loads in flight before it stores them. Columns of A and rows of B
-// past K are written as zeros; rows of A past M and columns of B past N are not written at all:
-// they only reach accumulator rows and columns that are never stored.
+// one stage -- A rows [row0, row0+ROWS) and B columns [col0, col0+COLS) of K block kb -- in the
+// same 128-byte-swizzled layouts the TMA loads produce. It works in bytes, so 16-bit (EB = 2) and
+// 8-bit (EB = 1) operands share it: consecutive lanes read consecutive W-byte pieces of one row
+// (coalesced; W = 4 when every row of the operand starts 4-byte aligned, else the widest the
+// alignment allows), and each lane keeps up to 16 loads in flight before it stores them. Bytes
+// past K (columns of A, rows of B) are written as zeros; rows of A past M and columns of B past N
+// are not written at all: they only reach accumulator rows and columns that are never stored.
 constexpr int kLsuBatch = 16;  // loads in flight per lane before their stores
 
-template <int V>
-__device__ __forceinline__ uint32_t lsu_load(const unsigned short* src, int c, int limit) {
-  if (V == 2 && c + 1 < limit) return __ldg(reinterpret_cast<const unsigned int*>(src + c));
-  return c < limit ? static_cast<uint32_t>(__ldg(src + c)) : 0u;
+// W bytes at src + bi, with every element at or past `limit` bytes read as zero (limit is a
+// multiple of EB; bi and W are multiples of EB).
+template <int W, int EB>
+__device__ __forceinline__ uint32_t lsu_load(const uint8_t* src, int bi, int limit) {
+  if (bi + W <= limit) {
+    if (W == 4) return __ldg(reinterpret_cast<const unsigned int*>(src + bi));
+    if (W == 2) return __ldg(reinterpret_cast<const unsigned short*>(src + bi));
+    return __ldg(src + bi);
+  }
+  if constexpr (W == EB) {
+    return 0u;  // one element, past the limit
+  } else if constexpr (EB == 2) {
+    return bi < limit ? static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned short*>(src + bi))) : 0u;
+  } else {
+    uint32_t v = 0u;  // 8-bit elements: the 1 to W-1 bytes before the limit
+#pragma unroll
+    for (int e = 0; e < W - 1; ++e)
+      if (bi + e < limit) v |= static_cast<uint32_t>(__ldg(src + bi + e)) << (8 * e);
+    return v;
+  }
 }
 
-template <int V>
+template <int W>
 __device__ __forceinline__ void lsu_store(uint8_t* dst, uint32_t v) {
-  if (V == 2) *reinterpret_cast<uint32_t*>(dst) = v;
-  else *reinterpret_cast<unsigned short*>(dst) = static_cast<unsigned short>(v);
+  if (W == 4) *reinterpret_cast<uint32_t*>(dst) = v;
+  else if (W == 2) *reinterpret_cast<unsigned short*>(dst) = static_cast<unsigned short>(v);
+  else *dst = static_cast<uint8_t>(v);
 }
 
-template <int ROWS, int V>
-__device__ __forceinline__ void lsu_fill_a(uint8_t* as, const unsigned short* a16, int lda, int rows, int k, int row0,
-                                           int k0, int pw, int ln) {
+// K-major tile: ROWS rows of 128 bytes (the K block), row r at r * 128, 16-byte units XOR-swizzled
+// by r & 7. Source row r starts at base + (row0 + r) * ld_bytes + k0_bytes; kbytes of it lie
+// inside K.
+template <int ROWS, int W, int EB>
+__device__ __forceinline__ void lsu_fill_kmajor(uint8_t* dst, const uint8_t* base, int64_t ld_bytes, int rows,
+                                                int kbytes, int row0, int64_t k0_bytes, int pw, int ln) {
   constexpr int kW = kProdThreads / 32;
-  constexpr int kPer = 2 / V;  // loads per lane per row (a row is 64 elements)
+  constexpr int kPer = 128 / (32 * W);  // loads per lane per row
   constexpr int kB = (kLsuBatch / kPer) < (ROWS / kW) ? (kLsuBatch / kPer) : (ROWS / kW);  // rows per batch
-  const int klim = k - k0;            // columns of this K block inside K
+  const int klim = kbytes < 128 ? kbytes : 128;
 #pragma unroll 1
   for (int rb = pw; rb < rows; rb += kW * kB) {
     uint32_t v[kB][kPer];
 #pragma unroll
     for (int i = 0; i < kB; ++i) {
       const int r = rb + i * kW;
-      const unsigned short* src = a16 + static_cast<int64_t>(row0 + (r < rows ? r : 0)) * lda + k0;
+      const uint8_t* src = base + static_cast<int64_t>(row0 + (r < rows ? r : 0)) * ld_bytes + k0_bytes;
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) v[i][j] = r < rows ? lsu_load<V>(src, j * 32 + V * ln, klim) : 0u;
+      for (int j = 0; j < kPer; ++j) v[i][j] = r < rows ? lsu_load<W, EB>(src, j * 32 * W + W * ln, klim) : 0u;
     }
 #pragma unroll
     for (int i = 0; i < kB; ++i) {
@@ -498,28 +519,32 @@ __device__ __forceinline__ void lsu_fill_a(uint8_t* as, const unsigned short* a1
       if (r < rows) {
         const int sw = (r & 7) << 4;
 #pragma unroll
-        for (int j = 0; j < kPer; ++j) lsu_store<V>(as + r * 128 + (((j * 32 + V * ln) * 2) ^ sw), v[i][j]);
+        for (int j = 0; j < kPer; ++j) lsu_store<W>(dst + r * 128 + ((j * 32 * W + W * ln) ^ sw), v[i][j]);
       }
     }
   }
 }
 
-template <int COLS, int V>
-__device__ __forceinline__ void lsu_fill_b(uint8_t* bs, const unsigned short* b16, int ldb, int cols, int k, int col0,
-                                           int k0, int pw, int ln) {
+// MN-major tile: KB K rows (the K block) x COLS_BYTES bytes of columns, stored as 128-byte-wide
+// column chunks of KB rows (chunk c at c * KB * 128), row kr of a chunk at kr * 128, swizzled by
+// kr & 7. Source K row kr starts at base + (k0 + kr) * ld_bytes + col0_bytes; cbytes of it lie
+// inside N; rows at or past kvalid are zero.
+template <int COLS_BYTES, int KB, int W, int EB>
+__device__ __forceinline__ void lsu_fill_mnmajor(uint8_t* dst, const uint8_t* base, int64_t ld_bytes, int cbytes,
+                                                 int kvalid, int64_t col0_bytes, int k0, int pw, int ln) {
   constexpr int kW = kProdThreads / 32;
-  constexpr int kPer = COLS / (32 * V);  // loads per lane per K row
-  constexpr int kB = (kLsuBatch / kPer) < (kBK / kW) ? (kLsuBatch / kPer) : (kBK / kW);  // K rows per batch
+  constexpr int kPer = COLS_BYTES / (32 * W);  // loads per lane per K row
+  constexpr int kB = (kLsuBatch / kPer) < (KB / kW) ? (kLsuBatch / kPer) : (KB / kW);  // K rows per batch
 #pragma unroll 1
-  for (int rb = pw; rb < kBK; rb += kW * kB) {
+  for (int rb = pw; rb < KB; rb += kW * kB) {
     uint32_t v[kB][kPer];
 #pragma unroll
     for (int i = 0; i < kB; ++i) {
       const int kr = rb + i * kW;
-      const bool kin = k0 + kr < k;
-      const unsigned short* src = b16 + static_cast<int64_t>(kin ? k0 + kr : 0) * ldb + col0;
+      const bool kin = kr < kvalid;
+      const uint8_t* src = base + static_cast<int64_t>(kin ? k0 + kr : 0) * ld_bytes + col0_bytes;
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) v[i][j] = kin ? lsu_load<V>(src, j * 32 * V + V * ln, cols) : 0u;
+      for (int j = 0; j < kPer; ++j) v[i][j] = kin ? lsu_load<W, EB>(src, j * 32 * W + W * ln, cbytes) : 0u;
     }
 #pragma unroll
     for (int i = 0; i < kB; ++i) {
@@ -527,42 +552,63 @@ __device__ __forceinline__ void lsu_fill_b(uint8_t* bs, const unsigned short* b1
       const int sw = (kr & 7) << 4;
 #pragma unroll
       for (int j = 0; j < kPer; ++j) {
-        const int c = j * 32 * V + V * ln;
-        if (c < cols) lsu_store<V>(bs + (c >> 6) * 8192 + kr * 128 + (((c & 63) * 2) ^ sw), v[i][j]);
+        const int c = j * 32 * W + W * ln;
+        if (c < cbytes) lsu_store<W>(dst + (c >> 7) * (KB * 128) + kr * 128 + ((c & 127) ^ sw), v[i][j]);
       }
     }
   }
 }
 
+// Widest load (4, 2 or 1 bytes) that every row of an operand allows: base and row pitch in bytes.
+__device__ __forceinline__ int lsu_width(const void* p, int64_t ld_bytes) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p) | static_cast<uintptr_t>(ld_bytes);
+  return (a & 3u) == 0u ? 4 : (a & 1u) == 0u ? 2 : 1;
+}
+
+// One operand of the stage. kmajor: a K-major tile of NV rows (row-major A, column-major B);
+// else an MN-major tile of NV columns (row-major B, column-major A). nv_valid rows/columns from
+// v0 on and K from k0 on lie inside the problem.
+template <int NV, int EB>
+__device__ __forceinline__ void lsu_fill_operand(uint8_t* dst, const void* p, int ld, bool kmajor, int nv_valid,
+                                                 int k, int v0, int k0, int pw, int ln) {
+  constexpr int KB = EB == 2 ? kBK : 2 * kBK;  // K values in one 128-byte row
+  const uint8_t* base = static_cast<const uint8_t*>(p);
+  const int64_t ld_bytes = static_cast<int64_t>(ld) * EB;
+  const int w = lsu_width(p, ld_bytes);
+  if (kmajor) {
+    const int kbytes = (k - k0) * EB;
+    const int64_t k0b = static_cast<int64_t>(k0) * EB;
+    if (w == 4) lsu_fill_kmajor<NV, 4, EB>(dst, base, ld_bytes, nv_valid, kbytes, v0, k0b, pw, ln);
+    else if (w == 2 || EB == 2) lsu_fill_kmajor<NV, 2, EB>(dst, base, ld_bytes, nv_valid, kbytes, v0, k0b, pw, ln);
+    else lsu_fill_kmajor<NV, 1, EB>(dst, base, ld_bytes, nv_valid, kbytes, v0, k0b, pw, ln);
+  } else if constexpr (NV * EB >= 128) {  // narrower MN-major 8-bit tiles are refused on the host
+    const int cbytes = nv_valid * EB;
+    const int kvalid = k - k0 < KB ? k - k0 : KB;
+    const int64_t c0b = static_cast<int64_t>(v0) * EB;
+    if (w == 4) lsu_fill_mnmajor<NV * EB, KB, 4, EB>(dst, base, ld_bytes, cbytes, kvalid, c0b, k0, pw, ln);
+    else if (w == 2 || EB == 2)
+      lsu_fill_mnmajor<NV * EB, KB, 2, EB>(dst, base, ld_bytes, cbytes, kvalid, c0b, k0, pw, ln);
+    else lsu_fill_mnmajor<NV * EB, KB, 1, EB>(dst, base, ld_bytes, cbytes, kvalid, c0b, k0, pw, ln);
+  }
+}
+
 // `col_a` / `col_b`: the operand is stored column-major, so A (k x m) fills the MN-major chunk
-// layout of row-major B and B (n x k) the K-major row layout of row-major A.
+// layout of row-major B and B (n x k) the K-major row layout of row-major A. f8: 8-bit operands.
 template <int ROWS, int COLS>
 __device__ __forceinline__ void lsu_fill_stage(uint8_t* as, uint8_t* bs, const __half* a, int lda, const __half* b,
                                                int ldb, int m, int n, int k, int row0, int col0, int kb, int ptid,
-                                               bool col_a, bool col_b) {
-  const unsigned short* a16 = reinterpret_cast<const unsigned short*>(a);
-  const unsigned short* b16 = reinterpret_cast<const unsigned short*>(b);
+                                               bool col_a, bool col_b, bool f8) {
   const int pw = ptid >> 5, ln = ptid & 31;
-  const int k0 = kb * kBK;
   const int rows = min(ROWS, m - row0);
   const int cols = min(COLS, n - col0);
-  const bool a4 = ((lda & 1) == 0) && ((reinterpret_cast<uintptr_t>(a) & 3u) == 0u);
-  const bool b4 = ((ldb & 1) == 0) && ((reinterpret_cast<uintptr_t>(b) & 3u) == 0u);
-  if (col_a) {
-    if (a4) lsu_fill_b<ROWS, 2>(as, a16, lda, rows, k, row0, k0, pw, ln);
-    else lsu_fill_b<ROWS, 1>(as, a16, lda, rows, k, row0, k0, pw, ln);
+  if (f8) {
+    const int k0 = kb * 2 * kBK;
+    lsu_fill_operand<ROWS, 1>(as, a, lda, !col_a, rows, k, row0, k0, pw, ln);
+    if (cols > 0) lsu_fill_operand<COLS, 1>(bs, b, ldb, col_b, cols, k, col0, k0, pw, ln);
   } else {
-    if (a4) lsu_fill_a<ROWS, 2>(as, a16, lda, rows, k, row0, k0, pw, ln);
-    else lsu_fill_a<ROWS, 1>(as, a16, lda, rows, k, row0, k0, pw, ln);
-  }
-  if (cols > 0) {
-    if (col_b) {
-      if (b4) lsu_fill_a<COLS, 2>(bs, b16, ldb, cols, k, col0, k0, pw, ln);
-      else lsu_fill_a<COLS, 1>(bs, b16, ldb, cols, k, col0, k0, pw, ln);
-    } else {
-      if (b4) lsu_fill_b<COLS, 2>(bs, b16, ldb, cols, k, col0, k0, pw, ln);
-      else lsu_fill_b<COLS, 1>(bs, b16, ldb, cols, k, col0, k0, pw, ln);
-    }
+    const int k0 = kb * kBK;
+    lsu_fill_operand<ROWS, 2>(as, a, lda, !col_a, rows, k, row0, k0, pw, ln);
+    if (cols > 0) lsu_fill_operand<COLS, 2>(bs, b, ldb, col_b, cols, k, col0, k0, pw, ln);
   }
 }
 
@@ -846,10 +892,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
           }
           uint8_t* as = smem + st * L::kStageBytes;
           uint8_t* bs = as + L::kABytes;
-          // 16-bit operands only: the host sends every 8-bit problem with work through TMA.
-          if (!f8)
-            lsu_fill_stage<BM, BN>(as, bs, a, lda, b, ldb, m, n, k, tile_m * BM, tile_n * BN, kb, ptid,
-                                   (mode & kModeACol) != 0, (mode & kModeBCol) != 0);
+          lsu_fill_stage<BM, BN>(as, bs, a, lda, b, ldb, m, n, k, tile_m * BM, tile_n * BN, kb, ptid,
+                                 (mode & kModeACol) != 0, (mode & kModeBCol) != 0, f8);
           ptx::fence_proxy_async_smem();
           ptx::named_bar_sync(1, kProdThreads);
           if (ptid == 0) ptx::mbar_arrive(full_bar(st));

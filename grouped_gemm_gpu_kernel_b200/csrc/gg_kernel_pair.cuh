@@ -272,10 +272,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* as = smem + st * L::kStageBytes;
           uint8_t* bs = as + L::kABytes;
-          // 16-bit operands only: the host sends every 8-bit problem with work through TMA.
-          if (!f8)
-            lsu_fill_stage<128, HB>(as, bs, a, lda, b, ldb, m, n, k, row_base, col_base, kb, ptid,
-                                    (mode & kModeACol) != 0, (mode & kModeBCol) != 0);
+          lsu_fill_stage<128, HB>(as, bs, a, lda, b, ldb, m, n, k, row_base, col_base, kb, ptid,
+                                  (mode & kModeACol) != 0, (mode & kModeBCol) != 0, f8);
           ptx::fence_proxy_async_all();  // the leader's tensor cores read this CTA's shared memory
           ptx::named_bar_sync(1, kProdThreads);
           if (ptid == 0) {

@@ -175,16 +175,16 @@ class DeviceProblemSet:
         self.a, self.b, self.a_off, self.b_off, self.lda, self.ldb = a2, b2, a_off, b_off, lda, ldb
         self.a_col, self.b_col = a_col, b_col
 
-    def to_fp8(self, fmt: int) -> "DeviceProblemSet":
+    def to_fp8(self, fmt: int, pad: int = 16) -> "DeviceProblemSet":
         """A and B re-encoded as 8-bit floats for runs with KernelConfig.input_type = fmt (2 E4M3,
         3 E5M2): each FP16 value rounded to the nearest 8-bit value by torch, one byte per element,
-        in new uint8 slabs whose row pitches are padded to multiples of 16 elements and whose
-        operands start on 256-byte boundaries (the tensor-core path loads 8-bit operands by TMA,
-        which needs 16-byte-aligned rows). The storage layouts are kept."""
+        in new uint8 slabs whose operands start on 256-byte boundaries, row pitches padded to
+        multiples of `pad` elements (16: every row 16-byte aligned, so TMA loads them; 1: packed,
+        odd pitches go through the zero-fill loader). The storage layouts are kept."""
         import torch
 
         dt = {2: torch.float8_e4m3fn, 3: torch.float8_e5m2}[int(fmt)]
-        self._relayout(lambda t: t.to(dt).view(torch.uint8), torch.uint8, self.a_col, self.b_col, 16)
+        self._relayout(lambda t: t.to(dt).view(torch.uint8), torch.uint8, self.a_col, self.b_col, pad)
         self.in_fmt = int(fmt)
         return self
 

@@ -79,9 +79,9 @@ typedef struct gg_problem {
  * is NaN) and GG_INPUT_E5M2 (1-5-2, bias 15, IEEE-style infinities and NaNs), one byte per element,
  * multiplied exactly and accumulated in FP32 (tcgen05 kind::f8f6f4). With 8-bit inputs the tensor
  * -core path needs tiles whose per-CTA B width is a multiple of 128 (128x128, 128x256, 64x128,
- * 256x256; others are an invalid config) and, for every problem with work, A and B bases that are
- * 16-byte aligned with lda and ldb multiples of 16 (else the build returns 1); the CUDA-core path
- * takes any tile and any alignment.
+ * 256x256; others are an invalid config, unless B is column-major, see b_layout); any pointer
+ * alignment and pitch is taken (16-byte aligned rows load by TMA, others by the zero-fill loader).
+ * The CUDA-core path takes any tile.
  * output_type (no reference counterpart): the element type of every C and D of the set,
  * GG_OUTPUT_F32 (0, the reference's), GG_OUTPUT_F16 or GG_OUTPUT_BF16. The accumulation and the
  * epilogue arithmetic stay FP32; D is rounded to nearest even once, at the store.

@@ -259,24 +259,18 @@ def test_fp8_and_fp16_decode_differ(cuda):
     assert not torch.equal(outs[0][valid], outs[1][valid])
 
 
-def test_fp8_problem_that_tma_cannot_load_is_refused(cuda):
-    """8-bit operands on the tensor-core path go through TMA only: a row pitch that is not a
-    multiple of 16 bytes makes the build fail with cudaErrorInvalidValue (1); the CUDA-core path
-    takes the same problem."""
-    import torch
-
-    m, n, k = 40, 48, 37  # lda = 37 bytes
-    A = torch.zeros((m, k), dtype=torch.uint8, device=cuda)
-    B = torch.zeros((k, n), dtype=torch.uint8, device=cuda)
-    D = torch.zeros((m, n), device=cuda)
-    p = gg.ProblemDesc(m, n, k, A.data_ptr(), B.data_ptr(), None, D.data_ptr(), k, n, n, n)
-    for tc, want in ((True, 1), (False, 0)):
-        cfg = gg.KernelConfig(128, 128, 64, use_tensor_cores=tc, input_type=E4M3)
-        ex = gg.GroupedGemmExecutor()
-        assert ex.build(gg.prepare_problem_set([p], cfg, 0), cfg) == want
-        if want == 0:
-            assert ex.run() == 0
-            torch.cuda.synchronize()
-            assert ex.status() == 0
-        ex.close()
-    assert torch.equal(D, torch.zeros_like(D))  # zero inputs: zero products
+@pytest.mark.parametrize("cfg", [gg.KernelConfig(128, 256, 64), gg.KernelConfig(128, 128, 64),
+                                 gg.KernelConfig(256, 256, 64)], ids=_cfg_id)
+def test_fp8_packed_pitches_take_the_zero_fill_loader(cuda, cfg):
+    """8-bit operands whose rows TMA cannot load (packed odd pitches: 1-, 2- and 4-byte aligned
+    rows) go through the zero-fill loader on the tensor cores, in both storage layouts."""
+    fmt = E4M3
+    for a_col, b_col in ((False, False), (True, True)):
+        run_cfg = gg.KernelConfig(cfg.cta_m, cfg.cta_n, cfg.cta_k, input_type=fmt, a_layout=int(a_col),
+                                  b_layout=int(b_col))
+        for shapes in (W.make_shapes("small16", seed=5), W.make_shapes("tiny4096", seed=6)):
+            ps = W.allocate(shapes, seed=11).to_layout(a_col, b_col).to_fp8(fmt, pad=1)
+            run_set(ps, run_cfg, None)
+            worst = check_problems(ps)
+            assert worst <= 1.0, f"{shapes.name} layouts {a_col, b_col}: error/tolerance {worst:.3f}"
+            assert padding_untouched(ps)
