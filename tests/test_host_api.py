@@ -330,3 +330,20 @@ def test_layouts_are_validated_on_the_host():
         got = ex.build(gg.prepare_problem_set([], cfg, 0), cfg)
         ex.close()
         assert got == (0 if simt and a_l in (0, 1) and b_l in (0, 1) else want), (shape, in_t, a_l, b_l, simt)
+
+
+def test_ipc_entry_points_check_arguments_before_device_work():
+    """gg_ipc_export / gg_ipc_open / gg_ipc_close reject null arguments, and closing a pointer that
+    gg_ipc_open did not return, with cudaErrorInvalidValue (1) and no CUDA call."""
+    import ctypes
+
+    lib = gg.capi.load()
+    h = gg.capi.GGIpcHandle()
+    assert lib.gg_ipc_export(None, ctypes.byref(h)) == 1
+    assert lib.gg_ipc_export(ctypes.c_void_p(0x1000), None) == 1
+    ptr = ctypes.c_void_p()
+    assert lib.gg_ipc_open(None, ctypes.byref(ptr)) == 1
+    assert lib.gg_ipc_open(ctypes.byref(h), None) == 1
+    assert lib.gg_ipc_close(None) == 1
+    assert lib.gg_ipc_close(ctypes.c_void_p(0x1000)) == 1
+    assert ctypes.sizeof(gg.capi.GGIpcHandle) == 80
