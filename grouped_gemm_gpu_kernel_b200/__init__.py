@@ -26,6 +26,7 @@ __all__ = [
     "prepare_problem_set", "sort_mode_name", "query_occupancy", "run_grouped_gemm_once",
     "run_baseline_per_problem", "count_non_empty_problems", "partition", "ShardPiece", "problem_from_tensors",
     "NATIVE_CONFIGS", "REFERENCE_CONFIGS", "PAIR_CONFIGS", "selftest_wait_timeout", "capi", "MoePlan",
+    "selftest_wait_timeout_word", "baseline_status", "noalloc_status",
     "InputType", "OutputType", "Activation", "Layout",
 ]
 
@@ -378,6 +379,33 @@ def selftest_wait_timeout(timeout_ns: int = 20_000_000):
     out = ctypes.c_int(0)
     st = capi.load().gg_selftest_wait_timeout(int(timeout_ns), ctypes.byref(out))
     return st, out.value
+
+
+def selftest_wait_timeout_word(word: int, timeout_ns: int = 20_000_000) -> int:
+    """The bounded-wait self-test recording into the baseline's (capi.GG_STATUS_WORD_BASELINE) or
+    the no-allocation entry point's (capi.GG_STATUS_WORD_NOALLOC) status word; returns the
+    cudaError_t of the launch."""
+    return capi.load().gg_selftest_wait_timeout_word(int(word), int(timeout_ns))
+
+
+def baseline_status() -> int:
+    """Synchronises; returns (then clears) the GG_STATUS_* bits raised by run_baseline_per_problem
+    launches on the current device."""
+    out = ctypes.c_int(0)
+    st = capi.load().gg_baseline_status(ctypes.byref(out))
+    if st != 0:
+        raise RuntimeError(f"gg_baseline_status failed with status {st}")
+    return out.value
+
+
+def noalloc_status() -> int:
+    """Synchronises; returns (then clears) the GG_STATUS_* bits of the last no-allocation call
+    (gg_run_grouped_gemm_noalloc) on the current device."""
+    out = ctypes.c_int(0)
+    st = capi.load().gg_noalloc_status(ctypes.byref(out))
+    if st != 0:
+        raise RuntimeError(f"gg_noalloc_status failed with status {st}")
+    return out.value
 
 
 def problem_from_tensors(a, b, c, d, alpha: float = 1.0, beta: float = 0.0) -> ProblemDesc:

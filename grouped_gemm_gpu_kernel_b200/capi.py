@@ -20,6 +20,7 @@ EXPORTED_SYMBOLS = (
     "gg_executor_problem_count", "gg_executor_total_tiles", "gg_executor_grid_ctas", "gg_executor_status",
     "gg_run_grouped_gemm_once", "gg_run_baseline_per_problem", "gg_count_non_empty_problems",
     "gg_partition", "gg_selftest_wait_timeout", "gg_run_grouped_gemm_noalloc", "gg_copy_rects",
+    "gg_baseline_status", "gg_noalloc_status", "gg_selftest_wait_timeout_word",
     "gg_moe_plan_create", "gg_moe_plan_run", "gg_moe_plan_status", "gg_moe_plan_destroy",
     "gg_ipc_export", "gg_ipc_open", "gg_ipc_close",
 )
@@ -42,10 +43,13 @@ GG_STATUS_TIMEOUT_PRODUCER = 0x1
 GG_STATUS_TIMEOUT_MMA = 0x2
 GG_STATUS_TIMEOUT_EPILOGUE = 0x4
 GG_STATUS_TIMEOUT_SCHEDULER = 0x8
+GG_STATUS_WORD_BASELINE = 0
+GG_STATUS_WORD_NOALLOC = 1
 
 CUDA_SUCCESS = 0
 CUDA_ERROR_INVALID_VALUE = 1
 CUDA_ERROR_INVALID_DEVICE_POINTER = 17
+CUDA_ERROR_LAUNCH_TIMEOUT = 702
 
 
 class GGProblem(ctypes.Structure):
@@ -132,6 +136,9 @@ def load() -> ctypes.CDLL:
                           P(ctypes.c_double)], ctypes.c_int),
         "gg_selftest_wait_timeout": ([ctypes.c_ulonglong, i32p], ctypes.c_int),
         "gg_run_grouped_gemm_noalloc": ([pp, ctypes.c_int, ctypes.c_int, pc, vp], ctypes.c_int),
+        "gg_baseline_status": ([i32p], ctypes.c_int),
+        "gg_noalloc_status": ([i32p], ctypes.c_int),
+        "gg_selftest_wait_timeout_word": ([ctypes.c_int, ctypes.c_ulonglong], ctypes.c_int),
         "gg_copy_rects": ([vp, vp, ctypes.c_int, ctypes.c_int, vp], ctypes.c_int),
         "gg_moe_plan_create": ([P(GGMoeProblem), pc, P(vp)], ctypes.c_int),
         "gg_moe_plan_run": ([vp, vp, vp], ctypes.c_int),

@@ -114,20 +114,28 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, int
 
 // False when p is device memory of another GPU (a peer buffer mapped into this process, e.g. the
 // root's D of a gather fused into the kernel): such a D is written with plain stores, never TMA.
-// Everything else counts as this device's. The last allocation range looked up is cached, so a
-// problem set whose D matrices share one buffer costs one query.
+// A pointer whose device cannot be queried counts as another GPU's too (plain stores are correct
+// for any device memory; a TMA store is not). The last allocation range looked up is cached, so a
+// problem set whose D matrices share one buffer costs one query; opening or closing an IPC
+// mapping invalidates the cache, since a mapping can reuse the addresses of a freed buffer.
 bool on_this_device(const void* p) {
   static thread_local uintptr_t lo = 0, hi = 0;
   static thread_local int cached_dev = -1;
-  static thread_local bool cached_local = true;
+  static thread_local bool cached_local = false;
+  static thread_local unsigned cached_gen = 0;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return true;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;  // unknown: plain stores are correct for any device memory
+  }
   const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-  if (dev == cached_dev && a >= lo && a < hi) return cached_local;
+  // A mapping opened or closed since the range was cached may reuse its addresses: look again.
+  const unsigned gen = ipc_mapping_generation();
+  if (dev == cached_dev && gen == cached_gen && a >= lo && a < hi) return cached_local;
   cudaPointerAttributes attr{};
   if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
     (void)cudaGetLastError();
-    return true;
+    return false;
   }
   const bool local = !(attr.type == cudaMemoryTypeDevice && attr.device != dev);
   static PFN_cuMemGetAddressRange_v3020 range = [] {
@@ -145,6 +153,7 @@ bool on_this_device(const void* p) {
     hi = lo + size;
     cached_dev = dev;
     cached_local = local;
+    cached_gen = gen;
   }
   return local;
 }
@@ -266,13 +275,14 @@ DeviceProblemDesc make_device_problem(const gg_problem& p, Variant v, const gg_c
 }
 
 // Per-device status word for launches that have no executor (the per-problem baseline).
-int* device_status_word() {
+// create = false: the word if it exists, else null (nothing was launched on the device yet).
+int* device_status_word(bool create = true) {
   static std::mutex mu;
   static int* words[kMaxDevices] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
   std::lock_guard<std::mutex> lock(mu);
-  if (!words[dev]) {
+  if (!words[dev] && create) {
     int* w = nullptr;
     if (cudaMalloc(&w, sizeof(int)) != cudaSuccess) return nullptr;
     if (cudaMemset(w, 0, sizeof(int)) != cudaSuccess) {
@@ -346,6 +356,17 @@ void set_formats(KernelParams& kp, const gg_config* c) {
 }
 
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Waits for the device, copies the status word to *bits and clears it. A null word reads as 0.
+cudaError_t take_status(int* word, int* bits) {
+  *bits = 0;
+  if (!word) return cudaSuccess;
+  cudaError_t st = cudaDeviceSynchronize();
+  if (st != cudaSuccess) return st;
+  st = cudaMemcpy(bits, word, sizeof(int), cudaMemcpyDeviceToHost);
+  if (st != cudaSuccess) return st;
+  return cudaMemset(word, 0, sizeof(int));
+}
 
 }  // namespace
 }  // namespace gg
@@ -586,13 +607,7 @@ int gg_executor_grid_ctas(const gg_executor* ex) { return ex ? ex->grid_ctas : 0
 int gg_executor_status(const gg_executor* ex, int* device_status) {
   if (!ex) return cudaErrorInvalidDevicePointer;
   if (!device_status) return cudaErrorInvalidValue;
-  *device_status = 0;
-  if (!ex->d_status) return cudaSuccess;
-  cudaError_t st = cudaDeviceSynchronize();
-  if (st != cudaSuccess) return st;
-  st = cudaMemcpy(device_status, ex->d_status, sizeof(int), cudaMemcpyDeviceToHost);
-  if (st != cudaSuccess) return st;
-  return cudaMemset(ex->d_status, 0, sizeof(int));
+  return gg::take_status(ex->d_status, device_status);
 }
 
 int gg_run_grouped_gemm_once(const gg_problem* problems, int count, int sort_mode, const gg_config* config,
@@ -607,7 +622,15 @@ int gg_run_grouped_gemm_once(const gg_problem* problems, int count, int sort_mod
   gg_executor ex;
   st = gg_executor_build(&ex, sorted.data(), count, offs.data(), count + 1, total, config);
   if (st == cudaSuccess) st = gg_executor_run(&ex, stream);
-  ex.release();  // like the reference, freeing the temporary state synchronises
+  // The call synchronises anyway (freeing the temporary state, as in the reference), so the
+  // kernel's status word is read here: a bounded wait that ran out left D partly written, which
+  // the caller learns as cudaErrorLaunchTimeout.
+  if (st == cudaSuccess && ex.d_status) {
+    int bits = 0;
+    st = gg_executor_status(&ex, &bits);
+    if (st == cudaSuccess && bits != 0) st = cudaErrorLaunchTimeout;
+  }
+  ex.release();
   return st;
 }
 
@@ -646,6 +669,11 @@ int gg_run_baseline_per_problem(const gg_problem* problems, int count, const gg_
     if (st != cudaSuccess) return st;
   }
   return cudaSuccess;
+}
+
+int gg_baseline_status(int* device_status) {
+  if (!device_status) return cudaErrorInvalidValue;
+  return gg::take_status(gg::device_status_word(false), device_status);
 }
 
 int gg_count_non_empty_problems(const gg_problem* problems, int count, const gg_config* config) {
@@ -885,6 +913,43 @@ extern "C" int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count
   kp.single_mode = 0;
   gg::set_formats(kp, config);
   return gg::launch_path(config->use_tensor_cores != 0, v, kp, grid, s);
+}
+
+namespace gg {
+namespace {
+// The status word of the no-allocation entry point on the current device (in its fixed array).
+cudaError_t noalloc_status_word(int** word) {
+  void* scratch = nullptr;
+  const cudaError_t st = noalloc_scratch(&scratch);
+  if (st != cudaSuccess) return st;
+  *word = reinterpret_cast<int*>(static_cast<unsigned char*>(scratch) + kNoAllocCounterOff + sizeof(int));
+  return cudaSuccess;
+}
+}  // namespace
+}  // namespace gg
+
+extern "C" int gg_noalloc_status(int* device_status) {
+  if (!device_status) return cudaErrorInvalidValue;
+  *device_status = 0;
+  int* word = nullptr;
+  const cudaError_t st = gg::noalloc_status_word(&word);
+  if (st != cudaSuccess) return st;
+  return gg::take_status(word, device_status);
+}
+
+extern "C" int gg_selftest_wait_timeout_word(int word, unsigned long long timeout_ns) {
+  int* target = nullptr;
+  if (word == GG_STATUS_WORD_BASELINE) {
+    target = gg::device_status_word();
+    if (!target) return cudaErrorMemoryAllocation;
+  } else if (word == GG_STATUS_WORD_NOALLOC) {
+    const cudaError_t st = gg::noalloc_status_word(&target);
+    if (st != cudaSuccess) return st;
+  } else {
+    return cudaErrorInvalidValue;
+  }
+  const cudaError_t st = gg::launch_wait_selftest(target, timeout_ns, nullptr);
+  return st != cudaSuccess ? st : cudaDeviceSynchronize();
 }
 
 // ---- grouped GEMM with device-side preparation (mixture-of-experts routing) ---------------------

@@ -41,6 +41,10 @@ cudaError_t kernel_occupancy(Variant v, int* active_blocks_per_sm, cudaFuncAttri
 cudaError_t kernel_resident_ctas(Variant v, int* ctas);
 cudaError_t launch_wait_selftest(int* status, unsigned long long timeout_ns, cudaStream_t stream);
 
+// Count of IPC mappings opened or closed in this process (gg_ipc.cu); a cached answer about which
+// GPU owns an address is stale once it changes.
+unsigned ipc_mapping_generation();
+
 // CUDA-core path (use_tensor_cores = false), gg_simt.cu: same parameters and tile numbering,
 // the variant only fixes the tile shape.
 cudaError_t launch_simt_kernel(Variant v, const KernelParams& params, int grid, cudaStream_t stream);

@@ -5,11 +5,13 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
 #include <vector>
 
+#include "gg_internal.h"
 #include "grouped_gemm_b200.h"
 
 namespace {
@@ -35,8 +37,13 @@ struct Mapping {
 
 std::mutex g_mu;
 std::vector<Mapping> g_open;  // mappings made by gg_ipc_open, closed by gg_ipc_close
+std::atomic<unsigned> g_generation{0};
 
 }  // namespace
+
+namespace gg {
+unsigned ipc_mapping_generation() { return g_generation.load(std::memory_order_acquire); }
+}  // namespace gg
 
 extern "C" {
 
@@ -64,6 +71,7 @@ int gg_ipc_open(const gg_ipc_handle* handle, void** ptr) {
   void* base = nullptr;
   const cudaError_t st = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
   if (st != cudaSuccess) return st;
+  g_generation.fetch_add(1, std::memory_order_acq_rel);
   char* b = static_cast<char*>(base);
   {
     std::lock_guard<std::mutex> lock(g_mu);
@@ -88,7 +96,9 @@ int gg_ipc_close(void* ptr) {
     }
   }
   if (!base) return cudaErrorInvalidValue;
-  return cudaIpcCloseMemHandle(base);
+  const cudaError_t st = cudaIpcCloseMemHandle(base);
+  g_generation.fetch_add(1, std::memory_order_acq_rel);
+  return st;
 }
 
 }  // extern "C"

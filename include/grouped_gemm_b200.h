@@ -14,7 +14,11 @@
  *   1  cudaErrorInvalidValue          unsupported config, negative dims, inconsistent prepared set,
  *                                     null output argument
  *   17 cudaErrorInvalidDevicePointer  null a/b/d in a problem, or a null/destroyed executor
+ *   702 cudaErrorLaunchTimeout        (gg_run_grouped_gemm_once only) a bounded wait inside the
+ *                                     kernel ran out; D may be partly written
  *   other values are CUDA runtime errors passed through unchanged.
+ * Asynchronous launches report such a timeout through a status word instead, read with
+ * gg_executor_status, gg_baseline_status, gg_noalloc_status or gg_moe_plan_status.
  * An empty problem set (or one with zero tiles) is a successful no-op that launches nothing.
  *
  * Each entry point replaces one function of the reference C++ API
@@ -217,14 +221,22 @@ int gg_executor_grid_ctas(const gg_executor* executor);
 int gg_executor_status(const gg_executor* executor, int* device_status);
 
 /* reference src/grouped_gemm.cu:1279-1291 (run_grouped_gemm_once): prepare + build + run. Like
- * the reference, the temporary executor is freed before returning, which synchronises. */
+ * the reference, the temporary executor is freed before returning, which synchronises; before
+ * that its status word is read, and a bounded wait that ran out inside the kernel returns
+ * cudaErrorLaunchTimeout (702) instead of success. */
 int gg_run_grouped_gemm_once(const gg_problem* problems, int count, int sort_mode,
                              const gg_config* config, void* stream);
 
 /* reference src/grouped_gemm.cu:1293-1317 (run_baseline_per_problem): one kernel launch per
- * non-empty problem, in input order, on the same tile code. */
+ * non-empty problem, in input order, on the same tile code. Asynchronous: the launches share one
+ * status word per device, read with gg_baseline_status. */
 int gg_run_baseline_per_problem(const gg_problem* problems, int count, const gg_config* config,
                                 void* stream);
+
+/* No reference counterpart (the reference kernels cannot time out). Synchronises the current
+ * device and returns in *device_status the GG_STATUS_* bits raised by gg_run_baseline_per_problem
+ * launches on it since the last query (0 when none ran), then clears them. */
+int gg_baseline_status(int* device_status);
 
 /* reference src/grouped_gemm.cu:1319-1329 (count_non_empty_problems). */
 int gg_count_non_empty_problems(const gg_problem* problems, int count, const gg_config* config);
@@ -246,6 +258,14 @@ int gg_partition(const gg_problem* problems, int count, const gg_config* config,
  * hang and that the context stays usable. */
 int gg_selftest_wait_timeout(unsigned long long timeout_ns, int* status);
 
+/* No reference counterpart. The same self-test, recording into the status word that
+ * gg_baseline_status (word GG_STATUS_WORD_BASELINE) or gg_noalloc_status (GG_STATUS_WORD_NOALLOC)
+ * reads on the current device, so that a caller can check that a timeout on those paths reaches
+ * the query. Synchronises. Unknown word -> cudaErrorInvalidValue. */
+#define GG_STATUS_WORD_BASELINE 0
+#define GG_STATUS_WORD_NOALLOC 1
+int gg_selftest_wait_timeout_word(int word, unsigned long long timeout_ns);
+
 /* No counterpart in the reference. The grouped GEMM of gg_run_grouped_gemm_once for callers that
  * cannot allocate device memory: code whose device memory is owned by a caching allocator or a
  * pool that forbids side allocations, latency-critical paths where cudaMalloc/cudaFree and the
@@ -265,6 +285,11 @@ int gg_selftest_wait_timeout(unsigned long long timeout_ns, int* status);
 #define GG_NOALLOC_MAX_PROBLEMS 1024
 int gg_run_grouped_gemm_noalloc(const gg_problem* problems, int count, int sort_mode,
                                 const gg_config* config, void* stream);
+
+/* No counterpart in the reference. Synchronises the current device and returns in *device_status
+ * the GG_STATUS_* bits of the last gg_run_grouped_gemm_noalloc call on it (each call clears them
+ * first; a bounded wait that ran out leaves D partly written), then clears them. Allocates nothing. */
+int gg_noalloc_status(int* device_status);
 
 /* ---- grouped GEMM with device-side preparation (mixture-of-experts routing) ----------------
  * No counterpart in the reference, whose problem set is prepared on the host. Here the number of

@@ -5,8 +5,8 @@ set and exports it (gg_ipc_export); the other process maps it (gg_ipc_open) and 
 gg_partition pieces with D pointers into it (gather.fused_targets), while the root runs its own
 pieces into the same buffer locally. The buffer must then equal, bit for bit, D computed whole in
 one process, with every padding element untouched. On one GPU the mapping is same-device memory;
-across GPUs the same pointers are peer memory and the kernel writes them with plain stores (the
-2-GPU run of bench.py --gather exercises that path). Processes are spawned, never forked.
+with two GPUs visible the second process also runs on GPU 1, where the same pointers are peer
+memory that the kernel writes with plain stores over NVLink. Processes are spawned, never forked.
 """
 from __future__ import annotations
 
@@ -56,13 +56,14 @@ def _pieces(dims, cfg, world, rank):
     return gg.partition(probs, cfg, world, rank)[0]
 
 
-def _worker(name, cta, q_in, q_out):
+def _worker(name, cta, q_in, q_out, device=0):
     """Rank 1: maps the root's buffer, writes its pieces into it, reports, unmaps."""
     import torch
 
     from grouped_gemm_gpu_kernel_b200.gather import close_buffer, fused_targets, open_buffer
 
     try:
+        torch.cuda.set_device(device)
         cfg = gg.KernelConfig(*cta)
         shapes = _shapes(name)
         ps = W.allocate(shapes, seed=11)
@@ -77,8 +78,22 @@ def _worker(name, cta, q_in, q_out):
         q_out.put(("error", repr(e)))
 
 
-@pytest.mark.parametrize("name, cta", [("aligned", (128, 256, 64)), ("small16", (128, 128, 64))])
-def test_fused_gather_through_ipc_matches_whole_run(cuda, name, cta):
+def _two_devices():
+    import torch
+
+    return torch.cuda.is_available() and torch.cuda.device_count() >= 2
+
+
+@pytest.mark.parametrize("name, cta, peer", [
+    ("aligned", (128, 256, 64), False), ("small16", (128, 128, 64), False),
+    pytest.param("aligned", (128, 256, 64), True,
+                 marks=pytest.mark.skipif(not _two_devices(), reason="needs two GPUs")),
+    pytest.param("mixed512", (128, 256, 64), True,
+                 marks=pytest.mark.skipif(not _two_devices(), reason="needs two GPUs")),
+], ids=["aligned-1gpu", "small16-1gpu", "aligned-2gpu", "mixed512-2gpu"])
+def test_fused_gather_through_ipc_matches_whole_run(cuda, name, cta, peer):
+    """peer: the second process runs on GPU 1, so its kernel stores its tiles into GPU 0's memory
+    over NVLink (plain stores; its D is marked as another device's, never a TMA store)."""
     import torch
     import torch.multiprocessing as mp
 
@@ -92,7 +107,7 @@ def test_fused_gather_through_ipc_matches_whole_run(cuda, name, cta):
     buf = torch.full((total + 256,), float("nan"), device=cuda)
     ctx = mp.get_context("spawn")
     q_in, q_out = ctx.Queue(), ctx.Queue()
-    proc = ctx.Process(target=_worker, args=(name, cta, q_in, q_out))
+    proc = ctx.Process(target=_worker, args=(name, cta, q_in, q_out, 1 if peer else 0))
     proc.start()
     try:
         q_in.put(export_buffer(buf))

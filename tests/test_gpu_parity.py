@@ -119,6 +119,35 @@ def test_bounded_wait_selftest_reports_timeout_and_context_survives(cuda):
     assert float(x.sum()) == 1024.0
 
 
+def test_baseline_status_word_reports_a_timeout_then_clears(cuda):
+    """gg_baseline_status reads the per-device word of the per-problem baseline: the self-test's
+    timeout recorded there reaches the query once, and the query clears it."""
+    torch = _torch()
+    ps = W.allocate(W.make_shapes("small16"), cuda)
+    assert gg.run_baseline_per_problem(ps.problems(), gg.KernelConfig(128, 128, 64)) == 0
+    assert gg.baseline_status() == 0
+    assert gg.selftest_wait_timeout_word(capi.GG_STATUS_WORD_BASELINE, 5_000_000) == 0
+    bits = gg.baseline_status()
+    assert bits & capi.GG_STATUS_TIMEOUT_MMA and not (bits & 0x100)
+    assert gg.baseline_status() == 0
+    ps.d.fill_(float("nan"))
+    assert gg.run_baseline_per_problem(ps.problems(), gg.KernelConfig(128, 128, 64)) == 0
+    assert gg.baseline_status() == 0
+    assert check_full(ps) <= 1.0
+    assert gg.selftest_wait_timeout_word(7, 1_000_000) == capi.CUDA_ERROR_INVALID_VALUE
+    assert float(torch.ones(8, device=cuda).sum()) == 8.0
+
+
+def test_run_once_reads_its_status_word(cuda):
+    """run_grouped_gemm_once synchronises and checks its kernel's status before it returns
+    (a timeout would return cudaErrorLaunchTimeout); a normal call returns success."""
+    ps = W.allocate(W.make_shapes("small16"), cuda)
+    for cfg in (gg.KernelConfig(128, 128, 64), gg.KernelConfig(128, 128, 64, use_tensor_cores=False)):
+        ps.d.fill_(float("nan"))
+        assert gg.run_grouped_gemm_once(ps.problems(), gg.SortMode.kByK, cfg) == 0
+        assert check_full(ps) <= 1.0
+
+
 def test_occupancy_report(cuda):
     for cfg in ALL_CONFIGS:
         st, info = gg.query_occupancy(cfg)
@@ -555,32 +584,44 @@ def _ref_problems(problems):
     return arr
 
 
+def _rms(law, std):
+    """Root mean square of a workload's value law: U[-1, 1] or N(0, std)."""
+    return std if law == "normal" else 1.0 / np.sqrt(3.0)
+
+
 @needs_ref
-@pytest.mark.parametrize("name", ["small16", "tiny4096", "mixed512"])
-def test_agrees_with_reference_cuda_build(cuda, name):
-    """The reference's own kernels (sm_100a build) and this kernel agree on the same inputs."""
+@pytest.mark.parametrize("name, cfg", [("small16", (128, 128, 64)), ("tiny4096", (128, 128, 64)),
+                                       ("mixed512", (128, 128, 64)), ("moe", (128, 256, 64)),
+                                       ("skew", (128, 256, 64))])
+def test_agrees_with_reference_cuda_build(cuda, name, cfg):
+    """The reference's own kernels (sm_100a build, 64x64x16 tiles, sort by tiles) and this kernel
+    agree on the same inputs, every element of every problem: |ours - ref| / max(|ref|, s) within
+    the accuracy bound, s = sqrt(K) * rms(a) * rms(b) (the typical size of one output)."""
     torch = _torch()
-    ps = W.allocate(W.make_shapes(name), cuda)
+    shapes = W.make_shapes(name)
+    ps = W.allocate(shapes, cuda)
     probs = ps.problems()
     lib = O.load_ref()
     assert lib.ref_run_grouped_once(_ref_problems(probs), len(probs), 2, 64, 64, 16, 1, None) == 0
     torch.cuda.synchronize()
     ref_d = ps.d.clone()
     ps.d.fill_(float("nan"))
-    run_grouped(probs, gg.KernelConfig(128, 128, 64), gg.SortMode.kByTiles)
-    ours = ps.d.clone()
+    run_grouped(probs, gg.KernelConfig(*cfg), gg.SortMode.kByTiles)
+    ab_rms = _rms(shapes.a_law, shapes.a_std) * _rms(shapes.b_law, shapes.b_std)
     worst = 0.0
-    for i, (m, n, k) in enumerate(ps.shapes.dims):
+    for i, (m, n, k) in enumerate(shapes.dims):
         if m <= 0 or n <= 0:
             continue
         sl = slice(ps.d_off[i], ps.d_off[i] + m * n)
-        x, y = ours[sl].double(), ref_d[sl].double()
-        scale = torch.maximum(y.abs(), torch.full_like(y, np.sqrt(max(k, 1)) / 3.0))
+        x, y = ps.d[sl].double(), ref_d[sl].double()
+        scale = torch.clamp(y.abs(), min=float(np.sqrt(max(k, 1)) * ab_rms))
         worst = max(worst, float(((x - y).abs() / scale).max()) / O.tolerance(k))
+        del x, y, scale
     assert worst <= 1.0
-    if name != "mixed512":
+    if name in ("small16", "tiny4096"):
         ps.d.copy_(ref_d)
         assert check_full(ps) <= 1.0  # the reference itself meets the bar on these inputs
+    del ref_d, ps
 
 
 @needs_ref

@@ -115,6 +115,24 @@ def test_noalloc_does_not_change_free_device_memory(cuda):
     free0, _ = torch.cuda.mem_get_info()
     for _ in range(5):
         assert noalloc(ps.problems(), gg.SortMode.kByTiles, cfg) == 0
+        assert gg.noalloc_status() == 0  # the status query allocates nothing either
     torch.cuda.synchronize()
     free1, _ = torch.cuda.mem_get_info()
     assert free1 == free0
+
+
+def test_noalloc_status_word_reports_a_timeout_then_clears(cuda):
+    """gg_noalloc_status reads the status word kept in the fixed array: a timeout recorded there
+    (by the bounded-wait self-test, which runs the kernel's wait on a barrier nothing completes)
+    reaches the query once and is cleared by it, and every call clears the word before it launches."""
+    ps = W.allocate(W.make_shapes("small16"), cuda, seed=15)
+    cfg = gg.KernelConfig(128, 128, 64)
+    assert noalloc(ps.problems(), gg.SortMode.kNone, cfg) == 0
+    assert gg.noalloc_status() == 0
+    assert gg.selftest_wait_timeout_word(capi.GG_STATUS_WORD_NOALLOC, 5_000_000) == 0
+    bits = gg.noalloc_status()
+    assert bits & capi.GG_STATUS_TIMEOUT_MMA and not (bits & 0x100)
+    assert gg.noalloc_status() == 0
+    assert gg.selftest_wait_timeout_word(capi.GG_STATUS_WORD_NOALLOC, 5_000_000) == 0
+    assert noalloc(ps.problems(), gg.SortMode.kNone, cfg) == 0
+    assert gg.noalloc_status() == 0
