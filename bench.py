@@ -45,6 +45,11 @@ METRIC = "aggregate TFLOP/s (2·ΣMNK/s) at 1/2/4/8 B200, % of dense FP16 peak"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 DEFAULT_CTA = {"small16": (128, 128, 64), "mixed512": (128, 256, 64), "moe": (128, 256, 64),
                "tiny4096": (128, 64, 64), "skew": (128, 256, 64)}
+# sort mode per workload: by K for mixed512 (the fastest of the four there), by tiles elsewhere
+# (the largest problems first, which shortens the persistent schedule's tail)
+DEFAULT_SORT = {"small16": 2, "mixed512": 1, "moe": 2, "tiny4096": 2, "skew": 2}
+ROW_WORKLOADS = ("moe", "skew", "tiny4096", "small16")  # driver-timed beside the headline (N = 1)
+STRONG_WORKLOADS = ("skew", "moe")  # one fixed global set split over the N ranks
 
 
 def parse_args():
@@ -72,7 +77,11 @@ def parse_args():
     ap.add_argument("--b-layout", choices=["row", "col"], default="row",
                     help="storage of every B (col: n x k, the [out][in] weight layout; pitches padded to 16 bytes)")
     ap.add_argument("--gather", action="store_true",
-                    help="N>1: after the timed region, gather every rank's D to rank 0 over NCCL and time it")
+                    help="N>1: after the timed region, gather every rank's D to rank 0 over NCCL and fused into "
+                         "the kernel, and time both (the default at N>1 for the reference's FP32 output)")
+    ap.add_argument("--no-gather", action="store_true", help="N>1: skip the gather rows")
+    ap.add_argument("--no-rows", action="store_true",
+                    help="skip the per-workload rows (N=1) and the strong-scaling rows (every N)")
     return ap.parse_args()
 
 
@@ -84,6 +93,132 @@ def load_peaks():
         d["source"] = "measured"
         return d
     return dict(FALLBACK_PEAKS)
+
+
+def tail_work_share(prepared, cta_k):
+    """The reference's tail-balance figure (reference bench/benchmark_grouped_gemm.cu:580-607): the
+    work (tiles x ceil(K / cta_k)) of the last 10 % of the problems in launch order, over the total."""
+    n = len(prepared.sorted_problems)
+    if n == 0:
+        return 0.0
+    tail = max(1, n // 10)
+    total = tail_w = 0.0
+    for i, p in enumerate(prepared.sorted_problems):
+        w = (prepared.tile_offsets[i + 1] - prepared.tile_offsets[i]) * (-(-max(p.k, 0) // cta_k))
+        total += w
+        if i >= n - tail:
+            tail_w += w
+    return tail_w / total if total > 0 else 0.0
+
+
+def roofline_of(flops, alg_bytes, ms, peaks, in_type=0):
+    """Roofline of one launch: HBM-bound below the ridge point, tensor-bound above it."""
+    tensor_peak, tensor_src = peaks["bf16_tflops"], peaks["source"]
+    if in_type >= 2:  # no FP8 measurement: twice the measured dense BF16 rate (the FP8:BF16 ratio of B200)
+        tensor_peak, tensor_src = 2.0 * peaks["bf16_tflops"], "2 x " + peaks["source"] + " bf16"
+    ridge = tensor_peak * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    if flops / max(alg_bytes, 1.0) < ridge:
+        achieved = alg_bytes / (ms * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": None, "peak_source": peaks["source"],
+                "algorithmic_bytes_per_launch": alg_bytes}
+    achieved = flops / (ms * 1e-3) / 1e12
+    return {"bound": "tensor", "achieved": achieved, "peak": tensor_peak, "unit": "TFLOP/s",
+            "frac": achieved / tensor_peak, "traffic": None, "peak_source": tensor_src,
+            "algorithmic_flops_per_launch": flops}
+
+
+class StepTimer:
+    """Device time of executor runs on one stream. Footprints below twice L2 flush L2 before every
+    step (a write of a buffer larger than L2, then a read of a second one so no dirty line is left
+    to be written back inside the step) and time each step alone; larger ones run back to back."""
+
+    def __init__(self, dev, stream):
+        self.dev, self.stream = dev, stream
+        self._flush = self._flush_read = None
+
+    def flush_buffers(self):
+        import torch
+
+        if self._flush is None:
+            self._flush = torch.empty(4 * L2_BYTES, dtype=torch.uint8, device=self.dev)
+            self._flush_read = torch.ones(2 * L2_BYTES // 4, dtype=torch.float32, device=self.dev)
+        return self._flush, self._flush_read
+
+    def ms(self, run, steps, flush):
+        """Mean device ms per step of `steps` calls of run(stream); no host synchronisation inside."""
+        import torch
+
+        stream = self.stream
+        if not flush:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(steps):
+                run(stream)
+            e1.record(stream)
+            e1.synchronize()
+            return e0.elapsed_time(e1) / steps
+        fw, fr = self.flush_buffers()
+        evs = []
+        with torch.cuda.stream(stream):
+            sink = torch.zeros((), device=self.dev)
+            for _ in range(steps):
+                fw.zero_()
+                sink += fr.sum()
+                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a0.record(stream)
+                run(stream)
+                a1.record(stream)
+                evs.append((a0, a1))
+        evs[-1][1].synchronize()
+        return sum(a.elapsed_time(b) for a, b in evs) / steps
+
+    def median_of(self, run, steps, flush, repeats=5):
+        """(median, min, max) over `repeats` repeats of `steps` steps."""
+        xs = sorted(self.ms(run, steps, flush) for _ in range(repeats))
+        return xs[len(xs) // 2], xs[0], xs[-1]
+
+
+def link_peaks(dev, nbytes=256 << 20, reps=3):
+    """Measured pinned-host <-> device copy rates (GB/s) of this process's GPU: each direction alone
+    and both at once (full duplex, as the streamed end-to-end loop runs them), best of `reps`."""
+    import torch
+
+    h_in = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    h_out = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    d_in = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    d_out = torch.ones(nbytes, dtype=torch.uint8, device=dev)
+    s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def timed(fn):
+        best = None
+        for _ in range(reps):
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s1)
+            s2.wait_event(e0)
+            fn()
+            s1.wait_stream(s2)
+            e1.record(s1)
+            torch.cuda.synchronize()
+            t = e0.elapsed_time(e1)
+            best = t if best is None else min(best, t)
+        return best
+
+    def h2d():
+        with torch.cuda.stream(s1):
+            d_in.copy_(h_in, non_blocking=True)
+
+    def d2h():
+        with torch.cuda.stream(s2):
+            h_out.copy_(d_out, non_blocking=True)
+
+    t_in, t_out = timed(h2d), timed(d2h)
+    t_both = timed(lambda: (h2d(), d2h()))
+    return {"h2d_gbs": nbytes / (t_in * 1e-3) / 1e9, "d2h_gbs": nbytes / (t_out * 1e-3) / 1e9,
+            "duplex_gbs_each_way": nbytes / (t_both * 1e-3) / 1e9, "bytes": nbytes,
+            "how": "pinned host <-> HBM cudaMemcpyAsync of 256 MiB, CUDA events, best of 3; duplex = one copy "
+                   "each way at once on two streams"}
 
 
 # ---- clocks ------------------------------------------------------------------------------------
@@ -154,26 +289,34 @@ class ClockSampler:
 
 
 # ---- workload sharding -------------------------------------------------------------------------
-def rank_shapes(workload: str, world: int, rank: int, cfg):
-    """This rank's shard of the N-replica problem set, as a Shapes of independent pieces."""
+def shard(glob, world: int, rank: int, cfg):
+    """This rank's gg_partition pieces of the global set `glob` (a Shapes), as a Shapes of
+    independent problems, and every rank's partition weight."""
     import grouped_gemm_gpu_kernel_b200 as gg
+    from grouped_gemm_gpu_kernel_b200 import workloads as W
+
+    probs = [gg.ProblemDesc(m, n, k, 1, 1, None, 1, max(1, k), max(1, n), max(1, n), max(1, n)) for m, n, k in glob.dims]
+    parts = [gg.partition(probs, cfg, world, r) for r in range(world)]
+    pieces = parts[rank][0]
+    dims = [(pc.rows, pc.cols, glob.dims[pc.problem][2]) for pc in pieces]
+    out = W.Shapes(glob.name, dims, [glob.alpha[pc.problem] for pc in pieces], [glob.beta[pc.problem] for pc in pieces],
+                   glob.has_c, glob.a_law, glob.a_std, glob.b_law, glob.b_std)
+    return out, [w for _, w in parts]
+
+
+def rank_shapes(workload: str, world: int, rank: int, cfg):
+    """This rank's shard of the N-replica problem set (weak scaling), the global FLOPs and every
+    rank's partition weight."""
     from grouped_gemm_gpu_kernel_b200 import workloads as W
 
     reps = [W.make_shapes(workload, seed=42 + r) for r in range(world)]
     if world == 1:
-        return reps[0], reps[0].flops
-    glob_dims, glob_alpha, glob_beta = [], [], []
-    for s in reps:
-        glob_dims += s.dims
-        glob_alpha += s.alpha
-        glob_beta += s.beta
-    probs = [gg.ProblemDesc(m, n, k, 1, 1, None, 1, max(1, k), max(1, n), max(1, n), max(1, n)) for m, n, k in glob_dims]
-    pieces, _ = gg.partition(probs, cfg, world, rank)
-    base = reps[0]
-    dims = [(pc.rows, pc.cols, glob_dims[pc.problem][2]) for pc in pieces]
-    out = W.Shapes(workload, dims, [glob_alpha[pc.problem] for pc in pieces], [glob_beta[pc.problem] for pc in pieces],
-                   base.has_c, base.a_law, base.a_std, base.b_law, base.b_std)
-    return out, float(sum(s.flops for s in reps))
+        return reps[0], reps[0].flops, [1.0]
+    glob = W.Shapes(workload, [d for s in reps for d in s.dims], [a for s in reps for a in s.alpha],
+                    [b for s in reps for b in s.beta], reps[0].has_c, reps[0].a_law, reps[0].a_std, reps[0].b_law,
+                    reps[0].b_std)
+    out, weights = shard(glob, world, rank, cfg)
+    return out, float(sum(s.flops for s in reps)), weights
 
 
 # ---- CPU baselines -----------------------------------------------------------------------------
@@ -304,7 +447,7 @@ def main():
     cfg = gg.KernelConfig(*cta, input_type=in_type, output_type=out_type, activation=act, a_layout=int(a_col),
                           b_layout=int(b_col))
     plain = out_type == 0 and act == 0 and not args.bias and args.input_type == "f16" and not (a_col or b_col)
-    shapes, global_flops = rank_shapes(args.workload, world, rank, cfg)
+    shapes, global_flops, rank_weights = rank_shapes(args.workload, world, rank, cfg)
 
     def make_set():
         p = W.allocate(shapes, dev, seed=42 + rank, d_fill=0.0)
@@ -326,6 +469,7 @@ def main():
 
     ps, bias_ptrs = make_set()
     problems = ps.problems()
+    tail_share = tail_work_share(gg.prepare_problem_set(problems, cfg, args.sort_mode), cta[2])
     prep_t0 = time.perf_counter()
     ex, st = build(ps, bias_ptrs, args.sort_mode)
     prep_ms = 1e3 * (time.perf_counter() - prep_t0)
@@ -354,62 +498,31 @@ def main():
         assert ex.run(stream) == 0
     alg_bytes = shapes.algorithmic_bytes(4 if out_type == 0 else 2, args.bias, 1 if in_type >= 2 else 2)
     # Inputs smaller than twice L2 would stay cache-resident from one step to the next: such
-    # workloads flush L2 (write a buffer larger than L2) before every step and time each step
-    # alone; larger ones run back to back.
-    flush = None
-    if alg_bytes < 2 * L2_BYTES:
-        flush = torch.empty(4 * L2_BYTES, dtype=torch.uint8, device=dev)
-        # a read of a second buffer after the write evicts the flush's dirty lines before the
-        # step starts, so their write-back does not land inside the timed step
-        flush_read = torch.ones(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+    # workloads flush L2 before every step and time each step alone (StepTimer); larger ones run
+    # back to back.
+    flush = alg_bytes < 2 * L2_BYTES
+    timer = StepTimer(dev, stream)
+    if flush:
+        timer.flush_buffers()
     barrier()
     clocks.mark(True)
-    if flush is None:
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            ex.run(stream)
-        e1.record(stream)
-        barrier()
-        local_ms = e0.elapsed_time(e1) / args.steps
-    else:
-        evs = []
-        with torch.cuda.stream(stream):
-            sink = torch.zeros((), device=dev)
-            for _ in range(args.steps):
-                flush.zero_()
-                sink += flush_read.sum()
-                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a0.record(stream)
-                ex.run(stream)
-                a1.record(stream)
-                evs.append((a0, a1))
-        barrier()
-        local_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+    local_ms = timer.ms(ex.run, args.steps, flush)
+    barrier()
     clocks.mark(False)
     clock_info = clocks.stop()
     if ex.status() != 0:
         raise RuntimeError("a bounded wait timed out inside the kernel during the timed region")
     ms = max_over_ranks(local_ms)
     value = global_flops / (ms * 1e-3) / 1e12
+    # The survey's timing protocol as well: the median of 5 repeats of max(50, K) steps each.
+    rep_med, rep_min, rep_max = timer.median_of(ex.run, max(50, args.steps), flush)
+    rep_med, rep_min, rep_max = max_over_ranks(rep_med), max_over_ranks(rep_min), max_over_ranks(rep_max)
+    protocol = {"repeats": 5, "steps_per_repeat": max(50, args.steps), "median_ms": rep_med, "min_ms": rep_min,
+                "max_ms": rep_max, "median_value": global_flops / (rep_med * 1e-3) / 1e12}
 
     peaks = load_peaks()
     local_flops = shapes.flops
-    ai = local_flops / alg_bytes
-    tensor_peak, tensor_src = peaks["bf16_tflops"], peaks["source"]
-    if in_type >= 2:  # no FP8 measurement: twice the measured dense BF16 rate (the FP8:BF16 ratio of B200)
-        tensor_peak, tensor_src = 2.0 * peaks["bf16_tflops"], "2 x " + peaks["source"] + " bf16"
-    ridge = tensor_peak * 1e12 / (peaks["hbm_gbs"] * 1e9)
-    if ai < ridge:
-        achieved = alg_bytes / (local_ms * 1e-3) / 1e9
-        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": None, "peak_source": peaks["source"],
-                "algorithmic_bytes_per_launch": alg_bytes}
-    else:
-        achieved = local_flops / (local_ms * 1e-3) / 1e12
-        roof = {"bound": "tensor", "achieved": achieved, "peak": tensor_peak, "unit": "TFLOP/s",
-                "frac": achieved / tensor_peak, "traffic": None, "peak_source": tensor_src,
-                "algorithmic_flops_per_launch": local_flops}
+    roof = roofline_of(local_flops, alg_bytes, local_ms, peaks, in_type)
     traffic_path = os.path.join(REPO, "profiles", "traffic.json")
     if os.path.exists(traffic_path) and world == 1:
         with open(traffic_path) as f:
@@ -510,9 +623,20 @@ def main():
                "serial_value": global_flops / (serial_ms * 1e-3) / 1e12}
         ex_b.close()
         del ps_b
+        # The link's own roofline: every rank measures its pinned copy rates at the same time (the
+        # ranks share the host), and the streamed loop is bound by the slower direction at the
+        # duplex rate.
+        barrier()
+        lk = link_peaks(dev)
+        lk["duplex_gbs_each_way"] = -max_over_ranks(-lk["duplex_gbs_each_way"])
+        bound_ms = 1e3 * max(h2d, d2h) / (lk["duplex_gbs_each_way"] * 1e9)
+        lk.update({"bound_ms_per_step": bound_ms, "frac": bound_ms / e2e_ms,
+                   "bound": "max(h2d, d2h bytes per step) / the slowest rank's duplex copy rate"})
+        e2e["link"] = lk
 
     extras = {}
-    if args.gather and world > 1:
+    gather = world > 1 and not args.no_gather and (args.gather or plain)
+    if gather:
         extras["gather"] = gather_row(args, cfg, ps, world, rank, dev, max_over_ranks, barrier)
     if not args.no_extras and world == 1:
         sweep = {}
@@ -539,6 +663,15 @@ def main():
         if plain:  # the reference's kernels: FP16 in, FP32 out, no fused bias or activation
             extras["ref_gpu"] = reference_gpu_row(problems, stream, local_flops)
 
+    if not args.no_rows and plain:
+        torch.cuda.synchronize()
+        peaks_rows = load_peaks()
+        if world == 1:
+            extras["workloads"] = {name: workload_row(name, dev, stream, args.steps, peaks_rows)
+                                   for name in ROW_WORKLOADS if name != args.workload}
+        extras["strong"] = {name: strong_row(name, world, rank, dev, stream, args.steps, max_over_ranks, barrier)
+                            for name in STRONG_WORKLOADS}
+
     cpu = None
     if rank == 0 and world == 1:
         cpu = cpu_baseline(shapes, args.cpu_seconds)
@@ -553,13 +686,16 @@ def main():
                        "sort_mode": gg.sort_mode_name(args.sort_mode), "tiles": n_tiles, "grid_ctas": ex.grid_ctas(),
                        "global_gflop": global_flops / 1e9,
                        "l2": (f"inputs larger than L2 ({alg_bytes / 1e9:.2f} GB algorithmic footprint per GPU "
-                              "> 2 x 126 MB), steps back to back, no flush") if flush is None else
+                              "> 2 x 126 MB), steps back to back, no flush") if not flush else
                              (f"footprint {alg_bytes / 1e6:.1f} MB < 2 x L2: L2 flushed ({4 * L2_BYTES >> 20} MB "
                               f"write, then a {2 * L2_BYTES >> 20} MB read so no dirty line is left) before every "
                               "step, each step timed alone"),
                        "accumulate": "f32", "output_type": args.output_type, "activation": args.activation,
                        "bias": bool(args.bias), "a_layout": args.a_layout, "b_layout": args.b_layout,
-                       "prep_build_ms": prep_ms, "parallelism": f"dp{world} (tile-balanced shards)"},
+                       "prep_build_ms": prep_ms, "parallelism": f"dp{world} (tile-balanced shards)",
+                       "tail_work_share": tail_share,
+                       "rank_weight_max_over_mean": max(rank_weights) / (sum(rank_weights) / len(rank_weights))},
+            "timing_protocol": protocol,
             "pct_dense_fp16_peak": 100.0 * value / (world * peaks["bf16_tflops"]),
             "peak_source": peaks["source"],
             "roofline": roof,
@@ -715,6 +851,80 @@ def moe_plan_row(ps, shapes, cfg, stream, flops, executor_ms, bias_ptrs=None, ru
             "tiles": total, "bitwise_equal_to_executor": same,
             "how": "row counts in device memory; one-block prefix-scan kernel writes problem records and "
                    "tile offsets, the persistent kernel reads the tile count from the device"}
+
+
+def workload_row(name, dev, stream, steps, peaks, repeats=5):
+    """One BASELINE workload on this GPU with its default tile and sort mode: the median of
+    `repeats` repeats of max(steps, 10) executor runs, its roofline, its tail-work share."""
+    import torch
+
+    import grouped_gemm_gpu_kernel_b200 as gg
+    from grouped_gemm_gpu_kernel_b200 import workloads as W
+
+    shapes = W.make_shapes(name)
+    cta, mode = DEFAULT_CTA[name], DEFAULT_SORT[name]
+    cfg = gg.KernelConfig(*cta)
+    ps = W.allocate(shapes, dev, seed=42, d_fill=0.0)
+    prep = gg.prepare_problem_set(ps.problems(), cfg, mode)
+    ex = gg.GroupedGemmExecutor()
+    assert ex.build(prep, cfg) == 0
+    alg = shapes.algorithmic_bytes()
+    flush = alg < 2 * L2_BYTES
+    timer = StepTimer(dev, stream)
+    for _ in range(3):
+        assert ex.run(stream) == 0
+    med, lo, hi = timer.median_of(ex.run, max(steps, 10), flush, repeats)
+    status = ex.status()
+    row = {"ms": med, "min_ms": lo, "max_ms": hi, "tflops": shapes.flops / (med * 1e-3) / 1e12,
+           "cta": "x".join(map(str, cta)), "sort_mode": gg.sort_mode_name(mode), "problems": len(shapes.dims),
+           "tiles": ex.total_tiles(), "grid_ctas": ex.grid_ctas(), "gflop": shapes.flops / 1e9,
+           "algorithmic_gb": alg / 1e9, "roofline": roofline_of(shapes.flops, alg, med, peaks),
+           "tail_work_share": tail_work_share(prep, cta[2]), "status": status,
+           "timing": f"median of {repeats} repeats of {max(steps, 10)} steps; "
+                     + ("L2 flushed before every step, each step timed alone" if flush else
+                        "footprint larger than 2 x L2, steps back to back")}
+    ex.close()
+    del ps, prep
+    torch.cuda.empty_cache()
+    return row
+
+
+def strong_row(name, world, rank, dev, stream, steps, max_over_ranks, barrier):
+    """Strong scaling: ONE fixed global set (seed 42) split by gg_partition over the N ranks; each
+    rank materialises and runs only its pieces. Time = max over ranks of the per-step device time;
+    value = the global set's FLOPs / that time."""
+    import torch
+
+    import grouped_gemm_gpu_kernel_b200 as gg
+    from grouped_gemm_gpu_kernel_b200 import workloads as W
+
+    glob = W.make_shapes(name)
+    cta, mode = DEFAULT_CTA[name], DEFAULT_SORT[name]
+    cfg = gg.KernelConfig(*cta)
+    mine, weights = shard(glob, world, rank, cfg) if world > 1 else (glob, [1.0])
+    ps = W.allocate(mine, dev, seed=42 + rank, d_fill=0.0)
+    ex = gg.GroupedGemmExecutor()
+    assert ex.build(gg.prepare_problem_set(ps.problems(), cfg, mode), cfg) == 0
+    timer = StepTimer(dev, stream)
+    flush = mine.algorithmic_bytes() < 2 * L2_BYTES
+    for _ in range(3):
+        assert ex.run(stream) == 0
+    barrier()
+    local = timer.ms(ex.run, max(steps, 10), flush)
+    barrier()
+    ms = max_over_ranks(local)
+    fastest = -max_over_ranks(-local)
+    status = int(max_over_ranks(float(ex.status())))
+    tiles = int(max_over_ranks(float(ex.total_tiles())))
+    ex.close()
+    del ps
+    torch.cuda.empty_cache()
+    return {"ms": ms, "tflops": glob.flops / (ms * 1e-3) / 1e12, "n_gpus": world, "fastest_rank_ms": fastest,
+            "max_rank_tiles": tiles, "rank_weight_max_over_mean": max(weights) / (sum(weights) / len(weights)),
+            "cta": "x".join(map(str, cta)), "sort_mode": gg.sort_mode_name(mode), "gflop": glob.flops / 1e9,
+            "status": status,
+            "how": f"the one {name} set (seed 42) cut by gg_partition into {world} tile-weighted shards, one per "
+                   f"rank; {max(steps, 10)} steps timed on each rank, max over ranks"}
 
 
 def graph_row(ex, stream, flops, runs=20, replays=10):
