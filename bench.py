@@ -44,11 +44,13 @@ L2_BYTES = 126 << 20
 METRIC = "aggregate TFLOP/s (2·ΣMNK/s) at 1/2/4/8 B200, % of dense FP16 peak"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 DEFAULT_CTA = {"small16": (128, 128, 64), "mixed512": (128, 256, 64), "moe": (128, 256, 64),
-               "tiny4096": (128, 64, 64), "skew": (128, 256, 64)}
+               "tiny4096": (128, 64, 64), "skew": (128, 256, 64), "moe_reduced": (128, 256, 64)}
 # sort mode per workload: by K for mixed512 (the fastest of the four there), by tiles elsewhere
 # (the largest problems first, which shortens the persistent schedule's tail)
-DEFAULT_SORT = {"small16": 2, "mixed512": 1, "moe": 2, "tiny4096": 2, "skew": 2}
+DEFAULT_SORT = {"small16": 2, "mixed512": 1, "moe": 2, "tiny4096": 2, "skew": 2, "moe_reduced": 2}
 ROW_WORKLOADS = ("moe", "skew", "tiny4096", "small16")  # driver-timed beside the headline (N = 1)
+# The same two large workloads with CTA-pair tile classes (pair blocks + one-CTA rows)
+CLASS_ROWS = {"moe_pair_classes": "moe", "skew_pair_classes": "skew"}
 STRONG_WORKLOADS = ("skew", "moe")  # one fixed global set split over the N ranks
 
 
@@ -58,7 +60,9 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", default="mixed512", choices=["small16", "mixed512", "moe", "tiny4096", "skew"])
+    ap.add_argument("--workload", default="mixed512",
+                    choices=["small16", "mixed512", "moe", "tiny4096", "skew", "moe_reduced"],
+                    help="moe_reduced (8 experts, 2048 tokens) exists for small profiling captures")
     ap.add_argument("--sort-mode", type=int, default=1, help="0 none, 1 by K, 2 by tiles, 3 by tiles then K")
     ap.add_argument("--cta", default=None, help="tile shape MxNxK (default per workload)")
     ap.add_argument("--no-extras", action="store_true", help="skip the sort-mode sweep and the reference GPU row")
@@ -623,16 +627,6 @@ def main():
                "serial_value": global_flops / (serial_ms * 1e-3) / 1e12}
         ex_b.close()
         del ps_b
-        # The link's own roofline: every rank measures its pinned copy rates at the same time (the
-        # ranks share the host), and the streamed loop is bound by the slower direction at the
-        # duplex rate.
-        barrier()
-        lk = link_peaks(dev)
-        lk["duplex_gbs_each_way"] = -max_over_ranks(-lk["duplex_gbs_each_way"])
-        bound_ms = 1e3 * max(h2d, d2h) / (lk["duplex_gbs_each_way"] * 1e9)
-        lk.update({"bound_ms_per_step": bound_ms, "frac": bound_ms / e2e_ms,
-                   "bound": "max(h2d, d2h bytes per step) / the slowest rank's duplex copy rate"})
-        e2e["link"] = lk
 
     extras = {}
     gather = world > 1 and not args.no_gather and (args.gather or plain)
@@ -643,7 +637,7 @@ def main():
         for mode in range(4):
             ex2, st2 = build(ps, bias_ptrs, mode)
             assert st2 == 0
-            for _ in range(5):
+            for _ in range(10):
                 ex2.run(stream)
             torch.cuda.synchronize()
             a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -669,8 +663,22 @@ def main():
         if world == 1:
             extras["workloads"] = {name: workload_row(name, dev, stream, args.steps, peaks_rows)
                                    for name in ROW_WORKLOADS if name != args.workload}
+            for row, name in CLASS_ROWS.items():
+                extras["workloads"][row] = workload_row(name, dev, stream, args.steps, peaks_rows, classes=True)
         extras["strong"] = {name: strong_row(name, world, rank, dev, stream, args.steps, max_over_ranks, barrier)
                             for name in STRONG_WORKLOADS}
+
+    if e2e is not None:
+        # The link's own roofline, measured last (large pinned copies): every rank measures its
+        # pinned copy rates at the same time (the ranks share the host), and the streamed loop is
+        # bound by the slower direction at the duplex rate.
+        barrier()
+        lk = link_peaks(dev)
+        lk["duplex_gbs_each_way"] = -max_over_ranks(-lk["duplex_gbs_each_way"])
+        bound_ms = 1e3 * max(e2e["h2d_bytes_per_step"], e2e["d2h_bytes_per_step"]) / (lk["duplex_gbs_each_way"] * 1e9)
+        lk.update({"bound_ms_per_step": bound_ms, "frac": bound_ms / e2e["ms_per_step"],
+                   "bound": "max(h2d, d2h bytes per step) / the slowest rank's duplex copy rate"})
+        e2e["link"] = lk
 
     cpu = None
     if rank == 0 and world == 1:
@@ -853,17 +861,18 @@ def moe_plan_row(ps, shapes, cfg, stream, flops, executor_ms, bias_ptrs=None, ru
                    "tile offsets, the persistent kernel reads the tile count from the device"}
 
 
-def workload_row(name, dev, stream, steps, peaks, repeats=5):
-    """One BASELINE workload on this GPU with its default tile and sort mode: the median of
-    `repeats` repeats of max(steps, 10) executor runs, its roofline, its tail-work share."""
+def workload_row(name, dev, stream, steps, peaks, repeats=5, classes=False):
+    """One BASELINE workload on this GPU with its default tile and sort mode (classes: CTA-pair
+    256x256 tiles with tile classes instead): the median of `repeats` repeats of max(steps, 10)
+    executor runs, its roofline, its tail-work share."""
     import torch
 
     import grouped_gemm_gpu_kernel_b200 as gg
     from grouped_gemm_gpu_kernel_b200 import workloads as W
 
     shapes = W.make_shapes(name)
-    cta, mode = DEFAULT_CTA[name], DEFAULT_SORT[name]
-    cfg = gg.KernelConfig(*cta)
+    cta, mode = ((256, 256, 64) if classes else DEFAULT_CTA[name]), DEFAULT_SORT[name]
+    cfg = gg.KernelConfig(*cta, tile_classes=gg.TileClasses.kPairBlocks if classes else 0)
     ps = W.allocate(shapes, dev, seed=42, d_fill=0.0)
     prep = gg.prepare_problem_set(ps.problems(), cfg, mode)
     ex = gg.GroupedGemmExecutor()
@@ -876,7 +885,8 @@ def workload_row(name, dev, stream, steps, peaks, repeats=5):
     med, lo, hi = timer.median_of(ex.run, max(steps, 10), flush, repeats)
     status = ex.status()
     row = {"ms": med, "min_ms": lo, "max_ms": hi, "tflops": shapes.flops / (med * 1e-3) / 1e12,
-           "cta": "x".join(map(str, cta)), "sort_mode": gg.sort_mode_name(mode), "problems": len(shapes.dims),
+           "cta": "x".join(map(str, cta)) + (" tile classes" if classes else ""), "sort_mode": gg.sort_mode_name(mode),
+           "problems": len(shapes.dims),
            "tiles": ex.total_tiles(), "grid_ctas": ex.grid_ctas(), "gflop": shapes.flops / 1e9,
            "algorithmic_gb": alg / 1e9, "roofline": roofline_of(shapes.flops, alg, med, peaks),
            "tail_work_share": tail_work_share(prep, cta[2]), "status": status,

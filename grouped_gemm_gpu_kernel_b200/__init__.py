@@ -27,7 +27,7 @@ __all__ = [
     "run_baseline_per_problem", "count_non_empty_problems", "partition", "ShardPiece", "problem_from_tensors",
     "NATIVE_CONFIGS", "REFERENCE_CONFIGS", "PAIR_CONFIGS", "selftest_wait_timeout", "capi", "MoePlan",
     "selftest_wait_timeout_word", "baseline_status", "noalloc_status",
-    "InputType", "OutputType", "Activation", "Layout",
+    "InputType", "OutputType", "Activation", "Layout", "TileClasses",
 ]
 
 
@@ -58,6 +58,14 @@ class Layout(enum.IntEnum):
     column-major (A stored k x m with lda >= m, B stored n x k with ldb >= k)."""
     kRowMajor = capi.GG_LAYOUT_ROW_MAJOR
     kColMajor = capi.GG_LAYOUT_COL_MAJOR
+
+
+class TileClasses(enum.IntEnum):
+    """How an executor tiles its problems (GG_TILE_CLASSES_*): one tile shape for every problem (the
+    reference's), or, with a CTA-pair config, whole 256-row blocks on CTA pairs and the rows left
+    over on one-CTA 128-row tiles, as two launches that may overlap."""
+    kNone = capi.GG_TILE_CLASSES_NONE
+    kPairBlocks = capi.GG_TILE_CLASSES_PAIR_BLOCKS
 
 
 class Activation(enum.IntEnum):
@@ -107,11 +115,12 @@ class KernelConfig:
     activation: int = 0   # Activation applied after the bias
     a_layout: int = 0     # Layout of every A (row-major: the reference's)
     b_layout: int = 0     # Layout of every B
+    tile_classes: int = 0  # TileClasses: CTA-pair configs may cut problems into pair blocks + one-CTA rows
 
     def to_c(self) -> capi.GGConfig:
         return capi.GGConfig(self.cta_m, self.cta_n, self.cta_k, self.threads, self.persistent_ctas,
                              1 if self.use_tensor_cores else 0, int(self.input_type), int(self.output_type),
-                             int(self.activation), int(self.a_layout), int(self.b_layout))
+                             int(self.activation), int(self.a_layout), int(self.b_layout), int(self.tile_classes))
 
 
 # The reference's three tile shapes (reference src/grouped_gemm.cu:67-81) and the sm_100a ones.

@@ -37,6 +37,8 @@ GG_ACT_RELU = 1
 GG_ACT_GELU = 2
 GG_LAYOUT_ROW_MAJOR = 0
 GG_LAYOUT_COL_MAJOR = 1
+GG_TILE_CLASSES_NONE = 0
+GG_TILE_CLASSES_PAIR_BLOCKS = 1
 GG_NOALLOC_MAX_PROBLEMS = 1024
 
 GG_STATUS_TIMEOUT_PRODUCER = 0x1
@@ -65,7 +67,7 @@ class GGConfig(ctypes.Structure):
     _fields_ = [("cta_m", ctypes.c_int), ("cta_n", ctypes.c_int), ("cta_k", ctypes.c_int),
                 ("threads", ctypes.c_int), ("persistent_ctas", ctypes.c_int), ("use_tensor_cores", ctypes.c_int),
                 ("input_type", ctypes.c_int), ("output_type", ctypes.c_int), ("activation", ctypes.c_int),
-                ("a_layout", ctypes.c_int), ("b_layout", ctypes.c_int)]
+                ("a_layout", ctypes.c_int), ("b_layout", ctypes.c_int), ("tile_classes", ctypes.c_int)]
 
 
 class GGOccupancy(ctypes.Structure):

@@ -338,6 +338,10 @@ Variant variant_of(const gg_config* c) {
   const auto layout_ok = [](int l) { return l == GG_LAYOUT_ROW_MAJOR || l == GG_LAYOUT_COL_MAJOR; };
   if (!layout_ok(c->a_layout) || !layout_ok(c->b_layout)) return Variant::kUnsupported;
   const Variant v = resolve_variant(c->cta_m, c->cta_n, c->cta_k, c->threads);
+  // Tile classes cut problems into CTA-pair blocks and one-CTA rows: pair configs on tensor cores only.
+  if (c->tile_classes != GG_TILE_CLASSES_NONE &&
+      !(c->tile_classes == GG_TILE_CLASSES_PAIR_BLOCKS && c->use_tensor_cores && variant_is_pair(v)))
+    return Variant::kUnsupported;
   // 8-bit MN-major operands fill 128-wide chunks: on the tensor cores a row-major B needs per-CTA
   // B widths of 128 or 256, a column-major A 128 rows per CTA.
   if (v != Variant::kUnsupported && c->use_tensor_cores && in_geom(c->input_type).f8 &&
@@ -372,28 +376,74 @@ cudaError_t take_status(int* word, int* bits) {
 }  // namespace gg
 
 // ---- the executor ------------------------------------------------------------------------------
-struct gg_executor {
-  void* block = nullptr;  // one device allocation: maps | problems | offsets | counter | status
-  CUtensorMap* d_maps = nullptr;
-  DeviceProblemDesc* d_problems = nullptr;
-  int* d_offsets = nullptr;
-  int* d_counter = nullptr;
-  int* d_status = nullptr;
+namespace gg {
+namespace {
+
+// One launch of an executor: a kernel variant over its own table of problems.
+struct Part {
+  Variant variant = Variant::kUnsupported;
+  bool use_tc = true;
   int problem_count = 0;
+  int total_tiles = 0;
+  int grid = 0;
+  KernelParams params{};
+};
+
+// Host image of one part's device tables before upload: per problem its tensor maps and record,
+// the tile offsets, and (when a bias is given) one bias pointer per problem.
+struct PartImage {
+  Variant variant = Variant::kUnsupported;
+  std::vector<CUtensorMap> maps;
+  std::vector<DeviceProblemDesc> descs;
+  std::vector<int> offsets;
+  std::vector<const float*> bias;
+};
+
+// A problem's rows [row0, row0 + rows) as a problem of its own: A, C and D advanced by row0 rows
+// (A stored column-major: by row0 columns of its k x m storage).
+gg_problem row_slice(const gg_problem& p, int row0, int rows, const gg_config* c) {
+  gg_problem q = p;
+  q.m = rows;
+  const int64_t in_b = in_geom(c->input_type).bytes, out_b = out_bytes(c->output_type);
+  const int64_t a_step = c->a_layout == GG_LAYOUT_COL_MAJOR ? in_b : static_cast<int64_t>(p.lda) * in_b;
+  q.a = static_cast<const char*>(p.a) + row0 * a_step;
+  if (p.c) q.c = static_cast<const char*>(p.c) + static_cast<int64_t>(row0) * p.ldc * out_b;
+  q.d = static_cast<char*>(p.d) + static_cast<int64_t>(row0) * p.ldd * out_b;
+  return q;
+}
+
+// Appends problem p (bias `bias`, nullable) to the part's image.
+void add_problem(PartImage& img, const gg_problem& p, const gg_config* c, const float* bias) {
+  const int slot = static_cast<int>(img.descs.size());
+  img.maps.resize(img.maps.size() + kMapsPerProblem);
+  img.descs.push_back(make_device_problem(p, img.variant, c, &img.maps[static_cast<size_t>(slot) * kMapsPerProblem], slot));
+  if (img.offsets.empty()) img.offsets.push_back(0);
+  img.offsets.push_back(img.offsets.back() + tile_count(p.m, p.n, variant_bm(img.variant), variant_bn(img.variant)));
+  img.bias.push_back(bias);
+}
+
+}  // namespace
+}  // namespace gg
+
+struct gg_executor {
+  void* block = nullptr;  // one device allocation: every part's maps | problems | offsets | bias table,
+                          // then the tile counters (one per part) and the status word
+  int* d_counters = nullptr;
+  int* d_status = nullptr;
+  int parts = 0;          // launches per run: 1, or 2 with tile classes (CTA pairs, then one-CTA tiles)
+  gg::Part part[2];
+  int problem_count = 0;  // the prepared set's figures, as the reference reports them
   int total_tiles = 0;
   int grid_ctas = 0;
   gg::Variant variant = gg::Variant::kUnsupported;
   bool use_tc = true;  // tcgen05 kernel; false: the CUDA-core kernel
-  gg::KernelParams params{};
 
   void release() {
     if (block) cudaFree(block);
     block = nullptr;
-    d_maps = nullptr;
-    d_problems = nullptr;
-    d_offsets = nullptr;
-    d_counter = nullptr;
+    d_counters = nullptr;
     d_status = nullptr;
+    parts = 0;
   }
 };
 
@@ -522,13 +572,10 @@ int gg_executor_build_with_bias(gg_executor* ex, const gg_problem* sorted_proble
   ex->variant = v;
   ex->use_tc = config->use_tensor_cores != 0;
 
-  std::vector<DeviceProblemDesc> descs(static_cast<size_t>(count));
-  std::vector<CUtensorMap> maps(static_cast<size_t>(count) * gg::kMapsPerProblem);
   for (int i = 0; i < count; ++i) {
     const gg_problem& p = sorted_problems[i];
     if (p.m < 0 || p.n < 0 || p.k < 0) return cudaErrorInvalidValue;
     if (!p.a || !p.b || !p.d) return cudaErrorInvalidDevicePointer;
-    descs[static_cast<size_t>(i)] = gg::make_device_problem(p, v, config, &maps[static_cast<size_t>(i) * gg::kMapsPerProblem], i);
   }
   if (count == 0 || total_tiles <= 0) {
     ex->problem_count = count;
@@ -536,23 +583,69 @@ int gg_executor_build_with_bias(gg_executor* ex, const gg_problem* sorted_proble
     return cudaSuccess;  // nothing to launch
   }
 
-  int grid = 0;
-  cudaError_t st = gg::path_grid(ex->use_tc, v, total_tiles, config->persistent_ctas, &grid);
-  if (st != cudaSuccess) return st;
+  // The parts: one variant over the prepared set as given; or, with tile classes, the whole
+  // 256-row blocks of every problem on CTA pairs and the rows left over (fewer than 256, on
+  // one-CTA 128-row tiles of the same width), both in the prepared order.
+  gg::PartImage img[2];
+  int parts = 1;
+  if (config->tile_classes == GG_TILE_CLASSES_PAIR_BLOCKS) {
+    parts = 2;
+    img[0].variant = v;
+    img[1].variant = gg::variant_bn(v) == 256 ? gg::Variant::k128x256 : gg::Variant::k128x128;
+    for (int i = 0; i < count; ++i) {
+      const gg_problem& p = sorted_problems[i];
+      if (gg::tile_count(p.m, p.n, 256, gg::variant_bn(v)) == 0) continue;
+      const int blocks = p.m / 256 * 256;
+      const float* b = bias ? bias[i] : nullptr;
+      if (blocks > 0) gg::add_problem(img[0], gg::row_slice(p, 0, blocks, config), config, b);
+      if (p.m > blocks) gg::add_problem(img[1], gg::row_slice(p, blocks, p.m - blocks, config), config, b);
+    }
+  } else {
+    img[0].variant = v;
+    for (int i = 0; i < count; ++i) gg::add_problem(img[0], sorted_problems[i], config, bias ? bias[i] : nullptr);
+    img[0].offsets.assign(tile_offsets, tile_offsets + offsets_len);  // the prepared offsets, as given
+  }
 
-  const size_t maps_bytes = maps.size() * sizeof(CUtensorMap);
-  const size_t descs_off = gg::round_up(maps_bytes, 128);
-  const size_t offs_off = gg::round_up(descs_off + descs.size() * sizeof(DeviceProblemDesc), 128);
-  const size_t counter_off = gg::round_up(offs_off + static_cast<size_t>(offsets_len) * sizeof(int), 128);
-  const size_t bias_off = counter_off + 128;  // bias table (one pointer per problem), when given
-  const size_t bytes = bias_off + (bias ? static_cast<size_t>(count) * sizeof(const float*) : 0);
+  // Device layout: per part [maps | records | offsets | bias table], then counters and status.
+  struct Off {
+    size_t maps, descs, offs, bias;
+  } off[2]{};
+  size_t bytes = 0;
+  for (int j = 0; j < parts; ++j) {
+    const gg::PartImage& im = img[j];
+    off[j].maps = gg::round_up(bytes, 128);
+    off[j].descs = gg::round_up(off[j].maps + im.maps.size() * sizeof(CUtensorMap), 128);
+    off[j].offs = gg::round_up(off[j].descs + im.descs.size() * sizeof(DeviceProblemDesc), 128);
+    off[j].bias = gg::round_up(off[j].offs + im.offsets.size() * sizeof(int), 128);
+    bytes = off[j].bias + (bias ? im.bias.size() * sizeof(const float*) : 0);
+  }
+  const size_t counter_off = gg::round_up(bytes, 128);
+  bytes = counter_off + 128;  // counters at +0 (one int per part), status word at +64
   std::vector<unsigned char> image(bytes, 0);
-  std::memcpy(image.data(), maps.data(), maps_bytes);
-  std::memcpy(image.data() + descs_off, descs.data(), descs.size() * sizeof(DeviceProblemDesc));
-  std::memcpy(image.data() + offs_off, tile_offsets, static_cast<size_t>(offsets_len) * sizeof(int));
-  if (bias) std::memcpy(image.data() + bias_off, bias, static_cast<size_t>(count) * sizeof(const float*));
+  for (int j = 0; j < parts; ++j) {
+    const gg::PartImage& im = img[j];
+    if (!im.maps.empty()) std::memcpy(image.data() + off[j].maps, im.maps.data(), im.maps.size() * sizeof(CUtensorMap));
+    if (!im.descs.empty())
+      std::memcpy(image.data() + off[j].descs, im.descs.data(), im.descs.size() * sizeof(DeviceProblemDesc));
+    if (!im.offsets.empty()) std::memcpy(image.data() + off[j].offs, im.offsets.data(), im.offsets.size() * sizeof(int));
+    if (bias && !im.bias.empty())
+      std::memcpy(image.data() + off[j].bias, im.bias.data(), im.bias.size() * sizeof(const float*));
+  }
 
-  st = cudaMalloc(&ex->block, bytes);
+  gg::Part part[2];
+  for (int j = 0; j < parts; ++j) {
+    gg::Part& pt = part[j];
+    pt.variant = img[j].variant;
+    pt.use_tc = ex->use_tc;
+    pt.problem_count = static_cast<int>(img[j].descs.size());
+    pt.total_tiles = img[j].offsets.empty() ? 0 : img[j].offsets.back();
+    if (pt.total_tiles > 0) {
+      const cudaError_t st = gg::path_grid(pt.use_tc, pt.variant, pt.total_tiles, config->persistent_ctas, &pt.grid);
+      if (st != cudaSuccess) return st;
+    }
+  }
+
+  cudaError_t st = cudaMalloc(&ex->block, bytes);
   if (st != cudaSuccess) {
     ex->block = nullptr;
     return st;
@@ -563,30 +656,29 @@ int gg_executor_build_with_bias(gg_executor* ex, const gg_problem* sorted_proble
     return st;
   }
   unsigned char* base = static_cast<unsigned char*>(ex->block);
-  ex->d_maps = reinterpret_cast<CUtensorMap*>(base);
-  ex->d_problems = reinterpret_cast<DeviceProblemDesc*>(base + descs_off);
-  ex->d_offsets = reinterpret_cast<int*>(base + offs_off);
-  ex->d_counter = reinterpret_cast<int*>(base + counter_off);
+  ex->d_counters = reinterpret_cast<int*>(base + counter_off);
   ex->d_status = reinterpret_cast<int*>(base + counter_off + 64);
-
+  for (int j = 0; j < parts; ++j) {
+    gg::KernelParams& kp = part[j].params;
+    std::memset(&kp, 0, sizeof(kp));
+    kp.problems = reinterpret_cast<const DeviceProblemDesc*>(base + off[j].descs);
+    kp.tmaps = reinterpret_cast<const CUtensorMap*>(base + off[j].maps);
+    kp.tile_offsets = reinterpret_cast<const int*>(base + off[j].offs);
+    kp.tile_counter = ex->d_counters + j;
+    kp.status = ex->d_status;
+    kp.timeout_ns = gg::wait_timeout_ns();
+    kp.problem_count = part[j].problem_count;
+    kp.total_tiles = part[j].total_tiles;
+    kp.raster_group = gg::raster_group();
+    kp.single_mode = 0;
+    gg::set_formats(kp, config);
+    kp.bias = bias ? reinterpret_cast<const float* const*>(base + off[j].bias) : nullptr;
+    ex->part[j] = part[j];
+  }
+  ex->parts = parts;
   ex->problem_count = count;
   ex->total_tiles = total_tiles;
-  ex->grid_ctas = grid;
-
-  gg::KernelParams& kp = ex->params;
-  std::memset(&kp, 0, sizeof(kp));
-  kp.problems = ex->d_problems;
-  kp.tmaps = ex->d_maps;
-  kp.tile_offsets = ex->d_offsets;
-  kp.tile_counter = ex->d_counter;
-  kp.status = ex->d_status;
-  kp.timeout_ns = gg::wait_timeout_ns();
-  kp.problem_count = count;
-  kp.total_tiles = total_tiles;
-  kp.raster_group = gg::raster_group();
-  kp.single_mode = 0;
-  gg::set_formats(kp, config);
-  kp.bias = bias ? reinterpret_cast<const float* const*>(base + bias_off) : nullptr;
+  ex->grid_ctas = part[0].grid > 0 ? part[0].grid : part[1].grid;
   return cudaSuccess;
 }
 
@@ -595,9 +687,19 @@ int gg_executor_run(const gg_executor* ex, void* stream) {
   if (ex->total_tiles == 0 || ex->problem_count == 0) return cudaSuccess;
   if (!ex->block) return cudaErrorInvalidDevicePointer;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t st = cudaMemsetAsync(ex->d_counter, 0, sizeof(int), s);
+  cudaError_t st = cudaMemsetAsync(ex->d_counters, 0, 2 * sizeof(int), s);
   if (st != cudaSuccess) return st;
-  return gg::launch_path(ex->use_tc, ex->variant, ex->params, ex->grid_ctas, s);
+  bool after_pair = false;
+  for (int j = 0; j < ex->parts; ++j) {
+    const gg::Part& pt = ex->part[j];
+    if (pt.total_tiles <= 0) continue;
+    // The one-CTA part of a tile-class split may start while the pair part still runs.
+    st = after_pair ? gg::launch_grouped_kernel(pt.variant, pt.params, pt.grid, s, true)
+                    : gg::launch_path(pt.use_tc, pt.variant, pt.params, pt.grid, s);
+    if (st != cudaSuccess) return st;
+    after_pair = gg::variant_is_pair(pt.variant);
+  }
+  return cudaSuccess;
 }
 
 int gg_executor_problem_count(const gg_executor* ex) { return ex ? ex->problem_count : 0; }

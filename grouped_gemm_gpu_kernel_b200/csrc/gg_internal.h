@@ -35,7 +35,10 @@ int variant_ctas_per_tile(Variant v);
 
 // Raises the kernel's dynamic shared-memory limit on the current device (once per device).
 cudaError_t prepare_kernel(Variant v);
-cudaError_t launch_grouped_kernel(Variant v, const KernelParams& params, int grid, cudaStream_t stream);
+// overlap_previous: the grid may start while the previous kernel on the stream (a CTA-pair launch of
+// the same executor) still runs (one-CTA 128-row variants only).
+cudaError_t launch_grouped_kernel(Variant v, const KernelParams& params, int grid, cudaStream_t stream,
+                                  bool overlap_previous = false);
 cudaError_t kernel_occupancy(Variant v, int* active_blocks_per_sm, cudaFuncAttributes* attrs);
 // CTAs of this variant that can be resident on the device at once (whole pairs for pair variants).
 cudaError_t kernel_resident_ctas(Variant v, int* ctas);

@@ -168,6 +168,24 @@ __device__ __forceinline__ bool next_tile(const KernelParams& p, SchedState& ss,
   }
 }
 
+// At kernel start each CTA's scheduler brings its 1/gridDim share of the problem table and of the
+// tile offsets into L2 (`part` of `parts`), so that the searches and record loads of every CTA hit
+// L2 instead of DRAM once the first claims are out (cold tables cost one DRAM round trip per
+// dependent load of the search otherwise).
+__device__ __forceinline__ void prefetch_tables_l2(const KernelParams& p, int part, int parts, int lane) {
+  if (p.single_mode || p.problem_count <= 0) return;
+  const int64_t desc_bytes = static_cast<int64_t>(p.problem_count) * static_cast<int64_t>(sizeof(DeviceProblemDesc));
+  const int64_t offs_bytes = static_cast<int64_t>(p.problem_count + 1) * 4;
+  const int64_t desc_lines = (desc_bytes + 127) / 128, offs_lines = (offs_bytes + 127) / 128;
+  const int64_t lines = desc_lines + offs_lines;
+  const int64_t per = (lines + parts - 1) / parts;
+  for (int64_t i = part * per + lane; i < min(lines, (part + 1) * per); i += 32) {
+    const uint8_t* base = i < desc_lines ? reinterpret_cast<const uint8_t*>(p.problems) + 128 * i
+                                         : reinterpret_cast<const uint8_t*>(p.tile_offsets) + 128 * (i - desc_lines);
+    ptx::prefetch_l2(base);
+  }
+}
+
 // Warms the tensor maps a tile of this problem will use (only those that were encoded).
 __device__ __forceinline__ void prefetch_problem_maps(const CUtensorMap* maps, int q, unsigned flags, int lane) {
   const bool map_valid = (lane == kMapA || lane == kMapB) ? (flags & grouped_gemm::kFlagTmaAB) != 0u
@@ -446,9 +464,10 @@ __device__ __forceinline__ void epilogue_bias_prefetch(const EpiTile& e, int lan
 }
 
 // The chunk range [c_begin, c_end) of a tile's nchunks 32-column chunks that epilogue warp half
-// `half` stores: whole 64-column pairs, the first half taking the larger share.
+// `half` stores: whole 64-column pairs, the first half taking the larger share; a tile of two
+// chunks gives one to each half, so that both halves work on narrow tiles.
 __device__ __forceinline__ void epilogue_chunk_range(int nchunks, int half, int& c_begin, int& c_end) {
-  const int split = min(nchunks, 2 * ((nchunks + 3) / 4));
+  const int split = nchunks == 2 ? 1 : min(nchunks, 2 * ((nchunks + 3) / 4));
   c_begin = half ? split : 0;
   c_end = half ? nchunks : split;
 }
@@ -788,7 +807,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
   if (warp == kSchedWarp) {
     // ======================= scheduler =======================
     SchedState ss;
-    sched_init(p, ss, static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x), lane);
+    sched_init(p, ss, static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x), lane);  // first claim in flight
+    prefetch_tables_l2(p, static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x), lane);
     for (int t = 0;; ++t) {
       const int slot = t % kRing;
       const uint32_t par = static_cast<uint32_t>(t / kRing) & 1u;
@@ -902,8 +922,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
         if (aborted) break;
       }
     }
-    if (aborted && ptid == 0) {
-      // TMA loads issued for the last stages may still be landing: wait for them before exit.
+    if ((aborted || *abort_flag) && ptid == 0) {
+      // TMA loads issued for the last stages may still be landing: wait for them before exit
+      // (bounded: a stage that was never issued just runs out its short limit).
       const uint32_t n_back = it < static_cast<uint32_t>(S) ? it : static_cast<uint32_t>(S);
       for (uint32_t j = 1; j <= n_back; ++j) {
         const uint32_t i2 = it - j;

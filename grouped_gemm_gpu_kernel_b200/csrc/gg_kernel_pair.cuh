@@ -130,6 +130,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::fence_mbar_init();
   }
   ptx::cluster_sync();  // both CTAs' barriers exist before either touches the other's
+  // A one-CTA launch of the same executor may follow (the rows the pair tiles leave): it works on
+  // other problems' outputs, so it may start as soon as SMs free up.
+  if (threadIdx.x == 0) ptx::launch_dependents();
   if (warp == kMmaWarp) {
     ptx::tmem_alloc_pair(ptx::smem_addr(tmem_slot), L::kTmemCols);
     ptx::tmem_relinquish_pair();
@@ -155,6 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int pairs = static_cast<int>(gridDim.x >> 1);
       SchedState ss;
       sched_init(p, ss, pair_id, pairs, lane);
+      prefetch_tables_l2(p, pair_id, pairs, lane);
       for (int t = 0;; ++t) {
         const int slot = t % kRing;
         const uint32_t par = static_cast<uint32_t>(t / kRing) & 1u;

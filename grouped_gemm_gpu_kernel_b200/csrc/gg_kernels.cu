@@ -128,9 +128,39 @@ cudaError_t prepare_kernel(Variant v) {
   return st;
 }
 
-cudaError_t launch_grouped_kernel(Variant v, const KernelParams& params, int grid, cudaStream_t stream) {
+// Launch of a one-CTA variant that may start while the previous kernel on the stream (a CTA-pair
+// launch that triggers its dependents at start) still runs: the two work on disjoint outputs, so
+// this grid's CTAs take SMs as the previous grid's CTAs retire (programmatic stream serialisation;
+// the grid never waits on the previous one's results).
+template <int BM, int BN>
+cudaError_t launch_overlapping(const KernelParams& params, int grid, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = VariantTraits<BM, BN>::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, grouped_gemm_sm100_kernel<BM, BN>, params);
+}
+
+cudaError_t launch_grouped_kernel(Variant v, const KernelParams& params, int grid, cudaStream_t stream,
+                                  bool overlap_previous) {
   cudaError_t st = prepare_kernel(v);
   if (st != cudaSuccess) return st;
+  if (overlap_previous) {
+    switch (v) {
+      case Variant::k128x128:
+        return launch_overlapping<128, 128>(params, grid, stream);
+      case Variant::k128x256:
+        return launch_overlapping<128, 256>(params, grid, stream);
+      default:
+        return cudaErrorInvalidValue;
+    }
+  }
   switch (v) {
     case Variant::k64x64:
       grouped_gemm_sm100_kernel<64, 64><<<grid, kThreads, VariantTraits<64, 64>::kSmem, stream>>>(params);

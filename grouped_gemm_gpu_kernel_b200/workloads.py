@@ -25,6 +25,9 @@ from typing import Dict, List, Optional, Tuple
 import numpy as np
 
 CONFIG_NAMES = ("small16", "mixed512", "moe", "tiny4096", "skew")
+# A reduced MoE layer (8 experts, 2048 tokens, the same N and K) for profiling captures that must
+# stay small; not one of the benchmark configurations.
+PROFILE_NAMES = ("moe_reduced",)
 ALIGN_BYTES = 256
 
 
@@ -89,6 +92,10 @@ def make_shapes(name: str, seed: int = 42) -> Shapes:
         counts = zipf_split(16384, 64, 1.1, rng)
         dims = [(int(c), 14336, 4096) for c in counts]
         return Shapes(name, dims, [1.0] * 64, [0.0] * 64, False, "normal", 1.0, "normal", 0.02)
+    if name == "moe_reduced":
+        counts = zipf_split(2048, 8, 1.1, rng)
+        dims = [(int(c), 14336, 4096) for c in counts]
+        return Shapes(name, dims, [1.0] * 8, [0.0] * 8, False, "normal", 1.0, "normal", 0.02)
     if name == "tiny4096":
         d = rng.integers(1, 65, size=(4096, 3))
         dims = [tuple(int(x) for x in r) for r in d]
@@ -96,7 +103,7 @@ def make_shapes(name: str, seed: int = 42) -> Shapes:
     if name == "skew":
         dims = [(8192, 8192, 8192)] + [(128, 128, 128)] * 1023
         return Shapes(name, dims, [1.0] * 1024, [0.0] * 1024, False)
-    raise ValueError(f"unknown workload {name!r}; expected one of {CONFIG_NAMES}")
+    raise ValueError(f"unknown workload {name!r}; expected one of {CONFIG_NAMES + PROFILE_NAMES}")
 
 
 def _aligned(n_elems: int, elem_bytes: int) -> int:

@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define GG_ABI_VERSION 1
+#define GG_ABI_VERSION 2
 
 /* Sort modes; reference grouped_gemm.cuh:11-16 (SortMode). */
 #define GG_SORT_NONE 0
@@ -100,6 +100,16 @@ typedef struct gg_problem {
  *   MN-major shared-memory operands). With 8-bit inputs a column-major A needs 128-row tiles
  *   per CTA (not 64x128), and a column-major B lifts the 128-column rule. The mixture-of-experts
  *   plan takes a row-major A only.
+ * tile_classes (no reference counterpart, whose launch uses one tile shape): GG_TILE_CLASSES_NONE
+ *   (0: every problem is tiled with the config's tile) or, with a CTA-pair config (256x128x64,
+ *   256x256x64) on the tensor cores, GG_TILE_CLASSES_PAIR_BLOCKS: an executor cuts every problem
+ *   into its whole 256-row blocks, computed by CTA pairs, and the rows left over (fewer than 256),
+ *   computed by one-CTA tiles of 128 rows and the same width; the two launches of a run may
+ *   overlap on the GPU (the second takes SMs as the first retires). Large problems get the pair
+ *   tiles (half the B bytes per SM), and no pair tile is padded past a problem's last row. The
+ *   prepared set, its tile offsets and the executor's problem_count / total_tiles keep the config's
+ *   256-row tiling. Executors only: the no-allocation entry point, the per-problem baseline and
+ *   the mixture-of-experts plan run the config's tile everywhere.
  * Any other value of these fields is an invalid config. The C++ API of
  * grouped_gemm/grouped_gemm.cuh keeps the reference's KernelConfig and always passes 0 for all
  * of them. */
@@ -115,6 +125,8 @@ typedef struct gg_problem {
 #define GG_ACT_GELU 2
 #define GG_LAYOUT_ROW_MAJOR 0
 #define GG_LAYOUT_COL_MAJOR 1
+#define GG_TILE_CLASSES_NONE 0
+#define GG_TILE_CLASSES_PAIR_BLOCKS 1
 typedef struct gg_config {
   int cta_m;
   int cta_n;
@@ -127,6 +139,7 @@ typedef struct gg_config {
   int activation;      /* GG_ACT_NONE, GG_ACT_RELU or GG_ACT_GELU */
   int a_layout;        /* GG_LAYOUT_ROW_MAJOR or GG_LAYOUT_COL_MAJOR */
   int b_layout;        /* GG_LAYOUT_ROW_MAJOR or GG_LAYOUT_COL_MAJOR */
+  int tile_classes;    /* GG_TILE_CLASSES_NONE or GG_TILE_CLASSES_PAIR_BLOCKS */
 } gg_config;
 
 /* Resource report; field-for-field the reference's OccupancyInfo (grouped_gemm.cuh:54-83). */

@@ -32,14 +32,15 @@ F32, F16, BF16 = gg.OutputType.kF32, gg.OutputType.kF16, gg.OutputType.kBF16
 NONE, RELU, GELU = gg.Activation.kNone, gg.Activation.kReLU, gg.Activation.kGELU
 
 CONFIGS = [gg.KernelConfig(128, 256, 64), gg.KernelConfig(128, 128, 64), gg.KernelConfig(256, 256, 64),
-           gg.KernelConfig(64, 64, 16), gg.KernelConfig(128, 128, 64, use_tensor_cores=False)]
+           gg.KernelConfig(64, 64, 16), gg.KernelConfig(128, 128, 64, use_tensor_cores=False),
+           gg.KernelConfig(256, 128, 64, tile_classes=gg.TileClasses.kPairBlocks)]
 # (output type, activation, bias vectors: None, "aligned" (16-byte, vector loads) or "unaligned")
 CASES = [(F16, GELU, "unaligned"), (BF16, RELU, "aligned"), (F32, GELU, "aligned"), (F16, NONE, None),
          (BF16, NONE, "unaligned"), (F32, RELU, "unaligned")]
 
 
 def _cfg_id(c):
-    return f"{'' if c.use_tensor_cores else 'simt'}{c.cta_m}x{c.cta_n}x{c.cta_k}"
+    return f"{'' if c.use_tensor_cores else 'simt'}{c.cta_m}x{c.cta_n}x{c.cta_k}" + ("-classes" if c.tile_classes else "")
 
 
 def _case_id(case):

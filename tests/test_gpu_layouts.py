@@ -25,12 +25,13 @@ pytestmark = pytest.mark.gpu
 ROW, COL = gg.Layout.kRowMajor, gg.Layout.kColMajor
 CONFIGS = [gg.KernelConfig(128, 256, 64), gg.KernelConfig(128, 128, 64), gg.KernelConfig(64, 128, 32),
            gg.KernelConfig(64, 64, 16), gg.KernelConfig(256, 256, 64), gg.KernelConfig(256, 128, 64),
-           gg.KernelConfig(128, 128, 64, use_tensor_cores=False)]
+           gg.KernelConfig(128, 128, 64, use_tensor_cores=False),
+           gg.KernelConfig(256, 256, 64, tile_classes=gg.TileClasses.kPairBlocks)]
 LAYOUTS = [(COL, ROW), (ROW, COL), (COL, COL)]
 
 
 def _id(c):
-    return f"{'' if c.use_tensor_cores else 'simt'}{c.cta_m}x{c.cta_n}x{c.cta_k}"
+    return f"{'' if c.use_tensor_cores else 'simt'}{c.cta_m}x{c.cta_n}x{c.cta_k}" + ("-classes" if c.tile_classes else "")
 
 
 def _lid(l):

@@ -27,6 +27,13 @@ pytestmark = pytest.mark.gpu
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 ALL_CONFIGS = gg.REFERENCE_CONFIGS + gg.NATIVE_CONFIGS
 MODES = (gg.SortMode.kNone, gg.SortMode.kByK, gg.SortMode.kByTiles, gg.SortMode.kByTilesThenK)
+# CTA-pair configs whose executors cut problems into pair blocks and one-CTA rows (tile classes)
+TILE_CLASS_CONFIGS = (gg.KernelConfig(256, 256, 64, tile_classes=gg.TileClasses.kPairBlocks),
+                      gg.KernelConfig(256, 128, 64, tile_classes=gg.TileClasses.kPairBlocks))
+
+
+def _cfg_id(c):
+    return f"{c.cta_m}x{c.cta_n}" + ("-classes" if c.tile_classes else "")
 
 
 def _torch():
@@ -298,6 +305,45 @@ def test_skew_full_size_sampled(cuda, cfg):
     assert check_sampled(ps, rows_per=6, cols_per=64) <= 1.0
 
 
+@pytest.mark.parametrize("cfg", TILE_CLASS_CONFIGS, ids=_cfg_id)
+def test_tile_classes_match_oracle(cuda, cfg):
+    """Tile classes: every problem's whole 256-row blocks on CTA pairs, the rows left over on one-CTA
+    tiles (two launches). small16 in full; mixed512 and the MoE layer sampled, with the gaps between
+    problems' D untouched; the executor still reports the prepared set's 256-row tiling."""
+    torch = _torch()
+    ps = W.allocate(W.make_shapes("small16"), cuda)
+    for mode in (gg.SortMode.kNone, gg.SortMode.kByTiles):
+        ps.d.fill_(float("nan"))
+        run_grouped(ps.problems(), cfg, mode)
+        assert check_full(ps) <= 1.0
+    ps = W.allocate(W.make_shapes("mixed512"), cuda)
+    prep = gg.prepare_problem_set(ps.problems(), cfg, gg.SortMode.kByK)
+    ex = run_grouped(ps.problems(), cfg, gg.SortMode.kByK)
+    assert ex.total_tiles() == prep.total_tiles and ex.problem_count() == 512
+    assert check_sampled(ps, seed=3) <= 1.0
+    d = ps.d.cpu().numpy()
+    written = np.zeros(d.size, bool)
+    for i, (m, n, k) in enumerate(ps.shapes.dims):
+        written[ps.d_off[i]:ps.d_off[i] + m * n] = True
+    assert np.isnan(d[~written]).all() and np.isfinite(d[written]).all()
+    # same results as the one-variant pair launch, within the accuracy bound
+    ref = ps.d.clone()
+    ps.d.fill_(float("nan"))
+    run_grouped(ps.problems(), gg.KernelConfig(cfg.cta_m, cfg.cta_n, 64), gg.SortMode.kByK)
+    worst = 0.0
+    for i, (m, n, k) in enumerate(ps.shapes.dims):
+        sl = slice(ps.d_off[i], ps.d_off[i] + m * n)
+        x, y = ps.d[sl].double(), ref[sl].double()
+        worst = max(worst, float(((x - y).abs() / torch.clamp(y.abs(), min=float(np.sqrt(k) / 3))).max()) / O.tolerance(k))
+    assert worst <= 1.0
+    del ps, ref
+    if cfg.cta_n == 256:
+        ps = W.allocate(W.make_shapes("moe"), cuda)
+        run_grouped(ps.problems(), cfg, gg.SortMode.kByTiles)
+        assert check_sampled(ps, rows_per=3, cols_per=64) <= 1.0
+        del ps
+
+
 def test_determinism_bitwise(cuda):
     torch = _torch()
     ps = W.allocate(W.make_shapes("mixed512"), cuda)
@@ -396,12 +442,15 @@ EDGE_CASES = {
     "m_exact_tiles": dict(m=256, n=512, k=128, beta=0.25),
     "packed_small_misaligned": dict(m=50, n=40, k=37, a_shift=1, b_shift=3, beta=0.5),
     "packed_k64_misaligned": dict(m=70, n=200, k=64, a_shift=1, b_shift=1),
+    # rows past whole 256-row blocks (tile classes put them on one-CTA tiles)
+    "rows_513_odd_ld": dict(m=513, n=264, k=200, lda=203, ldc=266, ldd=265, beta=0.5),
+    "rows_767_aligned": dict(m=767, n=256, k=128, beta=-0.5),
 }
 
 
 @pytest.mark.parametrize("cfg", [gg.KernelConfig(128, 128, 64), gg.KernelConfig(64, 128, 32),
                                  gg.KernelConfig(128, 64, 32), gg.KernelConfig(256, 128, 64),
-                                 gg.KernelConfig(256, 256, 64)], ids=lambda c: f"{c.cta_m}x{c.cta_n}")
+                                 gg.KernelConfig(256, 256, 64)] + list(TILE_CLASS_CONFIGS), ids=_cfg_id)
 def test_edge_cases(cuda, cfg):
     cases = [(_edge_problem(cuda, seed=i, **kw)) for i, kw in enumerate(EDGE_CASES.values())]
     probs = [p for p, _ in cases]

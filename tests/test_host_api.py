@@ -46,7 +46,7 @@ def test_library_exports_every_declared_symbol():
     assert set(declared) <= exported
     # the static CUDA runtime stays private to the library
     assert not re.search(r" T cuda[A-Z]", out)
-    assert lib.gg_abi_version() == 1
+    assert lib.gg_abi_version() == 2
 
 
 def test_cpp_api_exported():
@@ -122,6 +122,11 @@ def test_tile_count_entry_point():
     (gg.KernelConfig(256, 128, 64), True), (gg.KernelConfig(256, 256, 64), True), (gg.KernelConfig(256, 64, 64), False),
     (gg.KernelConfig(64, 64, 16, threads=128), False), (gg.KernelConfig(32, 32, 16), False),
     (gg.KernelConfig(128, 128, 32), False), (gg.KernelConfig(256, 128, 32), False),
+    # tile classes: CTA-pair configs on the tensor cores only
+    (gg.KernelConfig(256, 256, 64, tile_classes=1), True), (gg.KernelConfig(256, 128, 64, tile_classes=1), True),
+    (gg.KernelConfig(128, 256, 64, tile_classes=1), False),
+    (gg.KernelConfig(256, 256, 64, tile_classes=1, use_tensor_cores=False), False),
+    (gg.KernelConfig(256, 256, 64, tile_classes=2), False),
 ])
 def test_build_config_validation(cfg, ok):
     """Unsupported configs fail with cudaErrorInvalidValue (reference src/grouped_gemm.cu:121-123)."""
@@ -202,7 +207,7 @@ def test_c_header_compiles_as_plain_c(tmp_path):
     subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I" + os.path.join(REPO, "include"), str(src), "-o", str(exe),
                     "-L" + lib_dir, "-lgrouped_gemm_b200", "-Wl,-rpath," + lib_dir], check=True)
     out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout
-    assert out.split() == ["1", "sort_by_tiles", "0"]
+    assert out.split() == ["2", "sort_by_tiles", "0"]
 
 
 @pytest.mark.skipif(shutil.which("nvcc") is None and not os.path.exists("/usr/local/cuda/bin/nvcc"), reason="no nvcc")
