@@ -49,8 +49,10 @@ DEFAULT_CTA = {"small16": (128, 128, 64), "mixed512": (128, 256, 64), "moe": (12
 # (the largest problems first, which shortens the persistent schedule's tail)
 DEFAULT_SORT = {"small16": 2, "mixed512": 1, "moe": 2, "tiny4096": 2, "skew": 2, "moe_reduced": 2}
 ROW_WORKLOADS = ("moe", "skew", "tiny4096", "small16")  # driver-timed beside the headline (N = 1)
-# The same two large workloads with CTA-pair tile classes (pair blocks + one-CTA rows)
-CLASS_ROWS = {"moe_pair_classes": "moe", "skew_pair_classes": "skew"}
+# Tile classes (gg_config.tile_classes): the two large workloads with CTA-pair blocks + one-CTA rows
+# (1), tiny4096 with its small problems on the CUDA-core kernel (2)
+CLASS_ROWS = {"moe_pair_classes": ("moe", 1), "skew_pair_classes": ("skew", 1),
+              "tiny4096_small_on_cuda_cores": ("tiny4096", 2)}
 STRONG_WORKLOADS = ("skew", "moe")  # one fixed global set split over the N ranks
 
 
@@ -663,8 +665,8 @@ def main():
         if world == 1:
             extras["workloads"] = {name: workload_row(name, dev, stream, args.steps, peaks_rows)
                                    for name in ROW_WORKLOADS if name != args.workload}
-            for row, name in CLASS_ROWS.items():
-                extras["workloads"][row] = workload_row(name, dev, stream, args.steps, peaks_rows, classes=True)
+            for row, (name, classes) in CLASS_ROWS.items():
+                extras["workloads"][row] = workload_row(name, dev, stream, args.steps, peaks_rows, classes=classes)
         extras["strong"] = {name: strong_row(name, world, rank, dev, stream, args.steps, max_over_ranks, barrier)
                             for name in STRONG_WORKLOADS}
 
@@ -861,18 +863,19 @@ def moe_plan_row(ps, shapes, cfg, stream, flops, executor_ms, bias_ptrs=None, ru
                    "tile offsets, the persistent kernel reads the tile count from the device"}
 
 
-def workload_row(name, dev, stream, steps, peaks, repeats=5, classes=False):
-    """One BASELINE workload on this GPU with its default tile and sort mode (classes: CTA-pair
-    256x256 tiles with tile classes instead): the median of `repeats` repeats of max(steps, 10)
-    executor runs, its roofline, its tail-work share."""
+def workload_row(name, dev, stream, steps, peaks, repeats=5, classes=0):
+    """One BASELINE workload on this GPU with its default tile and sort mode, or with tile classes
+    (1: CTA-pair 256x256 blocks + one-CTA rows; 2: the default tile, small problems on the CUDA
+    cores): the median of `repeats` repeats of max(steps, 10) executor runs, its roofline, its
+    tail-work share."""
     import torch
 
     import grouped_gemm_gpu_kernel_b200 as gg
     from grouped_gemm_gpu_kernel_b200 import workloads as W
 
     shapes = W.make_shapes(name)
-    cta, mode = ((256, 256, 64) if classes else DEFAULT_CTA[name]), DEFAULT_SORT[name]
-    cfg = gg.KernelConfig(*cta, tile_classes=gg.TileClasses.kPairBlocks if classes else 0)
+    cta, mode = ((256, 256, 64) if classes == 1 else DEFAULT_CTA[name]), DEFAULT_SORT[name]
+    cfg = gg.KernelConfig(*cta, tile_classes=classes)
     ps = W.allocate(shapes, dev, seed=42, d_fill=0.0)
     prep = gg.prepare_problem_set(ps.problems(), cfg, mode)
     ex = gg.GroupedGemmExecutor()
@@ -885,7 +888,9 @@ def workload_row(name, dev, stream, steps, peaks, repeats=5, classes=False):
     med, lo, hi = timer.median_of(ex.run, max(steps, 10), flush, repeats)
     status = ex.status()
     row = {"ms": med, "min_ms": lo, "max_ms": hi, "tflops": shapes.flops / (med * 1e-3) / 1e12,
-           "cta": "x".join(map(str, cta)) + (" tile classes" if classes else ""), "sort_mode": gg.sort_mode_name(mode),
+           "cta": "x".join(map(str, cta)) + {0: "", 1: " pair blocks + one-CTA rows",
+                                             2: " small problems on CUDA cores"}[classes],
+           "sort_mode": gg.sort_mode_name(mode),
            "problems": len(shapes.dims),
            "tiles": ex.total_tiles(), "grid_ctas": ex.grid_ctas(), "gflop": shapes.flops / 1e9,
            "algorithmic_gb": alg / 1e9, "roofline": roofline_of(shapes.flops, alg, med, peaks),

@@ -62,10 +62,12 @@ class Layout(enum.IntEnum):
 
 class TileClasses(enum.IntEnum):
     """How an executor tiles its problems (GG_TILE_CLASSES_*): one tile shape for every problem (the
-    reference's), or, with a CTA-pair config, whole 256-row blocks on CTA pairs and the rows left
-    over on one-CTA 128-row tiles, as two launches that may overlap."""
+    reference's); with a CTA-pair config, whole 256-row blocks on CTA pairs and the rows left over
+    on one-CTA 128-row tiles, as two launches that may overlap; or problems with m, n, k all at
+    most capi.GG_SMALL_PROBLEM_DIM on the CUDA-core kernel and the rest on the tensor cores."""
     kNone = capi.GG_TILE_CLASSES_NONE
     kPairBlocks = capi.GG_TILE_CLASSES_PAIR_BLOCKS
+    kSmallOnCudaCores = capi.GG_TILE_CLASSES_SMALL_ON_CUDA_CORES
 
 
 class Activation(enum.IntEnum):

@@ -338,9 +338,11 @@ Variant variant_of(const gg_config* c) {
   const auto layout_ok = [](int l) { return l == GG_LAYOUT_ROW_MAJOR || l == GG_LAYOUT_COL_MAJOR; };
   if (!layout_ok(c->a_layout) || !layout_ok(c->b_layout)) return Variant::kUnsupported;
   const Variant v = resolve_variant(c->cta_m, c->cta_n, c->cta_k, c->threads);
-  // Tile classes cut problems into CTA-pair blocks and one-CTA rows: pair configs on tensor cores only.
+  // Tile classes: CTA-pair blocks and one-CTA rows (pair configs on the tensor cores), or the
+  // small problems of a tensor-core config on the CUDA cores.
   if (c->tile_classes != GG_TILE_CLASSES_NONE &&
-      !(c->tile_classes == GG_TILE_CLASSES_PAIR_BLOCKS && c->use_tensor_cores && variant_is_pair(v)))
+      !(c->tile_classes == GG_TILE_CLASSES_PAIR_BLOCKS && c->use_tensor_cores && variant_is_pair(v)) &&
+      !(c->tile_classes == GG_TILE_CLASSES_SMALL_ON_CUDA_CORES && c->use_tensor_cores))
     return Variant::kUnsupported;
   // 8-bit MN-major operands fill 128-wide chunks: on the tensor cores a row-major B needs per-CTA
   // B widths of 128 or 256, a column-major A 128 rows per CTA.
@@ -587,8 +589,21 @@ int gg_executor_build_with_bias(gg_executor* ex, const gg_problem* sorted_proble
   // 256-row blocks of every problem on CTA pairs and the rows left over (fewer than 256, on
   // one-CTA 128-row tiles of the same width), both in the prepared order.
   gg::PartImage img[2];
+  bool part_tc[2] = {ex->use_tc, ex->use_tc};
   int parts = 1;
-  if (config->tile_classes == GG_TILE_CLASSES_PAIR_BLOCKS) {
+  if (config->tile_classes == GG_TILE_CLASSES_SMALL_ON_CUDA_CORES) {
+    // Problems no larger than GG_SMALL_PROBLEM_DIM in m, n and k on the CUDA-core kernel (several
+    // CTAs per SM hide their latency better), the others on the tensor cores; same tile shape.
+    parts = 2;
+    img[0].variant = v;
+    img[1].variant = v;
+    part_tc[1] = false;
+    for (int i = 0; i < count; ++i) {
+      const gg_problem& p = sorted_problems[i];
+      const bool small = p.m <= GG_SMALL_PROBLEM_DIM && p.n <= GG_SMALL_PROBLEM_DIM && p.k <= GG_SMALL_PROBLEM_DIM;
+      gg::add_problem(img[small ? 1 : 0], p, config, bias ? bias[i] : nullptr);
+    }
+  } else if (config->tile_classes == GG_TILE_CLASSES_PAIR_BLOCKS) {
     parts = 2;
     img[0].variant = v;
     img[1].variant = gg::variant_bn(v) == 256 ? gg::Variant::k128x256 : gg::Variant::k128x128;
@@ -636,7 +651,7 @@ int gg_executor_build_with_bias(gg_executor* ex, const gg_problem* sorted_proble
   for (int j = 0; j < parts; ++j) {
     gg::Part& pt = part[j];
     pt.variant = img[j].variant;
-    pt.use_tc = ex->use_tc;
+    pt.use_tc = part_tc[j];
     pt.problem_count = static_cast<int>(img[j].descs.size());
     pt.total_tiles = img[j].offsets.empty() ? 0 : img[j].offsets.back();
     if (pt.total_tiles > 0) {

@@ -108,8 +108,13 @@ typedef struct gg_problem {
  *   overlap on the GPU (the second takes SMs as the first retires). Large problems get the pair
  *   tiles (half the B bytes per SM), and no pair tile is padded past a problem's last row. The
  *   prepared set, its tile offsets and the executor's problem_count / total_tiles keep the config's
- *   256-row tiling. Executors only: the no-allocation entry point, the per-problem baseline and
- *   the mixture-of-experts plan run the config's tile everywhere.
+ *   256-row tiling. GG_TILE_CLASSES_SMALL_ON_CUDA_CORES, with any tensor-core config: problems
+ *   whose m, n and k are all at most GG_SMALL_PROBLEM_DIM run on the CUDA-core kernel (several
+ *   CTAs per SM hide the latency of one-tile problems; measured on B200 with L2 flushed, 4096
+ *   problems of 1..64: 157 us against 242 us on the tensor cores), the others on the tensor
+ *   cores, same tile shape, two launches one after the other. Executors only: the no-allocation
+ *   entry point, the per-problem baseline and the mixture-of-experts plan run the config's tile
+ *   and path everywhere.
  * Any other value of these fields is an invalid config. The C++ API of
  * grouped_gemm/grouped_gemm.cuh keeps the reference's KernelConfig and always passes 0 for all
  * of them. */
@@ -127,6 +132,8 @@ typedef struct gg_problem {
 #define GG_LAYOUT_COL_MAJOR 1
 #define GG_TILE_CLASSES_NONE 0
 #define GG_TILE_CLASSES_PAIR_BLOCKS 1
+#define GG_TILE_CLASSES_SMALL_ON_CUDA_CORES 2
+#define GG_SMALL_PROBLEM_DIM 64
 typedef struct gg_config {
   int cta_m;
   int cta_n;
@@ -139,7 +146,7 @@ typedef struct gg_config {
   int activation;      /* GG_ACT_NONE, GG_ACT_RELU or GG_ACT_GELU */
   int a_layout;        /* GG_LAYOUT_ROW_MAJOR or GG_LAYOUT_COL_MAJOR */
   int b_layout;        /* GG_LAYOUT_ROW_MAJOR or GG_LAYOUT_COL_MAJOR */
-  int tile_classes;    /* GG_TILE_CLASSES_NONE or GG_TILE_CLASSES_PAIR_BLOCKS */
+  int tile_classes;    /* GG_TILE_CLASSES_NONE, _PAIR_BLOCKS or _SMALL_ON_CUDA_CORES */
 } gg_config;
 
 /* Resource report; field-for-field the reference's OccupancyInfo (grouped_gemm.cuh:54-83). */

@@ -266,6 +266,24 @@ def test_tiny4096_full(cuda, cfg):
     assert check_full(ps) <= 1.0
 
 
+@pytest.mark.parametrize("cfg", [gg.KernelConfig(128, 128, 64), gg.KernelConfig(64, 64, 16), gg.KernelConfig(128, 64, 64),
+                                 gg.KernelConfig(256, 128, 64), gg.KernelConfig(128, 128, 64, use_tensor_cores=False)],
+                         ids=lambda c: f"{'' if c.use_tensor_cores else 'simt'}{c.cta_m}x{c.cta_n}")
+def test_exhaustive_small_dims(cuda, cfg):
+    """Every (m, n, k) in 1..17 (4913 problems, packed odd leading dimensions, beta != 0), one
+    grouped launch, every element against the FP64 oracle; the gaps between problems' D untouched."""
+    dims = [(m, n, k) for m in range(1, 18) for n in range(1, 18) for k in range(1, 18)]
+    shapes = W.Shapes("exhaustive17", dims, [1.25] * len(dims), [-0.75] * len(dims), True)
+    ps = W.allocate(shapes, cuda, seed=17)
+    run_grouped(ps.problems(), cfg, gg.SortMode.kByTiles)
+    assert check_full(ps) <= 1.0
+    d = ps.d.cpu().numpy()
+    written = np.zeros(d.size, bool)
+    for i, (m, n, k) in enumerate(dims):
+        written[ps.d_off[i]:ps.d_off[i] + m * n] = True
+    assert np.isnan(d[~written]).all()
+
+
 def test_mixed512_all_modes_sampled(cuda):
     ps = W.allocate(W.make_shapes("mixed512"), cuda)
     for mode in MODES:
@@ -342,6 +360,32 @@ def test_tile_classes_match_oracle(cuda, cfg):
         run_grouped(ps.problems(), cfg, gg.SortMode.kByTiles)
         assert check_sampled(ps, rows_per=3, cols_per=64) <= 1.0
         del ps
+
+
+@pytest.mark.parametrize("cfg", [gg.KernelConfig(128, 64, 64, tile_classes=gg.TileClasses.kSmallOnCudaCores),
+                                 gg.KernelConfig(128, 256, 64, tile_classes=gg.TileClasses.kSmallOnCudaCores)],
+                         ids=lambda c: f"{c.cta_m}x{c.cta_n}")
+def test_small_problems_on_cuda_cores(cuda, cfg):
+    """Tile class 'small on CUDA cores': problems with m, n, k <= 64 on the CUDA-core kernel, the
+    others on the tensor cores. tiny4096 (all small), small16 (mostly large) and a set mixing both
+    with odd and aligned pitches, every element against the FP64 oracle."""
+    ps = W.allocate(W.make_shapes("tiny4096"), cuda)
+    run_grouped(ps.problems(), cfg, gg.SortMode.kByTiles)
+    assert check_full(ps) <= 1.0
+    ps = W.allocate(W.make_shapes("small16"), cuda)
+    run_grouped(ps.problems(), cfg, gg.SortMode.kByK)
+    assert check_full(ps) <= 1.0
+    rng = np.random.default_rng(8)
+    dims = [(int(rng.integers(1, 65)), int(rng.integers(1, 65)), int(rng.integers(1, 65))) for _ in range(200)]
+    dims += [(int(8 * rng.integers(8, 40)), int(8 * rng.integers(8, 40)), int(8 * rng.integers(1, 40)))
+             for _ in range(40)]
+    order = rng.permutation(len(dims))
+    shapes = W.Shapes("mixed_small", [dims[i] for i in order], [1.5] * len(dims), [0.25] * len(dims), True)
+    ps = W.allocate(shapes, cuda, seed=9)
+    for mode in (gg.SortMode.kNone, gg.SortMode.kByTiles):
+        ps.d.fill_(float("nan"))
+        run_grouped(ps.problems(), cfg, mode)
+        assert check_full(ps) <= 1.0
 
 
 def test_determinism_bitwise(cuda):

@@ -126,7 +126,10 @@ def test_tile_count_entry_point():
     (gg.KernelConfig(256, 256, 64, tile_classes=1), True), (gg.KernelConfig(256, 128, 64, tile_classes=1), True),
     (gg.KernelConfig(128, 256, 64, tile_classes=1), False),
     (gg.KernelConfig(256, 256, 64, tile_classes=1, use_tensor_cores=False), False),
-    (gg.KernelConfig(256, 256, 64, tile_classes=2), False),
+    (gg.KernelConfig(256, 256, 64, tile_classes=3), False),
+    # small problems on the CUDA cores: any tensor-core config
+    (gg.KernelConfig(128, 64, 64, tile_classes=2), True), (gg.KernelConfig(64, 64, 16, tile_classes=2), True),
+    (gg.KernelConfig(128, 64, 64, tile_classes=2, use_tensor_cores=False), False),
 ])
 def test_build_config_validation(cfg, ok):
     """Unsupported configs fail with cudaErrorInvalidValue (reference src/grouped_gemm.cu:121-123)."""
