@@ -887,13 +887,20 @@ def workload_row(name, dev, stream, steps, peaks, repeats=5, classes=0):
         assert ex.run(stream) == 0
     med, lo, hi = timer.median_of(ex.run, max(steps, 10), flush, repeats)
     status = ex.status()
+    roof = roofline_of(shapes.flops, alg, med, peaks)
+    traffic_path = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(traffic_path) and not classes:
+        with open(traffic_path) as f:
+            tr = json.load(f).get(f"{name}/{cta[0]}x{cta[1]}x{cta[2]}")
+        if tr:
+            roof["traffic"], roof["traffic_source"] = tr["bytes_per_launch"], tr["source"]
     row = {"ms": med, "min_ms": lo, "max_ms": hi, "tflops": shapes.flops / (med * 1e-3) / 1e12,
            "cta": "x".join(map(str, cta)) + {0: "", 1: " pair blocks + one-CTA rows",
                                              2: " small problems on CUDA cores"}[classes],
            "sort_mode": gg.sort_mode_name(mode),
            "problems": len(shapes.dims),
            "tiles": ex.total_tiles(), "grid_ctas": ex.grid_ctas(), "gflop": shapes.flops / 1e9,
-           "algorithmic_gb": alg / 1e9, "roofline": roofline_of(shapes.flops, alg, med, peaks),
+           "algorithmic_gb": alg / 1e9, "roofline": roof,
            "tail_work_share": tail_work_share(prep, cta[2]), "status": status,
            "timing": f"median of {repeats} repeats of {max(steps, 10)} steps; "
                      + ("L2 flushed before every step, each step timed alone" if flush else
