@@ -656,6 +656,8 @@ def main():
         extras["cuda_graph"] = graph_row(ex, stream, local_flops)
         if args.workload == "moe":
             extras["device_prep"] = moe_plan_row(ps, shapes, cfg, stream, local_flops, ms, bias_ptrs)
+        elif plain and not gg.variant_is_pair(cfg):
+            extras["device_prepared"] = device_plan_row(problems, cfg, args.sort_mode, stream, local_flops, ms)
         if plain:  # the reference's kernels: FP16 in, FP32 out, no fused bias or activation
             extras["ref_gpu"] = reference_gpu_row(problems, stream, local_flops)
 
@@ -947,6 +949,34 @@ def strong_row(name, world, rank, dev, stream, steps, max_over_ranks, barrier):
             "status": status,
             "how": f"the one {name} set (seed 42) cut by gg_partition into {world} tile-weighted shards, one per "
                    f"rank; {max(steps, 10)} steps timed on each rank, max over ranks"}
+
+
+def device_plan_row(problems, cfg, mode, stream, flops, executor_ms, runs=20):
+    """The same problem set prepared on the device (gg_device_plan): descriptors and count copied to
+    device memory once; each run = the one-block preparation kernel (sort, tile scan, records) +
+    the grouped kernel, with no host work. No TMA descriptors on this path (zero-fill loads)."""
+    import torch
+
+    import grouped_gemm_gpu_kernel_b200 as gg
+
+    plan = gg.DevicePlan(cfg, len(problems))
+    raw = torch.frombuffer(bytearray(gg.DevicePlan.pack_problems(problems)), dtype=torch.uint8).to(stream.device)
+    count = torch.tensor([len(problems)], dtype=torch.int32, device=stream.device)
+    for _ in range(3):
+        assert plan.run(raw, count, mode, stream) == 0
+    torch.cuda.synchronize()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(runs):
+        plan.run(raw, count, mode, stream)
+    a1.record(stream)
+    torch.cuda.synchronize()
+    t = a0.elapsed_time(a1) / runs
+    bits, total = plan.status()
+    plan.close()
+    return {"ms": t, "tflops": flops / (t * 1e-3) / 1e12, "executor_ms": executor_ms, "status": bits, "tiles": total,
+            "how": "problem descriptors and count in device memory; one-block preparation kernel (validation, "
+                   "sort, tile scan, records) + the grouped kernel per run; zero-fill loads (no TMA descriptors)"}
 
 
 def graph_row(ex, stream, flops, runs=20, replays=10):

@@ -26,7 +26,7 @@ __all__ = [
     "prepare_problem_set", "sort_mode_name", "query_occupancy", "run_grouped_gemm_once",
     "run_baseline_per_problem", "count_non_empty_problems", "partition", "ShardPiece", "problem_from_tensors",
     "NATIVE_CONFIGS", "REFERENCE_CONFIGS", "PAIR_CONFIGS", "selftest_wait_timeout", "capi", "MoePlan",
-    "selftest_wait_timeout_word", "baseline_status", "noalloc_status",
+    "selftest_wait_timeout_word", "baseline_status", "noalloc_status", "DevicePlan",
     "InputType", "OutputType", "Activation", "Layout", "TileClasses",
 ]
 
@@ -187,6 +187,11 @@ def _stream_ptr(stream) -> Optional[int]:
     if isinstance(stream, int):
         return stream or None
     return getattr(stream, "cuda_stream", None) or None
+
+
+def variant_is_pair(config: KernelConfig) -> bool:
+    """True for the CTA-pair tile shapes (256 rows: a cluster of two CTAs per tile)."""
+    return config.cta_m == 256
 
 
 def sort_mode_name(sort_mode: int) -> str:
@@ -376,6 +381,70 @@ class MoePlan:
     def close(self):
         if self._h:
             self._lib.gg_moe_plan_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class DevicePlan:
+    """Grouped GEMM whose problem descriptors and count live in device memory (gg_device_plan_*).
+
+    `run(problems, count, sort_mode)` takes a device buffer holding an array of gg_problem records
+    (see `pack_problems`) and a device int32 count, and enqueues the device-side preparation
+    (validation, the sort mode's order, tile offsets, records, TMA descriptors) and the grouped
+    kernel, with no host synchronisation. One-CTA tensor-core configs or the CUDA-core path,
+    row-major A and B.
+    """
+
+    def __init__(self, config: KernelConfig, max_problems: int):
+        self._lib = capi.load()
+        self._h = None
+        h = ctypes.c_void_p()
+        cfg = config.to_c()
+        st = self._lib.gg_device_plan_create(ctypes.byref(cfg), int(max_problems), ctypes.byref(h))
+        if st != 0:
+            raise ValueError(f"gg_device_plan_create failed with status {st}")
+        self._h = h
+        self.max_problems = int(max_problems)
+
+    @staticmethod
+    def pack_problems(problems: Sequence[ProblemDesc]) -> bytes:
+        """The gg_problem records of `problems` as bytes (copy them to device memory for run)."""
+        arr = _problems_array(problems)
+        return ctypes.string_at(ctypes.addressof(arr), ctypes.sizeof(capi.GGProblem) * len(problems))
+
+    def run(self, problems, count, sort_mode: int = 0, stream=None) -> int:
+        """problems / count: device pointers (ints) or tensors (a uint8 tensor of packed records, an
+        int32 tensor holding the count)."""
+        pp = problems if isinstance(problems, int) else problems.data_ptr()
+        cp = count if isinstance(count, int) else count.data_ptr()
+        return self._lib.gg_device_plan_run(self._h, ctypes.c_void_p(pp), ctypes.c_void_p(cp), int(sort_mode),
+                                            _stream_ptr(stream))
+
+    def status(self):
+        """Synchronises; returns (GG_STATUS_* bits, then cleared; tile count of the last run)."""
+        bits, total = ctypes.c_int(0), ctypes.c_int(0)
+        st = self._lib.gg_device_plan_status(self._h, ctypes.byref(bits), ctypes.byref(total))
+        if st != 0:
+            raise RuntimeError(f"gg_device_plan_status failed with status {st}")
+        return bits.value, total.value
+
+    def prepared(self, count: int):
+        """Synchronises; (sorted_to_original, tile_offsets) of the last run's first `count` slots."""
+        order = (ctypes.c_int * max(1, count))()
+        offs = (ctypes.c_int * (count + 1))()
+        st = self._lib.gg_device_plan_prepared(self._h, order, offs, int(count))
+        if st != 0:
+            raise RuntimeError(f"gg_device_plan_prepared failed with status {st}")
+        return list(order)[:count], list(offs)
+
+    def close(self):
+        if self._h:
+            self._lib.gg_device_plan_destroy(self._h)
             self._h = None
 
     def __del__(self):

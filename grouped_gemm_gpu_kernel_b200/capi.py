@@ -23,8 +23,12 @@ EXPORTED_SYMBOLS = (
     "gg_baseline_status", "gg_noalloc_status", "gg_selftest_wait_timeout_word",
     "gg_moe_plan_create", "gg_moe_plan_run", "gg_moe_plan_status", "gg_moe_plan_destroy",
     "gg_ipc_export", "gg_ipc_open", "gg_ipc_close",
+    "gg_device_plan_create", "gg_device_plan_run", "gg_device_plan_status", "gg_device_plan_prepared",
+    "gg_device_plan_destroy",
 )
 GG_STATUS_BAD_ROWS = 0x100
+GG_STATUS_BAD_PROBLEMS = 0x200
+GG_DEVICE_PLAN_MAX_PROBLEMS = 4096
 GG_INPUT_F16 = 0
 GG_INPUT_BF16 = 1
 GG_INPUT_E4M3 = 2
@@ -151,6 +155,11 @@ def load() -> ctypes.CDLL:
         "gg_ipc_export": ([vp, P(GGIpcHandle)], ctypes.c_int),
         "gg_ipc_open": ([P(GGIpcHandle), P(vp)], ctypes.c_int),
         "gg_ipc_close": ([vp], ctypes.c_int),
+        "gg_device_plan_create": ([pc, ctypes.c_int, P(vp)], ctypes.c_int),
+        "gg_device_plan_run": ([vp, vp, vp, ctypes.c_int, vp], ctypes.c_int),
+        "gg_device_plan_status": ([vp, i32p, i32p], ctypes.c_int),
+        "gg_device_plan_prepared": ([vp, i32p, i32p, ctypes.c_int], ctypes.c_int),
+        "gg_device_plan_destroy": ([vp], None),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

@@ -5,6 +5,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
@@ -585,9 +586,10 @@ int gg_executor_build_with_bias(gg_executor* ex, const gg_problem* sorted_proble
     return cudaSuccess;  // nothing to launch
   }
 
-  // The parts: one variant over the prepared set as given; or, with tile classes, the whole
-  // 256-row blocks of every problem on CTA pairs and the rows left over (fewer than 256, on
-  // one-CTA 128-row tiles of the same width), both in the prepared order.
+  // The parts: one variant over the prepared set as given; or, with tile classes, either the small
+  // problems on the CUDA cores and the rest on the tensor cores, or the whole 256-row blocks of
+  // every problem on CTA pairs and the rows left over (fewer than 256, on one-CTA 128-row tiles of
+  // the same width); each part in the prepared order.
   gg::PartImage img[2];
   bool part_tc[2] = {ex->use_tc, ex->use_tc};
   int parts = 1;
@@ -1401,6 +1403,332 @@ int gg_moe_plan_status(gg_moe_plan* plan, int* status, int* total_tiles) {
 }
 
 void gg_moe_plan_destroy(gg_moe_plan* plan) {
+  if (!plan) return;
+  if (plan->block) cudaFree(plan->block);
+  delete plan;
+}
+
+}  // extern "C"
+
+// ---- grouped GEMM prepared on the device (problem descriptors in device memory) ---------------
+// The problem set itself -- dims, pointers, leading dimensions, alpha and beta of every problem --
+// lives in device memory (written by an earlier kernel, e.g. a router or a planner on the GPU),
+// and so does the problem count. A run is a one-block preparation kernel and the persistent grouped
+// kernel: the preparation validates the problems, orders them by the reference's sort rules
+// (stable; the same order prepare_problem_set gives on the host), prefix-sums their tile counts
+// and writes the problem records. No host synchronisation and no host copy per run. The problems
+// have no TMA descriptors (those are encoded on the host): their operands take the zero-fill
+// loader and D the masked coalesced stores, which work for any pitch and alignment.
+namespace gg {
+namespace {
+
+constexpr int kDevPlanMax = GG_DEVICE_PLAN_MAX_PROBLEMS;
+constexpr int kDevPrepThreads = kMoePrepThreads;  // block_exclusive_scan's block size
+
+// Tile geometry the preparation needs (from the plan's config).
+struct DevGeom {
+  int bm, bn;   // tile
+  int kblock;   // K elements per pipeline stage (64 for 16-bit inputs, 128 for 8-bit)
+  int out_fmt;  // GG_OUTPUT_*: element type of C and D
+};
+
+int next_pow2(int x) {
+  int p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+size_t dev_prep_smem(int max_problems) {
+  return static_cast<size_t>(next_pow2(max_problems)) * (sizeof(long long) + 3 * sizeof(int));
+}
+
+// True when problem x goes before problem y under sort mode `mode`: the reference's rules
+// (src/grouped_gemm.cu:977-1005: K descending, ties by m*n descending; by tiles: tile count
+// descending, ties by the K rule), ties by input index (a stable sort); -1 (padding) goes last.
+__device__ __forceinline__ bool dev_before(int x, int y, int mode, const int* tiles, const int* ks,
+                                           const long long* mns) {
+  if (x < 0) return false;
+  if (y < 0) return true;
+  const bool by_tiles = mode == GG_SORT_BY_TILES || mode == GG_SORT_BY_TILES_THEN_K;
+  if (by_tiles && tiles[x] != tiles[y]) return tiles[x] > tiles[y];
+  if (by_tiles || mode == GG_SORT_BY_K) {
+    if (ks[x] != ks[y]) return ks[x] > ks[y];
+    if (mns[x] != mns[y]) return mns[x] > mns[y];
+  }
+  return x < y;
+}
+
+__device__ __forceinline__ bool dev_aligned(const void* p, unsigned a) {
+  return (reinterpret_cast<uintptr_t>(p) & (a - 1u)) == 0;
+}
+
+// One block. descs: one record per sorted slot; offsets: max_problems + 1 prefix sums (flat past
+// the count); order: the sorted-to-input index of every slot (-1 past the count).
+__global__ void __launch_bounds__(kDevPrepThreads) device_prepare_kernel(
+    const gg_problem* __restrict__ problems, const int* __restrict__ count_ptr, int max_problems, int p2, int mode,
+    DevGeom g, DeviceProblemDesc* __restrict__ descs, int* __restrict__ offsets, int* __restrict__ order,
+    int* total_tiles, int* counter, int* status) {
+  extern __shared__ __align__(16) unsigned char dsm[];
+  long long* s_mn = reinterpret_cast<long long*>(dsm);
+  int* s_tiles = reinterpret_cast<int*>(s_mn + p2);
+  int* s_k = s_tiles + p2;
+  int* s_idx = s_k + p2;
+  __shared__ int s_warp[kDevPrepThreads / 32];
+  const int tid = static_cast<int>(threadIdx.x);
+
+  int count = *count_ptr;
+  int bad = count < 0 || count > max_problems;
+  if (bad) count = 0;
+  for (int i = tid; i < p2; i += kDevPrepThreads) {
+    int t = 0, k = 0, idx = -1;
+    long long mn = 0;
+    if (i < count) {
+      const gg_problem q = problems[i];
+      // the checks of GroupedGemmExecutor::build (src/grouped_gemm.cu:1169-1174) and of the pitches
+      if (q.m < 0 || q.n < 0 || q.k < 0 || !q.a || !q.b || !q.d || q.lda < max(1, q.k) || q.ldb < max(1, q.n) ||
+          q.ldd < max(1, q.n) || (q.c && q.beta != 0.0f && q.ldc < max(1, q.n)))
+        bad = 1;
+      t = (q.m > 0 && q.n > 0) ? ((q.m + g.bm - 1) / g.bm) * ((q.n + g.bn - 1) / g.bn) : 0;
+      k = q.k;
+      mn = static_cast<long long>(q.m) * q.n;
+      idx = i;
+    }
+    s_tiles[i] = t;
+    s_k[i] = k;
+    s_mn[i] = mn;
+    s_idx[i] = idx;
+  }
+  bad = __syncthreads_or(bad);
+  if (bad) {  // nothing runs: zero tiles
+    if (tid == 0) {
+      *total_tiles = 0;
+      *counter = 0;
+      atomicOr(status, GG_STATUS_BAD_PROBLEMS);
+    }
+    return;
+  }
+
+  // Bitonic sort of the input indices; the order is total (ties by index), so the result is the
+  // stable order of the reference's rules.
+  if (mode == GG_SORT_BY_K || mode == GG_SORT_BY_TILES || mode == GG_SORT_BY_TILES_THEN_K) {
+    for (int k2 = 2; k2 <= p2; k2 <<= 1) {
+      for (int j = k2 >> 1; j > 0; j >>= 1) {
+        for (int i = tid; i < p2; i += kDevPrepThreads) {
+          const int ixj = i ^ j;
+          if (ixj > i) {
+            const int x = s_idx[i], y = s_idx[ixj];
+            const bool up = (i & k2) == 0;
+            if (up ? dev_before(y, x, mode, s_tiles, s_k, s_mn) : dev_before(x, y, mode, s_tiles, s_k, s_mn)) {
+              s_idx[i] = y;
+              s_idx[ixj] = x;
+            }
+          }
+        }
+        __syncthreads();
+      }
+    }
+  }
+
+  // Tile offsets in sorted order (flat past the count) and the order itself.
+  int carry = 0;
+  for (int base = 0; base < max(p2, kDevPrepThreads); base += kDevPrepThreads) {
+    const int s = base + tid;
+    const int x = s < p2 ? s_idx[s] : -1;
+    int total;
+    const int excl = block_exclusive_scan<int>(x >= 0 ? s_tiles[x] : 0, s_warp, &total);
+    if (s < max_problems) {
+      offsets[s] = carry + excl;
+      order[s] = x;
+    }
+    carry += total;
+  }
+
+  // Problem records and TMA descriptors of the sorted slots.
+  for (int s = tid; s < count; s += kDevPrepThreads) {
+    const int x = s_idx[s];
+    const gg_problem q = problems[x];
+    DeviceProblemDesc d{};
+    d.m = q.m;
+    d.n = q.n;
+    d.k = q.k;
+    d.a = static_cast<const __half*>(q.a);
+    d.b = static_cast<const __half*>(q.b);
+    d.c = q.c;
+    d.d = q.d;
+    d.lda = q.lda;
+    d.ldb = q.ldb;
+    d.ldc = q.ldc;
+    d.ldd = q.ldd;
+    d.alpha = q.alpha;
+    d.beta = q.beta;
+    const bool has_tiles = q.m > 0 && q.n > 0;
+    d.tiles_m = has_tiles ? (q.m + g.bm - 1) / g.bm : 0;
+    d.tiles_n = has_tiles ? (q.n + g.bn - 1) / g.bn : 0;
+    d.k_blocks = q.k > 0 ? (q.k + g.kblock - 1) / g.kblock : 0;
+    d.tma_row0 = 0;
+    d.map_slot = 0;  // no tensor maps: zero-fill loads and masked stores
+    unsigned flags = 0;
+    if (q.c != nullptr && q.beta != 0.0f) flags |= grouped_gemm::kFlagReadC;
+    const bool f32 = g.out_fmt == GG_OUTPUT_F32;
+    if (dev_aligned(q.c, 16) && q.ldc % (f32 ? 4 : 8) == 0) flags |= grouped_gemm::kFlagCVec;
+    if (dev_aligned(q.d, f32 ? 16u : 8u) && q.ldd % 4 == 0) flags |= grouped_gemm::kFlagDVec;
+    d.flags = flags;
+    descs[s] = d;
+  }
+  if (tid == 0) {
+    offsets[max_problems] = carry;
+    *total_tiles = carry;
+    *counter = 0;
+  }
+}
+
+std::atomic<unsigned long long> g_dev_prep_attr{0};  // one bit per device: dynamic smem raised
+
+}  // namespace
+}  // namespace gg
+
+struct gg_device_plan {
+  void* block = nullptr;  // unused map group | records | offsets | order | total, counter, status
+  DeviceProblemDesc* d_descs = nullptr;
+  int* d_offsets = nullptr;
+  int* d_order = nullptr;
+  int* d_total = nullptr;
+  int* d_counter = nullptr;
+  int* d_status = nullptr;
+  int max_problems = 0;
+  int p2 = 1;
+  gg::DevGeom geom{};
+  gg::Variant variant = gg::Variant::kUnsupported;
+  bool use_tc = true;
+  int grid_ctas = 0;
+  gg::KernelParams params{};
+};
+
+extern "C" {
+
+int gg_device_plan_create(const gg_config* config, int max_problems, gg_device_plan** out) {
+  if (!out) return cudaErrorInvalidValue;
+  *out = nullptr;
+  const gg::Variant v = gg::variant_of(config);
+  if (v == gg::Variant::kUnsupported || gg::variant_is_pair(v) || config->tile_classes != GG_TILE_CLASSES_NONE ||
+      config->a_layout != GG_LAYOUT_ROW_MAJOR || config->b_layout != GG_LAYOUT_ROW_MAJOR || max_problems < 1 ||
+      max_problems > gg::kDevPlanMax)
+    return cudaErrorInvalidValue;
+  int dev = 0;
+  cudaError_t st = cudaGetDevice(&dev);
+  if (st != cudaSuccess) return st;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(gg::g_dev_prep_attr.load() & bit)) {
+    st = cudaFuncSetAttribute(gg::device_prepare_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(gg::dev_prep_smem(gg::kDevPlanMax)));
+    if (st != cudaSuccess) return st;
+    gg::g_dev_prep_attr.fetch_or(bit);
+  }
+
+  const gg::InGeom ig = gg::in_geom(config->input_type);
+  const gg::DevGeom geom{gg::variant_bm(v), gg::variant_bn(v), ig.kblock, config->output_type};
+  const size_t M = static_cast<size_t>(max_problems);
+  const size_t descs_off = gg::round_up(gg::kMapsPerProblem * sizeof(CUtensorMap), 128);  // one zeroed map group
+  const size_t offs_off = gg::round_up(descs_off + M * sizeof(DeviceProblemDesc), 128);
+  const size_t order_off = gg::round_up(offs_off + (M + 1) * sizeof(int), 128);
+  const size_t words_off = gg::round_up(order_off + M * sizeof(int), 128);
+  const size_t bytes = words_off + 128;
+
+  gg_device_plan* plan = new (std::nothrow) gg_device_plan();
+  if (!plan) return cudaErrorMemoryAllocation;
+  st = cudaMalloc(&plan->block, bytes);
+  if (st != cudaSuccess) {
+    delete plan;
+    return st;
+  }
+  st = cudaMemset(plan->block, 0, bytes);
+  if (st != cudaSuccess) {
+    cudaFree(plan->block);
+    delete plan;
+    return st;
+  }
+  unsigned char* base = static_cast<unsigned char*>(plan->block);
+  const bool use_tc = config->use_tensor_cores != 0;
+  int grid = 0;
+  st = gg::path_grid(use_tc, v, 1 << 30, config->persistent_ctas, &grid);
+  if (st != cudaSuccess) {
+    cudaFree(plan->block);
+    delete plan;
+    return st;
+  }
+  plan->d_descs = reinterpret_cast<DeviceProblemDesc*>(base + descs_off);
+  plan->d_offsets = reinterpret_cast<int*>(base + offs_off);
+  plan->d_order = reinterpret_cast<int*>(base + order_off);
+  plan->d_total = reinterpret_cast<int*>(base + words_off);
+  plan->d_counter = reinterpret_cast<int*>(base + words_off + 4);
+  plan->d_status = reinterpret_cast<int*>(base + words_off + 8);
+  plan->max_problems = max_problems;
+  plan->p2 = gg::next_pow2(max_problems);
+  plan->geom = geom;
+  plan->variant = v;
+  plan->use_tc = use_tc;
+  plan->grid_ctas = grid;
+
+  gg::KernelParams& kp = plan->params;
+  std::memset(&kp, 0, sizeof(kp));
+  kp.problems = plan->d_descs;
+  kp.tmaps = reinterpret_cast<const CUtensorMap*>(base);
+  kp.tile_offsets = plan->d_offsets;
+  kp.tile_counter = plan->d_counter;
+  kp.total_tiles_dev = plan->d_total;
+  kp.status = plan->d_status;
+  kp.timeout_ns = gg::wait_timeout_ns();
+  kp.problem_count = max_problems;  // slots past the count own no tiles
+  kp.total_tiles = 0;
+  kp.raster_group = gg::raster_group();
+  kp.single_mode = 0;
+  gg::set_formats(kp, config);
+  *out = plan;
+  return cudaSuccess;
+}
+
+int gg_device_plan_run(gg_device_plan* plan, const gg_problem* problems, const int* count, int sort_mode,
+                       void* stream) {
+  if (!plan || !plan->block) return cudaErrorInvalidDevicePointer;
+  if (!problems || !count) return cudaErrorInvalidValue;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  gg::device_prepare_kernel<<<1, gg::kDevPrepThreads, gg::dev_prep_smem(plan->max_problems), s>>>(
+      problems, count, plan->max_problems, plan->p2, sort_mode, plan->geom, plan->d_descs, plan->d_offsets,
+      plan->d_order, plan->d_total, plan->d_counter, plan->d_status);
+  cudaError_t st = cudaGetLastError();
+  if (st != cudaSuccess) return st;
+  return gg::launch_path(plan->use_tc, plan->variant, plan->params, plan->grid_ctas, s);
+}
+
+int gg_device_plan_status(gg_device_plan* plan, int* status, int* total_tiles) {
+  if (!plan || !plan->block) return cudaErrorInvalidDevicePointer;
+  if (!status) return cudaErrorInvalidValue;
+  cudaError_t st = cudaDeviceSynchronize();
+  if (st != cudaSuccess) return st;
+  int words[3] = {0, 0, 0};
+  st = cudaMemcpy(words, plan->d_total, sizeof(words), cudaMemcpyDeviceToHost);
+  if (st != cudaSuccess) return st;
+  *status = words[2];
+  if (total_tiles) *total_tiles = words[0];
+  return cudaMemset(plan->d_status, 0, sizeof(int));
+}
+
+int gg_device_plan_prepared(gg_device_plan* plan, int* sorted_to_original, int* tile_offsets, int capacity) {
+  if (!plan || !plan->block) return cudaErrorInvalidDevicePointer;
+  if (capacity < 0 || capacity > plan->max_problems || (capacity > 0 && !sorted_to_original) || !tile_offsets)
+    return cudaErrorInvalidValue;
+  cudaError_t st = cudaDeviceSynchronize();
+  if (st != cudaSuccess) return st;
+  if (capacity > 0) {
+    st = cudaMemcpy(sorted_to_original, plan->d_order, static_cast<size_t>(capacity) * sizeof(int),
+                    cudaMemcpyDeviceToHost);
+    if (st != cudaSuccess) return st;
+  }
+  return cudaMemcpy(tile_offsets, plan->d_offsets, static_cast<size_t>(capacity + 1) * sizeof(int),
+                    cudaMemcpyDeviceToHost);
+}
+
+void gg_device_plan_destroy(gg_device_plan* plan) {
   if (!plan) return;
   if (plan->block) cudaFree(plan->block);
   delete plan;

@@ -358,6 +358,40 @@ int gg_moe_plan_run(gg_moe_plan* plan, const int* rows, void* stream);
 int gg_moe_plan_status(gg_moe_plan* plan, int* status, int* total_tiles);
 void gg_moe_plan_destroy(gg_moe_plan* plan);
 
+/* ---- grouped GEMM prepared on the device ----------------------------------------------------
+ * No counterpart in the reference, whose problem set is prepared on the host
+ * (src/grouped_gemm.cu:967-1022 prepare_problem_set, 1132-1239 build). Here the problem
+ * descriptors themselves -- an array of gg_problem -- and their count are in device memory (written
+ * by an earlier kernel: a planner or router on the GPU) and never travel to the host. A run
+ * enqueues a one-block preparation kernel, which checks the problems (the checks of
+ * gg_executor_build; a failure computes nothing and raises GG_STATUS_BAD_PROBLEMS), orders them by
+ * the sort mode's rules (the same stable order as gg_prepare), prefix-sums their tiles and writes
+ * the problem records, and then the persistent grouped kernel. No host synchronisation, no host
+ * copy per run: a run can be captured in a CUDA graph and replayed over new problems. The problems
+ * get no TMA descriptors (those are encoded on the host): A and B take the zero-fill loader and D
+ * the masked stores, which take any pitch and alignment but move fewer bytes per cycle than TMA.
+ * Configs: one-CTA tiles (not the CTA-pair shapes), row-major A and B, no tile classes; any input
+ * and output type, activation, and the CUDA-core path. D must be this GPU's memory. */
+#define GG_DEVICE_PLAN_MAX_PROBLEMS 4096
+#define GG_STATUS_BAD_PROBLEMS 0x200
+typedef struct gg_device_plan gg_device_plan;
+/* Allocates the plan's device tables for up to max_problems (1..GG_DEVICE_PLAN_MAX_PROBLEMS)
+ * problems and encodes its descriptor templates. Invalid config or size -> cudaErrorInvalidValue. */
+int gg_device_plan_create(const gg_config* config, int max_problems, gg_device_plan** out);
+/* problems: device array of gg_problem (device pointers inside); count: device int, at most the
+ * plan's max_problems (else GG_STATUS_BAD_PROBLEMS); sort_mode: GG_SORT_*. Enqueues on `stream`.
+ * Runs of one plan on two streams at once race on its tables. */
+int gg_device_plan_run(gg_device_plan* plan, const gg_problem* problems, const int* count, int sort_mode,
+                       void* stream);
+/* Synchronises; returns (then clears) the GG_STATUS_* bits of the plan's runs and the tile count
+ * of the last run (nullable). */
+int gg_device_plan_status(gg_device_plan* plan, int* status, int* total_tiles);
+/* Synchronises; copies the last run's sorted-to-original order (capacity entries, -1 past the
+ * count) and tile offsets (capacity + 1 entries) to the host: what gg_prepare returns for the same
+ * problems and sort mode. */
+int gg_device_plan_prepared(gg_device_plan* plan, int* sorted_to_original, int* tile_offsets, int capacity);
+void gg_device_plan_destroy(gg_device_plan* plan);
+
 /* No counterpart in the reference (which is single-GPU). One FP32 rectangle of a strided
  * row-major matrix and its place in a packed buffer, for gg_copy_rects. */
 typedef struct gg_rect_copy {

@@ -355,3 +355,16 @@ def test_ipc_entry_points_check_arguments_before_device_work():
     assert lib.gg_ipc_close(None) == 1
     assert lib.gg_ipc_close(ctypes.c_void_p(0x1000)) == 1
     assert ctypes.sizeof(gg.capi.GGIpcHandle) == 80
+
+
+@pytest.mark.parametrize("cfg,max_problems", [
+    (gg.KernelConfig(256, 256, 64), 16),                          # CTA pairs
+    (gg.KernelConfig(128, 128, 64, a_layout=1), 16),              # column-major A
+    (gg.KernelConfig(128, 128, 64, tile_classes=2), 16),          # tile classes
+    (gg.KernelConfig(32, 32, 16), 16),                            # unsupported tile
+    (gg.KernelConfig(128, 128, 64), 0),                           # no room
+    (gg.KernelConfig(128, 128, 64), capi.GG_DEVICE_PLAN_MAX_PROBLEMS + 1),
+])
+def test_device_plan_rejects_configs_before_device_work(cfg, max_problems):
+    with pytest.raises(ValueError, match="status 1"):
+        gg.DevicePlan(cfg, max_problems)
