@@ -364,7 +364,8 @@ void gg_moe_plan_destroy(gg_moe_plan* plan);
  * descriptors themselves -- an array of gg_problem -- and their count are in device memory (written
  * by an earlier kernel: a planner or router on the GPU) and never travel to the host. A run
  * enqueues a one-block preparation kernel, which checks the problems (the checks of
- * gg_executor_build; a failure computes nothing and raises GG_STATUS_BAD_PROBLEMS), orders them by
+ * gg_executor_build, and that lda >= k, ldb >= n, ldd >= n and, when C is read, ldc >= n; a failure
+ * computes nothing and raises GG_STATUS_BAD_PROBLEMS), orders them by
  * the sort mode's rules (the same stable order as gg_prepare), prefix-sums their tiles and writes
  * the problem records, and then the persistent grouped kernel. No host synchronisation, no host
  * copy per run: a run can be captured in a CUDA graph and replayed over new problems. The problems
