@@ -976,7 +976,8 @@ def device_plan_row(problems, cfg, mode, stream, flops, executor_ms, runs=20):
     plan.close()
     return {"ms": t, "tflops": flops / (t * 1e-3) / 1e12, "executor_ms": executor_ms, "status": bits, "tiles": total,
             "how": "problem descriptors and count in device memory; one-block preparation kernel (validation, "
-                   "sort, tile scan, records) + the grouped kernel per run; zero-fill loads (no TMA descriptors)"}
+                   "sort, tile scan, records) + the grouped kernel per run; 16-byte cp.async stage fills "
+                   "(no TMA descriptors)"}
 
 
 def graph_row(ex, stream, flops, runs=20, replays=10):

@@ -1429,6 +1429,7 @@ constexpr int kDevPrepThreads = kMoePrepThreads;  // block_exclusive_scan's bloc
 struct DevGeom {
   int bm, bn;   // tile
   int kblock;   // K elements per pipeline stage (64 for 16-bit inputs, 128 for 8-bit)
+  int in_b;     // bytes per A / B element
   int out_fmt;  // GG_OUTPUT_*: element type of C and D
 };
 
@@ -1566,8 +1567,12 @@ __global__ void __launch_bounds__(kDevPrepThreads) device_prepare_kernel(
     d.tiles_n = has_tiles ? (q.n + g.bn - 1) / g.bn : 0;
     d.k_blocks = q.k > 0 ? (q.k + g.kblock - 1) / g.kblock : 0;
     d.tma_row0 = 0;
-    d.map_slot = 0;  // no tensor maps: zero-fill loads and masked stores
+    d.map_slot = 0;  // no tensor maps: cp.async or zero-fill loads, masked stores
     unsigned flags = 0;
+    // 16-byte copies for A and B when every row starts 16-byte aligned (the rules of TMA)
+    if (has_tiles && q.k > 0 && dev_aligned(q.a, 16) && dev_aligned(q.b, 16) &&
+        (static_cast<long long>(q.lda) * g.in_b) % 16 == 0 && (static_cast<long long>(q.ldb) * g.in_b) % 16 == 0)
+      flags |= grouped_gemm::kFlagCpAsync;
     if (q.c != nullptr && q.beta != 0.0f) flags |= grouped_gemm::kFlagReadC;
     const bool f32 = g.out_fmt == GG_OUTPUT_F32;
     if (dev_aligned(q.c, 16) && q.ldc % (f32 ? 4 : 8) == 0) flags |= grouped_gemm::kFlagCVec;
@@ -1582,7 +1587,22 @@ __global__ void __launch_bounds__(kDevPrepThreads) device_prepare_kernel(
   }
 }
 
-std::atomic<unsigned long long> g_dev_prep_attr{0};  // one bit per device: dynamic smem raised
+// Raises the preparation kernel's dynamic shared-memory limit on the current device to at least
+// `bytes` (only above the 48 KB default; once per device and size).
+cudaError_t dev_prep_reserve_smem(size_t bytes) {
+  static std::mutex mu;
+  static size_t raised[kMaxDevices] = {};
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  int dev = 0;
+  cudaError_t st = cudaGetDevice(&dev);
+  if (st != cudaSuccess) return st;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (raised[dev] >= bytes) return cudaSuccess;
+  st = cudaFuncSetAttribute(device_prepare_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (st == cudaSuccess) raised[dev] = bytes;
+  return st;
+}
 
 }  // namespace
 }  // namespace gg
@@ -1614,19 +1634,11 @@ int gg_device_plan_create(const gg_config* config, int max_problems, gg_device_p
       config->a_layout != GG_LAYOUT_ROW_MAJOR || config->b_layout != GG_LAYOUT_ROW_MAJOR || max_problems < 1 ||
       max_problems > gg::kDevPlanMax)
     return cudaErrorInvalidValue;
-  int dev = 0;
-  cudaError_t st = cudaGetDevice(&dev);
+  cudaError_t st = gg::dev_prep_reserve_smem(gg::dev_prep_smem(max_problems));
   if (st != cudaSuccess) return st;
-  const unsigned long long bit = 1ull << (dev & 63);
-  if (!(gg::g_dev_prep_attr.load() & bit)) {
-    st = cudaFuncSetAttribute(gg::device_prepare_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(gg::dev_prep_smem(gg::kDevPlanMax)));
-    if (st != cudaSuccess) return st;
-    gg::g_dev_prep_attr.fetch_or(bit);
-  }
 
   const gg::InGeom ig = gg::in_geom(config->input_type);
-  const gg::DevGeom geom{gg::variant_bm(v), gg::variant_bn(v), ig.kblock, config->output_type};
+  const gg::DevGeom geom{gg::variant_bm(v), gg::variant_bn(v), ig.kblock, ig.bytes, config->output_type};
   const size_t M = static_cast<size_t>(max_problems);
   const size_t descs_off = gg::round_up(gg::kMapsPerProblem * sizeof(CUtensorMap), 128);  // one zeroed map group
   const size_t offs_off = gg::round_up(descs_off + M * sizeof(DeviceProblemDesc), 128);

@@ -631,6 +631,61 @@ __device__ __forceinline__ void lsu_fill_stage(uint8_t* as, uint8_t* bs, const _
   }
 }
 
+// Stage fill with 16-byte cp.async, for row-major A and B whose rows start 16-byte aligned but that
+// have no tensor maps (problem sets prepared on the device): the same 128-byte-swizzled layouts the
+// TMA loads write. A: ROWS rows of one 128-byte K row each (K-major); B: the K block's rows of COLS
+// columns as 128-byte-wide chunks (MN-major). Bytes of A past K and K rows of B past K are
+// zero-filled by the copies themselves (source size below 16); rows of A past M and columns of B
+// past N are not written (they only reach accumulator rows and columns that are never stored).
+// The copies are issued, not awaited: the caller tracks them on the stage's mbarrier.
+template <int ROWS, int COLS, bool F8>
+__device__ __forceinline__ void cpasync_fill_stage(uint32_t as, uint32_t bs, const uint8_t* a, int64_t lda_b,
+                                                   const uint8_t* b, int64_t ldb_b, int m, int n, int k, int row0,
+                                                   int col0, int kb, int ptid) {
+  constexpr int EB = F8 ? 1 : 2;
+  constexpr int KB = F8 ? 2 * kBK : kBK;  // K values per 128-byte row, K rows of B per stage
+  constexpr int kSegs = COLS * EB / 16;   // 16-byte pieces of one K row of B
+  constexpr int kRowsB = kProdThreads / kSegs;  // K rows of B per pass of the producer threads
+  static_assert(kProdThreads == 64 && kSegs <= kProdThreads && kProdThreads % kSegs == 0, "copy split");
+  const int k0 = kb * KB;
+  // A: thread = (row mod 8, 16-byte piece j); its swizzled column and source size stay fixed.
+  {
+    const int r0 = ptid >> 3, j = ptid & 7;
+    const int sb = max(0, min(16, (k - k0) * EB - 16 * j));
+    const int rows = min(ROWS, m - row0);
+    uint32_t d = as + static_cast<uint32_t>(r0 * 128 + ((j ^ r0) << 4));
+    const uint8_t* src = a + static_cast<int64_t>(row0 + r0) * lda_b + static_cast<int64_t>(k0) * EB + 16 * j;
+    const int64_t step = 8 * lda_b;
+#pragma unroll 4
+    for (int r = r0; r < rows; r += 8) {
+      ptx::cp_async_16(d, sb > 0 ? src : a, static_cast<uint32_t>(sb));
+      d += 1024;
+      src += step;
+    }
+  }
+  // B: thread = (K row mod kRowsB, 16-byte piece of the row); columns past N are not written.
+  {
+    const int seg = ptid % kSegs, kr0 = ptid / kSegs;
+    const int c = seg * 16;
+    const int cbytes = min(COLS, n - col0) * EB;
+    if (c < cbytes) {
+      const int cb = min(16, cbytes - c);
+      const int kvalid = min(KB, k - k0);
+      const int cs = (c & 127) >> 4;
+      const uint32_t dcol = bs + static_cast<uint32_t>((c >> 7) * (KB * 128));
+      const uint8_t* src = b + static_cast<int64_t>(k0 + kr0) * ldb_b + static_cast<int64_t>(col0) * EB + c;
+      const int64_t step = kRowsB * ldb_b;
+#pragma unroll 8
+      for (int kr = kr0; kr < KB; kr += kRowsB) {
+        const int sb = kr < kvalid ? cb : 0;
+        ptx::cp_async_16(dcol + static_cast<uint32_t>(kr * 128 + ((cs ^ (kr & 7)) << 4)), sb > 0 ? src : b,
+                         static_cast<uint32_t>(sb));
+        src += step;
+      }
+    }
+  }
+}
+
 // ---- mainloop helpers ------------------------------------------------------------------------
 // Operand modes of a launch, one bit each: 8-bit A/B, A stored column-major (k x m: MN-major in
 // shared memory), B stored column-major (n x k: K-major in shared memory). The per-stage helpers
@@ -897,6 +952,40 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
           it += static_cast<uint32_t>(kb_count);
         }
         if (aborted) break;
+      } else if (flags & grouped_gemm::kFlagCpAsync) {
+        // 16-byte cp.async: every producer thread issues its copies and ties them to the stage's
+        // full barrier (one pending arrival each, received when its copies land); after a named
+        // barrier, one thread adds the barrier's expected arrival. The MMA thread fences the
+        // generic-proxy writes before its tensor-core reads.
+        for (int kb = 0; kb < kb_count; ++kb) {
+          const int st = static_cast<int>(it % S);
+          const uint32_t ph = (it / S) & 1u;
+          if (ptid == 0) {
+            const bool got = wait_phase(empty_bar(st), ph ^ 1u, abort_flag, p.status, tmo, GG_STATUS_TIMEOUT_PRODUCER);
+            *prod_go = got ? 1 : 0;
+          }
+          ptx::named_bar_sync(1, kProdThreads);
+          if (!*prod_go) {
+            aborted = true;
+            break;
+          }
+          const uint32_t as = sbase + static_cast<uint32_t>(st * L::kStageBytes);
+          const uint32_t bs = as + L::kABytes;
+          const int64_t lda_b = static_cast<int64_t>(lda) * (f8 ? 1 : 2), ldb_b = static_cast<int64_t>(ldb) * (f8 ? 1 : 2);
+          if (f8)
+            cpasync_fill_stage<BM, BN, true>(as, bs, reinterpret_cast<const uint8_t*>(a), lda_b,
+                                             reinterpret_cast<const uint8_t*>(b), ldb_b, m, n, k, tile_m * BM,
+                                             tile_n * BN, kb, ptid);
+          else
+            cpasync_fill_stage<BM, BN, false>(as, bs, reinterpret_cast<const uint8_t*>(a), lda_b,
+                                              reinterpret_cast<const uint8_t*>(b), ldb_b, m, n, k, tile_m * BM,
+                                              tile_n * BN, kb, ptid);
+          ptx::cp_async_mbar_arrive(full_bar(st));
+          ptx::named_bar_sync(1, kProdThreads);  // every pending arrival is registered
+          if (ptid == 0) ptx::mbar_arrive(full_bar(st));
+          ++it;
+        }
+        if (aborted) break;
       } else {
         for (int kb = 0; kb < kb_count; ++kb) {
           const int st = static_cast<int>(it % S);
@@ -922,6 +1011,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
         if (aborted) break;
       }
     }
+    ptx::cp_async_wait_all();  // this thread's 16-byte copies, if any, have landed
     if ((aborted || *abort_flag) && ptid == 0) {
       // TMA loads issued for the last stages may still be landing: wait for them before exit
       // (bounded: a stage that was never issued just runs out its short limit).
@@ -945,6 +1035,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
         if (!wait_phase(ringf_bar(slot), par, abort_flag, p.status, tmo, GG_STATUS_TIMEOUT_MMA)) break;
         const int q = ring[slot].problem;
         const int kb_count = ring[slot].desc.k_blocks;
+        const bool cpasync_tile = (ring[slot].desc.flags & grouped_gemm::kFlagCpAsync) != 0u;
         ptx::mbar_arrive(ringe_bar(slot));
         if (q < 0) break;
         const int buf = t % kAcc;
@@ -966,6 +1057,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
             break;
           }
           ptx::tc_fence_after_sync();
+          if (cpasync_tile) ptx::fence_proxy_async_smem();  // cp.async wrote the stage (generic proxy)
           const uint32_t a0 = sbase + static_cast<uint32_t>(st * L::kStageBytes);
           const uint32_t b0 = a0 + L::kABytes;
           mma_kblock_any<false>(mode, d_tmem, a0, b0, kIdesc, kb == 0);

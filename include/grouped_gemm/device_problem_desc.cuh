@@ -22,6 +22,8 @@ enum DeviceProblemFlags : unsigned {
   kFlagPackedRows = 64u,  // the A and D maps span the packed rows of every problem: TMA row
                           // coordinates add tma_row0, and D goes out by TMA only in whole
                           // 32-row boxes (a partial box would reach the next problem's rows)
+  kFlagCpAsync = 128u,  // no tensor maps (prepared on the device), but A and B rows are 16-byte
+                        // aligned: the producers copy stages with 16-byte cp.async (row-major A, B)
 };
 
 struct DeviceProblemDesc {

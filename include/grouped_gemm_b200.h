@@ -369,8 +369,10 @@ void gg_moe_plan_destroy(gg_moe_plan* plan);
  * the sort mode's rules (the same stable order as gg_prepare), prefix-sums their tiles and writes
  * the problem records, and then the persistent grouped kernel. No host synchronisation, no host
  * copy per run: a run can be captured in a CUDA graph and replayed over new problems. The problems
- * get no TMA descriptors (those are encoded on the host): A and B take the zero-fill loader and D
- * the masked stores, which take any pitch and alignment but move fewer bytes per cycle than TMA.
+ * get no TMA descriptors (those are encoded on the host): A and B rows that start 16-byte aligned
+ * (base and pitch in bytes multiples of 16) load by 16-byte cp.async into the same swizzled stages,
+ * other A and B by the zero-fill loader; D takes the masked stores. Both take fewer bytes per cycle
+ * than TMA.
  * Configs: one-CTA tiles (not the CTA-pair shapes), row-major A and B, no tile classes; any input
  * and output type, activation, and the CUDA-core path. D must be this GPU's memory. */
 #define GG_DEVICE_PLAN_MAX_PROBLEMS 4096

@@ -59,7 +59,7 @@ def test_device_plan_matches_host_preparation(cuda, cfg):
                         ("tiny4096", (gg.SortMode.kNone, gg.SortMode.kByTilesThenK))):
         ps = W.allocate(W.make_shapes(name), cuda)
         probs = ps.problems()
-        plan = gg.DevicePlan(cfg, len(probs) + 3)
+        plan = gg.DevicePlan(cfg, min(len(probs) + 3, capi.GG_DEVICE_PLAN_MAX_PROBLEMS))  # spare slots past the count
         for mode in modes:
             prep = gg.prepare_problem_set(probs, cfg, mode)
             ps.d.fill_(float("nan"))
