@@ -11,10 +11,17 @@
 // are widened to FP32 and accumulated with FP32 FMA (a product of two 16-bit values is exact in
 // FP32), so the result differs from the tensor-core path only in the order of the FP32 additions.
 //
-// A CTA computes its tile as 64 x 64 sub-tiles: 256 threads, each 4 x 4 outputs; K in steps of 32
+// A CTA computes its tile as 64 x 64 sub-tiles: 256 threads, each 4 x 4 outputs; K in steps of 64
 // through shared memory (A stored k-major so a thread reads its 4 rows with one 16-byte load),
 // operands loaded with plain zero-filled loads (any leading dimension, any alignment). No
 // spin-waits: only atomics and block barriers.
+//
+// Small problems are a chain of dependent round trips per tile (claim, problem lookup, record,
+// operands, C), so the kernel shortens the chain and keeps more chains in flight: four CTAs per SM;
+// the next tile's claim in flight during the current tile; the lookup guessed in one round trip
+// before any search; the problem record read once into shared memory by one warp; the tables
+// brought into L2 at start; a problem of K <= 64 loaded in one step; C brought into L2 while the
+// operands load; warps whose rows all lie past M skip the FMAs.
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
@@ -27,25 +34,48 @@ namespace {
 
 constexpr int kSimtThreads = 256;
 constexpr int kSub = 64;     // sub-tile edge
-constexpr int kSimtBK = 32;  // K per shared-memory step
+constexpr int kSimtBK = 64;  // K per shared-memory step: a problem of K <= 64 loads in one step
 constexpr int kPad = 4;      // keeps 16-byte alignment of every row, spreads banks
+constexpr int kPerThread = kSub * kSimtBK / kSimtThreads;  // elements of each operand a thread loads per step
+constexpr int kRowStep = kSimtThreads / kSub;                // stored rows between a thread's loads
+static_assert(kSub == kSimtBK && kSimtThreads % kSub == 0, "square operand tiles, whole rows per pass");
 
-// Operand element i widened to FP32, exactly: FP16; BF16 (its bits are the top half of an FP32);
-// E4M3 / E5M2 (one byte per element; every value of both is an FP16 value).
-__device__ __forceinline__ float widen(const __half* x, long long i, int fmt) {
-  if (fmt == GG_INPUT_BF16)
-    return __uint_as_float(static_cast<unsigned>(reinterpret_cast<const unsigned short*>(x)[i]) << 16);
-  if (fmt == GG_INPUT_E4M3 || fmt == GG_INPUT_E5M2) {
-    const __nv_fp8_storage_t v = reinterpret_cast<const unsigned char*>(x)[i];
-    return __half2float(__half(__nv_cvt_fp8_to_halfraw(v, fmt == GG_INPUT_E4M3 ? __NV_E4M3 : __NV_E5M2)));
-  }
-  return __half2float(x[i]);
+// The raw bits of an operand element (two bytes, or one for the 8-bit formats), and their FP32
+// value, exactly: FP16; BF16 (its bits are the top half of an FP32); E4M3 / E5M2 (every value of
+// both is an FP16 value). Split so that a thread can issue all its loads of a K step before it
+// needs the first value. Bits 0 widen to +0 in every format.
+__device__ __forceinline__ unsigned load_bits(const char* x, bool f8) {
+  return f8 ? static_cast<unsigned>(*reinterpret_cast<const unsigned char*>(x))
+            : static_cast<unsigned>(*reinterpret_cast<const unsigned short*>(x));
+}
+
+__device__ __forceinline__ float widen_bits(unsigned v, int fmt) {
+  if (fmt == GG_INPUT_BF16) return __uint_as_float(v << 16);
+  if (fmt == GG_INPUT_E4M3 || fmt == GG_INPUT_E5M2)
+    return __half2float(__half(__nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(v),
+                                                       fmt == GG_INPUT_E4M3 ? __NV_E4M3 : __NV_E5M2)));
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(v)));
 }
 
 // D = act(alpha * acc + (beta * C + bias)) for this thread's 4 x 4 outputs, C and D in format F.
+// Every C and bias value is loaded before the first D store: a D store may alias a later C read
+// as far as the compiler knows, so interleaved they would be one round trip per element.
 template <int F>
 __device__ __forceinline__ void store_block(const DeviceProblemDesc& d, const float* bias, int act, bool read_c,
                                             const float (&acc)[4][4], int r0, int c0) {
+  float add[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int gr = r0 + i;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int gc = c0 + j;
+      const bool in = gr < d.m && gc < d.n;
+      float v = (in && read_c) ? d.beta * load_out<F>(d.c, static_cast<long long>(gr) * d.ldc + gc) : 0.0f;
+      if (bias && in) v += __ldg(bias + gc);
+      add[i][j] = v;
+    }
+  }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int gr = r0 + i;
@@ -54,115 +84,208 @@ __device__ __forceinline__ void store_block(const DeviceProblemDesc& d, const fl
     for (int j = 0; j < 4; ++j) {
       const int gc = c0 + j;
       if (gc >= d.n) continue;
-      float add = read_c ? d.beta * load_out<F>(d.c, static_cast<long long>(gr) * d.ldc + gc) : 0.0f;
-      if (bias) add += __ldg(bias + gc);
-      store_out<F>(d.d, static_cast<long long>(gr) * d.ldd + gc, activate(fmaf(d.alpha, acc[i][j], add), act));
+      store_out<F>(d.d, static_cast<long long>(gr) * d.ldd + gc, activate(fmaf(d.alpha, acc[i][j], add[i][j]), act));
     }
   }
 }
 
-// Last q with offs[q] <= tile (offs has count + 1 entries, offs[count] = total > tile).
-__device__ int find_problem(const int* offs, int count, int tile) {
-  int lo = 0, hi = count;
+// Index q with offs[q] <= tile < offs[q+1] (warp-collective; offs has count + 1 entries and
+// offs[count] = total > tile). One round trip when problem `guess` holds the tile (the caller
+// guesses problem `tile`, right whenever every problem before it has one tile, as small problems
+// do); otherwise a 32-ary search inside the bracket the guess leaves, one round trip per 32x.
+__device__ int find_problem_warp(const int* __restrict__ offs, int count, int tile, int guess, int lane) {
+  guess = min(max(guess, 0), count - 1);
+  const int probe = lane < 2 ? __ldg(offs + guess + lane) : 0;
+  const int g0 = __shfl_sync(0xffffffffu, probe, 0), g1 = __shfl_sync(0xffffffffu, probe, 1);
+  if (g0 <= tile && tile < g1) return guess;
+  int lo = g0 <= tile ? guess : 0, hi = g0 <= tile ? count : guess;  // offs[lo] <= tile < offs[hi]
   while (hi - lo > 1) {
-    const int mid = (lo + hi) >> 1;
-    if (offs[mid] <= tile) lo = mid;
-    else hi = mid;
+    const int step = (hi - lo + 31) >> 5;
+    const int idx = lo + lane * step;
+    const bool le = idx < hi && __ldg(offs + idx) <= tile;
+    const unsigned mask = __ballot_sync(0xffffffffu, le);
+    const int last = mask ? 31 - __clz(static_cast<int>(mask)) : 0;
+    lo += last * step;
+    hi = min(hi, lo + step);
   }
   return lo;
 }
 
-__global__ void __launch_bounds__(kSimtThreads) grouped_gemm_simt_kernel(const __grid_constant__ KernelParams p,
+__global__ void __launch_bounds__(kSimtThreads, 3) grouped_gemm_simt_kernel(const __grid_constant__ KernelParams p,
                                                                         int bm, int bn) {
   __shared__ __align__(16) float As[kSimtBK][kSub + kPad];  // As[k][row]
   __shared__ __align__(16) float Bs[kSimtBK][kSub + kPad];  // Bs[k][col]
+  __shared__ __align__(16) DeviceProblemDesc s_desc;        // the current tile's problem record
   __shared__ int s_work[3];                                 // problem, tile_m, tile_n
 
   const DeviceProblemDesc* problems = p.single_mode ? &p.single_desc : p.problems;
   const int total = p.total_tiles_dev ? *p.total_tiles_dev : p.total_tiles;
   const int tid = static_cast<int>(threadIdx.x);
+  const int lane = tid & 31;
   const int tx = tid & 15, ty = tid >> 4;
   const int in_fmt = p.input_format;
+  const bool f8 = in_fmt == GG_INPUT_E4M3 || in_fmt == GG_INPUT_E5M2;
+  const int eb = f8 ? 1 : 2;  // bytes per A / B element
   const bool a_col = (p.layout & 1) != 0;  // A stored k x m
   const bool b_col = (p.layout & 2) != 0;  // B stored n x k
+  // Warp 0 schedules. Lane 0 keeps one claim in flight (the next tile is claimed when the current
+  // one is handed out, so the atomic's round trip overlaps the tile), and the warp caches the last
+  // problem's tile range so that tiles of the same problem skip the search and the record load.
   int static_next = static_cast<int>(blockIdx.x);
+  int claimed = 0;
+  int cq = -1, cq_first = 0, cq_end = 0, ctm = 0, ctn = 0;  // cached problem, its range and grid
+  if (tid < 32) {
+    if (!p.single_mode && p.problem_count > 0) {
+      // this CTA's share of the problem table and tile offsets, brought into L2 once
+      const long long desc_lines = (static_cast<long long>(p.problem_count) * sizeof(DeviceProblemDesc) + 127) / 128;
+      const long long offs_lines = (static_cast<long long>(p.problem_count + 1) * 4 + 127) / 128;
+      const long long lines = desc_lines + offs_lines;
+      const long long per = (lines + gridDim.x - 1) / gridDim.x;
+      for (long long i = blockIdx.x * per + lane; i < min(lines, (blockIdx.x + 1) * per); i += 32) {
+        const char* line = i < desc_lines ? reinterpret_cast<const char*>(p.problems) + 128 * i
+                                          : reinterpret_cast<const char*>(p.tile_offsets) + 128 * (i - desc_lines);
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(line));
+      }
+    }
+    if (lane == 0) {
+      if (p.single_mode) {
+        claimed = static_next;
+        static_next += static_cast<int>(gridDim.x);
+      } else {
+        claimed = atomicAdd(p.tile_counter, 1);
+      }
+    }
+  }
 
   for (;;) {
-    if (tid == 0) {
+    if (tid < 32) {
       int q = -1, tm = 0, tn = 0;
       for (;;) {
-        int tile;
-        if (p.single_mode) {
-          tile = static_next;
-          static_next += static_cast<int>(gridDim.x);
-        } else {
-          tile = atomicAdd(p.tile_counter, 1);
-        }
+        const int tile = __shfl_sync(0xffffffffu, claimed, 0);
         if (tile >= total) break;
-        const int pq = p.single_mode ? 0 : find_problem(p.tile_offsets, p.problem_count, tile);
-        const int local = tile - (p.single_mode ? 0 : p.tile_offsets[pq]);
-        const int tiles_m = problems[pq].tiles_m, tiles_n = problems[pq].tiles_n;
+        if (lane == 0) {  // the next claim, in flight while this tile is placed and computed
+          if (p.single_mode) {
+            claimed = static_next;
+            static_next += static_cast<int>(gridDim.x);
+          } else {
+            claimed = atomicAdd(p.tile_counter, 1);
+          }
+        }
+        if (!(cq >= 0 && tile >= cq_first && tile < cq_end)) {
+          const int pq = p.single_mode ? 0 : find_problem_warp(p.tile_offsets, p.problem_count, tile, tile, lane);
+          const int w = lane < kDescWords ? reinterpret_cast<const int*>(problems + pq)[lane] : 0;
+          if (lane < kDescWords) reinterpret_cast<int*>(&s_desc)[lane] = w;
+          cq = pq;
+          cq_first = p.single_mode ? 0 : __ldg(p.tile_offsets + pq);
+          cq_end = p.single_mode ? total : __ldg(p.tile_offsets + pq + 1);
+          ctm = __shfl_sync(0xffffffffu, w, static_cast<int>(offsetof(DeviceProblemDesc, tiles_m) / 4));
+          ctn = __shfl_sync(0xffffffffu, w, static_cast<int>(offsetof(DeviceProblemDesc, tiles_n) / 4));
+        }
+        const int local = tile - cq_first;
         // a tile outside its problem's grid (a prepared set inconsistent with the config) is
         // skipped, as the reference kernel does (src/grouped_gemm.cu:662-672)
-        if (local < 0 || tiles_m <= 0 || tiles_n <= 0 || local >= tiles_m * tiles_n) continue;
-        q = pq;
-        tm = local / tiles_n;
-        tn = local % tiles_n;
+        if (local < 0 || ctm <= 0 || ctn <= 0 || local >= ctm * ctn) continue;
+        q = cq;
+        tm = local / ctn;
+        tn = local % ctn;
         break;
       }
-      s_work[0] = q;
-      s_work[1] = tm;
-      s_work[2] = tn;
+      if (lane == 0) {
+        s_work[0] = q;
+        s_work[1] = tm;
+        s_work[2] = tn;
+      }
     }
     __syncthreads();
     const int q = s_work[0], tile_m = s_work[1], tile_n = s_work[2];
-    __syncthreads();  // s_work is rewritten for the next tile only after every thread read it
     if (q < 0) break;
-
-    const DeviceProblemDesc& d = problems[q];
-    const int m = d.m, n = d.n, k = d.k;
-    const __half* a = d.a;
-    const __half* b = d.b;
-    const int lda = d.lda, ldb = d.ldb;
-    const bool read_c = (d.flags & grouped_gemm::kFlagReadC) != 0u;
-    const float* bias = p.bias ? p.bias[d.map_slot] : nullptr;
+    const int m = s_desc.m, n = s_desc.n, k = s_desc.k;
+    const __half* a = s_desc.a;
+    const __half* b = s_desc.b;
+    const int lda = s_desc.lda, ldb = s_desc.ldb;
+    const bool read_c = (s_desc.flags & grouped_gemm::kFlagReadC) != 0u;
+    DeviceProblemDesc d;  // the epilogue's fields
+    d.m = m;
+    d.n = n;
+    d.c = s_desc.c;
+    d.d = s_desc.d;
+    d.ldc = s_desc.ldc;
+    d.ldd = s_desc.ldd;
+    d.alpha = s_desc.alpha;
+    d.beta = s_desc.beta;
+    const float* bias = p.bias ? p.bias[s_desc.map_slot] : nullptr;
+    __syncthreads();  // s_work and s_desc are rewritten for the next tile only after every thread read them
 
     for (int sm = 0; sm < bm; sm += kSub) {
       const int row0 = tile_m * bm + sm;
       if (row0 >= m) break;
+      // rows of this warp's two thread rows (8 rows) past M: it skips the FMAs (it still loads and syncs)
+      const bool warp_rows = row0 + (tid >> 5) * 8 < m;
       for (int sn = 0; sn < bn; sn += kSub) {
         const int col0 = tile_n * bn + sn;
         if (col0 >= n) break;
+        if (read_c) {  // C of this thread's 4 x 4 outputs into L2 while the operands load
+          const int gr = row0 + ty * 4 + (lane & 3), gc = col0 + tx * 4;
+          if (gr < m && gc < n)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(static_cast<const char*>(d.c) +
+                                                          (static_cast<long long>(gr) * d.ldc + gc) *
+                                                              (p.output_format == kOutF32 ? 4 : 2)));
+        }
         float acc[4][4];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
           for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
         for (int k0 = 0; k0 < k; k0 += kSimtBK) {
-          // consecutive threads take consecutive elements of the stored layout (coalesced reads)
-          for (int i = tid; i < kSub * kSimtBK; i += kSimtThreads) {
-            const int r = a_col ? i % kSub : i / kSimtBK, kk = a_col ? i / kSub : i % kSimtBK;
-            const int gr = row0 + r, gk = k0 + kk;
-            const long long ai = a_col ? static_cast<long long>(gk) * lda + gr : static_cast<long long>(gr) * lda + gk;
-            As[kk][r] = (gr < m && gk < k) ? widen(a, ai, in_fmt) : 0.0f;
+          // Consecutive threads take consecutive elements of the stored layout (coalesced reads):
+          // a thread keeps one index along the stored rows (u) and steps 4 rows at a time (o).
+          // Every load of the step is issued before the first value is stored: one round trip.
+          unsigned va[kPerThread], vb[kPerThread];
+          const int u = tid & (kSub - 1), o0 = tid / kSub;
+          {
+            const int outer0 = a_col ? k0 : row0, inner0 = a_col ? row0 : k0;  // stored row, element
+            const int outer_lim = a_col ? k : m;
+            const bool u_ok = inner0 + u < (a_col ? m : k);
+            const char* pa = reinterpret_cast<const char*>(a) +
+                             (static_cast<long long>(outer0 + o0) * lda + inner0 + u) * eb;
+            const long long step = static_cast<long long>(kRowStep) * lda * eb;
+#pragma unroll
+            for (int j = 0; j < kPerThread; ++j)
+              va[j] = (u_ok && outer0 + o0 + kRowStep * j < outer_lim) ? load_bits(pa + j * step, f8) : 0u;
           }
-          for (int i = tid; i < kSimtBK * kSub; i += kSimtThreads) {
-            const int kk = b_col ? i % kSimtBK : i / kSub, c = b_col ? i / kSimtBK : i % kSub;
-            const int gk = k0 + kk, gc = col0 + c;
-            const long long bi = b_col ? static_cast<long long>(gc) * ldb + gk : static_cast<long long>(gk) * ldb + gc;
-            Bs[kk][c] = (gk < k && gc < n) ? widen(b, bi, in_fmt) : 0.0f;
+          {
+            const int outer0 = b_col ? col0 : k0, inner0 = b_col ? k0 : col0;
+            const int outer_lim = b_col ? n : k;
+            const bool u_ok = inner0 + u < (b_col ? k : n);
+            const char* pb = reinterpret_cast<const char*>(b) +
+                             (static_cast<long long>(outer0 + o0) * ldb + inner0 + u) * eb;
+            const long long step = static_cast<long long>(kRowStep) * ldb * eb;
+#pragma unroll
+            for (int j = 0; j < kPerThread; ++j)
+              vb[j] = (u_ok && outer0 + o0 + kRowStep * j < outer_lim) ? load_bits(pb + j * step, f8) : 0u;
+          }
+#pragma unroll
+          for (int j = 0; j < kPerThread; ++j) {
+            const int o = o0 + kRowStep * j;
+            if (a_col) As[o][u] = widen_bits(va[j], in_fmt);
+            else As[u][o] = widen_bits(va[j], in_fmt);
+            if (b_col) Bs[u][o] = widen_bits(vb[j], in_fmt);
+            else Bs[o][u] = widen_bits(vb[j], in_fmt);
           }
           __syncthreads();
+          if (warp_rows) {
+            const int kn = min(kSimtBK, k - k0);  // K values of this step (the rest are zeros)
 #pragma unroll 8
-          for (int kk = 0; kk < kSimtBK; ++kk) {
-            const float4 av = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
-            const float4 bv = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
-            const float ar[4] = {av.x, av.y, av.z, av.w};
-            const float br[4] = {bv.x, bv.y, bv.z, bv.w};
+            for (int kk = 0; kk < kn; ++kk) {
+              const float4 av = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+              const float4 bv = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+              const float ar[4] = {av.x, av.y, av.z, av.w};
+              const float br[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+              for (int i = 0; i < 4; ++i)
 #pragma unroll
-              for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(ar[i], br[j], acc[i][j]);
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(ar[i], br[j], acc[i][j]);
+            }
           }
           __syncthreads();
         }
