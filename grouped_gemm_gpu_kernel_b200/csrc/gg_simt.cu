@@ -44,17 +44,22 @@ static_assert(kSub == kSimtBK && kSimtThreads % kSub == 0, "square operand tiles
 // value, exactly: FP16; BF16 (its bits are the top half of an FP32); E4M3 / E5M2 (every value of
 // both is an FP16 value). Split so that a thread can issue all its loads of a K step before it
 // needs the first value. Bits 0 widen to +0 in every format.
-__device__ __forceinline__ unsigned load_bits(const char* x, bool f8) {
-  return f8 ? static_cast<unsigned>(*reinterpret_cast<const unsigned char*>(x))
-            : static_cast<unsigned>(*reinterpret_cast<const unsigned short*>(x));
+template <int kIn>
+__device__ __forceinline__ unsigned load_bits(const char* x) {
+  if constexpr (kIn == GG_INPUT_E4M3 || kIn == GG_INPUT_E5M2)
+    return static_cast<unsigned>(*reinterpret_cast<const unsigned char*>(x));
+  else
+    return static_cast<unsigned>(*reinterpret_cast<const unsigned short*>(x));
 }
 
-__device__ __forceinline__ float widen_bits(unsigned v, int fmt) {
-  if (fmt == GG_INPUT_BF16) return __uint_as_float(v << 16);
-  if (fmt == GG_INPUT_E4M3 || fmt == GG_INPUT_E5M2)
+template <int kIn>
+__device__ __forceinline__ float widen_bits(unsigned v) {
+  if constexpr (kIn == GG_INPUT_BF16) return __uint_as_float(v << 16);
+  else if constexpr (kIn == GG_INPUT_E4M3 || kIn == GG_INPUT_E5M2)
     return __half2float(__half(__nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(v),
-                                                       fmt == GG_INPUT_E4M3 ? __NV_E4M3 : __NV_E5M2)));
-  return __half2float(__ushort_as_half(static_cast<unsigned short>(v)));
+                                                       kIn == GG_INPUT_E4M3 ? __NV_E4M3 : __NV_E5M2)));
+  else
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(v)));
 }
 
 // D = act(alpha * acc + (beta * C + bias)) for this thread's 4 x 4 outputs, C and D in format F.
@@ -111,8 +116,10 @@ __device__ int find_problem_warp(const int* __restrict__ offs, int count, int ti
   return lo;
 }
 
+// kIn: the input format (GG_INPUT_*), one instantiation each.
+template <int kIn>
 __global__ void __launch_bounds__(kSimtThreads, 3) grouped_gemm_simt_kernel(const __grid_constant__ KernelParams p,
-                                                                        int bm, int bn) {
+                                                                           int bm, int bn) {
   __shared__ __align__(16) float As[kSimtBK][kSub + kPad];  // As[k][row]
   __shared__ __align__(16) float Bs[kSimtBK][kSub + kPad];  // Bs[k][col]
   __shared__ __align__(16) DeviceProblemDesc s_desc;        // the current tile's problem record
@@ -122,10 +129,13 @@ __global__ void __launch_bounds__(kSimtThreads, 3) grouped_gemm_simt_kernel(cons
   const int total = p.total_tiles_dev ? *p.total_tiles_dev : p.total_tiles;
   const int tid = static_cast<int>(threadIdx.x);
   const int lane = tid & 31;
-  const int tx = tid & 15, ty = tid >> 4;
-  const int in_fmt = p.input_format;
-  const bool f8 = in_fmt == GG_INPUT_E4M3 || in_fmt == GG_INPUT_E5M2;
-  const int eb = f8 ? 1 : 2;  // bytes per A / B element
+  // A warp computes a 16-row x 32-column band of the 64 x 64 sub-tile (8 x 4 threads of 4 x 4
+  // outputs), so that it can skip the FMAs when its rows or its columns lie past the problem.
+  const int warp = tid >> 5;
+  const int rb = warp & 3, cb = warp >> 2;  // the warp's row band (16 rows) and column band (32 columns)
+  const int ty = rb * 4 + (lane >> 3);      // rows ty * 4 .. ty * 4 + 3 of the sub-tile
+  const int tx = cb * 8 + (lane & 7);       // columns tx * 4 .. tx * 4 + 3
+  constexpr int eb = (kIn == GG_INPUT_E4M3 || kIn == GG_INPUT_E5M2) ? 1 : 2;  // bytes per A / B element
   const bool a_col = (p.layout & 1) != 0;  // A stored k x m
   const bool b_col = (p.layout & 2) != 0;  // B stored n x k
   // Warp 0 schedules. Lane 0 keeps one claim in flight (the next tile is claimed when the current
@@ -219,11 +229,11 @@ __global__ void __launch_bounds__(kSimtThreads, 3) grouped_gemm_simt_kernel(cons
     for (int sm = 0; sm < bm; sm += kSub) {
       const int row0 = tile_m * bm + sm;
       if (row0 >= m) break;
-      // rows of this warp's two thread rows (8 rows) past M: it skips the FMAs (it still loads and syncs)
-      const bool warp_rows = row0 + (tid >> 5) * 8 < m;
       for (int sn = 0; sn < bn; sn += kSub) {
         const int col0 = tile_n * bn + sn;
         if (col0 >= n) break;
+        // the warp's band inside the problem: otherwise it skips the FMAs (it still loads and syncs)
+        const bool warp_active = row0 + rb * 16 < m && col0 + cb * 32 < n;
         if (read_c) {  // C of this thread's 4 x 4 outputs into L2 while the operands load
           const int gr = row0 + ty * 4 + (lane & 3), gc = col0 + tx * 4;
           if (gr < m && gc < n)
@@ -240,41 +250,54 @@ __global__ void __launch_bounds__(kSimtThreads, 3) grouped_gemm_simt_kernel(cons
           // Consecutive threads take consecutive elements of the stored layout (coalesced reads):
           // a thread keeps one index along the stored rows (u) and steps 4 rows at a time (o).
           // Every load of the step is issued before the first value is stored: one round trip.
+          // Stored rows past the operand's edge, and warps whose 32 elements all lie past it, are
+          // neither loaded nor stored: those shared-memory rows and columns feed only outputs
+          // that are never written (rows past M, columns past N) or K values the FMA loop does
+          // not reach, whatever they hold.
           unsigned va[kPerThread], vb[kPerThread];
           const int u = tid & (kSub - 1), o0 = tid / kSub;
+          int na, nb;  // stored rows this thread loads, in steps of kRowStep
           {
             const int outer0 = a_col ? k0 : row0, inner0 = a_col ? row0 : k0;  // stored row, element
-            const int outer_lim = a_col ? k : m;
-            const bool u_ok = inner0 + u < (a_col ? m : k);
+            const int outer_lim = a_col ? k : m, inner_lim = a_col ? m : k;
+            const int rows = outer_lim - outer0 - o0;
+            na = (rows <= 0 || inner0 + (u & ~31) >= inner_lim) ? 0 : min(kPerThread, (rows + kRowStep - 1) / kRowStep);
+            const bool u_ok = inner0 + u < inner_lim;
             const char* pa = reinterpret_cast<const char*>(a) +
                              (static_cast<long long>(outer0 + o0) * lda + inner0 + u) * eb;
             const long long step = static_cast<long long>(kRowStep) * lda * eb;
 #pragma unroll
-            for (int j = 0; j < kPerThread; ++j)
-              va[j] = (u_ok && outer0 + o0 + kRowStep * j < outer_lim) ? load_bits(pa + j * step, f8) : 0u;
+            for (int j = 0; j < kPerThread; ++j) va[j] = (u_ok && j < na) ? load_bits<kIn>(pa + j * step) : 0u;
           }
           {
             const int outer0 = b_col ? col0 : k0, inner0 = b_col ? k0 : col0;
-            const int outer_lim = b_col ? n : k;
-            const bool u_ok = inner0 + u < (b_col ? k : n);
+            const int outer_lim = b_col ? n : k, inner_lim = b_col ? k : n;
+            const int rows = outer_lim - outer0 - o0;
+            nb = (rows <= 0 || inner0 + (u & ~31) >= inner_lim) ? 0 : min(kPerThread, (rows + kRowStep - 1) / kRowStep);
+            const bool u_ok = inner0 + u < inner_lim;
             const char* pb = reinterpret_cast<const char*>(b) +
                              (static_cast<long long>(outer0 + o0) * ldb + inner0 + u) * eb;
             const long long step = static_cast<long long>(kRowStep) * ldb * eb;
 #pragma unroll
-            for (int j = 0; j < kPerThread; ++j)
-              vb[j] = (u_ok && outer0 + o0 + kRowStep * j < outer_lim) ? load_bits(pb + j * step, f8) : 0u;
+            for (int j = 0; j < kPerThread; ++j) vb[j] = (u_ok && j < nb) ? load_bits<kIn>(pb + j * step) : 0u;
           }
 #pragma unroll
           for (int j = 0; j < kPerThread; ++j) {
+            if (j >= na) break;
             const int o = o0 + kRowStep * j;
-            if (a_col) As[o][u] = widen_bits(va[j], in_fmt);
-            else As[u][o] = widen_bits(va[j], in_fmt);
-            if (b_col) Bs[u][o] = widen_bits(vb[j], in_fmt);
-            else Bs[o][u] = widen_bits(vb[j], in_fmt);
+            if (a_col) As[o][u] = widen_bits<kIn>(va[j]);
+            else As[u][o] = widen_bits<kIn>(va[j]);
+          }
+#pragma unroll
+          for (int j = 0; j < kPerThread; ++j) {
+            if (j >= nb) break;
+            const int o = o0 + kRowStep * j;
+            if (b_col) Bs[u][o] = widen_bits<kIn>(vb[j]);
+            else Bs[o][u] = widen_bits<kIn>(vb[j]);
           }
           __syncthreads();
-          if (warp_rows) {
-            const int kn = min(kSimtBK, k - k0);  // K values of this step (the rest are zeros)
+          if (warp_active) {
+            const int kn = min(kSimtBK, k - k0);  // K values of this step
 #pragma unroll 8
             for (int kk = 0; kk < kn; ++kk) {
               const float4 av = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
@@ -308,24 +331,38 @@ cudaError_t simt_resident_ctas(int* ctas) {
   cudaError_t st = cudaGetDevice(&dev);
   if (st == cudaSuccess) st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (st == cudaSuccess)
-    st = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, grouped_gemm_simt_kernel, kSimtThreads, 0);
+    st = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, grouped_gemm_simt_kernel<GG_INPUT_F16>, kSimtThreads,
+                                                       0);
   if (st != cudaSuccess) return st;
   *ctas = sms * (per_sm > 0 ? per_sm : 1);
   return cudaSuccess;
 }
 
 cudaError_t simt_occupancy(int* active_blocks_per_sm, cudaFuncAttributes* attrs) {
-  cudaError_t st = cudaFuncGetAttributes(attrs, grouped_gemm_simt_kernel);
+  cudaError_t st = cudaFuncGetAttributes(attrs, grouped_gemm_simt_kernel<GG_INPUT_F16>);
   if (st != cudaSuccess) return st;
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(active_blocks_per_sm, grouped_gemm_simt_kernel, kSimtThreads,
-                                                       0);
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(active_blocks_per_sm, grouped_gemm_simt_kernel<GG_INPUT_F16>,
+                                                       kSimtThreads, 0);
 }
 
 int simt_threads() { return kSimtThreads; }
 
 cudaError_t launch_simt_kernel(Variant v, const KernelParams& params, int grid, cudaStream_t stream) {
   if (grid <= 0) return cudaSuccess;
-  grouped_gemm_simt_kernel<<<grid, kSimtThreads, 0, stream>>>(params, variant_bm(v), variant_bn(v));
+  switch (params.input_format) {
+    case GG_INPUT_BF16:
+      grouped_gemm_simt_kernel<GG_INPUT_BF16><<<grid, kSimtThreads, 0, stream>>>(params, variant_bm(v), variant_bn(v));
+      break;
+    case GG_INPUT_E4M3:
+      grouped_gemm_simt_kernel<GG_INPUT_E4M3><<<grid, kSimtThreads, 0, stream>>>(params, variant_bm(v), variant_bn(v));
+      break;
+    case GG_INPUT_E5M2:
+      grouped_gemm_simt_kernel<GG_INPUT_E5M2><<<grid, kSimtThreads, 0, stream>>>(params, variant_bm(v), variant_bn(v));
+      break;
+    default:
+      grouped_gemm_simt_kernel<GG_INPUT_F16><<<grid, kSimtThreads, 0, stream>>>(params, variant_bm(v), variant_bn(v));
+      break;
+  }
   return cudaGetLastError();
 }
 
