@@ -52,7 +52,7 @@ ROW_WORKLOADS = ("moe", "skew", "tiny4096", "small16")  # driver-timed beside th
 # Tile classes (gg_config.tile_classes): the two large workloads with CTA-pair blocks + one-CTA rows
 # (1), tiny4096 with its small problems on the CUDA-core kernel (2)
 CLASS_ROWS = {"moe_pair_classes": ("moe", 1), "skew_pair_classes": ("skew", 1),
-              "tiny4096_small_on_cuda_cores": ("tiny4096", 2)}
+              "tiny4096_small_on_cuda_cores": ("tiny4096", 2), "small16_small_on_cuda_cores": ("small16", 2)}
 STRONG_WORKLOADS = ("skew", "moe")  # one fixed global set split over the N ranks
 
 

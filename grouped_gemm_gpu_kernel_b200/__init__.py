@@ -63,8 +63,10 @@ class Layout(enum.IntEnum):
 class TileClasses(enum.IntEnum):
     """How an executor tiles its problems (GG_TILE_CLASSES_*): one tile shape for every problem (the
     reference's); with a CTA-pair config, whole 256-row blocks on CTA pairs and the rows left over
-    on one-CTA 128-row tiles, as two launches that may overlap; or problems with m, n, k all at
-    most capi.GG_SMALL_PROBLEM_DIM on the CUDA-core kernel and the rest on the tensor cores."""
+    on one-CTA 128-row tiles, as two launches that may overlap; or, on the CUDA-core kernel with
+    64 x 64 tiles, the problems with m, n, k all at most capi.GG_SMALL_PROBLEM_DIM and those of at
+    most capi.GG_SMALL_ZERO_FILL_VOLUME multiply-adds whose A or B TMA cannot load, the rest on the
+    tensor cores."""
     kNone = capi.GG_TILE_CLASSES_NONE
     kPairBlocks = capi.GG_TILE_CLASSES_PAIR_BLOCKS
     kSmallOnCudaCores = capi.GG_TILE_CLASSES_SMALL_ON_CUDA_CORES

@@ -45,6 +45,7 @@ GG_TILE_CLASSES_NONE = 0
 GG_TILE_CLASSES_PAIR_BLOCKS = 1
 GG_TILE_CLASSES_SMALL_ON_CUDA_CORES = 2
 GG_SMALL_PROBLEM_DIM = 64
+GG_SMALL_ZERO_FILL_VOLUME = 1 << 25
 GG_NOALLOC_MAX_PROBLEMS = 1024
 
 GG_STATUS_TIMEOUT_PRODUCER = 0x1

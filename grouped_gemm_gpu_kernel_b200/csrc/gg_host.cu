@@ -594,15 +594,23 @@ int gg_executor_build_with_bias(gg_executor* ex, const gg_problem* sorted_proble
   bool part_tc[2] = {ex->use_tc, ex->use_tc};
   int parts = 1;
   if (config->tile_classes == GG_TILE_CLASSES_SMALL_ON_CUDA_CORES) {
-    // Problems no larger than GG_SMALL_PROBLEM_DIM in m, n and k on the CUDA-core kernel (several
-    // CTAs per SM hide their latency better), the others on the tensor cores; same tile shape.
+    // On the CUDA-core kernel, with its own 64 x 64 tiles (several CTAs per SM hide the latency of
+    // short problems): problems no larger than GG_SMALL_PROBLEM_DIM in m, n and k, and problems of
+    // at most GG_SMALL_ZERO_FILL_VOLUME multiply-adds whose A or B TMA cannot load (the tensor
+    // cores would fill their stages with the zero-fill loader). The others on the tensor cores.
     parts = 2;
     img[0].variant = v;
-    img[1].variant = v;
+    img[1].variant = gg::Variant::k64x64;
     part_tc[1] = false;
+    CUtensorMap scratch[gg::kMapsPerProblem];
     for (int i = 0; i < count; ++i) {
       const gg_problem& p = sorted_problems[i];
-      const bool small = p.m <= GG_SMALL_PROBLEM_DIM && p.n <= GG_SMALL_PROBLEM_DIM && p.k <= GG_SMALL_PROBLEM_DIM;
+      bool small = p.m <= GG_SMALL_PROBLEM_DIM && p.n <= GG_SMALL_PROBLEM_DIM && p.k <= GG_SMALL_PROBLEM_DIM;
+      if (!small && p.m > 0 && p.n > 0 && p.k > 0 &&
+          static_cast<long long>(p.m) * p.n * p.k <= GG_SMALL_ZERO_FILL_VOLUME) {
+        const DeviceProblemDesc d = gg::make_device_problem(p, v, config, scratch, 0);
+        small = (d.flags & grouped_gemm::kFlagTmaAB) == 0u;
+      }
       gg::add_problem(img[small ? 1 : 0], p, config, bias ? bias[i] : nullptr);
     }
   } else if (config->tile_classes == GG_TILE_CLASSES_PAIR_BLOCKS) {
@@ -706,15 +714,20 @@ int gg_executor_run(const gg_executor* ex, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t st = cudaMemsetAsync(ex->d_counters, 0, 2 * sizeof(int), s);
   if (st != cudaSuccess) return st;
-  bool after_pair = false;
+  bool after_tc = false;  // a tensor-core part was launched before this one
   for (int j = 0; j < ex->parts; ++j) {
     const gg::Part& pt = ex->part[j];
     if (pt.total_tiles <= 0) continue;
-    // The one-CTA part of a tile-class split may start while the pair part still runs.
-    st = after_pair ? gg::launch_grouped_kernel(pt.variant, pt.params, pt.grid, s, true)
-                    : gg::launch_path(pt.use_tc, pt.variant, pt.params, pt.grid, s);
+    // The second part of a tile-class split (one-CTA rows after the pair blocks, or the small
+    // problems on the CUDA cores) may start on the SMs the first part leaves free: the parts write
+    // disjoint outputs and count tiles on their own counters.
+    if (after_tc)
+      st = pt.use_tc ? gg::launch_grouped_kernel(pt.variant, pt.params, pt.grid, s, true)
+                     : gg::launch_simt_kernel(pt.variant, pt.params, pt.grid, s, true);
+    else
+      st = gg::launch_path(pt.use_tc, pt.variant, pt.params, pt.grid, s);
     if (st != cudaSuccess) return st;
-    after_pair = gg::variant_is_pair(pt.variant);
+    after_tc = pt.use_tc;
   }
   return cudaSuccess;
 }

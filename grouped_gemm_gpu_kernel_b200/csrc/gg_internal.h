@@ -50,7 +50,10 @@ unsigned ipc_mapping_generation();
 
 // CUDA-core path (use_tensor_cores = false), gg_simt.cu: same parameters and tile numbering,
 // the variant only fixes the tile shape.
-cudaError_t launch_simt_kernel(Variant v, const KernelParams& params, int grid, cudaStream_t stream);
+// overlap_previous: launched with programmatic stream serialisation, so its CTAs may start on
+// the SMs the previous grid of the stream leaves free (that grid must not produce its inputs).
+cudaError_t launch_simt_kernel(Variant v, const KernelParams& params, int grid, cudaStream_t stream,
+                               bool overlap_previous = false);
 cudaError_t simt_resident_ctas(int* ctas);
 cudaError_t simt_occupancy(int* active_blocks_per_sm, cudaFuncAttributes* attrs);
 int simt_threads();

@@ -854,6 +854,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
   __syncthreads();
   ptx::tc_fence_after_sync();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  // A CUDA-core launch of the same executor may follow (its small problems): it works on other
+  // problems' outputs, so it may take the SMs this grid leaves free.
+  if (threadIdx.x == 0) ptx::launch_dependents();
 
   const DeviceProblemDesc* problems = p.single_mode ? &p.single_desc : p.problems;
   const CUtensorMap* maps = p.single_mode ? p.single_maps : p.tmaps;

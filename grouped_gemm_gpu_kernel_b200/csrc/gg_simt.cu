@@ -347,23 +347,38 @@ cudaError_t simt_occupancy(int* active_blocks_per_sm, cudaFuncAttributes* attrs)
 
 int simt_threads() { return kSimtThreads; }
 
-cudaError_t launch_simt_kernel(Variant v, const KernelParams& params, int grid, cudaStream_t stream) {
+template <int kIn>
+cudaError_t launch_simt(Variant v, const KernelParams& params, int grid, cudaStream_t stream, bool overlap_previous) {
+  if (!overlap_previous) {
+    grouped_gemm_simt_kernel<kIn><<<grid, kSimtThreads, 0, stream>>>(params, variant_bm(v), variant_bn(v));
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(kSimtThreads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, grouped_gemm_simt_kernel<kIn>, params, variant_bm(v), variant_bn(v));
+}
+
+cudaError_t launch_simt_kernel(Variant v, const KernelParams& params, int grid, cudaStream_t stream,
+                               bool overlap_previous) {
   if (grid <= 0) return cudaSuccess;
   switch (params.input_format) {
     case GG_INPUT_BF16:
-      grouped_gemm_simt_kernel<GG_INPUT_BF16><<<grid, kSimtThreads, 0, stream>>>(params, variant_bm(v), variant_bn(v));
-      break;
+      return launch_simt<GG_INPUT_BF16>(v, params, grid, stream, overlap_previous);
     case GG_INPUT_E4M3:
-      grouped_gemm_simt_kernel<GG_INPUT_E4M3><<<grid, kSimtThreads, 0, stream>>>(params, variant_bm(v), variant_bn(v));
-      break;
+      return launch_simt<GG_INPUT_E4M3>(v, params, grid, stream, overlap_previous);
     case GG_INPUT_E5M2:
-      grouped_gemm_simt_kernel<GG_INPUT_E5M2><<<grid, kSimtThreads, 0, stream>>>(params, variant_bm(v), variant_bn(v));
-      break;
+      return launch_simt<GG_INPUT_E5M2>(v, params, grid, stream, overlap_previous);
     default:
-      grouped_gemm_simt_kernel<GG_INPUT_F16><<<grid, kSimtThreads, 0, stream>>>(params, variant_bm(v), variant_bn(v));
-      break;
+      return launch_simt<GG_INPUT_F16>(v, params, grid, stream, overlap_previous);
   }
-  return cudaGetLastError();
 }
 
 }  // namespace gg

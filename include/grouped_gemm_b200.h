@@ -109,12 +109,15 @@ typedef struct gg_problem {
  *   tiles (half the B bytes per SM), and no pair tile is padded past a problem's last row. The
  *   prepared set, its tile offsets and the executor's problem_count / total_tiles keep the config's
  *   256-row tiling. GG_TILE_CLASSES_SMALL_ON_CUDA_CORES, with any tensor-core config: problems
- *   whose m, n and k are all at most GG_SMALL_PROBLEM_DIM run on the CUDA-core kernel (several
- *   CTAs per SM hide the latency of one-tile problems; measured on B200 with L2 flushed, 4096
- *   problems of 1..64: 157 us against 242 us on the tensor cores), the others on the tensor
- *   cores, same tile shape, two launches one after the other. Executors only: the no-allocation
- *   entry point, the per-problem baseline and the mixture-of-experts plan run the config's tile
- *   and path everywhere.
+ *   whose m, n and k are all at most GG_SMALL_PROBLEM_DIM, and problems of at most
+ *   GG_SMALL_ZERO_FILL_VOLUME multiply-adds (m * n * k) whose A or B TMA cannot load (a row pitch
+ *   or base not 16-byte aligned), run on the CUDA-core kernel with 64 x 64 tiles; the others on
+ *   the tensor cores with the config's tile; two launches one after the other. Measured on B200
+ *   with L2 flushed before every run: 4096 problems of 1..64, 76 us against 241 us on the tensor
+ *   cores; 64 problems of 65^3, 20 against 43 us, of 257^3, 136 against 227 us, and 512 of 385^3,
+ *   2.5 against 3.8 ms (odd pitches), while with aligned pitches the tensor cores win from 96^3
+ *   up. Executors only: the no-allocation entry point, the per-problem baseline and the
+ *   mixture-of-experts plan run the config's tile and path everywhere.
  * Any other value of these fields is an invalid config. The C++ API of
  * grouped_gemm/grouped_gemm.cuh keeps the reference's KernelConfig and always passes 0 for all
  * of them. */
@@ -134,6 +137,7 @@ typedef struct gg_problem {
 #define GG_TILE_CLASSES_PAIR_BLOCKS 1
 #define GG_TILE_CLASSES_SMALL_ON_CUDA_CORES 2
 #define GG_SMALL_PROBLEM_DIM 64
+#define GG_SMALL_ZERO_FILL_VOLUME (1LL << 25)
 typedef struct gg_config {
   int cta_m;
   int cta_n;

@@ -366,9 +366,11 @@ def test_tile_classes_match_oracle(cuda, cfg):
                                  gg.KernelConfig(128, 256, 64, tile_classes=gg.TileClasses.kSmallOnCudaCores)],
                          ids=lambda c: f"{c.cta_m}x{c.cta_n}")
 def test_small_problems_on_cuda_cores(cuda, cfg):
-    """Tile class 'small on CUDA cores': problems with m, n, k <= 64 on the CUDA-core kernel, the
-    others on the tensor cores. tiny4096 (all small), small16 (mostly large) and a set mixing both
-    with odd and aligned pitches, every element against the FP64 oracle."""
+    """Tile class 'small on CUDA cores': problems with m, n, k <= 64, and problems of at most
+    2^25 multiply-adds that TMA cannot load (odd pitches), on the CUDA-core kernel with 64 x 64
+    tiles; the others (aligned, or odd and larger) on the tensor cores. tiny4096 (all small),
+    small16 (odd pitches, mostly routed to the CUDA cores) and a set mixing every kind, every
+    element against the FP64 oracle."""
     ps = W.allocate(W.make_shapes("tiny4096"), cuda)
     run_grouped(ps.problems(), cfg, gg.SortMode.kByTiles)
     assert check_full(ps) <= 1.0
@@ -379,6 +381,9 @@ def test_small_problems_on_cuda_cores(cuda, cfg):
     dims = [(int(rng.integers(1, 65)), int(rng.integers(1, 65)), int(rng.integers(1, 65))) for _ in range(200)]
     dims += [(int(8 * rng.integers(8, 40)), int(8 * rng.integers(8, 40)), int(8 * rng.integers(1, 40)))
              for _ in range(40)]
+    dims += [(int(2 * rng.integers(33, 160) + 1), int(2 * rng.integers(33, 160) + 1), int(2 * rng.integers(33, 160) + 1))
+             for _ in range(20)]                      # odd pitches, mostly below the volume bound
+    dims += [(333, 331, 337), (321, 513, 257)]        # odd pitches above it: tensor cores, zero-fill loader
     order = rng.permutation(len(dims))
     shapes = W.Shapes("mixed_small", [dims[i] for i in order], [1.5] * len(dims), [0.25] * len(dims), True)
     ps = W.allocate(shapes, cuda, seed=9)
