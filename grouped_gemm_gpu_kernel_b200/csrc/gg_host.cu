@@ -440,10 +440,19 @@ struct gg_executor {
   int grid_ctas = 0;
   gg::Variant variant = gg::Variant::kUnsupported;
   bool use_tc = true;  // tcgen05 kernel; false: the CUDA-core kernel
+  void* realign_scratch = nullptr;     // 16-byte-aligned copies of operands TMA cannot load
+  const gg::RealignJob* d_jobs = nullptr;  // in `block`: the copies each run makes first
+  int realign_jobs = 0;
+  long long realign_max_units = 0;  // most 16-byte chunks of one copy
 
   void release() {
     if (block) cudaFree(block);
+    if (realign_scratch) cudaFree(realign_scratch);
     block = nullptr;
+    realign_scratch = nullptr;
+    d_jobs = nullptr;
+    realign_jobs = 0;
+    realign_max_units = 0;
     d_counters = nullptr;
     d_status = nullptr;
     parts = 0;
@@ -593,25 +602,86 @@ int gg_executor_build_with_bias(gg_executor* ex, const gg_problem* sorted_proble
   gg::PartImage img[2];
   bool part_tc[2] = {ex->use_tc, ex->use_tc};
   int parts = 1;
+  std::vector<gg::RealignJob> jobs;
   if (config->tile_classes == GG_TILE_CLASSES_SMALL_ON_CUDA_CORES) {
     // On the CUDA-core kernel, with its own 64 x 64 tiles (several CTAs per SM hide the latency of
     // short problems): problems no larger than GG_SMALL_PROBLEM_DIM in m, n and k, and problems of
     // at most GG_SMALL_ZERO_FILL_VOLUME multiply-adds whose A or B TMA cannot load (the tensor
-    // cores would fill their stages with the zero-fill loader). The others on the tensor cores.
+    // cores would fill their stages with the zero-fill loader). The others on the tensor cores;
+    // of those, an A or B that TMA cannot load (base or row pitch not 16-byte aligned) is copied
+    // by every run into a scratch matrix with 16-byte-aligned rows, which the tensor cores load
+    // by TMA (one HBM-bound copy instead of the zero-fill loader).
     parts = 2;
     img[0].variant = v;
     img[1].variant = gg::Variant::k64x64;
     part_tc[1] = false;
     CUtensorMap scratch[gg::kMapsPerProblem];
+    const int eb = gg::in_geom(config->input_type).bytes;
+    const bool a_col = config->a_layout == GG_LAYOUT_COL_MAJOR, b_col = config->b_layout == GG_LAYOUT_COL_MAJOR;
+    // An operand the realignment can copy: fewer than 2^31 16-byte chunks (32 GB).
+    auto tma_ok = [&](const void* base, int ld) {
+      return gg::aligned16(base) && (static_cast<long long>(ld) * eb) % 16 == 0;
+    };
+    auto copyable = [&](int rows, int cols) {
+      return static_cast<long long>(rows) * ((static_cast<long long>(cols) * eb + 15) / 16) < (1LL << 31);
+    };
+    std::vector<int> klass(count, 0);  // 0 tensor cores, 1 CUDA cores, 2 tensor cores on realigned copies
+    size_t scratch_bytes = 0;
     for (int i = 0; i < count; ++i) {
       const gg_problem& p = sorted_problems[i];
+      const bool has_work = p.m > 0 && p.n > 0 && p.k > 0;
       bool small = p.m <= GG_SMALL_PROBLEM_DIM && p.n <= GG_SMALL_PROBLEM_DIM && p.k <= GG_SMALL_PROBLEM_DIM;
-      if (!small && p.m > 0 && p.n > 0 && p.k > 0 &&
-          static_cast<long long>(p.m) * p.n * p.k <= GG_SMALL_ZERO_FILL_VOLUME) {
+      if (!small && has_work && static_cast<long long>(p.m) * p.n * p.k <= GG_SMALL_ZERO_FILL_VOLUME) {
         const DeviceProblemDesc d = gg::make_device_problem(p, v, config, scratch, 0);
         small = (d.flags & grouped_gemm::kFlagTmaAB) == 0u;
       }
-      gg::add_problem(img[small ? 1 : 0], p, config, bias ? bias[i] : nullptr);
+      if (small) {
+        klass[i] = 1;
+        continue;
+      }
+      if (!has_work || (tma_ok(p.a, p.lda) && tma_ok(p.b, p.ldb))) continue;
+      if (!copyable(a_col ? p.k : p.m, a_col ? p.m : p.k) || !copyable(b_col ? p.n : p.k, b_col ? p.k : p.n)) continue;
+      klass[i] = 2;
+      if (!tma_ok(p.a, p.lda)) {
+        const long long row_bytes = static_cast<long long>(a_col ? p.m : p.k) * eb;
+        scratch_bytes += gg::round_up(static_cast<size_t>((a_col ? p.k : p.m) * gg::round_up(row_bytes, 16)), 256);
+      }
+      if (!tma_ok(p.b, p.ldb)) {
+        const long long row_bytes = static_cast<long long>(b_col ? p.k : p.n) * eb;
+        scratch_bytes += gg::round_up(static_cast<size_t>((b_col ? p.n : p.k) * gg::round_up(row_bytes, 16)), 256);
+      }
+    }
+    if (scratch_bytes > 0) {
+      const cudaError_t st = cudaMalloc(&ex->realign_scratch, scratch_bytes);
+      if (st != cudaSuccess) {
+        ex->realign_scratch = nullptr;
+        return st;
+      }
+    }
+    unsigned char* next = static_cast<unsigned char*>(ex->realign_scratch);
+    // One operand into the scratch: returns its copy and sets the copy's pitch in elements.
+    auto realign = [&](const void* src, int ld, int rows, int cols, int* new_ld) -> const void* {
+      const long long row_bytes = static_cast<long long>(cols) * eb;
+      const long long pitch = static_cast<long long>(gg::round_up(static_cast<size_t>(row_bytes), 16));
+      gg::RealignJob j{};
+      j.src = static_cast<const unsigned char*>(src);
+      j.dst = next;
+      j.src_pitch = static_cast<long long>(ld) * eb;
+      j.dst_pitch = pitch;
+      j.rows = rows;
+      j.row_bytes = static_cast<int>(row_bytes);
+      jobs.push_back(j);
+      next += gg::round_up(static_cast<size_t>(rows * pitch), 256);
+      *new_ld = static_cast<int>(pitch / eb);
+      return j.dst;
+    };
+    for (int i = 0; i < count; ++i) {
+      gg_problem p = sorted_problems[i];
+      if (klass[i] == 2) {
+        if (!tma_ok(p.a, p.lda)) p.a = realign(p.a, p.lda, a_col ? p.k : p.m, a_col ? p.m : p.k, &p.lda);
+        if (!tma_ok(p.b, p.ldb)) p.b = realign(p.b, p.ldb, b_col ? p.n : p.k, b_col ? p.k : p.n, &p.ldb);
+      }
+      gg::add_problem(img[klass[i] == 1 ? 1 : 0], p, config, bias ? bias[i] : nullptr);
     }
   } else if (config->tile_classes == GG_TILE_CLASSES_PAIR_BLOCKS) {
     parts = 2;
@@ -646,7 +716,10 @@ int gg_executor_build_with_bias(gg_executor* ex, const gg_problem* sorted_proble
   }
   const size_t counter_off = gg::round_up(bytes, 128);
   bytes = counter_off + 128;  // counters at +0 (one int per part), status word at +64
+  const size_t jobs_off = bytes;
+  bytes += jobs.size() * sizeof(gg::RealignJob);
   std::vector<unsigned char> image(bytes, 0);
+  if (!jobs.empty()) std::memcpy(image.data() + jobs_off, jobs.data(), jobs.size() * sizeof(gg::RealignJob));
   for (int j = 0; j < parts; ++j) {
     const gg::PartImage& im = img[j];
     if (!im.maps.empty()) std::memcpy(image.data() + off[j].maps, im.maps.data(), im.maps.size() * sizeof(CUtensorMap));
@@ -673,6 +746,7 @@ int gg_executor_build_with_bias(gg_executor* ex, const gg_problem* sorted_proble
   cudaError_t st = cudaMalloc(&ex->block, bytes);
   if (st != cudaSuccess) {
     ex->block = nullptr;
+    ex->release();
     return st;
   }
   st = cudaMemcpy(ex->block, image.data(), bytes, cudaMemcpyHostToDevice);
@@ -683,6 +757,10 @@ int gg_executor_build_with_bias(gg_executor* ex, const gg_problem* sorted_proble
   unsigned char* base = static_cast<unsigned char*>(ex->block);
   ex->d_counters = reinterpret_cast<int*>(base + counter_off);
   ex->d_status = reinterpret_cast<int*>(base + counter_off + 64);
+  ex->d_jobs = reinterpret_cast<const gg::RealignJob*>(base + jobs_off);
+  ex->realign_jobs = static_cast<int>(jobs.size());
+  for (const gg::RealignJob& j : jobs)
+    ex->realign_max_units = std::max(ex->realign_max_units, static_cast<long long>(j.rows) * ((j.row_bytes + 15) / 16));
   for (int j = 0; j < parts; ++j) {
     gg::KernelParams& kp = part[j].params;
     std::memset(&kp, 0, sizeof(kp));
@@ -713,6 +791,9 @@ int gg_executor_run(const gg_executor* ex, void* stream) {
   if (!ex->block) return cudaErrorInvalidDevicePointer;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t st = cudaMemsetAsync(ex->d_counters, 0, 2 * sizeof(int), s);
+  if (st != cudaSuccess) return st;
+  // this run's copies of the operands TMA cannot load, before the tensor-core part reads them
+  st = gg::launch_realign(ex->d_jobs, ex->realign_jobs, ex->realign_max_units, s);
   if (st != cudaSuccess) return st;
   bool after_tc = false;  // a tensor-core part was launched before this one
   for (int j = 0; j < ex->parts; ++j) {

@@ -50,6 +50,22 @@ unsigned ipc_mapping_generation();
 
 // CUDA-core path (use_tensor_cores = false), gg_simt.cu: same parameters and tile numbering,
 // the variant only fixes the tile shape.
+// One operand copied into a 16-byte-aligned scratch matrix so that TMA can load it: `rows` rows of
+// `row_bytes` bytes, from `src` (any alignment, pitch src_pitch bytes) to `dst` (16-byte aligned,
+// pitch dst_pitch bytes, a multiple of 16).
+struct RealignJob {
+  const unsigned char* src;
+  unsigned char* dst;
+  long long src_pitch;
+  long long dst_pitch;
+  int rows;
+  int row_bytes;
+};
+
+// Runs every job of the device array `jobs` in one launch on `stream` (max_units: the most
+// 16-byte destination chunks of any job, which sizes the grid).
+cudaError_t launch_realign(const RealignJob* jobs, int count, long long max_units, cudaStream_t stream);
+
 // overlap_previous: launched with programmatic stream serialisation, so its CTAs may start on
 // the SMs the previous grid of the stream leaves free (that grid must not produce its inputs).
 cudaError_t launch_simt_kernel(Variant v, const KernelParams& params, int grid, cudaStream_t stream,

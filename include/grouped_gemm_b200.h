@@ -112,7 +112,11 @@ typedef struct gg_problem {
  *   whose m, n and k are all at most GG_SMALL_PROBLEM_DIM, and problems of at most
  *   GG_SMALL_ZERO_FILL_VOLUME multiply-adds (m * n * k) whose A or B TMA cannot load (a row pitch
  *   or base not 16-byte aligned), run on the CUDA-core kernel with 64 x 64 tiles; the others on
- *   the tensor cores with the config's tile; two launches one after the other. Measured on B200
+ *   the tensor cores with the config's tile, where an A or B that TMA cannot load is copied by
+ *   every run, before the tensor-core launch, into a scratch matrix with 16-byte-aligned rows
+ *   that the executor allocates at build time (rows x the row's bytes rounded up to 16, per
+ *   such operand) and loaded from there by TMA (D is bit-identical to the zero-fill loader's).
+ *   The CUDA-core launch starts on the SMs the tensor-core launch leaves free. Measured on B200
  *   with L2 flushed before every run: 4096 problems of 1..64, 76 us against 241 us on the tensor
  *   cores; 64 problems of 65^3, 20 against 43 us, of 257^3, 136 against 227 us, and 512 of 385^3,
  *   2.5 against 3.8 ms (odd pitches), while with aligned pitches the tensor cores win from 96^3

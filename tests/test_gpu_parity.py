@@ -393,6 +393,32 @@ def test_small_problems_on_cuda_cores(cuda, cfg):
         assert check_full(ps) <= 1.0
 
 
+@pytest.mark.parametrize("fmt", [0, 1], ids=["fp16", "bf16"])
+def test_small_class_realigns_large_odd_pitches(cuda, fmt):
+    """Tile class 'small on CUDA cores', problems above 2^25 multiply-adds whose A or B TMA cannot
+    load (packed odd pitches): each run copies those operands into 16-byte-aligned scratch and
+    the tensor cores load the copies by TMA. The tensor cores compute the same MMAs in the same
+    order as with the zero-fill loader (the class off), so D is bit-identical; and every element
+    against the FP64 oracle. A only, B only and both misaligned."""
+    torch = _torch()
+    dims = [(321, 333, 345), (333, 320, 345), (333, 321, 344), (512, 264, 300), (300, 1000, 129)]
+    assert all(m * n * k > capi.GG_SMALL_ZERO_FILL_VOLUME for m, n, k in dims)
+    shapes = W.Shapes("odd_large", dims, [1.25] * len(dims), [0.5] * len(dims), True)
+    ps = W.allocate(shapes, cuda, seed=11)
+    if fmt == 1:
+        ps = ps.to_bf16()
+    outs = []
+    for classes in (gg.TileClasses.kNone, gg.TileClasses.kSmallOnCudaCores):
+        ps.d.fill_(float("nan"))
+        run_grouped(ps.problems(), gg.KernelConfig(128, 256, 64, input_type=fmt, tile_classes=classes),
+                    gg.SortMode.kByTiles)
+        torch.cuda.synchronize()
+        outs.append(ps.d.clone())
+    # bit patterns (the NaN fill stays in the slab's padding between problems)
+    assert torch.equal(outs[0].view(torch.int32), outs[1].view(torch.int32))
+    assert check_full(ps, fmt=fmt) <= 1.0
+
+
 def test_determinism_bitwise(cuda):
     torch = _torch()
     ps = W.allocate(W.make_shapes("mixed512"), cuda)
