@@ -304,8 +304,7 @@ int gg_selftest_wait_timeout_word(int word, unsigned long long timeout_ns);
  * loads the library until the process exits). The caller still provides A, B, C and D.
  *   - At most GG_NOALLOC_MAX_PROBLEMS problems; more returns cudaErrorMemoryAllocation (2) and
  *     launches nothing. Other errors as for gg_run_grouped_gemm_once.
- *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress);
- *     make that first call before any stream capture.
+ *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress).
  *   - Every call uses the same array and it keeps the last call's contents (the tile counter
  *     and status word are cleared by each call). Calls whose work overlaps on the GPU -- on two
  *     streams, or from two host threads on different streams -- race on it: order them on one
