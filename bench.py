@@ -86,6 +86,11 @@ def parse_args():
                     help="N>1: after the timed region, gather every rank's D to rank 0 over NCCL and fused into "
                          "the kernel, and time both (the default at N>1 for the reference's FP32 output)")
     ap.add_argument("--no-gather", action="store_true", help="N>1: skip the gather rows")
+    ap.add_argument("--tile-classes", type=int, choices=[0, 1, 2], default=0,
+                    help="gg_config.tile_classes of the headline executor: 0 one tile shape (the reference's), "
+                         "1 CTA-pair blocks + one-CTA rows (pair --cta), 2 small problems on the CUDA cores")
+    ap.add_argument("--cuda-cores", action="store_true",
+                    help="headline executor on the CUDA-core kernel (the reference's use_tensor_cores = false)")
     ap.add_argument("--no-rows", action="store_true",
                     help="skip the per-workload rows (N=1) and the strong-scaling rows (every N)")
     return ap.parse_args()
@@ -451,8 +456,9 @@ def main():
     in_type = {"f16": 0, "bf16": 1, "e4m3": 2, "e5m2": 3}[args.input_type]
     a_col, b_col = args.a_layout == "col", args.b_layout == "col"
     cfg = gg.KernelConfig(*cta, input_type=in_type, output_type=out_type, activation=act, a_layout=int(a_col),
-                          b_layout=int(b_col))
-    plain = out_type == 0 and act == 0 and not args.bias and args.input_type == "f16" and not (a_col or b_col)
+                          b_layout=int(b_col), use_tensor_cores=not args.cuda_cores, tile_classes=args.tile_classes)
+    plain = (out_type == 0 and act == 0 and not args.bias and args.input_type == "f16" and not (a_col or b_col)
+             and args.tile_classes == 0 and not args.cuda_cores)
     shapes, global_flops, rank_weights = rank_shapes(args.workload, world, rank, cfg)
 
     def make_set():
@@ -704,6 +710,8 @@ def main():
                               "step, each step timed alone"),
                        "accumulate": "f32", "output_type": args.output_type, "activation": args.activation,
                        "bias": bool(args.bias), "a_layout": args.a_layout, "b_layout": args.b_layout,
+                       "tile_classes": args.tile_classes,
+                       "path": "cuda_cores" if args.cuda_cores else "tensor_cores",
                        "prep_build_ms": prep_ms, "parallelism": f"dp{world} (tile-balanced shards)",
                        "tail_work_share": tail_share,
                        "rank_weight_max_over_mean": max(rank_weights) / (sum(rank_weights) / len(rank_weights))},
@@ -714,7 +722,7 @@ def main():
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clock_info,
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * ex.launches(),
         }
         line.update(extras)
         print(json.dumps(line), flush=True)

@@ -297,6 +297,10 @@ class GroupedGemmExecutor:
     def grid_ctas(self) -> int:
         return self._lib.gg_executor_grid_ctas(self._h)
 
+    def launches(self) -> int:
+        """Kernel launches of one run (1 without tile classes)."""
+        return self._lib.gg_executor_launches(self._h)
+
 
 def run_grouped_gemm_once(problems: Sequence[ProblemDesc], sort_mode: int, config: KernelConfig, stream=None) -> int:
     cfg = config.to_c()

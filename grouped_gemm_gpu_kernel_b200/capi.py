@@ -17,7 +17,8 @@ EXPORTED_SYMBOLS = (
     "gg_abi_version", "gg_sort_mode_name", "gg_tile_count", "gg_prepare", "gg_query_occupancy",
     "gg_executor_create", "gg_executor_destroy", "gg_executor_build", "gg_executor_build_with_bias",
     "gg_executor_run",
-    "gg_executor_problem_count", "gg_executor_total_tiles", "gg_executor_grid_ctas", "gg_executor_status",
+    "gg_executor_problem_count", "gg_executor_total_tiles", "gg_executor_grid_ctas", "gg_executor_launches",
+    "gg_executor_status",
     "gg_run_grouped_gemm_once", "gg_run_baseline_per_problem", "gg_count_non_empty_problems",
     "gg_partition", "gg_selftest_wait_timeout", "gg_run_grouped_gemm_noalloc", "gg_copy_rects",
     "gg_baseline_status", "gg_noalloc_status", "gg_selftest_wait_timeout_word",
@@ -137,6 +138,7 @@ def load() -> ctypes.CDLL:
         "gg_executor_problem_count": ([vp], ctypes.c_int),
         "gg_executor_total_tiles": ([vp], ctypes.c_int),
         "gg_executor_grid_ctas": ([vp], ctypes.c_int),
+        "gg_executor_launches": ([vp], ctypes.c_int),
         "gg_executor_status": ([vp, i32p], ctypes.c_int),
         "gg_run_grouped_gemm_once": ([pp, ctypes.c_int, ctypes.c_int, pc, vp], ctypes.c_int),
         "gg_run_baseline_per_problem": ([pp, ctypes.c_int, pc, vp], ctypes.c_int),

@@ -816,6 +816,12 @@ int gg_executor_run(const gg_executor* ex, void* stream) {
 int gg_executor_problem_count(const gg_executor* ex) { return ex ? ex->problem_count : 0; }
 int gg_executor_total_tiles(const gg_executor* ex) { return ex ? ex->total_tiles : 0; }
 int gg_executor_grid_ctas(const gg_executor* ex) { return ex ? ex->grid_ctas : 0; }
+int gg_executor_launches(const gg_executor* ex) {
+  if (!ex || !ex->block || ex->total_tiles == 0 || ex->problem_count == 0) return 0;
+  int n = ex->realign_jobs > 0 ? 1 : 0;
+  for (int j = 0; j < ex->parts; ++j) n += ex->part[j].total_tiles > 0 ? 1 : 0;
+  return n;
+}
 
 int gg_executor_status(const gg_executor* ex, int* device_status) {
   if (!ex) return cudaErrorInvalidDevicePointer;

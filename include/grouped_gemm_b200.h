@@ -242,6 +242,10 @@ int gg_executor_run(const gg_executor* executor, void* stream);
 int gg_executor_problem_count(const gg_executor* executor);
 int gg_executor_total_tiles(const gg_executor* executor);
 int gg_executor_grid_ctas(const gg_executor* executor);
+/* No reference counterpart (its run is one launch). Kernel launches one gg_executor_run makes: 0
+ * with nothing to compute, 1, or with tile classes one per non-empty part plus one for the
+ * operand copies of the small-problem class. */
+int gg_executor_launches(const gg_executor* executor);
 
 /* No reference counterpart (the reference kernels cannot time out). Synchronises the device and
  * returns in *device_status the GG_STATUS_* bits raised by this executor's launches so far, then

@@ -419,6 +419,26 @@ def test_small_class_realigns_large_odd_pitches(cuda, fmt):
     assert check_full(ps, fmt=fmt) <= 1.0
 
 
+def test_executor_launches_per_run(cuda):
+    """gg_executor_launches: 1 without tile classes; with the small-problem class one launch per
+    non-empty part plus the operand copy when a problem is realigned."""
+    def launches(shapes, classes):
+        ps = W.allocate(shapes, cuda, seed=3)
+        cfg = gg.KernelConfig(128, 256, 64, tile_classes=classes)
+        ex = gg.GroupedGemmExecutor()
+        assert ex.build(gg.prepare_problem_set(ps.problems(), cfg, gg.SortMode.kByTiles), cfg) == 0
+        n = ex.launches()
+        ex.close()
+        return n
+    tiny = W.Shapes("t", [(5, 7, 9), (64, 64, 64)], [1.0] * 2, [0.0] * 2, True)
+    both = W.Shapes("b", [(5, 7, 9), (256, 256, 256)], [1.0] * 2, [0.0] * 2, True)
+    odd = W.Shapes("o", [(5, 7, 9), (321, 333, 345)], [1.0] * 2, [0.0] * 2, True)
+    assert launches(tiny, gg.TileClasses.kNone) == 1
+    assert launches(tiny, gg.TileClasses.kSmallOnCudaCores) == 1      # CUDA-core part only
+    assert launches(both, gg.TileClasses.kSmallOnCudaCores) == 2      # tensor-core + CUDA-core parts
+    assert launches(odd, gg.TileClasses.kSmallOnCudaCores) == 3       # + the operand copy
+
+
 def test_determinism_bitwise(cuda):
     torch = _torch()
     ps = W.allocate(W.make_shapes("mixed512"), cuda)
