@@ -715,7 +715,9 @@ int gg_executor_build_with_bias(gg_executor* ex, const gg_problem* sorted_proble
     bytes = off[j].bias + (bias ? im.bias.size() * sizeof(const float*) : 0);
   }
   const size_t counter_off = gg::round_up(bytes, 128);
-  bytes = counter_off + 128;  // counters at +0 (one int per part), status word at +64
+  bytes = counter_off + 128;  // tile counters at +0 (one int per part), finished-CTA counts at +8,
+                             // status word at +64; zero in the image, and every launch leaves them
+                             // zero for the next run
   const size_t jobs_off = bytes;
   bytes += jobs.size() * sizeof(gg::RealignJob);
   std::vector<unsigned char> image(bytes, 0);
@@ -768,6 +770,7 @@ int gg_executor_build_with_bias(gg_executor* ex, const gg_problem* sorted_proble
     kp.tmaps = reinterpret_cast<const CUtensorMap*>(base + off[j].maps);
     kp.tile_offsets = reinterpret_cast<const int*>(base + off[j].offs);
     kp.tile_counter = ex->d_counters + j;
+    kp.done_counter = ex->d_counters + 2 + j;  // the kernel clears both for the next run
     kp.status = ex->d_status;
     kp.timeout_ns = gg::wait_timeout_ns();
     kp.problem_count = part[j].problem_count;
@@ -790,10 +793,9 @@ int gg_executor_run(const gg_executor* ex, void* stream) {
   if (ex->total_tiles == 0 || ex->problem_count == 0) return cudaSuccess;
   if (!ex->block) return cudaErrorInvalidDevicePointer;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t st = cudaMemsetAsync(ex->d_counters, 0, 2 * sizeof(int), s);
-  if (st != cudaSuccess) return st;
+  // No counter reset here: the last CTA of each launch clears its part's counters (finish_launch).
   // this run's copies of the operands TMA cannot load, before the tensor-core part reads them
-  st = gg::launch_realign(ex->d_jobs, ex->realign_jobs, ex->realign_max_units, s);
+  cudaError_t st = gg::launch_realign(ex->d_jobs, ex->realign_jobs, ex->realign_max_units, s);
   if (st != cudaSuccess) return st;
   bool after_tc = false;  // a tensor-core part was launched before this one
   for (int j = 0; j < ex->parts; ++j) {

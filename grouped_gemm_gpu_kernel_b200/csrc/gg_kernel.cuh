@@ -125,7 +125,7 @@ __device__ __forceinline__ int claim_tile(const KernelParams& p, SchedState& ss,
     ss.static_next += stride;
     return t;
   }
-  return atomicAdd(p.tile_counter, 1);
+  return stride + atomicAdd(p.tile_counter, 1);  // tiles below stride are the CTAs' first tiles
 }
 
 __device__ __forceinline__ void sched_init(const KernelParams& p, SchedState& ss, int first_static, int stride,
@@ -137,7 +137,9 @@ __device__ __forceinline__ void sched_init(const KernelParams& p, SchedState& ss
   ss.q_end = 0;
   ss.w = 0;
   ss.cur = 0;
-  if (lane == 0) ss.cur = claim_tile(p, ss, stride);
+  // the first tile of a CTA is its index (no claim on the start-up path); later claims count
+  // from `stride`
+  if (lane == 0) ss.cur = p.single_mode ? claim_tile(p, ss, stride) : first_static;
 }
 
 // Next tile of this CTA (warp-collective): returns false when the work is exhausted, else the
@@ -1142,6 +1144,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_sm100_kernel(const _
   }
 
   __syncthreads();
+  if (threadIdx.x == 0) finish_launch(p);
   if (warp == kMmaWarp) {
     ptx::tc_fence_after_sync();
     ptx::tmem_dealloc(tmem_base, L::kTmemCols);

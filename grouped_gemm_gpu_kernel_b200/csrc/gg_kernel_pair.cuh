@@ -419,6 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Neither CTA leaves (or frees TMEM) while the other may still read or signal its shared memory.
   ptx::cluster_sync();
+  if (threadIdx.x == 0) finish_launch(p);
   if (*abort_flag) {
     // After an abort, loads issued by the other CTA may still be landing here: give them time.
     const uint64_t t0 = ptx::global_timer_ns();

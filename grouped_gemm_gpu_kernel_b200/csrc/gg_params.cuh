@@ -88,6 +88,9 @@ struct KernelParams {
   const CUtensorMap* tmaps;           // grouped launch: kMapsPerProblem maps per problem (64-byte aligned)
   const int* tile_offsets;            // grouped launch: problem_count + 1 prefix sums
   int* tile_counter;                  // grouped launch: claim counter, zero at launch
+  int* done_counter;                  // when set: CTAs of the launch that have finished; the last one
+                                      // sets tile_counter and this back to zero for the next launch
+                                      // (null: the host clears tile_counter before every launch)
   const int* total_tiles_dev;         // when set: the tile count, written on the device by an
                                       // earlier launch (device-side preparation); else total_tiles
   int* status;                        // GG_STATUS_* bits
@@ -102,5 +105,19 @@ struct KernelParams {
   int layout;         // bit 0: every A stored column-major (k x m); bit 1: every B column-major (n x k)
   const float* const* bias;  // per map slot: that problem's bias (n FP32 values) or null; null: none
 };
+
+#ifdef __CUDACC__
+// Called once per CTA (one thread) after the CTA's last tile claim: the last CTA of the grid to
+// get here clears the claim counter and the finished count, so the next launch with the same
+// counters needs no host-side reset before it.
+__device__ __forceinline__ void finish_launch(const KernelParams& p) {
+  if (!p.done_counter) return;
+  __threadfence();
+  if (atomicAdd(p.done_counter, 1) == static_cast<int>(gridDim.x) - 1) {
+    atomicExch(p.tile_counter, 0);
+    atomicExch(p.done_counter, 0);
+  }
+}
+#endif
 
 }  // namespace gg

@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(kSimtThreads, 3) grouped_gemm_simt_kernel(cons
         claimed = static_next;
         static_next += static_cast<int>(gridDim.x);
       } else {
-        claimed = atomicAdd(p.tile_counter, 1);
+        claimed = static_cast<int>(blockIdx.x);  // a CTA's first tile is its index: no claim at start
       }
     }
   }
@@ -178,7 +178,7 @@ __global__ void __launch_bounds__(kSimtThreads, 3) grouped_gemm_simt_kernel(cons
             claimed = static_next;
             static_next += static_cast<int>(gridDim.x);
           } else {
-            claimed = atomicAdd(p.tile_counter, 1);
+            claimed = static_cast<int>(gridDim.x) + atomicAdd(p.tile_counter, 1);
           }
         }
         if (!(cq >= 0 && tile >= cq_first && tile < cq_end)) {
@@ -208,7 +208,10 @@ __global__ void __launch_bounds__(kSimtThreads, 3) grouped_gemm_simt_kernel(cons
     }
     __syncthreads();
     const int q = s_work[0], tile_m = s_work[1], tile_n = s_work[2];
-    if (q < 0) break;
+    if (q < 0) {
+      if (tid == 0) finish_launch(p);  // warp 0 has made its last claim
+      break;
+    }
     const int m = s_desc.m, n = s_desc.n, k = s_desc.k;
     const __half* a = s_desc.a;
     const __half* b = s_desc.b;

@@ -233,9 +233,12 @@ int gg_executor_build_with_bias(gg_executor* executor, const gg_problem* sorted_
                                 const int* tile_offsets, int offsets_len, int total_tiles,
                                 const gg_config* config, const float* const* bias);
 
-/* reference src/grouped_gemm.cu:1241-1265 (GroupedGemmExecutor::run): resets the tile counter
- * and launches the persistent kernel on `stream`. Runs of one executor on two streams at the
- * same time race on its tile counter: use one executor per concurrent stream. */
+/* reference src/grouped_gemm.cu:1241-1265 (GroupedGemmExecutor::run): launches the persistent
+ * kernel on `stream` (with tile classes, its parts; see gg_executor_launches). The reference
+ * resets the tile counter with a memset before every launch; here the last CTA of each launch
+ * sets it back to zero for the next run, so a run is its kernel launches alone. Runs of one
+ * executor on two streams at the same time race on its tile counter: use one executor per
+ * concurrent stream. */
 int gg_executor_run(const gg_executor* executor, void* stream);
 
 /* reference src/grouped_gemm.cu:1267-1277 (problem_count / total_tiles / grid_ctas). */

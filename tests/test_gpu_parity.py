@@ -439,6 +439,35 @@ def test_executor_launches_per_run(cuda):
     assert launches(odd, gg.TileClasses.kSmallOnCudaCores) == 3       # + the operand copy
 
 
+@pytest.mark.parametrize("cfg", [gg.KernelConfig(128, 256, 64), gg.KernelConfig(256, 256, 64),
+                                 gg.KernelConfig(128, 64, 64, use_tensor_cores=False),
+                                 gg.KernelConfig(128, 256, 64, tile_classes=gg.TileClasses.kSmallOnCudaCores),
+                                 gg.KernelConfig(256, 256, 64, tile_classes=gg.TileClasses.kPairBlocks)],
+                         ids=_cfg_id)
+def test_runs_back_to_back_reset_their_own_counters(cuda, cfg):
+    """An executor run is its kernel launches alone: the last CTA of each launch sets the tile
+    counter back to zero. Five runs in a row on one stream, with no host work between them, each
+    writing D from NaN: every run computes every tile (bit-identical D each time)."""
+    torch = _torch()
+    shapes = W.Shapes("mix", [(200, 300, 100), (7, 9, 11), (513, 129, 64), (64, 64, 64), (1, 1000, 33)],
+                      [1.0] * 5, [0.5] * 5, True)
+    ps = W.allocate(shapes, cuda, seed=5)
+    ex = gg.GroupedGemmExecutor()
+    assert ex.build(gg.prepare_problem_set(ps.problems(), cfg, gg.SortMode.kByTiles), cfg) == 0
+    stream = torch.cuda.current_stream()
+    outs = []
+    for _ in range(5):
+        ps.d.fill_(float("nan"))
+        assert ex.run(stream) == 0
+        outs.append(ps.d.clone())
+    torch.cuda.synchronize()
+    assert ex.status() == 0
+    ex.close()
+    for o in outs[1:]:
+        assert torch.equal(o.view(torch.int32), outs[0].view(torch.int32))
+    assert check_full(ps) <= 1.0
+
+
 def test_determinism_bitwise(cuda):
     torch = _torch()
     ps = W.allocate(W.make_shapes("mixed512"), cuda)
