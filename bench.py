@@ -526,7 +526,7 @@ def main():
         raise RuntimeError("a bounded wait timed out inside the kernel during the timed region")
     ms = max_over_ranks(local_ms)
     value = global_flops / (ms * 1e-3) / 1e12
-    # The survey's timing protocol as well: the median of 5 repeats of max(50, K) steps each.
+    # A second protocol beside the K timed steps: the median of 5 repeats of max(50, K) steps each.
     rep_med, rep_min, rep_max = timer.median_of(ex.run, max(50, args.steps), flush)
     rep_med, rep_min, rep_max = max_over_ranks(rep_med), max_over_ranks(rep_min), max_over_ranks(rep_max)
     protocol = {"repeats": 5, "steps_per_repeat": max(50, args.steps), "median_ms": rep_med, "min_ms": rep_min,
